@@ -1,0 +1,268 @@
+"""fence_b200 — Python view of libfence_b200.so, the B200 (sm_100a) decode engine for Fence's GGUF
+token loop.
+
+The product is the C-ABI shared library built next to this file (``make``); this module only binds
+it with ctypes for the test suite and the benchmark. Everything the library computes runs in its
+own CUDA kernels: if the library is missing, importing this module raises instead of falling back.
+
+Device buffers are passed as raw addresses (e.g. ``torch.Tensor.data_ptr()``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfence_b200.so")
+
+FENCE_KV_BF16 = 0
+FENCE_KV_F16 = 1
+GGML_Q8_0 = 8
+GGML_Q6_K = 14
+
+_c_float_p = ctypes.POINTER(ctypes.c_float)
+_c_int_p = ctypes.POINTER(ctypes.c_int)
+_vp = ctypes.c_void_p
+
+
+class FenceError(RuntimeError):
+    """A fence_* call returned a non-zero status."""
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int), ("embed_dim", ctypes.c_int), ("ff_dim", ctypes.c_int),
+        ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("vocab_size", ctypes.c_int), ("max_ctx", ctypes.c_int),
+        ("rope_freq_base", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("top_k", ctypes.c_int),
+        ("repetition_penalty", ctypes.c_float), ("min_p", ctypes.c_float), ("dynamic_temp", ctypes.c_int),
+        ("linear_type", ctypes.c_int), ("embd_type", ctypes.c_int), ("has_qk_norm", ctypes.c_int),
+        ("n_experts", ctypes.c_int), ("n_experts_used", ctypes.c_int), ("kv_dtype", ctypes.c_int),
+        ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("weight_bytes", ctypes.c_size_t),
+    ]
+
+
+class LoadOpts(ctypes.Structure):
+    _fields_ = [
+        ("max_ctx", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("device", ctypes.c_int),
+        ("use_graph", ctypes.c_int), ("verbose", ctypes.c_int), ("tp_rank", ctypes.c_int),
+        ("tp_size", ctypes.c_int), ("nccl_comm", ctypes.c_void_p),
+    ]
+
+
+class SynthSpec(ctypes.Structure):
+    _fields_ = [
+        ("arch", ctypes.c_char_p),
+        ("n_layers", ctypes.c_int), ("embed_dim", ctypes.c_int), ("ff_dim", ctypes.c_int),
+        ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("vocab_size", ctypes.c_int), ("rope_freq_base", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("linear_type", ctypes.c_int), ("embd_type", ctypes.c_int), ("qk_norm", ctypes.c_int),
+        ("n_experts", ctypes.c_int), ("n_experts_used", ctypes.c_int), ("write_tokenizer", ctypes.c_int),
+        ("gguf_version", ctypes.c_int), ("alignment", ctypes.c_uint32), ("seed", ctypes.c_uint64),
+        ("q6k_d", ctypes.c_float), ("q8_d", ctypes.c_float), ("norm_value", ctypes.c_float),
+    ]
+
+
+# (name, restype, argtypes) of every symbol declared in include/fence_b200.h
+SIGNATURES = [
+    ("fence_last_error", ctypes.c_char_p, []),
+    ("fence_device_error", ctypes.c_int, []),
+    ("fence_gemv_q6k", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("fence_gemv_q6k_bias", ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("fence_gemv_q8_0", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("fence_embed_q8_0", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
+    ("fence_rms_norm", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_float, _vp]),
+    ("fence_rms_norm_inplace", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_float, _vp]),
+    ("fence_rms_norm_per_head", ctypes.c_int, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("fence_apply_rope", ctypes.c_int,
+     [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp]),
+    ("fence_silu_elementwise_mul", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp]),
+    ("fence_residual_add", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_softmax", ctypes.c_int, [_vp, ctypes.c_int, _vp]),
+    ("fence_f32_to_f16", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_float_to_half", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_half_to_float", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_store_kv", ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
+    ("fence_gqa_attention", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]),
+    ("fence_argmax", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_load_opts_default", None, [ctypes.POINTER(LoadOpts)]),
+    ("fence_model_load", _vp, [ctypes.c_char_p, ctypes.POINTER(LoadOpts)]),
+    ("fence_model_free", None, [_vp]),
+    ("fence_model_config", ctypes.c_int, [_vp, ctypes.POINTER(Config)]),
+    ("fence_set_sampling", ctypes.c_int, [_vp, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_float]),
+    ("fence_forward", _vp, [_vp, ctypes.c_int, ctypes.c_int]),
+    ("fence_sample_greedy", ctypes.c_int, [_vp, _vp]),
+    ("fence_sample_nucleus", ctypes.c_int, [_vp, _vp, _c_int_p, ctypes.c_int]),
+    ("fence_set_seed", ctypes.c_int, [_vp, ctypes.c_uint64]),
+    ("fence_generate", ctypes.c_int,
+     [_vp, _c_int_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_int_p, ctypes.c_int, _c_int_p]),
+    ("fence_decode_greedy", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_int_p]),
+    ("fence_copy_logits", ctypes.c_int, [_vp, _c_float_p]),
+    ("fence_time_decode", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_float_p]),
+    ("fence_synth_spec_default", None, [ctypes.POINTER(SynthSpec)]),
+    ("fence_synth_write_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), ctypes.c_int]),
+    ("fence_synth_fill_blocks", ctypes.c_int,
+     [_vp, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
+]
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libfence_b200.so (once) and declares every exported signature."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run `make` in {HERE}")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, res, args in SIGNATURES:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return (lib().fence_last_error() or b"").decode(errors="replace")
+
+
+def check(rc: int, what: str = "fence call") -> None:
+    if rc != 0:
+        raise FenceError(f"{what} failed ({rc}): {last_error()}")
+
+
+def call(name: str, *args) -> None:
+    """Calls a status-returning entry point and raises FenceError on a non-zero status."""
+    check(getattr(lib(), name)(*args), name)
+
+
+# ------------------------------------------------------------------ synthetic models
+CONFIGS = {
+    # config 1: Qwen3-4B shape, Q6_K linears, Q8_0 embedding
+    "qwen3-4b": dict(arch=b"qwen3", n_layers=36, embed_dim=2560, ff_dim=9728, n_heads=32, n_kv_heads=8,
+                     head_dim=128, vocab_size=151936, rope_freq_base=1e6, rms_eps=1e-6,
+                     linear_type=GGML_Q6_K, qk_norm=1),
+    # config 2: Llama-3.1-8B shape, all Q8_0, no q/k-norm
+    "llama3-8b-q8": dict(arch=b"llama", n_layers=32, embed_dim=4096, ff_dim=14336, n_heads=32, n_kv_heads=8,
+                         head_dim=128, vocab_size=128256, rope_freq_base=5e5, rms_eps=1e-5,
+                         linear_type=GGML_Q8_0, qk_norm=0),
+    # config 3: Qwen3-14B shape, Q6_K linears
+    "qwen3-14b": dict(arch=b"qwen3", n_layers=40, embed_dim=5120, ff_dim=17408, n_heads=40, n_kv_heads=8,
+                      head_dim=128, vocab_size=151936, rope_freq_base=1e6, rms_eps=1e-6,
+                      linear_type=GGML_Q6_K, qk_norm=1),
+    # small shapes for fast parity runs
+    "tiny-q6k": dict(arch=b"qwen3", n_layers=2, embed_dim=512, ff_dim=1024, n_heads=8, n_kv_heads=2,
+                     head_dim=128, vocab_size=2048, rope_freq_base=1e6, rms_eps=1e-6,
+                     linear_type=GGML_Q6_K, qk_norm=1),
+    "tiny-q8": dict(arch=b"llama", n_layers=2, embed_dim=512, ff_dim=1024, n_heads=8, n_kv_heads=2,
+                    head_dim=128, vocab_size=2048, rope_freq_base=5e5, rms_eps=1e-5,
+                    linear_type=GGML_Q8_0, qk_norm=0),
+}
+
+
+def synth_spec(**kw) -> SynthSpec:
+    s = SynthSpec()
+    lib().fence_synth_spec_default(ctypes.byref(s))
+    for k, v in kw.items():
+        setattr(s, k, v)
+    return s
+
+
+def synth_write(path: str, config: str | None = None, threads: int = 0, **kw) -> None:
+    """Writes a seeded synthetic GGUF model (one of CONFIGS, overridden by keyword fields)."""
+    fields = dict(CONFIGS[config]) if config else {}
+    fields.update(kw)
+    spec = synth_spec(**fields)
+    check(lib().fence_synth_write_gguf(path.encode(), ctypes.byref(spec), threads), "synth_write_gguf")
+
+
+def synth_blocks(ggml_type: int, n_blocks: int, seed: int, stream: int = 0, d: float | None = None) -> bytes:
+    if d is None:
+        d = 1.5e-5 if ggml_type == GGML_Q6_K else 1.6e-4
+    size = n_blocks * (210 if ggml_type == GGML_Q6_K else 34)
+    buf = ctypes.create_string_buffer(size)
+    check(lib().fence_synth_fill_blocks(buf, ggml_type, n_blocks, seed, stream, d), "synth_fill_blocks")
+    return buf.raw
+
+
+# ------------------------------------------------------------------ engine
+class Model:
+    """The reference's Qwen3Model API over the engine handle."""
+
+    def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_BF16, device: int = 0,
+                 use_graph: bool = True, verbose: bool = False):
+        L = lib()
+        o = LoadOpts()
+        L.fence_load_opts_default(ctypes.byref(o))
+        o.max_ctx, o.kv_dtype, o.device, o.use_graph, o.verbose = max_ctx, kv_dtype, device, int(use_graph), int(verbose)
+        h = L.fence_model_load(path.encode(), ctypes.byref(o))
+        if not h:
+            raise FenceError(f"model load failed: {last_error()}")
+        self._h = h
+        c = Config()
+        check(L.fence_model_config(h, ctypes.byref(c)), "model_config")
+        self.config = c
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().fence_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, token: int, pos: int) -> int:
+        p = lib().fence_forward(self._h, token, pos)
+        if not p:
+            raise FenceError(f"forward failed: {last_error()}")
+        return p
+
+    def logits(self):
+        import numpy as np
+        out = np.empty(self.config.vocab_size, dtype=np.float32)
+        check(lib().fence_copy_logits(self._h, out.ctypes.data_as(_c_float_p)), "copy_logits")
+        return out
+
+    def sample_greedy(self, d_logits: int) -> int:
+        r = lib().fence_sample_greedy(self._h, d_logits)
+        if r < 0:
+            raise FenceError(last_error())
+        return r
+
+    def sample_nucleus(self, d_logits: int, history) -> int:
+        arr = (ctypes.c_int * len(history))(*history)
+        r = lib().fence_sample_nucleus(self._h, d_logits, arr, len(history))
+        if r < 0:
+            raise FenceError(last_error())
+        return r
+
+    def set_sampling(self, temperature: float, top_p: float, top_k: int, rep_penalty: float) -> None:
+        check(lib().fence_set_sampling(self._h, temperature, top_p, top_k, rep_penalty), "set_sampling")
+
+    def set_seed(self, seed: int) -> None:
+        check(lib().fence_set_seed(self._h, seed), "set_seed")
+
+    def generate(self, prompt, max_new: int, eos_id: int = -1):
+        n = len(prompt)
+        arr = (ctypes.c_int * n)(*prompt)
+        cap = n + max_new + 1
+        out = (ctypes.c_int * cap)()
+        n_out = ctypes.c_int(0)
+        check(lib().fence_generate(self._h, arr, n, max_new, eos_id, out, cap, ctypes.byref(n_out)), "generate")
+        return list(out[: n_out.value])
+
+    def decode_greedy(self, token: int, pos: int, n_steps: int):
+        out = (ctypes.c_int * max(n_steps, 1))()
+        check(lib().fence_decode_greedy(self._h, token, pos, n_steps, out), "decode_greedy")
+        return list(out[:n_steps])
+
+    def time_decode(self, token: int, pos: int, n_steps: int) -> float:
+        ms = ctypes.c_float(0)
+        check(lib().fence_time_decode(self._h, token, pos, n_steps, ctypes.byref(ms)), "time_decode")
+        return ms.value

@@ -1,0 +1,388 @@
+// attention.cuh — single-query grouped-query attention over a KV cache, split over the context
+// (flash-decode), for sm_100a.
+//
+// Reference semantics (src/kernels/ops.cuh:320-403): for query head qh with kv head
+// qh / (Hq/Hkv): s_t = (q . k_t) * head_dim^-1/2 for t < seq_len; p = softmax(s); out = sum_t p_t v_t,
+// all in fp32 over an fp16 cache. The reference runs one CTA per query head over the whole
+// context with thread-per-position dot products and re-reads every K/V row once per query head.
+//
+// Here one CTA handles one KV head and one chunk of positions for ALL query heads of its group,
+// so every K/V byte is read from HBM once per token. Each CTA writes the chunk's running max,
+// exp-sum and unnormalised output; chunks are merged in a fixed order (deterministic).
+//  * K/V rows are staged in shared memory with 16-byte cp.async copies whose chunk index is XORed
+//    with (row & 7), which makes the thread-per-position reads of K conflict-free.
+//  * Fused engine mode additionally: applies q/k RMSNorm (ops.cuh:66-95) and NeoX RoPE
+//    (ops.cuh:115-167) to the raw QKV-GEMV output, writes the new K/V row of position `pos` into the
+//    cache (ops.cuh:419-433) — the CTA owning that position uses the rounded values itself — and
+//    the last CTA of each KV head merges the chunks (arrival counter), so attention is one launch.
+//    The chunk length adapts to the context so short contexts still spread over many SMs.
+//  * KV element type: fp16 (reference numerics) or bf16.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace fence {
+
+constexpr int ATTN_THREADS = 128;
+constexpr int ATTN_CMAX = 128;  // positions per shared-memory tile
+constexpr int ATTN_MAX_G = 8;   // query heads per KV head supported
+
+template <typename T>
+struct KVConv;
+template <>
+struct KVConv<__half> {
+    static __device__ __forceinline__ __half from(float f) { return __float2half_rn(f); }
+    static __device__ __forceinline__ float to(__half h) { return __half2float(h); }
+    static __device__ __forceinline__ float2 pair(uint32_t w) {
+        return __half22float2(*reinterpret_cast<const __half2*>(&w));
+    }
+};
+template <>
+struct KVConv<__nv_bfloat16> {
+    static __device__ __forceinline__ __nv_bfloat16 from(float f) { return __float2bfloat16_rn(f); }
+    static __device__ __forceinline__ float to(__nv_bfloat16 h) { return __bfloat162float(h); }
+    static __device__ __forceinline__ float2 pair(uint32_t w) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
+};
+
+struct AttnArgs {
+    const float* q;       // [Hq*HD]: final q (drop-in) or raw q from the QKV GEMV (fused)
+    const void* kc;       // K cache base (element type KVT)
+    const void* vc;
+    long long stride_t;   // elements between positions
+    long long stride_h;   // elements between KV heads
+    int n_q_heads, n_kv_heads;
+    int seq_len;          // drop-in: positions [0, seq_len)
+    int nchunk;           // chunks per KV head in the grid (gridDim.x)
+    int chunk_fixed;      // drop-in: positions per chunk; 0 = adaptive (fused)
+    float* part;          // [Hkv][nchunk][G][HD+2] partials
+    // fused mode
+    const DecodeState* state;
+    const float* k_new;   // raw k [Hkv*HD] of position pos
+    const float* v_new;
+    void* kc_w;           // writable cache bases (same as kc/vc)
+    void* vc_w;
+    const float* q_norm_w;  // [HD] or null
+    const float* k_norm_w;
+    float eps;
+    const float2* rope;   // [max_ctx][HD/2] (cos, sin) table
+    float* out;           // [Hq*HD] merged output (fp32)
+    unsigned int* counter;  // [Hkv] arrival counters, zero between launches
+};
+
+__device__ __forceinline__ int attn_chunk_len(int seq_len, int nchunk) {
+    // smallest multiple of 16 with ceil(seq_len / C) <= nchunk, capped at ATTN_CMAX
+    int c = (seq_len + nchunk - 1) / nchunk;
+    c = (c + 15) & ~15;
+    if (c < 16) c = 16;
+    if (c > ATTN_CMAX) c = ATTN_CMAX;
+    return c;
+}
+
+// RMSNorm of one head (HD values in smem row) by a warp, weight w[HD]; reference order w*x*rms.
+template <int HD>
+__device__ __forceinline__ void head_rmsnorm_warp(float* v, const float* w, float eps, int lane) {
+    float ss = 0.f;
+    for (int d = lane; d < HD; d += 32) ss += v[d] * v[d];
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / (float)HD + eps);
+    __syncwarp();
+    for (int d = lane; d < HD; d += 32) v[d] = w[d] * v[d] * r;
+    __syncwarp();
+}
+// NeoX rotation of one head in smem with table row cs[HD/2].
+template <int HD>
+__device__ __forceinline__ void head_rope_warp(float* v, const float2* cs, int lane) {
+    for (int i = lane; i < HD / 2; i += 32) {
+        const float2 t = cs[i];
+        const float a = v[i], b = v[i + HD / 2];
+        v[i] = a * t.x - b * t.y;
+        v[i + HD / 2] = a * t.y + b * t.x;
+    }
+    __syncwarp();
+}
+
+template <typename KVT, int HD, bool FUSED>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid_constant__ AttnArgs a) {
+    using C = KVConv<KVT>;
+    constexpr int CH = HD * (int)sizeof(KVT) / 16;  // 16-byte chunks per row
+    constexpr int EPC = 16 / (int)sizeof(KVT);      // elements per chunk
+    constexpr int KP = (ATTN_MAX_G * HD / 2 + ATTN_THREADS - 1) / ATTN_THREADS;  // PV pairs per thread
+    static_assert(CH >= 8, "head_dim too small for the swizzle");
+    extern __shared__ __align__(128) uint8_t sm[];
+    KVT* sk = reinterpret_cast<KVT*>(sm);
+    KVT* sv = sk + ATTN_CMAX * HD;
+    float* sq = reinterpret_cast<float*>(sv + ATTN_CMAX * HD);  // [G][HD]
+    float* ss = sq + ATTN_MAX_G * HD;                            // [G][CMAX]
+    float* smax = ss + ATTN_MAX_G * ATTN_CMAX;                   // [G] running max
+    float* ssum = smax + ATTN_MAX_G;                             // [G] running exp-sum
+    float* sresc = ssum + ATTN_MAX_G;                            // [G] rescale of the old accumulator
+    int* sflag = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int h = blockIdx.y;
+    const int G = a.n_q_heads / a.n_kv_heads;
+    int seq_len, pos, clen;
+    if (FUSED) {
+        pos = a.state->pos;
+        seq_len = pos + 1;
+        clen = attn_chunk_len(seq_len, a.nchunk);
+    } else {
+        seq_len = a.seq_len;
+        pos = seq_len - 1;
+        clen = a.chunk_fixed;
+    }
+    const int n_active = (seq_len + clen - 1) / clen;
+    const int c = blockIdx.x;
+    if (c >= n_active) {
+        if (tid == 0) pdl_launch_dependents();
+        return;
+    }
+    const int t0 = c * clen;
+    const int t1 = min(t0 + clen, seq_len);
+    const bool owns_new = FUSED && (pos >= t0 && pos < t1);  // fused: clen <= ATTN_CMAX, one tile
+
+    const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
+    const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
+    auto stage_tile = [&](int ts, int te) {
+        for (int idx = tid; idx < (te - ts) * CH; idx += ATTN_THREADS) {
+            const int r = idx / CH, ch = idx - r * CH;
+            const int t = ts + r;
+            const int pch = ch ^ (r & 7);
+            cp_async16(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16,
+                       reinterpret_cast<const uint8_t*>(kb + (long long)t * a.stride_t) + ch * 16);
+            cp_async16(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16,
+                       reinterpret_cast<const uint8_t*>(vb + (long long)t * a.stride_t) + ch * 16);
+        }
+        cp_async_commit();
+    };
+
+    // ---- first tile of cached rows: independent of the preceding kernel, issued before the wait
+    {
+        const int te = min(t0 + ATTN_CMAX, t1);
+        stage_tile(t0, owns_new ? pos : te);
+    }
+    if (tid == 0) pdl_launch_dependents();
+    pdl_wait();
+
+    // ---- q for the G heads of this group (normed + rotated in fused mode)
+    const int qh0 = h * G;
+    for (int i = tid; i < G * HD; i += ATTN_THREADS) sq[i] = a.q[(long long)qh0 * HD + i];
+    if (tid < ATTN_MAX_G) {
+        smax[tid] = -INFINITY;
+        ssum[tid] = 0.f;
+    }
+    __syncthreads();
+    if (FUSED) {
+        const float2* cs = a.rope + (long long)pos * (HD / 2);
+        for (int g = warp; g < G; g += ATTN_THREADS / 32) {
+            if (a.q_norm_w) head_rmsnorm_warp<HD>(sq + g * HD, a.q_norm_w, a.eps, lane);
+            head_rope_warp<HD>(sq + g * HD, cs, lane);
+        }
+        if (owns_new && warp == (ATTN_THREADS / 32) - 1) {
+            // new K row: norm + rope in fp32, round to the cache type, store; V row: round + store
+            float* kt = ss;  // borrow score space (HD floats)
+            for (int d = lane; d < HD; d += 32) kt[d] = a.k_new[(long long)h * HD + d];
+            __syncwarp();
+            if (a.k_norm_w) head_rmsnorm_warp<HD>(kt, a.k_norm_w, a.eps, lane);
+            head_rope_warp<HD>(kt, cs, lane);
+            KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+            KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+            const int r = pos - t0;
+            for (int d = lane; d < HD; d += 32) {
+                const KVT kq = C::from(kt[d]);
+                const KVT vq = C::from(a.v_new[(long long)h * HD + d]);
+                kw[d] = kq;
+                vw[d] = vq;
+                const int ch = d / EPC, within = d % EPC;
+                const int pch = ch ^ (r & 7);
+                reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16)[within] = kq;
+                reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16)[within] = vq;
+            }
+        }
+    }
+
+    const float scale = 1.0f / sqrtf((float)HD);
+    float o[KP][2];
+#pragma unroll
+    for (int k = 0; k < KP; ++k) o[k][0] = o[k][1] = 0.f;
+
+    for (int ts = t0; ts < t1; ts += ATTN_CMAX) {
+        const int te = min(ts + ATTN_CMAX, t1);
+        const int nt = te - ts;
+        if (ts != t0) stage_tile(ts, te);
+        cp_async_wait_all();
+        __syncthreads();
+
+        // ---- scores: thread <-> position
+        for (int r = tid; r < nt; r += ATTN_THREADS) {
+            float acc[ATTN_MAX_G];
+#pragma unroll
+            for (int g = 0; g < ATTN_MAX_G; ++g) acc[g] = 0.f;
+            const uint8_t* krow = reinterpret_cast<const uint8_t*>(sk + r * HD);
+            for (int ch = 0; ch < CH; ++ch) {
+                const uint4 w = *reinterpret_cast<const uint4*>(krow + ((ch ^ (r & 7)) * 16));
+                float kf[8];
+                const float2 f0 = C::pair(w.x), f1 = C::pair(w.y), f2 = C::pair(w.z), f3 = C::pair(w.w);
+                kf[0] = f0.x; kf[1] = f0.y; kf[2] = f1.x; kf[3] = f1.y;
+                kf[4] = f2.x; kf[5] = f2.y; kf[6] = f3.x; kf[7] = f3.y;
+#pragma unroll
+                for (int g = 0; g < ATTN_MAX_G; ++g) {
+                    if (g < G) {
+                        const float* qg = sq + g * HD + ch * EPC;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[g] = fmaf(qg[e], kf[e], acc[g]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < ATTN_MAX_G; ++g)
+                if (g < G) ss[g * ATTN_CMAX + r] = acc[g] * scale;
+        }
+        __syncthreads();
+
+        // ---- online softmax statistics per head (warp per head)
+        for (int g = warp; g < G; g += ATTN_THREADS / 32) {
+            float m = -INFINITY;
+            for (int t = lane; t < nt; t += 32) m = fmaxf(m, ss[g * ATTN_CMAX + t]);
+            m = warp_max(m);
+            const float m_old = smax[g];
+            const float m_new = fmaxf(m_old, m);
+            float l = 0.f;
+            for (int t = lane; t < nt; t += 32) {
+                const float e = expf(ss[g * ATTN_CMAX + t] - m_new);
+                ss[g * ATTN_CMAX + t] = e;
+                l += e;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                sresc[g] = f;
+                ssum[g] = ssum[g] * f + l;
+                smax[g] = m_new;
+            }
+        }
+        __syncthreads();
+
+        // ---- P.V accumulate: thread <-> (head, dim pair)
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+            const int pidx = tid + k * ATTN_THREADS;
+            if (pidx < G * (HD / 2)) {
+                const int g = pidx / (HD / 2);
+                const int d = 2 * (pidx - g * (HD / 2));
+                const int ch = d / EPC, within = d % EPC;
+                const float f = sresc[g];
+                float o0 = o[k][0] * f, o1 = o[k][1] * f;
+                const float* pg = ss + g * ATTN_CMAX;
+                for (int r = 0; r < nt; ++r) {
+                    const uint32_t w = *reinterpret_cast<const uint32_t*>(
+                        reinterpret_cast<const uint8_t*>(sv + r * HD) + ((ch ^ (r & 7)) * 16) + within * sizeof(KVT));
+                    const float2 vv = C::pair(w);
+                    const float pr = pg[r];
+                    o0 = fmaf(pr, vv.x, o0);
+                    o1 = fmaf(pr, vv.y, o1);
+                }
+                o[k][0] = o0;
+                o[k][1] = o1;
+            }
+        }
+        __syncthreads();  // before the next tile overwrites sk/sv/ss
+    }
+
+    const int part_stride = HD + 2;
+    if (!FUSED && n_active == 1) {
+        // whole context in one chunk: normalise and write the output directly
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+            const int pidx = tid + k * ATTN_THREADS;
+            if (pidx < G * (HD / 2)) {
+                const int g = pidx / (HD / 2);
+                const int d = 2 * (pidx - g * (HD / 2));
+                const float inv = 1.0f / ssum[g];
+                a.out[(long long)(qh0 + g) * HD + d] = o[k][0] * inv;
+                a.out[(long long)(qh0 + g) * HD + d + 1] = o[k][1] * inv;
+            }
+        }
+        return;
+    }
+
+    float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * part_stride;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int pidx = tid + k * ATTN_THREADS;
+        if (pidx < G * (HD / 2)) {
+            const int g = pidx / (HD / 2);
+            const int d = 2 * (pidx - g * (HD / 2));
+            pbase[g * part_stride + d] = o[k][0];
+            pbase[g * part_stride + d + 1] = o[k][1];
+        }
+    }
+    if (tid < G) {
+        pbase[tid * part_stride + HD] = smax[tid];
+        pbase[tid * part_stride + HD + 1] = ssum[tid];
+    }
+
+    if (FUSED) {
+        // ---- last CTA of this KV head merges all chunks
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned prev = atomicAdd(&a.counter[h], 1u);
+            *sflag = (prev == (unsigned)n_active - 1) ? 1 : 0;
+        }
+        __syncthreads();
+        if (*sflag) {
+            __threadfence();
+            const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
+            for (int pidx = tid; pidx < G * HD; pidx += ATTN_THREADS) {
+                const int g = pidx / HD, d = pidx - g * HD;
+                float M = -INFINITY;
+                for (int cc = 0; cc < n_active; ++cc)
+                    M = fmaxf(M, ((volatile const float*)hb)[((long long)cc * G + g) * part_stride + HD]);
+                float L = 0.f, O = 0.f;
+                for (int cc = 0; cc < n_active; ++cc) {
+                    const volatile float* pr = hb + ((long long)cc * G + g) * part_stride;
+                    const float f = expf(pr[HD] - M);
+                    L += pr[HD + 1] * f;
+                    O += pr[d] * f;
+                }
+                a.out[(long long)(qh0 + g) * HD + d] = O / L;
+            }
+            if (tid == 0) a.counter[h] = 0u;
+        }
+    }
+}
+
+// Drop-in merge: one CTA per query head, thread per dimension.
+template <int HD>
+__global__ void attn_merge_kernel(const float* __restrict__ part, float* __restrict__ out, int n_q_heads,
+                                  int n_kv_heads, int nchunk, int n_active) {
+    const int qh = blockIdx.x;
+    const int G = n_q_heads / n_kv_heads;
+    const int h = qh / G, g = qh - h * G;
+    const int part_stride = HD + 2;
+    const float* hb = part + ((long long)h * nchunk * G) * part_stride;
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+        float M = -INFINITY;
+        for (int cc = 0; cc < n_active; ++cc) M = fmaxf(M, hb[((long long)cc * G + g) * part_stride + HD]);
+        float L = 0.f, O = 0.f;
+        for (int cc = 0; cc < n_active; ++cc) {
+            const float* pr = hb + ((long long)cc * G + g) * part_stride;
+            const float f = expf(pr[HD] - M);
+            L += pr[HD + 1] * f;
+            O += pr[d] * f;
+        }
+        out[(long long)qh * HD + d] = O / L;
+    }
+}
+
+template <typename KVT, int HD>
+constexpr int attn_smem_bytes() {
+    return 2 * ATTN_CMAX * HD * (int)sizeof(KVT) + ATTN_MAX_G * HD * 4 + ATTN_MAX_G * ATTN_CMAX * 4 +
+           (3 * ATTN_MAX_G + 8) * 4;
+}
+
+}  // namespace fence

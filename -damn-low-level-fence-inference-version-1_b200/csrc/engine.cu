@@ -1,0 +1,790 @@
+// engine.cu — the batch-1 decode engine: the reference's Qwen3Model (src/model/qwen3.h:115-155,
+// src/model/qwen3.cu:47-519) rebuilt around the fused sm_100a kernels.
+//
+// Token step (reference order qwen3.cu:241-341, ~16 launches and ~9 device syncs per layer there):
+//   embed(token read from device state)
+//   per layer:
+//     1. QKV GEMV      prologue RMSNorm(attn_norm) [+fp16 rounding for Q6_K]; q, k, v in one launch
+//     2. attention     q/k-norm + RoPE + KV-cache store + split-context attention + merge
+//     3. O GEMV        prologue fp32 -> [fp16]; epilogue hidden += (residual add)
+//     4. gate/up GEMV  prologue RMSNorm(ffn_norm); epilogue SwiGLU -> act (fp16 for a Q6_K down)
+//     5. down GEMV     epilogue hidden +=
+//   LM head (tied token_embd, Q8_0)  prologue RMSNorm(output_norm); epilogue logits + argmax; the
+//   last CTA writes the sampled id and pos+1 into the device decode state.
+// Five launches per layer, chained with programmatic dependent launch so each kernel streams its
+// weights while the previous one drains, all captured once in a CUDA graph that is replayed per
+// token with no host synchronisation.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "gguf.h"
+#include "host.h"
+
+namespace fence {
+
+GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas);
+void fill_plan(GemvArgs& a, const GemvPlan& pl);
+template <int WT, int XM, int EPI>
+cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t st, bool pdl);
+int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
+                        float top_p, int top_k, float rep_penalty, float min_p, bool dynamic_temp,
+                        std::mt19937& rng);
+
+struct LayerW {
+    const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
+    const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
+    int t_qkv = 14, t_o = 14, t_gu = 14, t_down = 14;  // GGML type ids
+    const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    const float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
+};
+
+struct LayerLaunch {
+    GemvArgs qkv, o, gu, down;
+    GemvPlan pqkv, po, pgu, pdown;
+    AttnArgs attn;
+};
+
+}  // namespace fence
+
+using namespace fence;
+
+struct fence_model {
+    fence_config cfg{};
+    fence_load_opts opts{};
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    GGUFFile gguf;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    std::vector<LayerW> layers;
+    const uint8_t* tok_embd = nullptr;
+    const float* out_norm = nullptr;
+    void* kcache = nullptr;
+    void* vcache = nullptr;
+    float *hidden = nullptr, *qkv = nullptr, *attn_out = nullptr, *logits = nullptr, *attn_part = nullptr;
+    void* act = nullptr;
+    unsigned int* counters = nullptr;  // [Hkv] attention + [1] LM head
+    float* lm_val = nullptr;
+    int* lm_idx = nullptr;
+    DecodeState* state = nullptr;
+    int* token_log = nullptr;
+    int token_log_cap = 0;
+    float2* rope = nullptr;
+    DecodeState* h_state = nullptr;  // pinned staging ring
+    int h_state_n = 0;
+    int* h_token = nullptr;          // pinned
+    std::vector<LayerLaunch> launches;
+    GemvArgs lm;
+    GemvPlan plm{};
+    int attn_nchunk = 0;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    std::mt19937 rng{0x5eed};
+    std::vector<float> h_logits;
+};
+
+namespace {
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int wtype_id(GGMLType t) { return (int)t; }
+
+// ---- one launch of the GEMV template selected by weight type / modes
+cudaError_t gemv_dispatch(int gtype, int xm, int epi, const GemvArgs& a, const GemvPlan& pl, cudaStream_t st) {
+#define CASE(WT, XM, EPI) \
+    if (wt == WT && xm == XM && epi == EPI) return launch_gemv<WT, XM, EPI>(a, pl, st, true);
+    const int wt = gtype == 14 ? WT_Q6K : WT_Q80;
+    CASE(WT_Q6K, X_NORM_R16, EPI_STORE)
+    CASE(WT_Q80, X_NORM, EPI_STORE)
+    CASE(WT_Q6K, X_F32_R16, EPI_RESID)
+    CASE(WT_Q80, X_F32, EPI_RESID)
+    CASE(WT_Q6K, X_NORM_R16, EPI_SWIGLU)
+    CASE(WT_Q80, X_NORM, EPI_SWIGLU)
+    CASE(WT_Q6K, X_F16, EPI_RESID)
+    CASE(WT_Q80, X_NORM, EPI_LMHEAD)
+    CASE(WT_Q6K, X_NORM, EPI_LMHEAD)
+#undef CASE
+    return cudaErrorInvalidValue;
+}
+
+__global__ void embed_state_kernel(float* __restrict__ out, const uint8_t* __restrict__ W,
+                                   const DecodeState* __restrict__ st, int dim) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    const int t = st->token;
+    const uint8_t* blk = W + ((size_t)t * (dim / 32) + i / 32) * 34;
+    out[i] = half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + (i & 31)];
+}
+
+template <typename KVT>
+cudaError_t launch_attn(const AttnArgs& a, int nchunk, int nkv, cudaStream_t st) {
+    auto kern = attn_partial_kernel<KVT, 128, true>;
+    constexpr int smem = attn_smem_bytes<KVT, 128>();
+    static int set_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(set_mask & (1 << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        set_mask |= 1 << (dev & 31);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(nchunk, nkv);
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+// Enqueue one token step on m->stream.
+int enqueue_step(fence_model* m) {
+    const fence_config& c = m->cfg;
+    cudaStream_t st = m->stream;
+    embed_state_kernel<<<(c.embed_dim + 255) / 256, 256, 0, st>>>(m->hidden, m->tok_embd, m->state, c.embed_dim);
+    FENCE_CUDA_TRY(cudaGetLastError());
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerW& w = m->layers[l];
+        const LayerLaunch& L = m->launches[l];
+        const int q6 = 14;
+        FENCE_CUDA_TRY(gemv_dispatch(w.t_qkv, w.t_qkv == q6 ? X_NORM_R16 : X_NORM, EPI_STORE, L.qkv, L.pqkv, st));
+        if (c.kv_dtype == FENCE_KV_F16) FENCE_CUDA_TRY(launch_attn<__half>(L.attn, m->attn_nchunk, c.n_kv_heads, st));
+        else FENCE_CUDA_TRY(launch_attn<__nv_bfloat16>(L.attn, m->attn_nchunk, c.n_kv_heads, st));
+        FENCE_CUDA_TRY(gemv_dispatch(w.t_o, w.t_o == q6 ? X_F32_R16 : X_F32, EPI_RESID, L.o, L.po, st));
+        FENCE_CUDA_TRY(gemv_dispatch(w.t_gu, w.t_gu == q6 ? X_NORM_R16 : X_NORM, EPI_SWIGLU, L.gu, L.pgu, st));
+        FENCE_CUDA_TRY(gemv_dispatch(w.t_down, w.t_down == q6 ? X_F16 : X_F32, EPI_RESID, L.down, L.pdown, st));
+    }
+    FENCE_CUDA_TRY(gemv_dispatch(c.embd_type, X_NORM, EPI_LMHEAD, m->lm, m->plm, st));
+    return FENCE_OK;
+}
+
+int run_step(fence_model* m) {
+    if (m->gexec) return cuda_status(cudaGraphLaunch(m->gexec, m->stream), "graph launch");
+    return enqueue_step(m);
+}
+
+int capture_graph(fence_model* m) {
+    FENCE_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_step(m);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+    if (rc != FENCE_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    FENCE_CUDA_TRY(e);
+    m->graph = g;
+    FENCE_CUDA_TRY(cudaGraphInstantiate(&m->gexec, g, 0));
+    return FENCE_OK;
+}
+
+// Sets the device decode state from the host (pinned ring slot; async, ordered on the stream).
+int set_state(fence_model* m, int token, int pos, int step) {
+    static thread_local int slot = 0;
+    slot = (slot + 1) % m->h_state_n;
+    DecodeState* hs = m->h_state + slot;
+    // the slot was used h_state_n launches ago; make sure that copy has executed
+    if (slot == 0) FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    hs->token = token;
+    hs->pos = pos;
+    hs->step = step;
+    hs->pad = 0;
+    FENCE_CUDA_TRY(cudaMemcpyAsync(m->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+    return FENCE_OK;
+}
+
+const GGUFTensorInfo* need(fence_model* m, const std::string& name, std::string& err) {
+    const GGUFTensorInfo* t = m->gguf.find_tensor(name);
+    if (!t && err.empty()) err = "missing tensor " + name;
+    return t;
+}
+
+bool check_linear(const GGUFTensorInfo* t, uint64_t K, uint64_t M, std::string& err) {
+    if (!t) return false;
+    if (t->type != GGMLType::Q6_K && t->type != GGMLType::Q8_0) {
+        err = "tensor " + t->name + " has type " + ggml_type_name(t->type) + " (engine streams Q6_K and Q8_0)";
+        return false;
+    }
+    if (t->n_dims != 2 || t->dims[0] != K || t->dims[1] != M) {
+        err = "tensor " + t->name + " has dims [" + std::to_string(t->dims[0]) + ", " + std::to_string(t->dims[1]) +
+              "], expected [" + std::to_string(K) + ", " + std::to_string(M) + "]";
+        return false;
+    }
+    return true;
+}
+bool check_vec(const GGUFTensorInfo* t, uint64_t n, std::string& err) {
+    if (!t) return true;  // optional vectors are checked by the caller
+    if (t->type != GGMLType::F32 || t->n_elements() != n) {
+        err = "tensor " + t->name + " must be F32 with " + std::to_string(n) + " elements";
+        return false;
+    }
+    return true;
+}
+
+void free_model(fence_model* m) {
+    if (!m) return;
+    if (!m->stream) {  // failed before any device work
+        m->gguf.close();
+        delete m;
+        return;
+    }
+    if (m->dev >= 0) cudaSetDevice(m->dev);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    cudaFree(m->arena);
+    cudaFree(m->kcache);
+    cudaFree(m->vcache);
+    cudaFree(m->hidden);
+    cudaFree(m->qkv);
+    cudaFree(m->attn_out);
+    cudaFree(m->logits);
+    cudaFree(m->attn_part);
+    cudaFree(m->act);
+    cudaFree(m->counters);
+    cudaFree(m->lm_val);
+    cudaFree(m->lm_idx);
+    cudaFree(m->state);
+    cudaFree(m->token_log);
+    cudaFree(m->rope);
+    if (m->h_state) cudaFreeHost(m->h_state);
+    if (m->h_token) cudaFreeHost(m->h_token);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    m->gguf.close();
+    delete m;
+}
+
+}  // namespace
+
+// =============================================================================================
+extern "C" void fence_load_opts_default(fence_load_opts* o) {
+    std::memset(o, 0, sizeof *o);
+    o->max_ctx = 4096;
+    o->kv_dtype = FENCE_KV_BF16;
+    o->device = 0;
+    o->use_graph = 1;
+    o->verbose = 0;
+    o->tp_rank = 0;
+    o->tp_size = 1;
+}
+
+extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts* opts_in) {
+    fence_load_opts opts;
+    if (opts_in) opts = *opts_in;
+    else fence_load_opts_default(&opts);
+    if (!path) {
+        set_error(FENCE_E_ARG, "model_load: null path");
+        return nullptr;
+    }
+    if (opts.tp_size > 1) {
+        set_error(FENCE_E_UNSUPPORTED, "model_load: tensor parallel loading is not built in this library");
+        return nullptr;
+    }
+    fence_model* m = new fence_model();
+    m->opts = opts;
+    m->dev = opts.device;
+    auto bail = [&](int code, const std::string& msg) -> fence_model* {
+        set_error(code, "%s", msg.c_str());
+        free_model(m);
+        return nullptr;
+    };
+    if (opts.verbose) printf("Loading GGUF: %s\n", path);
+    if (!m->gguf.open(path)) return bail(FENCE_E_FORMAT, "model_load: " + m->gguf.last_error());
+
+    // ---- config from metadata, with the reference's keys, types and fallbacks (qwen3.cu:116-160)
+    fence_config& c = m->cfg;
+    std::string arch = "qwen2";
+    try {
+        arch = m->gguf.get_string("general.architecture");
+    } catch (...) {
+    }
+    try {
+        c.n_layers = (int)m->gguf.get_u32(arch + ".block_count");
+        c.embed_dim = (int)m->gguf.get_u32(arch + ".embedding_length");
+        c.ff_dim = (int)m->gguf.get_u32(arch + ".feed_forward_length");
+        c.n_heads = (int)m->gguf.get_u32(arch + ".attention.head_count");
+        c.n_kv_heads = (int)m->gguf.get_u32(arch + ".attention.head_count_kv");
+    } catch (const std::exception& ex) {
+        return bail(FENCE_E_FORMAT, std::string("model_load: ") + ex.what());
+    }
+    try {
+        c.head_dim = (int)m->gguf.get_u32(arch + ".attention.key_length");
+    } catch (...) {
+        c.head_dim = c.n_heads ? c.embed_dim / c.n_heads : 0;
+        if (opts.verbose) printf("Config: head_dim not in metadata, inferred %d\n", c.head_dim);
+    }
+    try {
+        c.rope_freq_base = m->gguf.get_f32(arch + ".rope.freq_base");
+    } catch (...) {
+        c.rope_freq_base = 10000.0f;
+        if (opts.verbose) printf("Config: rope.freq_base not in metadata, using default %.0f\n", c.rope_freq_base);
+    }
+    try {
+        c.rms_eps = m->gguf.get_f32(arch + ".attention.layer_norm_rms_epsilon");
+    } catch (...) {
+        c.rms_eps = 1e-5f;
+        if (opts.verbose) printf("Config: rms_epsilon not in metadata, using default %.0e\n", c.rms_eps);
+    }
+    try {
+        c.n_experts = (int)m->gguf.get_u32(arch + ".expert_count");
+        c.n_experts_used = (int)m->gguf.get_u32(arch + ".expert_used_count");
+    } catch (...) {
+        c.n_experts = c.n_experts_used = 0;
+    }
+    const GGUFTensorInfo* embd = m->gguf.find_tensor("token_embd.weight");
+    if (!embd) return bail(FENCE_E_FORMAT, "model_load: missing token_embd.weight");
+    c.vocab_size = (int)embd->dims[1];
+    c.max_ctx = opts.max_ctx > 0 ? opts.max_ctx : 4096;
+    c.temperature = 0.7f;
+    c.top_p = 0.8f;
+    c.top_k = 50;
+    c.repetition_penalty = 1.15f;
+    c.min_p = 0.05f;
+    c.dynamic_temp = 1;
+    c.kv_dtype = opts.kv_dtype;
+    c.tp_rank = 0;
+    c.tp_size = 1;
+    c.embd_type = (int)embd->type;
+
+    if (c.n_layers <= 0 || c.embed_dim <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads)
+        return bail(FENCE_E_FORMAT, "model_load: inconsistent head counts / dimensions in metadata");
+    if (c.head_dim != 128)
+        return bail(FENCE_E_UNSUPPORTED, "model_load: head_dim " + std::to_string(c.head_dim) + " (engine kernels are built for 128)");
+    if (c.n_heads / c.n_kv_heads > ATTN_MAX_G)
+        return bail(FENCE_E_UNSUPPORTED, "model_load: more than 8 query heads per KV head");
+    if (c.n_experts > 0)
+        return bail(FENCE_E_UNSUPPORTED, "model_load: mixture-of-experts FFN is not built in this library");
+    if (embd->type != GGMLType::Q8_0 || embd->dims[0] != (uint64_t)c.embed_dim)
+        return bail(FENCE_E_UNSUPPORTED, "model_load: token_embd.weight must be Q8_0 [embed_dim, vocab]");
+    if (c.embed_dim % 64)
+        return bail(FENCE_E_UNSUPPORTED, "model_load: embed_dim must be a multiple of 64");
+
+    const uint64_t H = c.embed_dim, F = c.ff_dim, qd = (uint64_t)c.n_heads * c.head_dim,
+                   kvd = (uint64_t)c.n_kv_heads * c.head_dim;
+
+    // ---- collect and validate tensors, lay out the device arena
+    struct Up {
+        const GGUFTensorInfo* t;
+        size_t off;
+    };
+    std::vector<Up> ups;
+    size_t total = 0;
+    auto place = [&](const GGUFTensorInfo* t) -> size_t {
+        const size_t off = total;
+        ups.push_back({t, off});
+        total = align_up(total + t->data_size_bytes, 256);
+        return off;
+    };
+    std::string err;
+    const GGUFTensorInfo* onorm = need(m, "output_norm.weight", err);
+    if (!err.empty() || !check_vec(onorm, H, err)) return bail(FENCE_E_FORMAT, "model_load: " + err);
+    std::vector<std::vector<std::pair<const GGUFTensorInfo*, size_t>>> lt(c.n_layers);
+    const size_t off_embd = place(embd);
+    const size_t off_onorm = place(onorm);
+    struct LOff {
+        size_t q, k, v, o, g, u, d, an, fn, qn, kn, qb, kb, vb;
+        bool has_qn, has_kn, has_qb, has_kb, has_vb;
+    };
+    std::vector<LOff> lo(c.n_layers);
+    m->layers.resize(c.n_layers);
+    size_t bytes_per_token = embd->data_size_bytes;
+    c.linear_type = 0;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        const GGUFTensorInfo *an = need(m, p + "attn_norm.weight", err), *q = need(m, p + "attn_q.weight", err),
+                             *k = need(m, p + "attn_k.weight", err), *v = need(m, p + "attn_v.weight", err),
+                             *o = need(m, p + "attn_output.weight", err), *fn = need(m, p + "ffn_norm.weight", err),
+                             *g = need(m, p + "ffn_gate.weight", err), *u = need(m, p + "ffn_up.weight", err),
+                             *d = need(m, p + "ffn_down.weight", err);
+        if (!err.empty()) return bail(FENCE_E_FORMAT, "model_load: " + err);
+        const GGUFTensorInfo *qn = m->gguf.find_tensor(p + "attn_q_norm.weight"),
+                             *kn = m->gguf.find_tensor(p + "attn_k_norm.weight"),
+                             *qb = m->gguf.find_tensor(p + "attn_q.bias"), *kb = m->gguf.find_tensor(p + "attn_k.bias"),
+                             *vb = m->gguf.find_tensor(p + "attn_v.bias");
+        if (!check_linear(q, H, qd, err) || !check_linear(k, H, kvd, err) || !check_linear(v, H, kvd, err) ||
+            !check_linear(o, qd, H, err) || !check_linear(g, H, F, err) || !check_linear(u, H, F, err) ||
+            !check_linear(d, F, H, err) || !check_vec(an, H, err) || !check_vec(fn, H, err) ||
+            !check_vec(qn, c.head_dim, err) || !check_vec(kn, c.head_dim, err) || !check_vec(qb, qd, err) ||
+            !check_vec(kb, kvd, err) || !check_vec(vb, kvd, err))
+            return bail(FENCE_E_FORMAT, "model_load: " + err);
+        if (q->type != k->type || q->type != v->type || g->type != u->type)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: q/k/v (and gate/up) must share one quant type in a layer");
+        LayerW& w = m->layers[l];
+        w.t_qkv = (int)q->type;
+        w.t_o = (int)o->type;
+        w.t_gu = (int)g->type;
+        w.t_down = (int)d->type;
+        if (c.linear_type == 0) c.linear_type = (int)q->type;
+        LOff& L = lo[l];
+        L.an = place(an);
+        L.q = place(q);
+        L.k = place(k);
+        L.v = place(v);
+        L.o = place(o);
+        L.fn = place(fn);
+        L.g = place(g);
+        L.u = place(u);
+        L.d = place(d);
+        L.has_qn = qn && kn;  // the reference applies q/k-norm only when both exist (qwen3.cu:292)
+        L.has_kn = L.has_qn;
+        if (L.has_qn) {
+            L.qn = place(qn);
+            L.kn = place(kn);
+        }
+        L.has_qb = qb != nullptr;
+        L.has_kb = kb != nullptr;
+        L.has_vb = vb != nullptr;
+        if (qb) L.qb = place(qb);
+        if (kb) L.kb = place(kb);
+        if (vb) L.vb = place(vb);
+        bytes_per_token += q->data_size_bytes + k->data_size_bytes + v->data_size_bytes + o->data_size_bytes +
+                           g->data_size_bytes + u->data_size_bytes + d->data_size_bytes;
+    }
+    c.has_qk_norm = lo[0].has_qn ? 1 : 0;
+    c.weight_bytes = bytes_per_token;
+    m->arena_bytes = total;
+    if (opts.verbose) {
+        printf("Config: layers=%d embed=%d ff=%d heads=%d/%d head_dim=%d vocab=%d\n", c.n_layers, c.embed_dim,
+               c.ff_dim, c.n_heads, c.n_kv_heads, c.head_dim, c.vocab_size);
+        printf("Copying weights to GPU (%.2f GB)...\n", total / 1e9);
+    }
+
+    // ---- device allocations (everything above is host-side parsing and validation)
+    if (cudaSetDevice(m->dev) != cudaSuccess) return bail(FENCE_E_ARG, "model_load: cannot select CUDA device");
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(FENCE_E_NOMEM, "model_load: stream creation failed");
+    if (cudaMalloc(&m->arena, total) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: weight arena allocation failed");
+    auto t0 = std::chrono::steady_clock::now();
+    for (const Up& u : ups)
+        if (cudaMemcpy(m->arena + u.off, u.t->data, u.t->data_size_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(FENCE_E_NOMEM, "model_load: weight upload failed for " + u.t->name);
+    if (opts.verbose)
+        printf("Weights loaded in %.1f s\n", std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+    m->tok_embd = m->arena + off_embd;
+    m->out_norm = reinterpret_cast<const float*>(m->arena + off_onorm);
+    for (int l = 0; l < c.n_layers; ++l) {
+        LayerW& w = m->layers[l];
+        const LOff& L = lo[l];
+        auto P = [&](size_t off) { return m->arena + off; };
+        auto PF = [&](size_t off) { return reinterpret_cast<const float*>(m->arena + off); };
+        w.attn_norm = PF(L.an);
+        w.q = P(L.q);
+        w.k = P(L.k);
+        w.v = P(L.v);
+        w.o = P(L.o);
+        w.ffn_norm = PF(L.fn);
+        w.gate = P(L.g);
+        w.up = P(L.u);
+        w.down = P(L.d);
+        if (L.has_qn) {
+            w.q_norm = PF(L.qn);
+            w.k_norm = PF(L.kn);
+        }
+        if (L.has_qb) w.q_bias = PF(L.qb);
+        if (L.has_kb) w.k_bias = PF(L.kb);
+        if (L.has_vb) w.v_bias = PF(L.vb);
+    }
+
+    const int HD = c.head_dim, G = c.n_heads / c.n_kv_heads;
+    const size_t kv_elems = (size_t)c.n_layers * c.n_kv_heads * c.max_ctx * HD;
+    m->attn_nchunk = std::max(32, (c.max_ctx + ATTN_CMAX - 1) / ATTN_CMAX);
+    bool ok = cudaMalloc(&m->kcache, kv_elems * 2) == cudaSuccess && cudaMalloc(&m->vcache, kv_elems * 2) == cudaSuccess &&
+              cudaMemset(m->kcache, 0, kv_elems * 2) == cudaSuccess && cudaMemset(m->vcache, 0, kv_elems * 2) == cudaSuccess &&
+              cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qd + 2 * kvd) * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_out, qd * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_part, (size_t)c.n_kv_heads * m->attn_nchunk * G * (HD + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&m->act, F * 4) == cudaSuccess &&
+              cudaMalloc(&m->counters, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMemset(m->counters, 0, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMalloc(&m->lm_val, 4096 * 4) == cudaSuccess && cudaMalloc(&m->lm_idx, 4096 * 4) == cudaSuccess &&
+              cudaMalloc(&m->state, sizeof(DecodeState)) == cudaSuccess &&
+              cudaMemset(m->state, 0, sizeof(DecodeState)) == cudaSuccess &&
+              cudaMalloc(&m->rope, (size_t)c.max_ctx * (HD / 2) * sizeof(float2)) == cudaSuccess &&
+              cudaMallocHost(&m->h_state, 64 * sizeof(DecodeState)) == cudaSuccess &&
+              cudaMallocHost(&m->h_token, 64 * sizeof(int)) == cudaSuccess;
+    if (!ok) return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
+    m->h_state_n = 64;
+    m->token_log_cap = std::max(c.max_ctx, 4096);
+    if (cudaMalloc(&m->token_log, m->token_log_cap * sizeof(int)) != cudaSuccess)
+        return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
+
+    // RoPE table: angle pos * base^(-2i/HD) and its cos/sin in double, rounded once to float.
+    {
+        std::vector<float2> tab((size_t)c.max_ctx * (HD / 2));
+        for (int pos = 0; pos < c.max_ctx; ++pos)
+            for (int i = 0; i < HD / 2; ++i) {
+                const double ang = (double)pos * std::pow((double)c.rope_freq_base, -2.0 * i / (double)HD);
+                tab[(size_t)pos * (HD / 2) + i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+            }
+        if (cudaMemcpy(m->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(FENCE_E_NOMEM, "model_load: rope table upload failed");
+    }
+
+    // ---- per-layer launch arguments
+    m->launches.resize(c.n_layers);
+    const size_t kv_layer = (size_t)c.n_kv_heads * c.max_ctx * HD;
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerW& w = m->layers[l];
+        LayerLaunch& L = m->launches[l];
+        const int wq = w.t_qkv == 14 ? WT_Q6K : WT_Q80, wo = w.t_o == 14 ? WT_Q6K : WT_Q80,
+                  wg = w.t_gu == 14 ? WT_Q6K : WT_Q80, wd = w.t_down == 14 ? WT_Q6K : WT_Q80;
+        // QKV
+        L.pqkv = plan_gemv(wq, (int)H, (int)(qd + 2 * kvd), 0, 0);
+        L.po = plan_gemv(wo, (int)qd, (int)H, 0, 0);
+        L.pgu = plan_gemv(wg, (int)H, (int)F, 1, 0);
+        L.pdown = plan_gemv(wd, (int)F, (int)H, 0, 0);
+        if (!L.pqkv.ok || !L.po.ok || !L.pgu.ok || !L.pdown.ok)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: a layer shape does not fit the streaming GEMV");
+        GemvArgs a{};
+        a.nseg = 3;
+        a.seg[0] = GemvSeg{w.q, (int)qd, m->qkv, w.q_bias};
+        a.seg[1] = GemvSeg{w.k, (int)kvd, m->qkv + qd, w.k_bias};
+        a.seg[2] = GemvSeg{w.v, (int)kvd, m->qkv + qd + kvd, w.v_bias};
+        a.Mv = (int)(qd + 2 * kvd);
+        a.K = (int)H;
+        a.x = m->hidden;
+        a.norm_w = w.attn_norm;
+        a.eps = c.rms_eps;
+        fill_plan(a, L.pqkv);
+        L.qkv = a;
+        // O + residual
+        a = GemvArgs{};
+        a.nseg = 1;
+        a.seg[0] = GemvSeg{w.o, (int)H, nullptr, nullptr};
+        a.Mv = (int)H;
+        a.K = (int)qd;
+        a.x = m->attn_out;
+        a.resid = m->hidden;
+        fill_plan(a, L.po);
+        L.o = a;
+        // gate/up + SwiGLU
+        a = GemvArgs{};
+        a.nseg = 2;
+        a.dual = 1;
+        a.seg[0] = GemvSeg{w.gate, (int)F, nullptr, nullptr};
+        a.seg[1] = GemvSeg{w.up, (int)F, nullptr, nullptr};
+        a.Mv = (int)F;
+        a.K = (int)H;
+        a.x = m->hidden;
+        a.norm_w = w.ffn_norm;
+        a.eps = c.rms_eps;
+        a.act = m->act;
+        a.act_f16 = (w.t_down == 14) ? 1 : 0;
+        fill_plan(a, L.pgu);
+        L.gu = a;
+        // down + residual
+        a = GemvArgs{};
+        a.nseg = 1;
+        a.seg[0] = GemvSeg{w.down, (int)H, nullptr, nullptr};
+        a.Mv = (int)H;
+        a.K = (int)F;
+        a.x = m->act;
+        a.resid = m->hidden;
+        fill_plan(a, L.pdown);
+        L.down = a;
+        // attention
+        AttnArgs at{};
+        at.q = m->qkv;
+        at.kc = static_cast<uint8_t*>(m->kcache) + l * kv_layer * 2;
+        at.vc = static_cast<uint8_t*>(m->vcache) + l * kv_layer * 2;
+        at.kc_w = const_cast<void*>(at.kc);
+        at.vc_w = const_cast<void*>(at.vc);
+        at.stride_t = HD;
+        at.stride_h = (long long)c.max_ctx * HD;
+        at.n_q_heads = c.n_heads;
+        at.n_kv_heads = c.n_kv_heads;
+        at.nchunk = m->attn_nchunk;
+        at.part = m->attn_part;
+        at.state = m->state;
+        at.k_new = m->qkv + qd;
+        at.v_new = m->qkv + qd + kvd;
+        at.q_norm_w = w.q_norm;
+        at.k_norm_w = w.k_norm;
+        at.eps = c.rms_eps;
+        at.rope = m->rope;
+        at.out = m->attn_out;
+        at.counter = m->counters;
+        L.attn = at;
+        (void)wo;
+        (void)wd;
+        (void)wg;
+    }
+    // LM head: tied token_embd (the reference ignores output.weight, qwen3.cu:180-212,261)
+    m->plm = plan_gemv(WT_Q80, (int)H, c.vocab_size, 0, 0);
+    if (!m->plm.ok || m->plm.grid > 4096) return bail(FENCE_E_UNSUPPORTED, "model_load: LM head shape not supported");
+    {
+        GemvArgs a{};
+        a.nseg = 1;
+        a.seg[0] = GemvSeg{m->tok_embd, c.vocab_size, nullptr, nullptr};
+        a.Mv = c.vocab_size;
+        a.K = (int)H;
+        a.x = m->hidden;
+        a.norm_w = m->out_norm;
+        a.eps = c.rms_eps;
+        a.logits = m->logits;
+        a.cta_val = m->lm_val;
+        a.cta_idx = m->lm_idx;
+        a.counter = m->counters + c.n_kv_heads;
+        a.state = m->state;
+        a.token_log = m->token_log;
+        a.token_log_cap = m->token_log_cap;
+        fill_plan(a, m->plm);
+        m->lm = a;
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: device error during setup");
+    if (opts.use_graph) {
+        const int rc = capture_graph(m);
+        if (rc != FENCE_OK) return bail(rc, std::string("model_load: graph capture failed: ") + fence_last_error());
+    }
+    m->h_logits.resize(c.vocab_size);
+    if (opts.verbose) printf("Model ready!\n\n");
+    return m;
+}
+
+extern "C" void fence_model_free(fence_model* m) { free_model(m); }
+
+extern "C" int fence_model_config(const fence_model* m, fence_config* out) {
+    if (!m || !out) return set_error(FENCE_E_ARG, "model_config: null argument");
+    *out = m->cfg;
+    return FENCE_OK;
+}
+
+extern "C" int fence_set_sampling(fence_model* m, float temperature, float top_p, int top_k, float rep) {
+    if (!m) return set_error(FENCE_E_ARG, "set_sampling: null model");
+    m->cfg.temperature = temperature;
+    m->cfg.top_p = top_p;
+    m->cfg.top_k = top_k;
+    m->cfg.repetition_penalty = rep;
+    return FENCE_OK;
+}
+
+extern "C" int fence_set_seed(fence_model* m, uint64_t seed) {
+    if (!m) return set_error(FENCE_E_ARG, "set_seed: null model");
+    m->rng.seed((std::mt19937::result_type)(seed ^ (seed >> 32)));
+    return FENCE_OK;
+}
+
+extern "C" const float* fence_forward(fence_model* m, int token_id, int pos) {
+    if (!m) {
+        set_error(FENCE_E_ARG, "forward: null model");
+        return nullptr;
+    }
+    if (token_id < 0 || token_id >= m->cfg.vocab_size || pos < 0 || pos >= m->cfg.max_ctx) {
+        set_error(FENCE_E_ARG, "forward: token %d / pos %d out of range", token_id, pos);
+        return nullptr;
+    }
+    cudaSetDevice(m->dev);
+    if (set_state(m, token_id, pos, 0) != FENCE_OK) return nullptr;
+    if (run_step(m) != FENCE_OK) return nullptr;
+    if (cuda_status(cudaStreamSynchronize(m->stream), "forward") != FENCE_OK) return nullptr;
+    return m->logits;
+}
+
+extern "C" int fence_sample_greedy(fence_model* m, const float* d_logits) {
+    if (!m || !d_logits) return set_error(FENCE_E_ARG, "sample_greedy: null argument");
+    cudaSetDevice(m->dev);
+    if (d_logits == m->logits) {
+        // the LM head already reduced the argmax (reference tie order) into the decode state
+        FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_token, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    } else {
+        const int rc = fence_argmax(d_logits, m->lm_idx, m->cfg.vocab_size, m->stream);
+        if (rc) return rc;
+        FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_token, m->lm_idx, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    }
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return *m->h_token;
+}
+
+extern "C" int fence_sample_nucleus(fence_model* m, const float* d_logits, const int* history, int n_history) {
+    if (!m || !d_logits) return set_error(FENCE_E_ARG, "sample_nucleus: null argument");
+    const fence_config& c = m->cfg;
+    if (c.temperature <= 0.0f || c.top_k <= 1) return fence_sample_greedy(m, d_logits);
+    cudaSetDevice(m->dev);
+    FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_logits.data(), d_logits, (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return host_sample_nucleus(m->h_logits.data(), c.vocab_size, history, n_history, c.temperature, c.top_p, c.top_k,
+                               c.repetition_penalty, c.min_p, c.dynamic_temp != 0, m->rng);
+}
+
+extern "C" int fence_generate(fence_model* m, const int* prompt, int n_prompt, int max_new, int eos_id, int* out,
+                              int out_cap, int* n_out) {
+    if (!m || !prompt || n_prompt <= 0 || !out || !n_out) return set_error(FENCE_E_ARG, "generate: bad arguments");
+    if (n_prompt > m->cfg.max_ctx) return set_error(FENCE_E_ARG, "generate: prompt longer than max_ctx");
+    cudaSetDevice(m->dev);
+    std::vector<int> output(prompt, prompt + n_prompt);
+    // prefill, token by token as in the reference (qwen3.cu:478-481); no host sync between tokens
+    for (int i = 0; i < n_prompt; ++i) {
+        if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab_size) return set_error(FENCE_E_ARG, "generate: prompt id out of range");
+        int rc = set_state(m, prompt[i], i, 0);
+        if (!rc) rc = run_step(m);
+        if (rc) return rc;
+    }
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    int pos = n_prompt;
+    for (int i = 0; i < max_new && pos < m->cfg.max_ctx; ++i) {
+        const int next = fence_sample_nucleus(m, m->logits, output.data(), (int)output.size());
+        if (next < 0) return next;
+        if (next == eos_id) break;
+        output.push_back(next);
+        int rc = set_state(m, next, pos, 0);
+        if (!rc) rc = run_step(m);
+        if (rc) return rc;
+        ++pos;
+    }
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    const int n = (int)std::min<size_t>(output.size(), (size_t)out_cap);
+    std::copy(output.begin(), output.begin() + n, out);
+    *n_out = (int)output.size();
+    return FENCE_OK;
+}
+
+extern "C" int fence_decode_greedy(fence_model* m, int token, int pos, int n_steps, int* out_tokens) {
+    if (!m || n_steps < 0 || !out_tokens) return set_error(FENCE_E_ARG, "decode_greedy: bad arguments");
+    if (pos < 0 || pos + n_steps > m->cfg.max_ctx || n_steps > m->token_log_cap)
+        return set_error(FENCE_E_ARG, "decode_greedy: positions [%d, %d) exceed max_ctx", pos, pos + n_steps);
+    cudaSetDevice(m->dev);
+    int rc = set_state(m, token, pos, 0);
+    if (rc) return rc;
+    for (int s = 0; s < n_steps; ++s)
+        if ((rc = run_step(m))) return rc;
+    FENCE_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->token_log, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return FENCE_OK;
+}
+
+extern "C" int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms) {
+    if (!m || !ms || n_steps <= 0) return set_error(FENCE_E_ARG, "time_decode: bad arguments");
+    if (pos < 0 || pos + n_steps > m->cfg.max_ctx) return set_error(FENCE_E_ARG, "time_decode: positions exceed max_ctx");
+    cudaSetDevice(m->dev);
+    cudaEvent_t e0, e1;
+    FENCE_CUDA_TRY(cudaEventCreate(&e0));
+    FENCE_CUDA_TRY(cudaEventCreate(&e1));
+    int rc = set_state(m, token, pos, 0);
+    if (!rc) rc = cuda_status(cudaEventRecord(e0, m->stream), "event record");
+    for (int s = 0; s < n_steps && !rc; ++s) rc = run_step(m);
+    if (!rc) rc = cuda_status(cudaEventRecord(e1, m->stream), "event record");
+    if (!rc) rc = cuda_status(cudaEventSynchronize(e1), "event sync");
+    if (!rc) rc = cuda_status(cudaEventElapsedTime(ms, e0, e1), "elapsed");
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return rc;
+}
+
+extern "C" int fence_copy_logits(fence_model* m, float* host_out) {
+    if (!m || !host_out) return set_error(FENCE_E_ARG, "copy_logits: null argument");
+    cudaSetDevice(m->dev);
+    FENCE_CUDA_TRY(cudaMemcpyAsync(host_out, m->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return FENCE_OK;
+}

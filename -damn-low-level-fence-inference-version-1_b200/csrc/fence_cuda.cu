@@ -1,0 +1,5 @@
+// fence_cuda.cu — the single CUDA translation unit of libfence_b200.so. Device globals (the
+// device error word) and every kernel live in one module, so no relocatable device code is needed.
+#include "gemv.cu"
+#include "ops.cu"
+#include "engine.cu"

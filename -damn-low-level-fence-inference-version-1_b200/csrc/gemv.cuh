@@ -1,0 +1,732 @@
+// gemv.cuh — HBM-streaming dequant-GEMV for batch-1 decode on B200 (sm_100a).
+//
+// Computes y[row] = sum_k W[row][k] * x[k] for Q6_K (src/kernels/gemv_q6k.cuh:45-83 in the
+// reference) and Q8_0 (src/kernels/gemv_q8_0.cuh:75-97) weights in their raw GGUF layouts, with
+// the producer/consumer work that surrounds the GEMV in the token loop fused in:
+//
+//   prologue  x from fp16 / fp32 global memory, optionally RMSNorm'd (ops.cuh:17-45) and rounded to
+//             fp16 (the reference's f32_to_f16 before every Q6_K GEMV, qwen3.cu:278,310,325,336)
+//   epilogue  plain store (+bias), residual add (ops.cuh:256-263), SwiGLU of a gate/up row pair
+//             (ops.cuh:183-195) written as the next GEMV's input, or LM-head logits + greedy argmax
+//             (ops.cuh:467-499) with the decode state advanced on the device.
+//
+// Design (B200-first; the reference is one warp per row with byte loads):
+//  * The weight bytes a CTA owns are streamed through a ring of shared-memory stages by one
+//    producer thread issuing 1-D TMA bulk copies (cp.async.bulk, no multicast) that complete on
+//    mbarriers, so tens of KB per SM are in flight with almost no issue cost. Stage boundaries are
+//    rounded to 16 B in global memory; the sub-16 B tail of a tensor is fetched with plain loads.
+//  * Each consumer thread owns one fixed 64-element "item" of the K dimension for every row it
+//    touches: for Q6_K the elements {h*128 + c*32 + l16*16 + j | c<4, j<16} of one super-block
+//    (h, l16 in {0,1}), so each of its four 16-element sub-blocks is complete inside the thread and
+//    its scale is applied once; for Q8_0 two consecutive 32-element blocks.
+//  * x is quantised per item to 16-bit integers split into a signed high byte and an unsigned low
+//    byte, so the 6-bit (or 8-bit) weights are dotted with dp4a in exact integer arithmetic:
+//    sum (q-32)*xq = 256*dp4a(q, xh) + dp4a(q, xl) - 32*sum(xq). The only rounding is xq itself
+//    (|err| <= max|x_item| / 65534 per element), well inside the 1e-3 relative bound the reference
+//    GEMV test applies (tests/test_gemv_q6k.cu:134-164).
+//  * The 6-bit unpack is four 3-input logic ops per 16 weights on whole 32-bit words.
+//  * Row sums are reduced through shared memory (double-buffered, one named barrier per stage) in
+//    a fixed order, so results are deterministic.
+//  * Programmatic dependent launch: the producer starts streaming weights before
+//    griddepcontrol.wait; only the x prologue waits for the previous kernel.
+#pragma once
+
+#include "common.cuh"
+
+namespace fence {
+
+enum : int { WT_Q6K = 0, WT_Q80 = 1 };
+enum : int { X_F16 = 0, X_F32 = 1, X_F32_R16 = 2, X_NORM = 3, X_NORM_R16 = 4 };
+enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LMHEAD = 3 };
+
+constexpr int GEMV_MAX_NT = 640;  // consumer threads + one producer warp
+constexpr int GEMV_MAX_SEG = 3;
+constexpr int GEMV_STAGE_SLACK = 256;  // per-stage bytes: <= 3 pieces x (30 B alignment + 31 B padding) + over-read
+
+struct GemvSeg {
+    const uint8_t* W;   // tensor base, 16-byte aligned
+    int rows;           // rows of this tensor covered by the launch
+    float* y;           // EPI_STORE output, indexed by the tensor's row
+    const float* bias;  // optional bias for EPI_STORE
+};
+
+// Device-resident decode state advanced by the LM head (token fed to the next step, its position).
+struct DecodeState {
+    int token;
+    int pos;
+    int step;
+    int pad;
+};
+
+struct GemvArgs {
+    GemvSeg seg[GEMV_MAX_SEG];
+    int nseg;
+    int dual;         // EPI_SWIGLU: seg[0] = gate, seg[1] = up, same rows
+    int Mv;           // virtual rows (dual: rows of each tensor)
+    int K;
+    int rowB;         // bytes per row
+    int I;            // items (64 elements) per row
+    int P;            // rows per stage
+    int ring;         // stages in the shared-memory ring
+    int stage_bytes;  // bytes per ring slot (multiple of 128)
+    int nt_cons;      // consumer threads (multiple of 32)
+    // x source
+    const void* x;
+    const float* norm_w;
+    float eps;
+    // epilogue targets
+    float* resid;      // EPI_RESID: resid[row] = dot + resid[row]
+    void* act;         // EPI_SWIGLU output (fp16 when act_f16, else fp32)
+    int act_f16;
+    float* logits;     // EPI_LMHEAD
+    float* cta_val;    // [gridDim.x] per-CTA best logit
+    int* cta_idx;      // [gridDim.x] per-CTA best index
+    unsigned int* counter;  // CTA arrival counter, zero between launches
+    DecodeState* state;     // EPI_LMHEAD: token/pos/step advanced by the last CTA
+    int* token_log;         // EPI_LMHEAD: token_log[step] = sampled id (may be null)
+    int token_log_cap;
+};
+
+template <int WT>
+struct WTraits;
+template <>
+struct WTraits<WT_Q6K> {
+    static constexpr int BLOCK_ELEMS = 256;
+    static constexpr int BLOCK_BYTES = 210;
+    static constexpr int XWORDS = 16;  // xh / xl words per item
+};
+template <>
+struct WTraits<WT_Q80> {
+    static constexpr int BLOCK_ELEMS = 32;
+    static constexpr int BLOCK_BYTES = 34;
+    static constexpr int XWORDS = 17;  // 9 (block 0, shifted by the 2-byte scale) + 8 (block 1)
+};
+
+// --------------------------------------------------------------------------------------------
+// Stage geometry: a stage covers `n` consecutive virtual rows starting at va, split into at most
+// three contiguous pieces of global memory (one per tensor touched). All indexing is static so the
+// pieces stay in registers.
+struct Piece {
+    const uint8_t* src;   // 16-byte aligned start of the bulk copy
+    uint32_t copy_bytes;  // multiple of 16
+    uint32_t tail_bytes;  // bytes after the bulk part fetched with plain loads (tensor end only)
+    uint32_t smem_off;    // offset of the copy inside the stage slot
+    uint32_t delta;       // offset of the first row inside the copy
+    int first_row;        // first stage-row index in this piece
+    int seg_row0;         // first tensor row
+    int valid;
+};
+
+struct StageGeo {
+    Piece p[GEMV_MAX_SEG];
+};
+
+__device__ __forceinline__ void make_piece(const GemvArgs& a, int s, int r0, int nr, int first, Piece& p) {
+    const uint64_t total = (uint64_t)a.seg[s].rows * (uint64_t)a.rowB;
+    const uint64_t g0 = (uint64_t)r0 * a.rowB;
+    const uint64_t g1 = (uint64_t)(r0 + nr) * a.rowB;
+    const uint64_t a0 = g0 & ~uint64_t(15);
+    uint64_t end;
+    uint32_t tail = 0;
+    if (g1 >= total) {
+        end = total & ~uint64_t(15);
+        tail = (uint32_t)(total - end);
+    } else {
+        end = (g1 + 15) & ~uint64_t(15);
+    }
+    p.src = a.seg[s].W + a0;
+    p.copy_bytes = (uint32_t)(end - a0);
+    p.tail_bytes = tail;
+    p.delta = (uint32_t)(g0 - a0);
+    p.first_row = first;
+    p.seg_row0 = r0;
+    p.valid = 1;
+}
+
+__device__ __forceinline__ void stage_geo(const GemvArgs& a, int va, int n, StageGeo& g) {
+#pragma unroll
+    for (int k = 0; k < GEMV_MAX_SEG; ++k) g.p[k].valid = 0;
+    if (a.dual) {
+        make_piece(a, 0, va, n, 0, g.p[0]);
+        make_piece(a, 1, va, n, n, g.p[1]);
+    } else {
+        int base = 0;
+#pragma unroll
+        for (int s = 0; s < GEMV_MAX_SEG; ++s) {
+            if (s < a.nseg) {
+                const int rs = a.seg[s].rows;
+                const int lo = max(va, base), hi = min(va + n, base + rs);
+                if (lo < hi) make_piece(a, s, lo - base, hi - lo, lo - va, g.p[s]);
+                base += rs;
+            }
+        }
+    }
+    uint32_t off = 0;
+#pragma unroll
+    for (int k = 0; k < GEMV_MAX_SEG; ++k) {
+        g.p[k].smem_off = off;
+        if (g.p[k].valid) off = (off + g.p[k].copy_bytes + g.p[k].tail_bytes + 16u + 15u) & ~15u;
+    }
+}
+
+// Piece index holding stage row r (pieces are ordered by first_row).
+__device__ __forceinline__ int piece_of(const StageGeo& g, int r) {
+    int k = 0;
+#pragma unroll
+    for (int j = 1; j < GEMV_MAX_SEG; ++j)
+        if (g.p[j].valid && r >= g.p[j].first_row) k = j;
+    return k;
+}
+
+// --------------------------------------------------------------------------------------------
+// Per-thread quantised activation slice.
+template <int WT>
+struct XSlice {
+    uint32_t xh[WTraits<WT>::XWORDS];
+    uint32_t xl[WTraits<WT>::XWORDS];
+    int corr[4];  // Q6_K: -32 * sum(xq) per column run
+    float xs0, xs1;
+};
+
+__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+
+// Quantise n floats (max |v| = amax) into xq (int), returns scale.
+__device__ __forceinline__ float quant_scale(float amax, float& inv) {
+    if (!isfinite(amax)) {  // propagate NaN/Inf like the reference's fp32 sums would
+        inv = 0.f;
+        return __int_as_float(0x7fc00000);
+    }
+    if (!(amax > 0.f)) {
+        inv = 0.f;
+        return 0.f;
+    }
+    inv = 32767.f / amax;
+    return amax / 32767.f;
+}
+__device__ __forceinline__ void split16(int q, uint32_t& hb, uint32_t& lb) {
+    hb = (uint32_t)((q >> 8) & 0xff);  // signed high byte (two's complement)
+    lb = (uint32_t)(q & 0xff);          // unsigned low byte
+}
+
+// Loads the 64 x values of an item in the order the weight words deliver them.
+//   Q6_K item (b, h, l16): v[c*16 + j] = x[b*256 + h*128 + c*32 + l16*16 + j]
+//   Q8_0 item i:          v[e] = x[i*64 + e]
+template <int WT, int XM>
+__device__ __forceinline__ void load_item_x(const GemvArgs& a, int item, float v[64]) {
+    int base[4];
+    if (WT == WT_Q6K) {
+        const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) base[c] = b * 256 + h * 128 + c * 32 + l16 * 16;
+    } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) base[c] = item * 64 + c * 16;
+    }
+    if (XM == X_F16) {
+        const uint16_t* x = static_cast<const uint16_t*>(a.x);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4* p = reinterpret_cast<const uint4*>(x + base[c]);
+            const uint4 u0 = p[0], u1 = p[1];
+            const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                v[c * 16 + 2 * k] = half_bits_to_float(w[k]);
+                v[c * 16 + 2 * k + 1] = half_bits_to_float(w[k] >> 16);
+            }
+        }
+    } else {
+        const float* x = static_cast<const float*>(a.x);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4* p = reinterpret_cast<const float4*>(x + base[c]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 f = p[k];
+                v[c * 16 + 4 * k + 0] = f.x;
+                v[c * 16 + 4 * k + 1] = f.y;
+                v[c * 16 + 4 * k + 2] = f.z;
+                v[c * 16 + 4 * k + 3] = f.w;
+            }
+        }
+    }
+    if (XM == X_NORM || XM == X_NORM_R16) {
+        // w[i] * x[i] * rms in the reference's operation order (ops.cuh:43)
+        const float* w = a.norm_w;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float4* p = reinterpret_cast<const float4*>(w + base[c]);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 f = p[k];
+                v[c * 16 + 4 * k + 0] *= f.x;
+                v[c * 16 + 4 * k + 1] *= f.y;
+                v[c * 16 + 4 * k + 2] *= f.z;
+                v[c * 16 + 4 * k + 3] *= f.w;
+            }
+        }
+    }
+}
+
+template <int WT, int XM>
+__device__ __forceinline__ void make_slice(const GemvArgs& a, int item, float rms, XSlice<WT>& s) {
+    float v[64];
+    load_item_x<WT, XM>(a, item, v);
+    if (XM == X_NORM || XM == X_NORM_R16) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = v[e] * rms;
+    }
+    if (XM == X_F32_R16 || XM == X_NORM_R16) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] = round_f16(v[e]);
+    }
+    if (WT == WT_Q6K) {
+        float amax = 0.f;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        float inv;
+        s.xs0 = quant_scale(amax, inv);
+        s.xs1 = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            int sum = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t hw = 0, lw = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int q = __float2int_rn(v[c * 16 + 4 * k + j] * inv);
+                    sum += q;
+                    uint32_t hb, lb;
+                    split16(q, hb, lb);
+                    hw |= hb << (8 * j);
+                    lw |= lb << (8 * j);
+                }
+                s.xh[c * 4 + k] = hw;
+                s.xl[c * 4 + k] = lw;
+            }
+            s.corr[c] = -32 * sum;
+        }
+    } else {
+        // two 32-element blocks with separate scales; block 0's words are shifted by the 2-byte
+        // scale that precedes its quants: word m, byte n <-> element 4m + n - 2.
+        float am0 = 0.f, am1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) am0 = fmaxf(am0, fabsf(v[e]));
+#pragma unroll
+        for (int e = 32; e < 64; ++e) am1 = fmaxf(am1, fabsf(v[e]));
+        float inv0, inv1;
+        s.xs0 = quant_scale(am0, inv0);
+        s.xs1 = quant_scale(am1, inv1);
+#pragma unroll
+        for (int m = 0; m < 9; ++m) {
+            uint32_t hw = 0, lw = 0;
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+                const int e = 4 * m + n - 2;
+                if (e >= 0 && e < 32) {
+                    const int q = __float2int_rn(v[e] * inv0);
+                    uint32_t hb, lb;
+                    split16(q, hb, lb);
+                    hw |= hb << (8 * n);
+                    lw |= lb << (8 * n);
+                }
+            }
+            s.xh[m] = hw;
+            s.xl[m] = lw;
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            uint32_t hw = 0, lw = 0;
+#pragma unroll
+            for (int n = 0; n < 4; ++n) {
+                const int q = __float2int_rn(v[32 + 4 * m + n] * inv1);
+                uint32_t hb, lb;
+                split16(q, hb, lb);
+                hw |= hb << (8 * n);
+                lw |= lb << (8 * n);
+            }
+            s.xh[9 + m] = hw;
+            s.xl[9 + m] = lw;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s.corr[c] = 0;
+    }
+}
+
+// Partial dot of one item of one row. `sb` points at the item's super-block (Q6_K) or at the
+// item's first block (Q8_0) in shared memory; 2-byte aligned.
+template <int WT>
+__device__ __forceinline__ float item_dot(const uint8_t* sb, int item, const XSlice<WT>& s) {
+    if (WT == WT_Q6K) {
+        const int h = (item >> 1) & 1, l16 = item & 1;
+        uint32_t ql0[4], ql1[4], qh[4];
+        lds_16B_a2(sb + h * 64 + l16 * 16, ql0);
+        lds_16B_a2(sb + h * 64 + 32 + l16 * 16, ql1);
+        lds_16B_a2(sb + 128 + h * 32 + l16 * 16, qh);
+        const uint32_t sA = lds_u32_a2(sb + 192 + 8 * h);
+        const uint32_t sB = lds_u32_a2(sb + 196 + 8 * h);
+        const uint32_t dbits = *reinterpret_cast<const uint16_t*>(sb + 208);
+        int hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
+        int lo0 = s.corr[0], lo1 = s.corr[1], lo2 = s.corr[2], lo3 = s.corr[3];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t qm = qh[k] & 0x33333333u;  // crumbs 0 (bits 0-1) and 2 (bits 4-5)
+            const uint32_t qn = qh[k] & 0xCCCCCCCCu;  // crumbs 1 (bits 2-3) and 3 (bits 6-7)
+            const uint32_t q0 = (ql0[k] & 0x0F0F0F0Fu) | ((qm << 4) & 0xF0F0F0F0u);
+            const uint32_t q1 = (ql1[k] & 0x0F0F0F0Fu) | ((qn << 2) & 0xF0F0F0F0u);
+            const uint32_t q2 = ((ql0[k] >> 4) & 0x0F0F0F0Fu) | (qm & 0xF0F0F0F0u);
+            const uint32_t q3 = ((ql1[k] >> 4) & 0x0F0F0F0Fu) | ((qn >> 2) & 0xF0F0F0F0u);
+            hi0 = dp4a_us(q0, s.xh[0 * 4 + k], hi0);
+            lo0 = dp4a_uu(q0, s.xl[0 * 4 + k], lo0);
+            hi1 = dp4a_us(q1, s.xh[1 * 4 + k], hi1);
+            lo1 = dp4a_uu(q1, s.xl[1 * 4 + k], lo1);
+            hi2 = dp4a_us(q2, s.xh[2 * 4 + k], hi2);
+            lo2 = dp4a_uu(q2, s.xl[2 * 4 + k], lo2);
+            hi3 = dp4a_us(q3, s.xh[3 * 4 + k], hi3);
+            lo3 = dp4a_uu(q3, s.xl[3 * 4 + k], lo3);
+        }
+        // sub-block scales: column c uses scales[8h + l16 + 2c]
+        const int sc0 = (int)(sA << (24 - 8 * l16)) >> 24;
+        const int sc1 = (int)(sA << (8 - 8 * l16)) >> 24;
+        const int sc2 = (int)(sB << (24 - 8 * l16)) >> 24;
+        const int sc3 = (int)(sB << (8 - 8 * l16)) >> 24;
+        const float t = (float)((hi0 * 256 + lo0) * sc0) + (float)((hi1 * 256 + lo1) * sc1) +
+                        (float)((hi2 * 256 + lo2) * sc2) + (float)((hi3 * 256 + lo3) * sc3);
+        return t * (half_bits_to_float(dbits) * s.xs0);
+    } else {
+        // 68 bytes = 17 words, 4-byte aligned (rows are 4-byte aligned when K % 64 == 0)
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(sb);
+        int hi0 = 0, lo0 = 0, hi1 = 0, lo1 = 0;
+        uint32_t w0 = 0, w8 = 0;
+#pragma unroll
+        for (int m = 0; m < 9; ++m) {
+            const uint32_t q = w[m];
+            if (m == 0) w0 = q;
+            if (m == 8) w8 = q;
+            hi0 = dp4a_ss(q, s.xh[m], hi0);
+            lo0 = dp4a_su(q, s.xl[m], lo0);
+        }
+#pragma unroll
+        for (int m = 9; m < 17; ++m) {
+            const uint32_t q = w[m];
+            hi1 = dp4a_ss(q, s.xh[m], hi1);
+            lo1 = dp4a_su(q, s.xl[m], lo1);
+        }
+        const float d0 = half_bits_to_float(w0);
+        const float d1 = half_bits_to_float(w8 >> 16);
+        return (float)(hi0 * 256 + lo0) * (d0 * s.xs0) + (float)(hi1 * 256 + lo1) * (d1 * s.xs1);
+    }
+}
+
+// Reference argmax order (ops.cuh:467-499): thread t of 256 keeps the first strict maximum of
+// x[t], x[t+256], ...; the tree step `if (s[t+s] > s[t])` keeps position t on ties, so two tied
+// threads meet at their lowest differing index bit and the one with a 0 there wins — i.e. the
+// smaller 8-bit-reversed thread index. NaN and values <= -1e30 never win.
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+    if (!(v > -1e30f)) return false;
+    if (bi < 0) return true;
+    if (v > bv) return true;
+    if (v < bv) return false;
+    const unsigned ki = __brev((unsigned)(i & 255)) >> 24, kb = __brev((unsigned)(bi & 255)) >> 24;
+    return ki < kb || (ki == kb && i < bi);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// --------------------------------------------------------------------------------------------
+template <int WT, int XM, int EPI>
+__global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int ncons_warps = a.nt_cons >> 5;
+    const bool is_producer = (tid >= a.nt_cons);
+
+    // ---- shared memory carve-up: ring | red[2][P*I] | bars | misc
+    uint8_t* ring = smem;
+    float* red = reinterpret_cast<float*>(smem + (size_t)a.ring * a.stage_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * a.P * a.I);
+    uint64_t* empty = full + a.ring;
+    float* misc = reinterpret_cast<float*>(empty + a.ring);  // [32] block reduction scratch
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
+    float* warp_best_v = misc + 40;                                  // [32]
+    int* warp_best_i = reinterpret_cast<int*>(misc + 72);            // [32]
+
+    // ---- CTA row range (virtual rows)
+    const int G = gridDim.x;
+    const int c = blockIdx.x;
+    const int v_begin = (int)(((long long)a.Mv * c) / G);
+    const int v_end = (int)(((long long)a.Mv * (c + 1)) / G);
+    const int rows_cta = v_end - v_begin;
+    const int step = a.dual ? a.P / 2 : a.P;  // virtual rows per stage (dual: gate/up pairs)
+    const int nstages = (rows_cta + step - 1) / step;
+
+    if (tid == 0) {
+        for (int s = 0; s < a.ring; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ncons_warps);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) pdl_launch_dependents();
+
+    if (is_producer) {
+        // ================= producer warp: lane 0 streams the CTA's weight bytes
+        if (lane == 0) {
+            for (int s = 0; s < nstages; ++s) {
+                const int slot = s % a.ring;
+                if (s >= a.ring) {
+                    bool ok = false;
+                    for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                        if (mbar_try_wait(&empty[slot], ((s / a.ring) - 1) & 1)) { ok = true; break; }
+                    if (!ok) {
+                        if (!*abort_flag) set_device_error(-5);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+                const int va = v_begin + s * step;
+                const int n = min(step, v_end - va);
+                StageGeo geo;
+                stage_geo(a, va, n, geo);
+                uint8_t* dst = ring + (size_t)slot * a.stage_bytes;
+                uint32_t tx = 0;
+#pragma unroll
+                for (int k = 0; k < GEMV_MAX_SEG; ++k) {
+                    const Piece& pk = geo.p[k];
+                    if (!pk.valid) continue;
+                    tx += pk.copy_bytes;
+                    // sub-16-byte tail of a tensor: plain 2-byte loads (released by the arrive)
+                    if (pk.tail_bytes) {
+                        const uint16_t* src = reinterpret_cast<const uint16_t*>(pk.src + pk.copy_bytes);
+                        uint16_t* d16 = reinterpret_cast<uint16_t*>(dst + pk.smem_off + pk.copy_bytes);
+                        for (uint32_t b = 0; b < pk.tail_bytes / 2; ++b) d16[b] = src[b];
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(&full[slot], tx);
+#pragma unroll
+                for (int k = 0; k < GEMV_MAX_SEG; ++k)
+                    if (geo.p[k].valid && geo.p[k].copy_bytes)
+                        bulk_g2s(dst + geo.p[k].smem_off, geo.p[k].src, geo.p[k].copy_bytes, &full[slot]);
+            }
+        }
+        // the producer warp takes part in the consumers' first barrier only via __syncthreads
+        // below; it idles afterwards.
+        pdl_wait();
+        return;
+    }
+
+    // ================= consumers
+    pdl_wait();  // x, residual and epilogue targets come from the previous kernel
+
+    const int P = a.P, I = a.I;
+    const int p = tid / I;             // row slot within a stage
+    const int item = tid - p * I;      // fixed K slice of this thread
+    const bool active = (p < P);       // threads beyond P*I only help with barriers/reductions
+
+    // ---- RMSNorm statistics (threads of row slot 0 cover all K once)
+    float rms = 1.f;
+    if (XM == X_NORM || XM == X_NORM_R16) {
+        float ss = 0.f;
+        if (p == 0) {
+            float v[64];
+            // raw x (no weight) for the sum of squares
+            const float* x = static_cast<const float*>(a.x);
+            int base[4];
+            if (WT == WT_Q6K) {
+                const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) base[cc] = b * 256 + h * 128 + cc * 32 + l16 * 16;
+            } else {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) base[cc] = item * 64 + cc * 16;
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const float4* q4 = reinterpret_cast<const float4*>(x + base[cc]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 f = q4[k];
+                    v[cc * 16 + 4 * k + 0] = f.x;
+                    v[cc * 16 + 4 * k + 1] = f.y;
+                    v[cc * 16 + 4 * k + 2] = f.z;
+                    v[cc * 16 + 4 * k + 3] = f.w;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) misc[warp] = ss;
+        named_bar_sync(1, a.nt_cons);
+        float tot = 0.f;
+        for (int w = 0; w < ncons_warps; ++w) tot += misc[w];
+        rms = rsqrtf(tot / (float)a.K + a.eps);
+    }
+
+    XSlice<WT> xs;
+    if (active) make_slice<WT, XM>(a, item, rms, xs);
+
+    const int blocks_per_item_bytes = (WT == WT_Q6K) ? 0 : 68;
+    float best_v = 0.f;
+    int best_i = -1;
+    int buf = 0;
+
+    for (int s = 0; s < nstages; ++s) {
+        const int slot = s % a.ring;
+        const int va = v_begin + s * step;
+        const int n = min(step, v_end - va);
+        StageGeo geo;
+        stage_geo(a, va, n, geo);
+        const int rows_in_stage = a.dual ? 2 * n : n;
+
+        bool ok = !*abort_flag;
+        if (ok) {
+            bool got = false;
+            for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                if (mbar_try_wait(&full[slot], (s / a.ring) & 1)) { got = true; break; }
+            if (!got) {
+                if (!*abort_flag) set_device_error(-5);
+                *abort_flag = 1;
+                ok = false;
+            }
+        }
+        // rows handled by this thread in the stage: slot p (single pass; P rows per stage, dual: P/2 pairs)
+        float part = 0.f;
+        if (ok && active && p < rows_in_stage) {
+            const int k = piece_of(geo, p);
+            uint32_t off = 0, delta = 0;
+            int first = 0;
+#pragma unroll
+            for (int j = 0; j < GEMV_MAX_SEG; ++j)
+                if (j == k) {
+                    off = geo.p[j].smem_off;
+                    delta = geo.p[j].delta;
+                    first = geo.p[j].first_row;
+                }
+            const uint8_t* rowp = ring + (size_t)slot * a.stage_bytes + off + delta + (size_t)(p - first) * a.rowB;
+            const uint8_t* sbp = (WT == WT_Q6K) ? rowp + (item >> 2) * 210 : rowp + item * blocks_per_item_bytes;
+            part = item_dot<WT>(sbp, item, xs);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (active) red[buf * P * I + tid] = part;
+        named_bar_sync(1, a.nt_cons);
+
+        // ---- reduce rows and run the epilogue (fixed order -> deterministic)
+        const int nred = a.dual ? n : rows_in_stage;
+        for (int r = warp; r < nred; r += ncons_warps) {
+            const float* rr = red + buf * P * I + r * I;
+            float sum = 0.f;
+            for (int j = lane; j < I; j += 32) sum += rr[j];
+            sum = warp_sum(sum);
+            float sum2 = 0.f;
+            if (a.dual) {
+                const float* r2 = red + buf * P * I + (r + n) * I;
+                for (int j = lane; j < I; j += 32) sum2 += r2[j];
+                sum2 = warp_sum(sum2);
+            }
+            if (lane == 0 && ok) {
+                if (EPI == EPI_SWIGLU) {
+                    const int row = va + r;
+                    const float g = sum, u = sum2;
+                    const float o = silu_mul(g, u);
+                    if (a.act_f16) reinterpret_cast<__half*>(a.act)[row] = __float2half_rn(o);
+                    else reinterpret_cast<float*>(a.act)[row] = o;
+                } else {
+                    // map virtual row -> tensor, row
+                    const int kk = piece_of(geo, r);
+                    int row = 0;
+                    float* yk = nullptr;
+                    const float* bk = nullptr;
+#pragma unroll
+                    for (int j = 0; j < GEMV_MAX_SEG; ++j)
+                        if (j == kk) {
+                            row = geo.p[j].seg_row0 + (r - geo.p[j].first_row);
+                            yk = a.seg[j].y;
+                            bk = a.seg[j].bias;
+                        }
+                    if (EPI == EPI_STORE) {
+                        yk[row] = bk ? sum + bk[row] : sum;
+                    } else if (EPI == EPI_RESID) {
+                        a.resid[row] = sum + a.resid[row];
+                    } else if (EPI == EPI_LMHEAD) {
+                        a.logits[row] = sum;
+                        if (argmax_better(sum, row, best_v, best_i)) {
+                            best_v = sum;
+                            best_i = row;
+                        }
+                    }
+                }
+            }
+        }
+        buf ^= 1;
+    }
+
+    if (EPI == EPI_LMHEAD) {
+        // CTA best -> global; the last CTA to arrive reduces all CTAs and advances the state.
+        if (lane == 0) {
+            warp_best_v[warp] = best_v;
+            warp_best_i[warp] = best_i;
+        }
+        named_bar_sync(1, a.nt_cons);
+        if (tid == 0) {
+            float bv = 0.f;
+            int bi = -1;
+            for (int w = 0; w < ncons_warps; ++w)
+                if (warp_best_i[w] >= 0 && argmax_better(warp_best_v[w], warp_best_i[w], bv, bi)) {
+                    bv = warp_best_v[w];
+                    bi = warp_best_i[w];
+                }
+            a.cta_val[c] = bv;
+            a.cta_idx[c] = bi;
+            __threadfence();
+            const unsigned int prev = atomicAdd(a.counter, 1u);
+            if (prev == (unsigned)G - 1) {
+                __threadfence();
+                float gv = 0.f;
+                int gi = -1;
+                for (int k = 0; k < G; ++k) {
+                    const int ik = ((volatile int*)a.cta_idx)[k];
+                    const float vk = ((volatile float*)a.cta_val)[k];
+                    if (ik >= 0 && argmax_better(vk, ik, gv, gi)) {
+                        gv = vk;
+                        gi = ik;
+                    }
+                }
+                if (gi < 0) gi = 0;
+                if (a.state) {
+                    DecodeState* st = a.state;
+                    st->token = gi;
+                    st->pos = st->pos + 1;
+                    if (a.token_log && st->step < a.token_log_cap) a.token_log[st->step] = gi;
+                    st->step = st->step + 1;
+                }
+                *a.counter = 0u;
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------------------------
+// Simple kernels for shapes the streaming kernel does not take (K % 64 != 0 for Q8_0, huge K,
+// misaligned weights): one warp per row, fp32 accumulation in the reference's per-lane order.
+__global__ void gemv_q6k_simple_kernel(const uint8_t* __restrict__ W, const uint16_t* __restrict__ x,
+                                       const float* __restrict__ bias, float* __restrict__ y, int M,
+                                       int K);
+__global__ void gemv_q8_0_simple_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x,
+                                        float* __restrict__ y, int M, int K);
+
+// Host-side launch planning for the streaming kernel.
+struct GemvPlan {
+    int ok;
+    int grid, block, smem;
+    int P, ring, stage_bytes, I, rowB, nt_cons;
+};
+
+}  // namespace fence

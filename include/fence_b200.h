@@ -1,0 +1,298 @@
+/*
+ * fence_b200.h — C-ABI of the B200 (sm_100a) decode engine for Fence's GGUF token loop.
+ *
+ * Two layers live behind this header, both exported from libfence_b200.so with C linkage:
+ *
+ *  1. Drop-in kernel launchers. Each `fence_<name>` replaces the inline host launcher of the same
+ *     name in the reference's header-only kernels (src/kernels/gemv_q6k.cuh, gemv_q8_0.cuh, ops.cuh):
+ *     same argument order, same meaning, caller-owned device pointers, asynchronous on `stream`,
+ *     never allocate. They return a status (0 = ok, else a cudaError_t value or a FENCE_E_* code),
+ *     where the reference returned void and left errors to the caller's next CUDA_CHECK.
+ *     Under C++ the header also defines `inline` wrappers with the reference's exact names, void
+ *     return and `cudaStream_t stream = 0` default, so reference call sites compile unchanged.
+ *
+ *  2. The engine: the reference's Qwen3Model (src/model/qwen3.h:115-155) — load / forward /
+ *     sample_greedy / sample_nucleus / generate — as opaque-handle C functions, plus the
+ *     synthetic-GGUF writer used by the tests and the benchmark.
+ *
+ * Layout contracts (identical to the reference):
+ *   block_q6_K  src/kernels/q6k_types.h:27-32   210 B / 256 weights: ql[128] qh[64] int8 scales[16] fp16 d
+ *   block_q8_0  src/kernels/q8_0_types.h:11-14   34 B / 32 weights: fp16 d, int8 qs[32]
+ *   Weight matrix W[M x K]: M rows, each row K/256 (Q6_K) or K/32 (Q8_0) consecutive blocks;
+ *   the GGUF dims of such a tensor are [K, M] (ne0 = input, ne1 = output).
+ *   KV cache (drop-in store_kv / gqa_attention): [max_ctx][n_kv_heads * head_dim] fp16 per layer.
+ *
+ * Preconditions beyond the reference's: weight pointers handed to the GEMV launchers must be
+ * 16-byte aligned (cudaMalloc and GGUF's 32-byte tensor alignment both give that); violations
+ * return FENCE_E_ALIGN instead of launching.
+ */
+#ifndef FENCE_B200_H
+#define FENCE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct CUstream_st; /* cudaStream_t is `struct CUstream_st*`; pass one directly (NULL = legacy stream). */
+typedef struct CUstream_st* fence_stream_t;
+
+/* ---- status codes (negative: library codes; positive: cudaError_t values) ---- */
+#define FENCE_OK              0
+#define FENCE_E_ARG         (-1)  /* bad shape / null pointer / unsupported size              */
+#define FENCE_E_ALIGN       (-2)  /* pointer alignment precondition violated                  */
+#define FENCE_E_FORMAT      (-3)  /* GGUF file malformed or missing tensors / metadata        */
+#define FENCE_E_UNSUPPORTED (-4)  /* a tensor type or shape the engine does not handle        */
+#define FENCE_E_DEVICE_WAIT (-5)  /* a device-side bounded wait expired (kernel gave up)       */
+#define FENCE_E_IO          (-6)  /* file could not be opened / written                       */
+#define FENCE_E_NOMEM       (-7)  /* device or host allocation failed                         */
+
+/* Thread-local text of the last error raised by any fence_* call on this thread ("" if none). */
+const char* fence_last_error(void);
+/* Returns and clears the device-side error word that kernels set when a bounded wait expires
+ * (0 if none). Synchronises the device. */
+int fence_device_error(void);
+
+/* ---- quant block types (byte-identical to the reference) ---- */
+#pragma pack(push, 1)
+typedef struct block_q6_K {
+    uint8_t ql[128];     /* low 4 bits of each 6-bit quant, 2 per byte          */
+    uint8_t qh[64];      /* high 2 bits, 4 per byte                              */
+    int8_t  scales[16];  /* signed scale per 16-element sub-block               */
+#if defined(__cplusplus) && defined(__CUDA_FP16_TYPES_EXIST__) && !defined(FENCE_BUILDING_LIBRARY)
+    __half  d;           /* fp16 super-block scale                               */
+#else
+    uint16_t d;          /* fp16 super-block scale (IEEE binary16 bits)          */
+#endif
+} block_q6_K;
+typedef struct block_q8_0 {
+#if defined(__cplusplus) && defined(__CUDA_FP16_TYPES_EXIST__) && !defined(FENCE_BUILDING_LIBRARY)
+    __half  d;
+#else
+    uint16_t d;
+#endif
+    int8_t  qs[32];
+} block_q8_0;
+#pragma pack(pop)
+
+/* =====================================================================================
+ * 1. Drop-in kernel launchers. All pointers are device pointers owned by the caller.
+ *    fp16 buffers are passed as uint16_t* (IEEE binary16 bit patterns, i.e. __half*).
+ * ===================================================================================== */
+
+/* y[M] = W_q6k[M x K] . x[K]; x fp16, y fp32, K % 256 == 0.
+ * Replaces gemv_q6k, src/kernels/gemv_q6k.cuh:89-102. */
+int fence_gemv_q6k(const block_q6_K* W, const uint16_t* x, float* y, int M, int K,
+                   fence_stream_t stream);
+/* y = W.x + bias. Replaces gemv_q6k_bias, src/kernels/gemv_q6k.cuh:140-151. */
+int fence_gemv_q6k_bias(const block_q6_K* W, const uint16_t* x, const float* bias, float* y,
+                        int M, int K, fence_stream_t stream);
+/* y[M] = W_q8_0[M x K] . x[K]; x fp32, y fp32, K % 32 == 0.
+ * Replaces gemv_q8_0, src/kernels/gemv_q8_0.cuh:99-104. */
+int fence_gemv_q8_0(const block_q8_0* W, const float* x, float* y, int M, int K,
+                    fence_stream_t stream);
+/* out[0..dim) = dequant(row token_id of a Q8_0 matrix with `dim` columns).
+ * Replaces embed_q8_0, src/kernels/gemv_q8_0.cuh:31-36. */
+int fence_embed_q8_0(float* out, const block_q8_0* weight, int token_id, int dim,
+                     fence_stream_t stream);
+
+/* out[i] = w[i] * x[i] * rsqrt(mean(x^2) + eps). Replaces rms_norm, src/kernels/ops.cuh:47-51. */
+int fence_rms_norm(float* out, const float* x, const float* w, int n, float eps,
+                   fence_stream_t stream);
+/* In-place form. Replaces rms_norm_inplace, src/kernels/ops.cuh:54-60. */
+int fence_rms_norm_inplace(float* x, const float* w, int n, float eps, fence_stream_t stream);
+/* RMSNorm of each head_dim slice of x (n_heads slices), weight w[head_dim] shared by all heads.
+ * Replaces rms_norm_per_head, src/kernels/ops.cuh:97-103. */
+int fence_rms_norm_per_head(float* x, const float* w, int n_heads, int head_dim, float eps,
+                            fence_stream_t stream);
+/* NeoX-pair rotary embedding of q [n_q_heads*head_dim] and k [n_kv_heads*head_dim] in place:
+ * pair (i, i+head_dim/2), angle = pos * freq_base^(-2i/head_dim).
+ * Replaces apply_rope, src/kernels/ops.cuh:169-177. */
+int fence_apply_rope(float* q, float* k, int head_dim, int n_q_heads, int n_kv_heads, int pos,
+                     float freq_base, fence_stream_t stream);
+/* out[i] = gate[i] / (1 + exp(-gate[i])) * up[i]. Replaces silu_elementwise_mul, ops.cuh:197-202. */
+int fence_silu_elementwise_mul(float* out, const float* gate, const float* up, int n,
+                               fence_stream_t stream);
+/* x[i] += residual[i]. Replaces residual_add, src/kernels/ops.cuh:265-270. */
+int fence_residual_add(float* x, const float* residual, int n, fence_stream_t stream);
+/* In-place softmax of x[0..n). Replaces softmax, src/kernels/ops.cuh:248-251. */
+int fence_softmax(float* x, int n, fence_stream_t stream);
+/* fp32 -> fp16 (round to nearest even). Replaces f32_to_f16, ops.cuh:457-462, and
+ * float_to_half, ops.cuh:284-289 (same operation). */
+int fence_f32_to_f16(uint16_t* out, const float* in, int n, fence_stream_t stream);
+int fence_float_to_half(uint16_t* out, const float* in, int n, fence_stream_t stream);
+/* fp16 -> fp32. Replaces half_to_float, src/kernels/ops.cuh:303-308. */
+int fence_half_to_float(float* out, const uint16_t* in, int n, fence_stream_t stream);
+/* k_cache[pos*kv_dim + i] = fp16(k[i]), same for v. Replaces store_kv, ops.cuh:435-443. */
+int fence_store_kv(uint16_t* k_cache, uint16_t* v_cache, const float* k, const float* v, int pos,
+                   int kv_dim, int max_ctx, fence_stream_t stream);
+/* Single-query grouped-query attention over positions [0, seq_len) of an fp16 KV cache laid out
+ * [max_ctx][n_kv_heads*head_dim]; q head h reads kv head h / (n_q_heads/n_kv_heads).
+ * score_buf: caller scratch of n_q_heads*max_ctx floats, as in the reference; this engine keeps
+ * its split-context partial results there. head_dim must be 64, 128 or 256.
+ * Replaces gqa_attention, src/kernels/ops.cuh:405-414. */
+int fence_gqa_attention(float* attn_out, const float* q, const uint16_t* k_cache,
+                        const uint16_t* v_cache, int head_dim, int n_q_heads, int n_kv_heads,
+                        int seq_len, int max_ctx, float* score_buf, fence_stream_t stream);
+/* *result = index of the largest x[i], with the reference's tie order (256-thread strided scan,
+ * then a tree that keeps the lower position on ties): among equal maxima the index whose
+ * (i mod 256) has the smallest 8-bit reversal wins, then the smallest index; NaN and values
+ * <= -1e30 never win; 0 when nothing qualifies. Replaces argmax, src/kernels/ops.cuh:501-505. */
+int fence_argmax(const float* x, int* result, int n, fence_stream_t stream);
+
+/* =====================================================================================
+ * 2. Engine — the reference's Qwen3Model (src/model/qwen3.h:115-155) as a C handle.
+ * ===================================================================================== */
+
+typedef struct fence_model fence_model;
+
+typedef struct fence_config {
+    int   n_layers, embed_dim, ff_dim, n_heads, n_kv_heads, head_dim, vocab_size, max_ctx;
+    float rope_freq_base, rms_eps;
+    /* sampling parameters (src/model/qwen3.h:31-37 defaults) */
+    float temperature, top_p;
+    int   top_k;
+    float repetition_penalty, min_p;
+    int   dynamic_temp;
+    /* engine facts */
+    int   linear_type;      /* GGML type id of the attention/FFN linears: 14 = Q6_K, 8 = Q8_0 */
+    int   embd_type;        /* GGML type id of token_embd (8 = Q8_0)                        */
+    int   has_qk_norm;      /* attn_q_norm/attn_k_norm present                               */
+    int   n_experts, n_experts_used;
+    int   kv_dtype;         /* FENCE_KV_BF16 or FENCE_KV_F16                                 */
+    int   tp_rank, tp_size;
+    size_t weight_bytes;    /* bytes of weights streamed per decode token (this rank)        */
+} fence_config;
+
+#define FENCE_KV_BF16 0
+#define FENCE_KV_F16  1
+
+typedef struct fence_load_opts {
+    int max_ctx;        /* context length to allocate (reference default 4096)            */
+    int kv_dtype;       /* FENCE_KV_BF16 (default) or FENCE_KV_F16 (reference numerics)   */
+    int device;         /* CUDA device ordinal                                            */
+    int use_graph;      /* capture the token step in a CUDA graph (default 1)             */
+    int verbose;        /* print the reference's load banner                              */
+    /* tensor parallel: rank `tp_rank` of `tp_size`; nccl_comm is an ncclComm_t or NULL */
+    int tp_rank, tp_size;
+    void* nccl_comm;
+} fence_load_opts;
+
+/* Fills *opts with defaults (max_ctx 4096, bf16 KV, device 0, graphs on, single rank). */
+void fence_load_opts_default(fence_load_opts* opts);
+
+/* Qwen3Model::load (src/model/qwen3.cu:116-228): mmap the GGUF, read the config from its metadata
+ * (same keys, types and fallbacks), upload weights, allocate KV cache and scratch.
+ * Returns NULL on failure (fence_last_error() says why). */
+fence_model* fence_model_load(const char* gguf_path, const fence_load_opts* opts);
+/* Qwen3Model::unload. Safe on NULL. */
+void fence_model_free(fence_model* m);
+int  fence_model_config(const fence_model* m, fence_config* out);
+/* Sets the sampling parameters the CLI flags --temp/--top-p/--top-k/--rep-penalty set. */
+int  fence_set_sampling(fence_model* m, float temperature, float top_p, int top_k,
+                        float repetition_penalty);
+
+/* Qwen3Model::forward (qwen3.cu:241-265): one token at position pos; returns the DEVICE pointer
+ * of the fp32 logits [vocab] (valid until the next forward), NULL on error. */
+const float* fence_forward(fence_model* m, int token_id, int pos);
+/* Qwen3Model::sample_greedy (qwen3.cu:344-349): argmax of device logits, reference tie order. */
+int fence_sample_greedy(fence_model* m, const float* d_logits);
+/* Qwen3Model::sample_nucleus (qwen3.cu:351-460): repetition penalty per occurrence in history,
+ * min-p 0.05, entropy-scaled temperature, top-k then top-p, draw from the survivors. The draw uses
+ * the engine's seeded mt19937 (fence_set_seed) where the reference seeds from random_device. */
+int fence_sample_nucleus(fence_model* m, const float* d_logits, const int* history, int n_history);
+int fence_set_seed(fence_model* m, uint64_t seed);
+
+/* Qwen3Model::generate (qwen3.cu:463-519): token-by-token prefill of `prompt`, then up to
+ * max_new_tokens sampled tokens, stopping at eos_id (pass -1 for no stop token) or max_ctx.
+ * out receives prompt + generated ids (capacity out_cap); *n_out their count. Every token crosses
+ * to the host, as in the reference. */
+int fence_generate(fence_model* m, const int* prompt, int n_prompt, int max_new_tokens,
+                   int eos_id, int* out, int out_cap, int* n_out);
+
+/* Device-resident greedy decode: starting from (token, pos) already fed, run n_steps token steps
+ * back to back with the sampled id fed to the next step on the device (no host round trip);
+ * the n_steps sampled ids are copied to out_tokens (host) at the end. */
+int fence_decode_greedy(fence_model* m, int token, int pos, int n_steps, int* out_tokens);
+
+/* Last logits / hidden state of the most recent step, copied to host (for parity tests). */
+int fence_copy_logits(fence_model* m, float* host_out);
+
+/* Times n_steps device-resident decode steps with CUDA events on the engine's stream; *ms = total. */
+int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms);
+
+/* =====================================================================================
+ * 3. Synthetic GGUF writer (seeded, counter-based, byte-reproducible).
+ * ===================================================================================== */
+typedef struct fence_synth_spec {
+    const char* arch;            /* general.architecture, e.g. "qwen3" or "llama"            */
+    int   n_layers, embed_dim, ff_dim, n_heads, n_kv_heads, head_dim, vocab_size;
+    float rope_freq_base, rms_eps;
+    int   linear_type;           /* 14 = Q6_K, 8 = Q8_0                                     */
+    int   embd_type;             /* 8 = Q8_0                                                */
+    int   qk_norm;               /* write attn_q_norm / attn_k_norm                         */
+    int   n_experts, n_experts_used; /* 0 = dense FFN                                       */
+    int   write_tokenizer;       /* write tokenizer.ggml.tokens (vocab_size strings)        */
+    int   gguf_version;          /* 2 or 3                                                  */
+    uint32_t alignment;          /* general.alignment                                       */
+    uint64_t seed;
+    float q6k_d, q8_d;           /* fp16 super-block scales (defaults 1.5e-5 / 1.6e-4)      */
+    float norm_value;            /* value of every norm weight (default 1.0)                */
+} fence_synth_spec;
+
+void fence_synth_spec_default(fence_synth_spec* s);
+/* Writes the model to `path` with n_threads workers. Returns 0 or a FENCE_E_* code. */
+int fence_synth_write_gguf(const char* path, const fence_synth_spec* spec, int n_threads);
+/* Fills a host buffer with n seeded blocks of the given type, the same generator the writer uses
+ * for tensor number `stream_id`. */
+int fence_synth_fill_blocks(void* dst, int ggml_type, size_t n_blocks, uint64_t seed,
+                            uint64_t stream_id, float d);
+
+#ifdef __cplusplus
+} /* extern "C" */
+
+/* ---- C++: the reference's launcher names, argument lists and default stream ---- */
+#if defined(__CUDA_FP16_TYPES_EXIST__) && defined(CUDART_VERSION)
+inline void gemv_q6k(const block_q6_K* W, const __half* x, float* y, int M, int K,
+                     cudaStream_t s = 0) { fence_gemv_q6k(W, (const uint16_t*)x, y, M, K, s); }
+inline void gemv_q6k_bias(const block_q6_K* W, const __half* x, const float* b, float* y, int M,
+                          int K, cudaStream_t s = 0) {
+    fence_gemv_q6k_bias(W, (const uint16_t*)x, b, y, M, K, s); }
+inline void gemv_q8_0(const block_q8_0* W, const float* x, float* y, int M, int K,
+                      cudaStream_t s = 0) { fence_gemv_q8_0(W, x, y, M, K, s); }
+inline void embed_q8_0(float* o, const block_q8_0* w, int tok, int dim, cudaStream_t s = 0) {
+    fence_embed_q8_0(o, w, tok, dim, s); }
+inline void rms_norm(float* o, const float* x, const float* w, int n, float eps,
+                     cudaStream_t s = 0) { fence_rms_norm(o, x, w, n, eps, s); }
+inline void rms_norm_inplace(float* x, const float* w, int n, float eps, cudaStream_t s = 0) {
+    fence_rms_norm_inplace(x, w, n, eps, s); }
+inline void rms_norm_per_head(float* x, const float* w, int nh, int hd, float eps,
+                              cudaStream_t s = 0) { fence_rms_norm_per_head(x, w, nh, hd, eps, s); }
+inline void apply_rope(float* q, float* k, int hd, int nq, int nkv, int pos, float base,
+                       cudaStream_t s = 0) { fence_apply_rope(q, k, hd, nq, nkv, pos, base, s); }
+inline void silu_elementwise_mul(float* o, const float* g, const float* u, int n,
+                                 cudaStream_t s = 0) { fence_silu_elementwise_mul(o, g, u, n, s); }
+inline void residual_add(float* x, const float* r, int n, cudaStream_t s = 0) {
+    fence_residual_add(x, r, n, s); }
+inline void softmax(float* x, int n, cudaStream_t s = 0) { fence_softmax(x, n, s); }
+inline void f32_to_f16(__half* o, const float* i, int n, cudaStream_t s = 0) {
+    fence_f32_to_f16((uint16_t*)o, i, n, s); }
+inline void float_to_half(__half* o, const float* i, int n, cudaStream_t s = 0) {
+    fence_float_to_half((uint16_t*)o, i, n, s); }
+inline void half_to_float(float* o, const __half* i, int n, cudaStream_t s = 0) {
+    fence_half_to_float(o, (const uint16_t*)i, n, s); }
+inline void store_kv(__half* kc, __half* vc, const float* k, const float* v, int pos, int kv_dim,
+                     int max_ctx, cudaStream_t s = 0) {
+    fence_store_kv((uint16_t*)kc, (uint16_t*)vc, k, v, pos, kv_dim, max_ctx, s); }
+inline void gqa_attention(float* o, const float* q, const __half* kc, const __half* vc, int hd,
+                          int nq, int nkv, int seq_len, int max_ctx, float* score_buf,
+                          cudaStream_t s = 0) {
+    fence_gqa_attention(o, q, (const uint16_t*)kc, (const uint16_t*)vc, hd, nq, nkv, seq_len,
+                        max_ctx, score_buf, s); }
+inline void argmax(const float* x, int* r, int n, cudaStream_t s = 0) { fence_argmax(x, r, n, s); }
+#endif /* fp16 + runtime headers */
+#endif /* __cplusplus */
+
+#endif /* FENCE_B200_H */

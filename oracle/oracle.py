@@ -1,0 +1,162 @@
+"""ctypes view of the checker libraries under oracle/ — TEST INFRASTRUCTURE ONLY.
+
+* liboracle.so       : the CPU restatement of the reference's token loop (fence_oracle.c)
+* _ref/libref_cpu.so : the reference's own fp64 host oracle and golden blocks, compiled from the
+                       reference tree (tests/test_gemv_q6k.cu, tests/test_q6k_dot.cu)
+* _ref/ref_model     : the reference's CUDA forward rebuilt for sm_100a (GPU only)
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_CPU_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
+REF_MODEL = os.path.join(HERE, "_ref", "ref_model")
+
+_vp = ctypes.c_void_p
+_o = None
+_r = None
+
+
+def oracle() -> ctypes.CDLL:
+    global _o
+    if _o is None:
+        L = ctypes.CDLL(ORACLE_SO)
+        sig = {
+            "oracle_h2f": (ctypes.c_float, [ctypes.c_uint16]),
+            "oracle_f2h": (ctypes.c_uint16, [ctypes.c_float]),
+            "oracle_bf2f": (ctypes.c_float, [ctypes.c_uint16]),
+            "oracle_f2bf": (ctypes.c_uint16, [ctypes.c_float]),
+            "oracle_q6k_dequant": (None, [_vp, _vp]),
+            "oracle_q6k_dot_block": (ctypes.c_double, [_vp, _vp]),
+            "oracle_gemv_q6k": (None, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+            "oracle_gemv_q8_0": (None, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+            "oracle_embed_q8_0": (None, [_vp, _vp, ctypes.c_int, ctypes.c_int]),
+            "oracle_rms_norm": (None, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_float]),
+            "oracle_rms_norm_per_head": (None, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
+            "oracle_rope": (None, [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float]),
+            "oracle_silu_mul": (None, [_vp, _vp, _vp, ctypes.c_int]),
+            "oracle_softmax": (None, [_vp, ctypes.c_int]),
+            "oracle_attention": (None, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_long, ctypes.c_long,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+            "oracle_argmax": (ctypes.c_int, [_vp, ctypes.c_int]),
+            "oracle_model_open": (_vp, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+            "oracle_model_close": (None, [_vp]),
+            "oracle_model_dims": (None, [_vp, _vp]),
+            "oracle_forward": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
+            "oracle_last_hidden": (None, [_vp, _vp]),
+        }
+        for n, (res, args) in sig.items():
+            f = getattr(L, n)
+            f.restype, f.argtypes = res, args
+        _o = L
+    return _o
+
+
+def ref_cpu() -> ctypes.CDLL | None:
+    """The reference's compiled host oracle, or None when oracle/_ref was not built."""
+    global _r
+    if _r is None:
+        if not os.path.exists(REF_CPU_SO):
+            return None
+        L = ctypes.CDLL(REF_CPU_SO)
+        L.ref_cpu_gemv_q6k.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int]
+        L.ref_cpu_gemv_q6k.restype = None
+        L.ref_cpu_q6k_dot_block.argtypes = [_vp, _vp]
+        L.ref_cpu_q6k_dot_block.restype = ctypes.c_double
+        L.ref_set_q6.argtypes = [_vp, ctypes.c_int, ctypes.c_int]
+        L.ref_set_q6.restype = None
+        L.ref_dot_case.argtypes = [ctypes.c_int, _vp, _vp, ctypes.POINTER(ctypes.c_double)]
+        L.ref_dot_case.restype = ctypes.c_int
+        L.ref_dot_case_name.argtypes = [ctypes.c_int]
+        L.ref_dot_case_name.restype = ctypes.c_char_p
+        _r = L
+    return _r
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(_vp)
+
+
+# ------------------------------------------------------------------ array helpers
+def f2h_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> fp16 bit patterns (round to nearest even)."""
+    return np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def gemv_q6k(W: bytes | np.ndarray, x_f16_bits: np.ndarray, M: int, K: int, threads: int = 8) -> np.ndarray:
+    Wb = np.frombuffer(W, dtype=np.uint8) if isinstance(W, (bytes, bytearray)) else W
+    y = np.zeros(M, dtype=np.float64)
+    xb = np.ascontiguousarray(x_f16_bits, dtype=np.uint16)
+    oracle().oracle_gemv_q6k(_p(Wb), _p(xb), _p(y), M, K, threads)
+    return y
+
+
+def gemv_q8_0(W: bytes | np.ndarray, x: np.ndarray, M: int, K: int, threads: int = 8) -> np.ndarray:
+    Wb = np.frombuffer(W, dtype=np.uint8) if isinstance(W, (bytes, bytearray)) else W
+    y = np.zeros(M, dtype=np.float64)
+    xf = np.ascontiguousarray(x, dtype=np.float32)
+    oracle().oracle_gemv_q8_0(_p(Wb), _p(xf), _p(y), M, K, threads)
+    return y
+
+
+def argmax(x: np.ndarray) -> int:
+    xf = np.ascontiguousarray(x, dtype=np.float32)
+    return int(oracle().oracle_argmax(_p(xf), xf.size))
+
+
+class OracleModel:
+    """CPU restatement of Qwen3Model over a GGUF file (kv_bf16 selects the cache rounding)."""
+
+    def __init__(self, path: str, max_ctx: int = 4096, kv_bf16: bool = True, threads: int = 8):
+        self._h = oracle().oracle_model_open(path.encode(), max_ctx, int(kv_bf16), threads)
+        if not self._h:
+            raise RuntimeError(f"oracle could not open {path}")
+        d = np.zeros(10, dtype=np.int32)
+        oracle().oracle_model_dims(self._h, _p(d))
+        (self.n_layers, self.embed_dim, self.ff_dim, self.n_heads, self.n_kv_heads, self.head_dim,
+         self.vocab_size, self.max_ctx, self.linear_type, self.qk_norm) = (int(v) for v in d)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        out = np.empty(self.vocab_size, dtype=np.float32)
+        if oracle().oracle_forward(self._h, token, pos, _p(out)) != 0:
+            raise RuntimeError("oracle forward failed")
+        return out
+
+    def close(self):
+        if self._h:
+            oracle().oracle_model_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def read_ref_dump(path: str):
+    """Reads the file written by _ref/ref_model: (vocab, n_prompt, ids[steps], logits[steps, vocab] or None)."""
+    raw = np.fromfile(path, dtype=np.int32, count=4)
+    magic, V, n_prompt, steps = (int(v) for v in raw)
+    if magic != 0x46524546:
+        raise ValueError("not a reference dump")
+    body = np.fromfile(path, dtype=np.uint8, offset=16)
+    rec = 4 + 4 * V
+    with_logits = body.size == steps * rec
+    ids = np.empty(steps, dtype=np.int32)
+    logits = np.empty((steps, V), dtype=np.float32) if with_logits else None
+    for s in range(steps):
+        if with_logits:
+            chunk = body[s * rec:(s + 1) * rec]
+            ids[s] = chunk[:4].view(np.int32)[0]
+            logits[s] = chunk[4:].view(np.float32)
+        else:
+            ids[s] = body[s * 4:(s + 1) * 4].view(np.int32)[0]
+    return V, n_prompt, ids, logits

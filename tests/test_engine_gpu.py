@@ -1,0 +1,117 @@
+"""The decode engine (fused kernels, CUDA graph) against the CPU oracle's restatement of the
+reference forward (src/model/qwen3.cu:241-341) on seeded synthetic GGUF models."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 2e-3  # engine vs fp64 oracle on the tiny models (north-star bound vs the reference: 2e-2)
+
+
+@pytest.fixture(scope="module")
+def models(fb, tmp_path_factory):
+    d = tmp_path_factory.mktemp("models")
+    out = {}
+    for cfg in ["tiny-q6k", "tiny-q8"]:
+        p = str(d / f"{cfg}.gguf")
+        fb.synth_write(p, cfg, seed=21)
+        out[cfg] = p
+    return out
+
+
+def run_teacher(fb, orc, path, kv, tokens, max_ctx=256, graph=True):
+    eng = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, use_graph=graph)
+    ora = orc.OracleModel(path, max_ctx=max_ctx, kv_bf16=(kv == fb.FENCE_KV_BF16), threads=8)
+    diffs, ids_e, ids_o, margins = [], [], [], []
+    for pos, tok in enumerate(tokens):
+        d = eng.forward(tok, pos)
+        le = eng.logits()
+        lo = ora.forward(tok, pos)
+        diffs.append(float(np.max(np.abs(le.astype(np.float64) - lo))))
+        ids_e.append(eng.sample_greedy(d))
+        ids_o.append(orc.argmax(lo))
+        s = np.sort(lo)
+        margins.append(float(s[-1] - s[-2]))
+    eng.close()
+    ora.close()
+    return np.array(diffs), ids_e, ids_o, margins
+
+
+@pytest.mark.parametrize("cfg", ["tiny-q6k", "tiny-q8"])
+@pytest.mark.parametrize("kv", [0, 1])
+def test_engine_matches_oracle_teacher_forced(fb, orc, models, cfg, kv):
+    tokens = list(np.random.default_rng(1).integers(0, 2048, 40))
+    diffs, ids_e, ids_o, margins = run_teacher(fb, orc, models[cfg], kv, tokens)
+    assert diffs.max() < LOGIT_ATOL, diffs
+    for e, o, m in zip(ids_e, ids_o, margins):
+        if m > 2 * LOGIT_ATOL:
+            assert e == o
+
+
+def test_graph_and_eager_are_identical(fb, models):
+    p = models["tiny-q6k"]
+    toks = [5, 9, 1000, 3, 77, 2047, 0]
+    outs = []
+    for graph in (True, False):
+        m = fb.Model(p, max_ctx=64, use_graph=graph)
+        for pos, t in enumerate(toks):
+            m.forward(t, pos)
+        outs.append(m.logits())
+        m.close()
+    assert np.array_equal(outs[0], outs[1])
+
+
+def test_decode_greedy_matches_stepwise(fb, models):
+    p = models["tiny-q8"]
+    m = fb.Model(p, max_ctx=128)
+    prompt = [11, 22, 33, 44]
+    for pos, t in enumerate(prompt[:-1]):
+        m.forward(t, pos)
+    dev_ids = m.decode_greedy(prompt[-1], len(prompt) - 1, 30)
+    m.close()
+    m = fb.Model(p, max_ctx=128)
+    ids = []
+    d = None
+    for pos, t in enumerate(prompt):
+        d = m.forward(t, pos)
+    pos = len(prompt)
+    for _ in range(30):
+        nxt = m.sample_greedy(d)
+        ids.append(nxt)
+        d = m.forward(nxt, pos)
+        pos += 1
+    assert ids == dev_ids
+    m.set_sampling(0.0, 0.8, 50, 1.15)
+    out = m.generate(prompt, 30)
+    assert out == prompt + dev_ids
+    m.close()
+
+
+def test_nucleus_sampling_seeded(fb, models):
+    m = fb.Model(models["tiny-q6k"], max_ctx=64)
+    m.set_sampling(0.7, 0.8, 50, 1.15)
+    runs = []
+    for _ in range(2):
+        m.set_seed(1234)
+        runs.append(m.generate([1, 2, 3], 20))
+    assert runs[0] == runs[1]
+    assert len(runs[0]) == 23 and all(0 <= t < 2048 for t in runs[0])
+    m.close()
+
+
+def test_long_context_positions(fb, orc, models):
+    """Positions beyond one attention tile and chunk (adaptive chunk length) stay exact-range."""
+    p = models["tiny-q6k"]
+    eng = fb.Model(p, max_ctx=1024, kv_dtype=fb.FENCE_KV_F16)
+    ora = orc.OracleModel(p, max_ctx=1024, kv_bf16=False, threads=8)
+    rng = np.random.default_rng(3)
+    worst = 0.0
+    for pos in range(600):
+        t = int(rng.integers(0, 2048))
+        eng.forward(t, pos)
+        lo = ora.forward(t, pos)
+        if pos % 50 == 49 or pos == 599:
+            worst = max(worst, float(np.max(np.abs(eng.logits() - lo))))
+    eng.close()
+    ora.close()
+    assert worst < LOGIT_ATOL
