@@ -24,9 +24,10 @@
 
 namespace fence {
 
-constexpr int ATTN_THREADS = 128;
+constexpr int ATTN_THREADS = 256;
 constexpr int ATTN_CMAX = 128;  // positions per shared-memory tile
 constexpr int ATTN_MAX_G = 8;   // query heads per KV head supported
+constexpr int ATTN_TPP = 4;     // threads per position in the score pass (each owns a quarter of head_dim)
 
 template <typename T>
 struct KVConv;
@@ -72,12 +73,14 @@ struct AttnArgs {
     unsigned int* counter;  // [Hkv] arrival counters, zero between launches
 };
 
+// Fused-mode split of the context: one chunk up to 256 positions (no merge step at all), then
+// ceil(seq_len / 256) chunks (at most nchunk), each a multiple of 16 positions.
 __device__ __forceinline__ int attn_chunk_len(int seq_len, int nchunk) {
-    // smallest multiple of 16 with ceil(seq_len / C) <= nchunk, capped at ATTN_CMAX
-    int c = (seq_len + nchunk - 1) / nchunk;
+    int n = (seq_len + 255) / 256;
+    if (n > nchunk) n = nchunk;
+    if (n < 1) n = 1;
+    int c = (seq_len + n - 1) / n;
     c = (c + 15) & ~15;
-    if (c < 16) c = 16;
-    if (c > ATTN_CMAX) c = ATTN_CMAX;
     return c;
 }
 
@@ -109,14 +112,20 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     using C = KVConv<KVT>;
     constexpr int CH = HD * (int)sizeof(KVT) / 16;  // 16-byte chunks per row
     constexpr int EPC = 16 / (int)sizeof(KVT);      // elements per chunk
+    constexpr int CPQ = CH / ATTN_TPP;              // chunks per quarter
     constexpr int KP = (ATTN_MAX_G * HD / 2 + ATTN_THREADS - 1) / ATTN_THREADS;  // PV pairs per thread
-    static_assert(CH >= 8, "head_dim too small for the swizzle");
+    constexpr int NW = ATTN_THREADS / 32;
+    static_assert(CH >= 8 && CH % ATTN_TPP == 0, "head_dim too small for the swizzle");
     extern __shared__ __align__(128) uint8_t sm[];
     KVT* sk = reinterpret_cast<KVT*>(sm);
     KVT* sv = sk + ATTN_CMAX * HD;
     float* sq = reinterpret_cast<float*>(sv + ATTN_CMAX * HD);  // [G][HD]
     float* ss = sq + ATTN_MAX_G * HD;                            // [G][CMAX]
-    float* smax = ss + ATTN_MAX_G * ATTN_CMAX;                   // [G] running max
+    float* skn = ss + ATTN_MAX_G * ATTN_CMAX;                    // [HD] new k row (fused)
+    float* sqw = skn + HD;                                       // [HD] q-norm weight
+    float* skw = sqw + HD;                                       // [HD] k-norm weight
+    float2* srope = reinterpret_cast<float2*>(skw + HD);         // [HD/2] cos/sin at pos
+    float* smax = reinterpret_cast<float*>(srope + HD / 2);      // [G] running max
     float* ssum = smax + ATTN_MAX_G;                             // [G] running exp-sum
     float* sresc = ssum + ATTN_MAX_G;                            // [G] rescale of the old accumulator
     int* sflag = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
@@ -126,7 +135,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     const int G = a.n_q_heads / a.n_kv_heads;
     int seq_len, pos, clen;
     if (FUSED) {
-        pos = a.state->pos;
+        pos = a.state->pos;  // written by the previous token step, independent of this step's GEMVs
         seq_len = pos + 1;
         clen = attn_chunk_len(seq_len, a.nchunk);
     } else {
@@ -142,11 +151,11 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     }
     const int t0 = c * clen;
     const int t1 = min(t0 + clen, seq_len);
-    const bool owns_new = FUSED && (pos >= t0 && pos < t1);  // fused: clen <= ATTN_CMAX, one tile
+    const bool owns_new = FUSED && (pos >= t0 && pos < t1);
 
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
     const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
-    auto stage_tile = [&](int ts, int te) {
+    auto stage_tile = [&](int ts, int te) {  // rows [ts, te) -> smem rows 0.., chunk XOR (row & 7)
         for (int idx = tid; idx < (te - ts) * CH; idx += ATTN_THREADS) {
             const int r = idx / CH, ch = idx - r * CH;
             const int t = ts + r;
@@ -159,47 +168,71 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         cp_async_commit();
     };
 
-    // ---- first tile of cached rows: independent of the preceding kernel, issued before the wait
+    // ---- everything that does not depend on the preceding kernel, before the wait:
+    //      cached K/V rows of the first tile, norm weights, the RoPE row of `pos`
     {
         const int te = min(t0 + ATTN_CMAX, t1);
-        stage_tile(t0, owns_new ? pos : te);
+        // in the tile that holds `pos`, row pos is produced below (the others are cached)
+        stage_tile(t0, (owns_new && pos < te) ? pos : te);
     }
-    if (tid == 0) pdl_launch_dependents();
-    pdl_wait();
-
-    // ---- q for the G heads of this group (normed + rotated in fused mode)
-    const int qh0 = h * G;
-    for (int i = tid; i < G * HD; i += ATTN_THREADS) sq[i] = a.q[(long long)qh0 * HD + i];
+    if (FUSED) {
+        for (int d = tid; d < HD; d += ATTN_THREADS) {
+            sqw[d] = a.q_norm_w ? a.q_norm_w[d] : 1.f;
+            skw[d] = a.k_norm_w ? a.k_norm_w[d] : 1.f;
+        }
+        for (int i = tid; i < HD / 2; i += ATTN_THREADS) srope[i] = a.rope[(long long)pos * (HD / 2) + i];
+    }
     if (tid < ATTN_MAX_G) {
         smax[tid] = -INFINITY;
         ssum[tid] = 0.f;
     }
+    if (tid == 0) pdl_launch_dependents();
+    pdl_wait();
+
+    // ---- q of the G heads (and the new K/V row) from the QKV GEMV
+    const int qh0 = h * G;
+    for (int i = tid; i < G * HD; i += ATTN_THREADS) sq[i] = a.q[(long long)qh0 * HD + i];
+    if (owns_new)
+        for (int d = tid; d < HD; d += ATTN_THREADS) skn[d] = a.k_new[(long long)h * HD + d];
     __syncthreads();
     if (FUSED) {
-        const float2* cs = a.rope + (long long)pos * (HD / 2);
-        for (int g = warp; g < G; g += ATTN_THREADS / 32) {
-            if (a.q_norm_w) head_rmsnorm_warp<HD>(sq + g * HD, a.q_norm_w, a.eps, lane);
-            head_rope_warp<HD>(sq + g * HD, cs, lane);
-        }
-        if (owns_new && warp == (ATTN_THREADS / 32) - 1) {
-            // new K row: norm + rope in fp32, round to the cache type, store; V row: round + store
-            float* kt = ss;  // borrow score space (HD floats)
-            for (int d = lane; d < HD; d += 32) kt[d] = a.k_new[(long long)h * HD + d];
+        // q/k RMSNorm (w * x * rms) then NeoX rotation, warp per head; one more warp for the new k
+        for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
+            float* v = (g < G) ? sq + g * HD : skn;
+            const bool norm = (g < G) ? (a.q_norm_w != nullptr) : (a.k_norm_w != nullptr);
+            const float* w = (g < G) ? sqw : skw;
+            if (norm) {
+                float s2 = 0.f;
+                for (int d = lane; d < HD; d += 32) s2 += v[d] * v[d];
+                s2 = warp_sum(s2);
+                const float r = rsqrtf(s2 / (float)HD + a.eps);
+                for (int d = lane; d < HD; d += 32) v[d] = w[d] * v[d] * r;
+                __syncwarp();
+            }
+            for (int i = lane; i < HD / 2; i += 32) {
+                const float2 t = srope[i];
+                const float x0 = v[i], x1 = v[i + HD / 2];
+                v[i] = x0 * t.x - x1 * t.y;
+                v[i + HD / 2] = x0 * t.y + x1 * t.x;
+            }
             __syncwarp();
-            if (a.k_norm_w) head_rmsnorm_warp<HD>(kt, a.k_norm_w, a.eps, lane);
-            head_rope_warp<HD>(kt, cs, lane);
-            KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
-            KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
-            const int r = pos - t0;
-            for (int d = lane; d < HD; d += 32) {
-                const KVT kq = C::from(kt[d]);
-                const KVT vq = C::from(a.v_new[(long long)h * HD + d]);
-                kw[d] = kq;
-                vw[d] = vq;
-                const int ch = d / EPC, within = d % EPC;
-                const int pch = ch ^ (r & 7);
-                reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16)[within] = kq;
-                reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16)[within] = vq;
+            if (g == G) {
+                // round to the cache type, store the new row (global) and into its tile slot
+                const int r = pos - t0;
+                KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+                KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+                for (int d = lane; d < HD; d += 32) {
+                    const KVT kq = C::from(v[d]);
+                    const KVT vq = C::from(a.v_new[(long long)h * HD + d]);
+                    kw[d] = kq;
+                    vw[d] = vq;
+                    if (r < ATTN_CMAX) {  // in the first tile; a later tile re-reads the row from global
+                        const int ch = d / EPC, within = d % EPC;
+                        const int pch = ch ^ (r & 7);
+                        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16)[within] = kq;
+                        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16)[within] = vq;
+                    }
+                }
             }
         }
     }
@@ -216,35 +249,55 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         cp_async_wait_all();
         __syncthreads();
 
-        // ---- scores: thread <-> position
-        for (int r = tid; r < nt; r += ATTN_THREADS) {
+        // ---- scores: ATTN_TPP threads per position, each over CPQ chunks, then a shuffle sum
+        for (int base = 0; base < nt; base += ATTN_THREADS / ATTN_TPP) {
+            const int r = base + tid / ATTN_TPP;
+            const int qtr = tid % ATTN_TPP;
             float acc[ATTN_MAX_G];
 #pragma unroll
             for (int g = 0; g < ATTN_MAX_G; ++g) acc[g] = 0.f;
-            const uint8_t* krow = reinterpret_cast<const uint8_t*>(sk + r * HD);
-            for (int ch = 0; ch < CH; ++ch) {
-                const uint4 w = *reinterpret_cast<const uint4*>(krow + ((ch ^ (r & 7)) * 16));
-                float kf[8];
-                const float2 f0 = C::pair(w.x), f1 = C::pair(w.y), f2 = C::pair(w.z), f3 = C::pair(w.w);
-                kf[0] = f0.x; kf[1] = f0.y; kf[2] = f1.x; kf[3] = f1.y;
-                kf[4] = f2.x; kf[5] = f2.y; kf[6] = f3.x; kf[7] = f3.y;
+            if (r < nt) {
+                const uint8_t* krow = reinterpret_cast<const uint8_t*>(sk + r * HD);
 #pragma unroll
-                for (int g = 0; g < ATTN_MAX_G; ++g) {
-                    if (g < G) {
-                        const float* qg = sq + g * HD + ch * EPC;
+                for (int i = 0; i < CPQ; ++i) {
+                    const int ch = qtr + ATTN_TPP * i;
+                    const uint4 w = *reinterpret_cast<const uint4*>(krow + ((ch ^ (r & 7)) * 16));
+                    float kf[8];
+                    const float2 f0 = C::pair(w.x), f1 = C::pair(w.y), f2 = C::pair(w.z), f3 = C::pair(w.w);
+                    kf[0] = f0.x; kf[1] = f0.y; kf[2] = f1.x; kf[3] = f1.y;
+                    kf[4] = f2.x; kf[5] = f2.y; kf[6] = f3.x; kf[7] = f3.y;
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[g] = fmaf(qg[e], kf[e], acc[g]);
+                    for (int g = 0; g < ATTN_MAX_G; ++g) {
+                        if (g < G) {
+                            const float4 qa = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC);
+                            const float4 qb = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC + 4);
+                            acc[g] = fmaf(qa.x, kf[0], acc[g]);
+                            acc[g] = fmaf(qa.y, kf[1], acc[g]);
+                            acc[g] = fmaf(qa.z, kf[2], acc[g]);
+                            acc[g] = fmaf(qa.w, kf[3], acc[g]);
+                            acc[g] = fmaf(qb.x, kf[4], acc[g]);
+                            acc[g] = fmaf(qb.y, kf[5], acc[g]);
+                            acc[g] = fmaf(qb.z, kf[6], acc[g]);
+                            acc[g] = fmaf(qb.w, kf[7], acc[g]);
+                        }
                     }
                 }
             }
 #pragma unroll
-            for (int g = 0; g < ATTN_MAX_G; ++g)
-                if (g < G) ss[g * ATTN_CMAX + r] = acc[g] * scale;
+            for (int g = 0; g < ATTN_MAX_G; ++g) {
+                acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+                acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
+            }
+            if (r < nt && qtr == 0) {
+#pragma unroll
+                for (int g = 0; g < ATTN_MAX_G; ++g)
+                    if (g < G) ss[g * ATTN_CMAX + r] = acc[g] * scale;
+            }
         }
         __syncthreads();
 
         // ---- online softmax statistics per head (warp per head)
-        for (int g = warp; g < G; g += ATTN_THREADS / 32) {
+        for (int g = warp; g < G; g += NW) {
             float m = -INFINITY;
             for (int t = lane; t < nt; t += 32) m = fmaxf(m, ss[g * ATTN_CMAX + t]);
             m = warp_max(m);
@@ -293,7 +346,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     }
 
     const int part_stride = HD + 2;
-    if (!FUSED && n_active == 1) {
+    if (n_active == 1) {
         // whole context in one chunk: normalise and write the output directly
 #pragma unroll
         for (int k = 0; k < KP; ++k) {
@@ -381,8 +434,8 @@ __global__ void attn_merge_kernel(const float* __restrict__ part, float* __restr
 
 template <typename KVT, int HD>
 constexpr int attn_smem_bytes() {
-    return 2 * ATTN_CMAX * HD * (int)sizeof(KVT) + ATTN_MAX_G * HD * 4 + ATTN_MAX_G * ATTN_CMAX * 4 +
-           (3 * ATTN_MAX_G + 8) * 4;
+    return 2 * ATTN_CMAX * HD * (int)sizeof(KVT) + ATTN_MAX_G * HD * 4 + ATTN_MAX_G * ATTN_CMAX * 4 + 3 * HD * 4 +
+           (HD / 2) * 8 + (3 * ATTN_MAX_G + 8) * 4;
 }
 
 }  // namespace fence

@@ -119,18 +119,36 @@ __device__ __forceinline__ float warp_max(float v) {
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+// ---------------------------------------------------------------- shared-memory loads by 32-bit
+// shared-window address (keeps them LDS instructions; volatile so they stay behind the mbarrier
+// wait that made the data visible)
+__device__ __forceinline__ uint32_t lds32(uint32_t sa) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(sa));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u16(uint32_t sa) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(sa));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t sa) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(sa));
+    return v;
+}
 // 32-bit word at a 2-byte aligned shared address: two aligned loads and a funnel shift.
-__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t* p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    return __funnelshift_r(w[0], w[1], (uint32_t)(a & 2u) * 8u);
+__device__ __forceinline__ uint32_t lds_u32_a2(uint32_t sa) {
+    const uint32_t w = sa & ~3u;
+    return __funnelshift_r(lds32(w), lds32(w + 4), (sa & 2u) * 8u);
 }
 // Four consecutive words starting at a 2-byte aligned shared address (reads 20 bytes).
-__device__ __forceinline__ void lds_16B_a2(const uint8_t* p, uint32_t out[4]) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
-    const uint32_t sh = (uint32_t)(a & 2u) * 8u;
-    const uint32_t w0 = w[0], w1 = w[1], w2 = w[2], w3 = w[3], w4 = w[4];
+__device__ __forceinline__ void lds_16B_a2(uint32_t sa, uint32_t out[4]) {
+    const uint32_t w = sa & ~3u;
+    const uint32_t sh = (sa & 2u) * 8u;
+    const uint32_t w0 = lds32(w), w1 = lds32(w + 4), w2 = lds32(w + 8), w3 = lds32(w + 12), w4 = lds32(w + 16);
     out[0] = __funnelshift_r(w0, w1, sh);
     out[1] = __funnelshift_r(w1, w2, sh);
     out[2] = __funnelshift_r(w2, w3, sh);

@@ -113,13 +113,11 @@ GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     const int rows_cta = (Mv + G - 1) / G;
     const int stages_cta = (rows_cta + step - 1) / step;
     const int stage_bytes = ((P * rowB + GEMV_STAGE_SLACK + 127) / 128) * 128;
-    const int red_bytes = 2 * P * I * 4;
-    const int misc_bytes = 512;
     const int budget = device_smem_optin(dev) - 1024;
-    int ring = (budget - red_bytes - misc_bytes) / (stage_bytes + 16);
-    if (ring > 16) ring = 16;
+    int ring = 16;
     if (ring > stages_cta) ring = stages_cta;
-    if (ring < 1) return pl;
+    while (ring > 1 && (int)gemv_smem_layout(ring, stage_bytes, P, I).total > budget) --ring;
+    if ((int)gemv_smem_layout(ring, stage_bytes, P, I).total > budget) return pl;
     pl.ok = 1;
     pl.I = I;
     pl.rowB = rowB;
@@ -129,7 +127,7 @@ GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     pl.nt_cons = (P * I + 31) / 32 * 32;
     pl.block = pl.nt_cons + 32;
     pl.grid = G;
-    pl.smem = ring * stage_bytes + red_bytes + 2 * ring * 8 + misc_bytes;
+    pl.smem = (int)gemv_smem_layout(ring, stage_bytes, P, I).total;
     return pl;
 }
 

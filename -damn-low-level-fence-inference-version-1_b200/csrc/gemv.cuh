@@ -354,10 +354,10 @@ __device__ __forceinline__ void make_slice(const GemvArgs& a, int item, float rm
     }
 }
 
-// Partial dot of one item of one row. `sb` points at the item's super-block (Q6_K) or at the
-// item's first block (Q8_0) in shared memory; 2-byte aligned.
+// Partial dot of one item of one row. `sb` is the 32-bit shared address of the item's super-block
+// (Q6_K) or of the item's first block (Q8_0); 2-byte aligned (Q6_K) / 4-byte aligned (Q8_0).
 template <int WT>
-__device__ __forceinline__ float item_dot(const uint8_t* sb, int item, const XSlice<WT>& s) {
+__device__ __forceinline__ float item_dot(uint32_t sb, int item, const XSlice<WT>& s) {
     if (WT == WT_Q6K) {
         const int h = (item >> 1) & 1, l16 = item & 1;
         uint32_t ql0[4], ql1[4], qh[4];
@@ -366,7 +366,7 @@ __device__ __forceinline__ float item_dot(const uint8_t* sb, int item, const XSl
         lds_16B_a2(sb + 128 + h * 32 + l16 * 16, qh);
         const uint32_t sA = lds_u32_a2(sb + 192 + 8 * h);
         const uint32_t sB = lds_u32_a2(sb + 196 + 8 * h);
-        const uint32_t dbits = *reinterpret_cast<const uint16_t*>(sb + 208);
+        const uint32_t dbits = lds_u16(sb + 208);
         int hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
         int lo0 = s.corr[0], lo1 = s.corr[1], lo2 = s.corr[2], lo3 = s.corr[3];
 #pragma unroll
@@ -396,12 +396,11 @@ __device__ __forceinline__ float item_dot(const uint8_t* sb, int item, const XSl
         return t * (half_bits_to_float(dbits) * s.xs0);
     } else {
         // 68 bytes = 17 words, 4-byte aligned (rows are 4-byte aligned when K % 64 == 0)
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(sb);
         int hi0 = 0, lo0 = 0, hi1 = 0, lo1 = 0;
         uint32_t w0 = 0, w8 = 0;
 #pragma unroll
         for (int m = 0; m < 9; ++m) {
-            const uint32_t q = w[m];
+            const uint32_t q = lds32(sb + 4 * m);
             if (m == 0) w0 = q;
             if (m == 8) w8 = q;
             hi0 = dp4a_ss(q, s.xh[m], hi0);
@@ -409,7 +408,7 @@ __device__ __forceinline__ float item_dot(const uint8_t* sb, int item, const XSl
         }
 #pragma unroll
         for (int m = 9; m < 17; ++m) {
-            const uint32_t q = w[m];
+            const uint32_t q = lds32(sb + 4 * m);
             hi1 = dp4a_ss(q, s.xh[m], hi1);
             lo1 = dp4a_su(q, s.xl[m], lo1);
         }
@@ -435,6 +434,71 @@ __device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
 // --------------------------------------------------------------------------------------------
+// Quantised-x record of one item in shared memory: xh[XW] | xl[XW] | corr[4] | xs0 | xs1 (40 words).
+constexpr int XQ_WORDS = 40;
+
+template <int WT>
+__device__ __forceinline__ void store_slice(uint32_t rec, const XSlice<WT>& s) {
+    constexpr int XW = WTraits<WT>::XWORDS;
+    uint32_t w[XQ_WORDS];
+#pragma unroll
+    for (int k = 0; k < XW; ++k) {
+        w[k] = s.xh[k];
+        w[XW + k] = s.xl[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[2 * XW + k] = (uint32_t)s.corr[k];
+    w[2 * XW + 4] = __float_as_uint(s.xs0);
+    w[2 * XW + 5] = __float_as_uint(s.xs1);
+#pragma unroll
+    for (int k = 2 * XW + 6; k < XQ_WORDS; ++k) w[k] = 0u;
+#pragma unroll
+    for (int k = 0; k < XQ_WORDS / 4; ++k)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rec + 16 * k), "r"(w[4 * k]),
+                     "r"(w[4 * k + 1]), "r"(w[4 * k + 2]), "r"(w[4 * k + 3])
+                     : "memory");
+}
+
+template <int WT>
+__device__ __forceinline__ void load_slice(uint32_t rec, XSlice<WT>& s) {
+    constexpr int XW = WTraits<WT>::XWORDS;
+    uint32_t w[XQ_WORDS];
+#pragma unroll
+    for (int k = 0; k < XQ_WORDS / 4; ++k) {
+        const uint4 u = lds128(rec + 16 * k);
+        w[4 * k] = u.x;
+        w[4 * k + 1] = u.y;
+        w[4 * k + 2] = u.z;
+        w[4 * k + 3] = u.w;
+    }
+#pragma unroll
+    for (int k = 0; k < XW; ++k) {
+        s.xh[k] = w[k];
+        s.xl[k] = w[XW + k];
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s.corr[k] = (int)w[2 * XW + k];
+    s.xs0 = __uint_as_float(w[2 * XW + 4]);
+    s.xs1 = __uint_as_float(w[2 * XW + 5]);
+}
+
+// Shared-memory carve-up (all regions 16-byte aligned); the host plan uses the same function.
+struct GemvSmem {
+    uint32_t red, xq, rowtab, rowinfo, bars, misc, total;
+};
+__host__ __device__ inline GemvSmem gemv_smem_layout(int ring, int stage_bytes, int P, int I) {
+    auto r16 = [](uint32_t x) { return (x + 15u) & ~15u; };
+    GemvSmem L;
+    L.red = (uint32_t)ring * (uint32_t)stage_bytes;
+    L.xq = L.red + r16(8u * P * I);
+    L.rowtab = L.xq + (uint32_t)I * XQ_WORDS * 4u;
+    L.rowinfo = L.rowtab + r16(4u * ring * P);
+    L.bars = L.rowinfo + r16(4u * ring * P);
+    L.misc = L.bars + r16(16u * ring);
+    L.total = L.misc + 512u;
+    return L;
+}
+
 template <int WT, int XM, int EPI>
 __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -443,16 +507,21 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
     const int warp = tid >> 5;
     const int ncons_warps = a.nt_cons >> 5;
     const bool is_producer = (tid >= a.nt_cons);
+    const int P = a.P, I = a.I;
 
-    // ---- shared memory carve-up: ring | red[2][P*I] | bars | misc
+    const GemvSmem SL = gemv_smem_layout(a.ring, a.stage_bytes, P, I);
     uint8_t* ring = smem;
-    float* red = reinterpret_cast<float*>(smem + (size_t)a.ring * a.stage_bytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(red + 2 * a.P * a.I);
+    float* red = reinterpret_cast<float*>(smem + SL.red);
+    const uint32_t smem_sa = smem_u32(smem);  // shared-window address of the dynamic allocation
+    const uint32_t xq_sa = smem_sa + SL.xq;
+    uint32_t* rowtab = reinterpret_cast<uint32_t*>(smem + SL.rowtab);   // [ring][P] byte offset of each row
+    int* rowinfo = reinterpret_cast<int*>(smem + SL.rowinfo);            // [ring][P] (tensor << 28) | row
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
     uint64_t* empty = full + a.ring;
-    float* misc = reinterpret_cast<float*>(empty + a.ring);  // [32] block reduction scratch
+    float* misc = reinterpret_cast<float*>(smem + SL.misc);  // [32] block reduction scratch
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
-    float* warp_best_v = misc + 40;                                  // [32]
-    int* warp_best_i = reinterpret_cast<int*>(misc + 72);            // [32]
+    float* warp_best_v = misc + 40;                        // [32]
+    int* warp_best_i = reinterpret_cast<int*>(misc + 72);  // [32]
 
     // ---- CTA row range (virtual rows)
     const int G = gridDim.x;
@@ -460,7 +529,7 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
     const int v_begin = (int)(((long long)a.Mv * c) / G);
     const int v_end = (int)(((long long)a.Mv * (c + 1)) / G);
     const int rows_cta = v_end - v_begin;
-    const int step = a.dual ? a.P / 2 : a.P;  // virtual rows per stage (dual: gate/up pairs)
+    const int step = a.dual ? P / 2 : P;  // virtual rows per stage (dual: gate/up pairs)
     const int nstages = (rows_cta + step - 1) / step;
 
     if (tid == 0) {
@@ -475,24 +544,44 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
     if (tid == 0) pdl_launch_dependents();
 
     if (is_producer) {
-        // ================= producer warp: lane 0 streams the CTA's weight bytes
-        if (lane == 0) {
-            for (int s = 0; s < nstages; ++s) {
-                const int slot = s % a.ring;
-                if (s >= a.ring) {
-                    bool ok = false;
+        // ================= producer warp: publishes each stage's row table, lane 0 streams the bytes
+        for (int s = 0; s < nstages; ++s) {
+            const int slot = s % a.ring;
+            if (s >= a.ring) {
+                int ok = 0;
+                if (lane == 0) {
                     for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
-                        if (mbar_try_wait(&empty[slot], ((s / a.ring) - 1) & 1)) { ok = true; break; }
+                        if (mbar_try_wait(&empty[slot], ((s / a.ring) - 1) & 1)) { ok = 1; break; }
                     if (!ok) {
                         if (!*abort_flag) set_device_error(-5);
                         *abort_flag = 1;
-                        break;
                     }
                 }
-                const int va = v_begin + s * step;
-                const int n = min(step, v_end - va);
-                StageGeo geo;
-                stage_geo(a, va, n, geo);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+            const int va = v_begin + s * step;
+            const int n = min(step, v_end - va);
+            StageGeo geo;
+            stage_geo(a, va, n, geo);
+            const int rows_in_stage = a.dual ? 2 * n : n;
+            if (lane < rows_in_stage) {
+                const int k = piece_of(geo, lane);
+                uint32_t off = 0, delta = 0;
+                int first = 0, r0 = 0;
+#pragma unroll
+                for (int j = 0; j < GEMV_MAX_SEG; ++j)
+                    if (j == k) {
+                        off = geo.p[j].smem_off;
+                        delta = geo.p[j].delta;
+                        first = geo.p[j].first_row;
+                        r0 = geo.p[j].seg_row0;
+                    }
+                rowtab[slot * P + lane] = (uint32_t)slot * a.stage_bytes + off + delta + (uint32_t)(lane - first) * a.rowB;
+                rowinfo[slot * P + lane] = (k << 28) | (r0 + lane - first);
+            }
+            __syncwarp();
+            if (lane == 0) {
                 uint8_t* dst = ring + (size_t)slot * a.stage_bytes;
                 uint32_t tx = 0;
 #pragma unroll
@@ -515,8 +604,6 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
                         bulk_g2s(dst + geo.p[k].smem_off, geo.p[k].src, geo.p[k].copy_bytes, &full[slot]);
             }
         }
-        // the producer warp takes part in the consumers' first barrier only via __syncthreads
-        // below; it idles afterwards.
         pdl_wait();
         return;
     }
@@ -524,18 +611,15 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
     // ================= consumers
     pdl_wait();  // x, residual and epilogue targets come from the previous kernel
 
-    const int P = a.P, I = a.I;
-    const int p = tid / I;             // row slot within a stage
-    const int item = tid - p * I;      // fixed K slice of this thread
-    const bool active = (p < P);       // threads beyond P*I only help with barriers/reductions
+    const int p = tid / I;         // row slot within a stage
+    const int item = tid - p * I;  // fixed K slice of this thread
+    const bool active = (p < P);   // threads beyond P*I only help with barriers/reductions
 
-    // ---- RMSNorm statistics (threads of row slot 0 cover all K once)
+    // ---- prologue: x of every item quantised once per CTA (threads of row slot 0)
     float rms = 1.f;
     if (XM == X_NORM || XM == X_NORM_R16) {
         float ss = 0.f;
         if (p == 0) {
-            float v[64];
-            // raw x (no weight) for the sum of squares
             const float* x = static_cast<const float*>(a.x);
             int base[4];
             if (WT == WT_Q6K) {
@@ -552,14 +636,9 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const float4 f = q4[k];
-                    v[cc * 16 + 4 * k + 0] = f.x;
-                    v[cc * 16 + 4 * k + 1] = f.y;
-                    v[cc * 16 + 4 * k + 2] = f.z;
-                    v[cc * 16 + 4 * k + 3] = f.w;
+                    ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
                 }
             }
-#pragma unroll
-            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
         }
         ss = warp_sum(ss);
         if (lane == 0) misc[warp] = ss;
@@ -568,11 +647,16 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
         for (int w = 0; w < ncons_warps; ++w) tot += misc[w];
         rms = rsqrtf(tot / (float)a.K + a.eps);
     }
-
+    if (p == 0) {
+        XSlice<WT> t;
+        make_slice<WT, XM>(a, item, rms, t);
+        store_slice<WT>(xq_sa + item * XQ_WORDS * 4, t);
+    }
+    named_bar_sync(1, a.nt_cons);
     XSlice<WT> xs;
-    if (active) make_slice<WT, XM>(a, item, rms, xs);
+    if (active) load_slice<WT>(xq_sa + item * XQ_WORDS * 4, xs);
 
-    const int blocks_per_item_bytes = (WT == WT_Q6K) ? 0 : 68;
+    const int item_off = (WT == WT_Q6K) ? (item >> 2) * 210 : item * 68;
     float best_v = 0.f;
     int best_i = -1;
     int buf = 0;
@@ -581,9 +665,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
         const int slot = s % a.ring;
         const int va = v_begin + s * step;
         const int n = min(step, v_end - va);
-        StageGeo geo;
-        stage_geo(a, va, n, geo);
         const int rows_in_stage = a.dual ? 2 * n : n;
+        const int nred = a.dual ? n : rows_in_stage;
 
         bool ok = !*abort_flag;
         if (ok) {
@@ -596,31 +679,21 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
                 ok = false;
             }
         }
-        // rows handled by this thread in the stage: slot p (single pass; P rows per stage, dual: P/2 pairs)
         float part = 0.f;
-        if (ok && active && p < rows_in_stage) {
-            const int k = piece_of(geo, p);
-            uint32_t off = 0, delta = 0;
-            int first = 0;
-#pragma unroll
-            for (int j = 0; j < GEMV_MAX_SEG; ++j)
-                if (j == k) {
-                    off = geo.p[j].smem_off;
-                    delta = geo.p[j].delta;
-                    first = geo.p[j].first_row;
-                }
-            const uint8_t* rowp = ring + (size_t)slot * a.stage_bytes + off + delta + (size_t)(p - first) * a.rowB;
-            const uint8_t* sbp = (WT == WT_Q6K) ? rowp + (item >> 2) * 210 : rowp + item * blocks_per_item_bytes;
-            part = item_dot<WT>(sbp, item, xs);
-        }
+        if (ok && active && p < rows_in_stage)
+            part = item_dot<WT>(smem_sa + rowtab[slot * P + p] + item_off, item, xs);
+        // rows this warp reduces below (warp, warp + nw, ...): lane j keeps the tensor/row of the
+        // j-th one, read before the slot is released
+        int myinfo = 0;
+        if (ok && warp + lane * ncons_warps < nred) myinfo = rowinfo[slot * P + warp + lane * ncons_warps];
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (active) red[buf * P * I + tid] = part;
         named_bar_sync(1, a.nt_cons);
 
         // ---- reduce rows and run the epilogue (fixed order -> deterministic)
-        const int nred = a.dual ? n : rows_in_stage;
-        for (int r = warp; r < nred; r += ncons_warps) {
+        for (int r = warp, q = 0; r < nred; r += ncons_warps, ++q) {
+            const int info = __shfl_sync(0xffffffffu, myinfo, q);
             const float* rr = red + buf * P * I + r * I;
             float sum = 0.f;
             for (int j = lane; j < I; j += 32) sum += rr[j];
@@ -632,35 +705,23 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
                 sum2 = warp_sum(sum2);
             }
             if (lane == 0 && ok) {
+                const int row = info & 0x0FFFFFFF;
                 if (EPI == EPI_SWIGLU) {
-                    const int row = va + r;
-                    const float g = sum, u = sum2;
-                    const float o = silu_mul(g, u);
+                    const float o = silu_mul(sum, sum2);
                     if (a.act_f16) reinterpret_cast<__half*>(a.act)[row] = __float2half_rn(o);
                     else reinterpret_cast<float*>(a.act)[row] = o;
-                } else {
-                    // map virtual row -> tensor, row
-                    const int kk = piece_of(geo, r);
-                    int row = 0;
-                    float* yk = nullptr;
-                    const float* bk = nullptr;
-#pragma unroll
-                    for (int j = 0; j < GEMV_MAX_SEG; ++j)
-                        if (j == kk) {
-                            row = geo.p[j].seg_row0 + (r - geo.p[j].first_row);
-                            yk = a.seg[j].y;
-                            bk = a.seg[j].bias;
-                        }
-                    if (EPI == EPI_STORE) {
-                        yk[row] = bk ? sum + bk[row] : sum;
-                    } else if (EPI == EPI_RESID) {
-                        a.resid[row] = sum + a.resid[row];
-                    } else if (EPI == EPI_LMHEAD) {
-                        a.logits[row] = sum;
-                        if (argmax_better(sum, row, best_v, best_i)) {
-                            best_v = sum;
-                            best_i = row;
-                        }
+                } else if (EPI == EPI_STORE) {
+                    const int sgi = info >> 28;
+                    float* yk = sgi == 0 ? a.seg[0].y : (sgi == 1 ? a.seg[1].y : a.seg[2].y);
+                    const float* bk = sgi == 0 ? a.seg[0].bias : (sgi == 1 ? a.seg[1].bias : a.seg[2].bias);
+                    yk[row] = bk ? sum + bk[row] : sum;
+                } else if (EPI == EPI_RESID) {
+                    a.resid[row] = sum + a.resid[row];
+                } else if (EPI == EPI_LMHEAD) {
+                    a.logits[row] = sum;
+                    if (argmax_better(sum, row, best_v, best_i)) {
+                        best_v = sum;
+                        best_i = row;
                     }
                 }
             }

@@ -30,7 +30,7 @@ def test_rms_norm_and_inplace(fb, orc, T):
         w = rng.standard_normal(n).astype(np.float32)
         ref = np.empty(n, np.float32)
         orc.oracle().oracle_rms_norm(P(ref), P(x), P(w), n, 1e-6)
-        dx, dw, dout = cu(T, x), cu(T, w), T.empty(n, device="cuda")
+        dx, dw, dout = cu(T, x), cu(T, w), T.empty(n, device="cuda")  # all kept alive across the launches
         fb.call("fence_rms_norm", dout.data_ptr(), dx.data_ptr(), dw.data_ptr(), n, 1e-6, None)
         fb.call("fence_rms_norm_inplace", dx.data_ptr(), dw.data_ptr(), n, 1e-6, None)
         np.testing.assert_allclose(dout.cpu().numpy(), ref, rtol=2e-5, atol=1e-6)
@@ -44,8 +44,8 @@ def test_rms_norm_per_head(fb, orc, T):
         w = rng.standard_normal(hd).astype(np.float32)
         ref = x.copy()
         orc.oracle().oracle_rms_norm_per_head(P(ref), P(w), nh, hd, 1e-6)
-        dx = cu(T, x)
-        fb.call("fence_rms_norm_per_head", dx.data_ptr(), cu(T, w).data_ptr(), nh, hd, 1e-6, None)
+        dx, dw = cu(T, x), cu(T, w)
+        fb.call("fence_rms_norm_per_head", dx.data_ptr(), dw.data_ptr(), nh, hd, 1e-6, None)
         np.testing.assert_allclose(dx.cpu().numpy(), ref, rtol=2e-5, atol=1e-6)
 
 
@@ -71,7 +71,8 @@ def test_silu_residual_softmax_convert(fb, orc, T):
     ref = np.empty(n, np.float32)
     orc.oracle().oracle_silu_mul(P(ref), P(g), P(u), n)
     out = T.empty(n, device="cuda")
-    fb.call("fence_silu_elementwise_mul", out.data_ptr(), cu(T, g).data_ptr(), cu(T, u).data_ptr(), n, None)
+    dg, du = cu(T, g), cu(T, u)  # keep the inputs alive: launches are asynchronous
+    fb.call("fence_silu_elementwise_mul", out.data_ptr(), dg.data_ptr(), du.data_ptr(), n, None)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=2e-6, atol=1e-7)
     x, r = cu(T, g), cu(T, u)
     fb.call("fence_residual_add", x.data_ptr(), r.data_ptr(), n, None)
@@ -83,7 +84,7 @@ def test_silu_residual_softmax_convert(fb, orc, T):
     fb.call("fence_softmax", ds.data_ptr(), s.size, None)
     np.testing.assert_allclose(ds.cpu().numpy(), rs, rtol=2e-5, atol=1e-12)
     h = T.empty(n, dtype=T.int16, device="cuda")
-    fb.call("fence_f32_to_f16", h.data_ptr(), cu(T, g).data_ptr(), n, None)
+    fb.call("fence_f32_to_f16", h.data_ptr(), dg.data_ptr(), n, None)
     assert np.array_equal(h.cpu().numpy().view(np.uint16), g.astype(np.float16).view(np.uint16))
     back = T.empty(n, device="cuda")
     fb.call("fence_half_to_float", back.data_ptr(), h.data_ptr(), n, None)
@@ -96,8 +97,8 @@ def test_store_kv(fb, T):
     vc = T.zeros(max_ctx * kv_dim, dtype=T.int16, device="cuda")
     k = np.random.default_rng(3).standard_normal(kv_dim).astype(np.float32)
     v = np.random.default_rng(4).standard_normal(kv_dim).astype(np.float32)
-    fb.call("fence_store_kv", kc.data_ptr(), vc.data_ptr(), cu(T, k).data_ptr(), cu(T, v).data_ptr(), 63, kv_dim,
-            max_ctx, None)
+    dk, dv = cu(T, k), cu(T, v)
+    fb.call("fence_store_kv", kc.data_ptr(), vc.data_ptr(), dk.data_ptr(), dv.data_ptr(), 63, kv_dim, max_ctx, None)
     kh = kc.cpu().numpy().view(np.uint16).reshape(max_ctx, kv_dim)
     assert np.array_equal(kh[63], k.astype(np.float16).view(np.uint16)) and not kh[:63].any()
     assert np.array_equal(vc.cpu().numpy().view(np.uint16).reshape(max_ctx, kv_dim)[63],
@@ -118,8 +119,8 @@ def test_gqa_attention(fb, orc, T, nq, nkv, hd, seq, max_ctx):
                                   nkv, seq)
     out = T.empty(nq * hd, device="cuda")
     score = T.full((nq * max_ctx,), float("nan"), device="cuda")
-    dk, dv = cu(T, kc.view(np.int16)), cu(T, vc.view(np.int16))
-    fb.call("fence_gqa_attention", out.data_ptr(), cu(T, q).data_ptr(), dk.data_ptr(), dv.data_ptr(), hd, nq, nkv,
+    dk, dv, dq = cu(T, kc.view(np.int16)), cu(T, vc.view(np.int16)), cu(T, q)
+    fb.call("fence_gqa_attention", out.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), hd, nq, nkv,
             seq, max_ctx, score.data_ptr(), None)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=2e-5)
 
@@ -138,5 +139,6 @@ def test_argmax_reference_order(fb, orc, T):
     cases.append(rng.standard_normal(128256).astype(np.float32))
     res = T.zeros(1, dtype=T.int32, device="cuda")
     for x in cases:
-        fb.call("fence_argmax", cu(T, x).data_ptr(), res.data_ptr(), x.size, None)
+        dx = cu(T, x)
+        fb.call("fence_argmax", dx.data_ptr(), res.data_ptr(), x.size, None)
         assert int(res.item()) == orc.argmax(x)
