@@ -15,6 +15,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libfence_b200.so")
 
+FENCE_LAUNCH_PDL = 1
 FENCE_KV_BF16 = 0
 FENCE_KV_F16 = 1
 GGML_Q8_0 = 8
@@ -68,6 +69,7 @@ class SynthSpec(ctypes.Structure):
 SIGNATURES = [
     ("fence_last_error", ctypes.c_char_p, []),
     ("fence_device_error", ctypes.c_int, []),
+    ("fence_set_launch_flags", ctypes.c_int, [ctypes.c_int]),
     ("fence_gemv_q6k", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("fence_gemv_q6k_bias", ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),
     ("fence_gemv_q8_0", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]),

@@ -4,6 +4,8 @@
 #include "gemv.cuh"
 #include "host.h"
 
+#include <algorithm>
+
 namespace fence {
 
 // ------------------------------------------------------------------ fallback kernels
@@ -87,6 +89,9 @@ static int device_smem_optin(int dev) {
     return cached[dev];
 }
 
+// Two GEMV CTAs fit on one SM (<= 320 threads, ~110 KB shared memory), so the CTA of the kernel
+// launched next (programmatic dependent launch) can already stream its weights while this one
+// finishes. Each consumer thread owns one 64-element item of K and takes R rows per stage.
 GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     GemvPlan pl{};
     const int blk_elems = (wt == WT_Q6K) ? 256 : 32;
@@ -94,40 +99,53 @@ GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     if (K <= 0 || Mv <= 0 || K % 64 != 0 || K % blk_elems != 0) return pl;
     const int I = K / 64;
     const int rowB = (K / blk_elems) * blk_bytes;
-    if (I > GEMV_MAX_NT - 32) return pl;
-    int P = 512 / I;
+    const int max_cons = GEMV_MAX_NT - 32;
+    if (I > max_cons) return pl;
+    int P = 256 / I;
     if (P < 1) P = 1;
     if (P > 16) P = 16;
-    if ((P * I + 31) / 32 * 32 + 32 > GEMV_MAX_NT) P = (GEMV_MAX_NT - 32) / I;
-    if (dual) {
-        P &= ~1;
-        if (P < 2) return pl;  // pairs need two row slots
-    }
+    if ((P * I + 31) / 32 * 32 > max_cons) P = max_cons / I;
     if (P < 1) return pl;
+    // rows per thread per stage (independent dot products in flight): as many as keep a stage
+    // within 28 KB, at most GEMV_MAX_R
+    int R = 28672 / (P * rowB);
+    if (R < 1) R = 1;
+    if (R > GEMV_MAX_R) R = GEMV_MAX_R;
+    int S = P * R;
+    if (dual && (S & 1)) {
+        if (R < GEMV_MAX_R) ++R;
+        else --R;
+        S = P * R;
+        if (S & 1 || S < 2) {
+            R = 2;
+            S = P * 2;
+        }
+    }
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sms(dev);
     int G = max_ctas > 0 ? max_ctas : sms;
     if (G > Mv) G = Mv;
-    const int step = dual ? P / 2 : P;
+    const int step = dual ? S / 2 : S;
     const int rows_cta = (Mv + G - 1) / G;
     const int stages_cta = (rows_cta + step - 1) / step;
-    const int stage_bytes = ((P * rowB + GEMV_STAGE_SLACK + 127) / 128) * 128;
-    const int budget = device_smem_optin(dev) - 1024;
-    int ring = 16;
+    const int stage_bytes = ((S * rowB + GEMV_STAGE_SLACK + 127) / 128) * 128;
+    const int budget = std::min(device_smem_optin(dev) - 1024, 112 * 1024);
+    int ring = 8;
     if (ring > stages_cta) ring = stages_cta;
-    while (ring > 1 && (int)gemv_smem_layout(ring, stage_bytes, P, I).total > budget) --ring;
-    if ((int)gemv_smem_layout(ring, stage_bytes, P, I).total > budget) return pl;
+    while (ring > 1 && (int)gemv_smem_layout(ring, stage_bytes, S, I).total > budget) --ring;
+    if ((int)gemv_smem_layout(ring, stage_bytes, S, I).total > budget) return pl;
     pl.ok = 1;
     pl.I = I;
     pl.rowB = rowB;
     pl.P = P;
+    pl.R = R;
     pl.ring = ring;
     pl.stage_bytes = stage_bytes;
     pl.nt_cons = (P * I + 31) / 32 * 32;
     pl.block = pl.nt_cons + 32;
     pl.grid = G;
-    pl.smem = (int)gemv_smem_layout(ring, stage_bytes, P, I).total;
+    pl.smem = (int)gemv_smem_layout(ring, stage_bytes, S, I).total;
     return pl;
 }
 
@@ -135,6 +153,7 @@ void fill_plan(GemvArgs& a, const GemvPlan& pl) {
     a.I = pl.I;
     a.rowB = pl.rowB;
     a.P = pl.P;
+    a.R = pl.R;
     a.ring = pl.ring;
     a.stage_bytes = pl.stage_bytes;
     a.nt_cons = pl.nt_cons;
@@ -185,6 +204,15 @@ FENCE_GEMV_INST(WT_Q6K, X_NORM, EPI_LMHEAD)
 
 using namespace fence;
 
+// Process-wide launch flags of the drop-in GEMVs (fence_set_launch_flags).
+static int g_launch_flags = 0;
+
+extern "C" int fence_set_launch_flags(int flags) {
+    const int old = g_launch_flags;
+    g_launch_flags = flags;
+    return old;
+}
+
 // ------------------------------------------------------------------ drop-in entries
 static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* bias, float* y,
                            int M, int K, cudaStream_t st) {
@@ -201,7 +229,7 @@ static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* 
         a.K = K;
         a.x = x;
         fill_plan(a, pl);
-        e = launch_gemv<WT_Q6K, X_F16, EPI_STORE>(a, pl, st, false);
+        e = launch_gemv<WT_Q6K, X_F16, EPI_STORE>(a, pl, st, (g_launch_flags & FENCE_LAUNCH_PDL) != 0);
     } else {
         const int threads = 128;
         gemv_q6k_simple_kernel<<<(M + 3) / 4, threads, 0, st>>>(reinterpret_cast<const uint8_t*>(W), x,
@@ -238,7 +266,7 @@ extern "C" int fence_gemv_q8_0(const block_q8_0* W, const float* x, float* y, in
         a.K = K;
         a.x = x;
         fill_plan(a, pl);
-        e = launch_gemv<WT_Q80, X_F32, EPI_STORE>(a, pl, st, false);
+        e = launch_gemv<WT_Q80, X_F32, EPI_STORE>(a, pl, st, (g_launch_flags & FENCE_LAUNCH_PDL) != 0);
     } else {
         gemv_q8_0_simple_kernel<<<(M + 3) / 4, 128, 0, st>>>(reinterpret_cast<const uint8_t*>(W), x, y, M, K);
         e = cudaGetLastError();

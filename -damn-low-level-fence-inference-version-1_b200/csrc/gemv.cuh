@@ -39,8 +39,9 @@ enum : int { WT_Q6K = 0, WT_Q80 = 1 };
 enum : int { X_F16 = 0, X_F32 = 1, X_F32_R16 = 2, X_NORM = 3, X_NORM_R16 = 4 };
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LMHEAD = 3 };
 
-constexpr int GEMV_MAX_NT = 640;  // consumer threads + one producer warp
+constexpr int GEMV_MAX_NT = 320;  // consumer threads + one producer warp; two CTAs fit on an SM
 constexpr int GEMV_MAX_SEG = 3;
+constexpr int GEMV_MAX_R = 4;  // rows per consumer thread per stage
 constexpr int GEMV_STAGE_SLACK = 256;  // per-stage bytes: <= 3 pieces x (30 B alignment + 31 B padding) + over-read
 
 struct GemvSeg {
@@ -66,7 +67,8 @@ struct GemvArgs {
     int K;
     int rowB;         // bytes per row
     int I;            // items (64 elements) per row
-    int P;            // rows per stage
+    int P;            // row slots of consumer threads (threads = P * I)
+    int R;            // rows each consumer thread handles per stage (stage = P * R rows)
     int ring;         // stages in the shared-memory ring
     int stage_bytes;  // bytes per ring slot (multiple of 128)
     int nt_cons;      // consumer threads (multiple of 32)
@@ -486,30 +488,30 @@ __device__ __forceinline__ void load_slice(uint32_t rec, XSlice<WT>& s) {
 struct GemvSmem {
     uint32_t red, xq, rowtab, rowinfo, bars, misc, total;
 };
-__host__ __device__ inline GemvSmem gemv_smem_layout(int ring, int stage_bytes, int P, int I) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int ring, int stage_bytes, int S, int I) {
     auto r16 = [](uint32_t x) { return (x + 15u) & ~15u; };
     GemvSmem L;
     L.red = (uint32_t)ring * (uint32_t)stage_bytes;
-    L.xq = L.red + r16(8u * P * I);
+    L.xq = L.red + r16(8u * S * I);
     L.rowtab = L.xq + (uint32_t)I * XQ_WORDS * 4u;
-    L.rowinfo = L.rowtab + r16(4u * ring * P);
-    L.bars = L.rowinfo + r16(4u * ring * P);
+    L.rowinfo = L.rowtab + r16(4u * ring * S);
+    L.bars = L.rowinfo + r16(4u * ring * S);
     L.misc = L.bars + r16(16u * ring);
     L.total = L.misc + 512u;
     return L;
 }
 
 template <int WT, int XM, int EPI>
-__global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
     const int ncons_warps = a.nt_cons >> 5;
     const bool is_producer = (tid >= a.nt_cons);
-    const int P = a.P, I = a.I;
+    const int P = a.P, I = a.I, R = a.R, S = a.P * a.R;  // S = rows per stage
 
-    const GemvSmem SL = gemv_smem_layout(a.ring, a.stage_bytes, P, I);
+    const GemvSmem SL = gemv_smem_layout(a.ring, a.stage_bytes, S, I);
     uint8_t* ring = smem;
     float* red = reinterpret_cast<float*>(smem + SL.red);
     const uint32_t smem_sa = smem_u32(smem);  // shared-window address of the dynamic allocation
@@ -529,7 +531,7 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
     const int v_begin = (int)(((long long)a.Mv * c) / G);
     const int v_end = (int)(((long long)a.Mv * (c + 1)) / G);
     const int rows_cta = v_end - v_begin;
-    const int step = a.dual ? P / 2 : P;  // virtual rows per stage (dual: gate/up pairs)
+    const int step = a.dual ? S / 2 : S;  // virtual rows per stage (dual: gate/up pairs)
     const int nstages = (rows_cta + step - 1) / step;
 
     if (tid == 0) {
@@ -565,8 +567,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
             StageGeo geo;
             stage_geo(a, va, n, geo);
             const int rows_in_stage = a.dual ? 2 * n : n;
-            if (lane < rows_in_stage) {
-                const int k = piece_of(geo, lane);
+            for (int rr = lane; rr < rows_in_stage; rr += 32) {
+                const int k = piece_of(geo, rr);
                 uint32_t off = 0, delta = 0;
                 int first = 0, r0 = 0;
 #pragma unroll
@@ -577,8 +579,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
                         first = geo.p[j].first_row;
                         r0 = geo.p[j].seg_row0;
                     }
-                rowtab[slot * P + lane] = (uint32_t)slot * a.stage_bytes + off + delta + (uint32_t)(lane - first) * a.rowB;
-                rowinfo[slot * P + lane] = (k << 28) | (r0 + lane - first);
+                rowtab[slot * S + rr] = (uint32_t)slot * a.stage_bytes + off + delta + (uint32_t)(rr - first) * a.rowB;
+                rowinfo[slot * S + rr] = (k << 28) | (r0 + rr - first);
             }
             __syncwarp();
             if (lane == 0) {
@@ -679,28 +681,38 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 1) gemv_stream_kernel(const __gri
                 ok = false;
             }
         }
-        float part = 0.f;
-        if (ok && active && p < rows_in_stage)
-            part = item_dot<WT>(smem_sa + rowtab[slot * P + p] + item_off, item, xs);
+        // this thread's R rows of the stage: p, p + P, ..., independent dot products (ILP)
+        float part[GEMV_MAX_R];
+#pragma unroll
+        for (int j = 0; j < GEMV_MAX_R; ++j) {
+            part[j] = 0.f;
+            const int rs = p + P * j;
+            if (j < R && ok && active && rs < rows_in_stage)
+                part[j] = item_dot<WT>(smem_sa + rowtab[slot * S + rs] + item_off, item, xs);
+        }
         // rows this warp reduces below (warp, warp + nw, ...): lane j keeps the tensor/row of the
         // j-th one, read before the slot is released
         int myinfo = 0;
-        if (ok && warp + lane * ncons_warps < nred) myinfo = rowinfo[slot * P + warp + lane * ncons_warps];
+        if (ok && warp + lane * ncons_warps < nred) myinfo = rowinfo[slot * S + warp + lane * ncons_warps];
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        if (active) red[buf * P * I + tid] = part;
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < GEMV_MAX_R; ++j)
+                if (j < R) red[(buf * S + p + P * j) * I + item] = part[j];
+        }
         named_bar_sync(1, a.nt_cons);
 
         // ---- reduce rows and run the epilogue (fixed order -> deterministic)
         for (int r = warp, q = 0; r < nred; r += ncons_warps, ++q) {
             const int info = __shfl_sync(0xffffffffu, myinfo, q);
-            const float* rr = red + buf * P * I + r * I;
+            const float* rr = red + (buf * S + r) * I;
             float sum = 0.f;
             for (int j = lane; j < I; j += 32) sum += rr[j];
             sum = warp_sum(sum);
             float sum2 = 0.f;
             if (a.dual) {
-                const float* r2 = red + buf * P * I + (r + n) * I;
+                const float* r2 = red + (buf * S + r + n) * I;
                 for (int j = lane; j < I; j += 32) sum2 += r2[j];
                 sum2 = warp_sum(sum2);
             }
@@ -787,7 +799,7 @@ __global__ void gemv_q8_0_simple_kernel(const uint8_t* __restrict__ W, const flo
 struct GemvPlan {
     int ok;
     int grid, block, smem;
-    int P, ring, stage_bytes, I, rowB, nt_cons;
+    int P, R, ring, stage_bytes, I, rowB, nt_cons;
 };
 
 }  // namespace fence

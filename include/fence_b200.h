@@ -82,6 +82,14 @@ typedef struct block_q8_0 {
  *    fp16 buffers are passed as uint16_t* (IEEE binary16 bit patterns, i.e. __half*).
  * ===================================================================================== */
 
+/* Launch flags of the drop-in GEMVs (process-wide; returns the previous flags).
+ * FENCE_LAUNCH_PDL: launch with programmatic dependent launch, so a GEMV starts streaming its
+ * weights while the preceding kernel in the stream is still running (its reads of x wait for that
+ * kernel to finish). Set it only when no earlier work in the stream writes the weight matrices.
+ * No counterpart in the reference (its launchers take only the stream). */
+#define FENCE_LAUNCH_PDL 1
+int fence_set_launch_flags(int flags);
+
 /* y[M] = W_q6k[M x K] . x[K]; x fp16, y fp32, K % 256 == 0.
  * Replaces gemv_q6k, src/kernels/gemv_q6k.cuh:89-102. */
 int fence_gemv_q6k(const block_q6_K* W, const uint16_t* x, float* y, int M, int K,
