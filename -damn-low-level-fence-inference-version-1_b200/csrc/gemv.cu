@@ -89,9 +89,12 @@ static int device_smem_optin(int dev) {
     return cached[dev];
 }
 
-// Two GEMV CTAs fit on one SM (<= 320 threads, ~110 KB shared memory), so the CTA of the kernel
-// launched next (programmatic dependent launch) can already stream its weights while this one
-// finishes. Each consumer thread owns one 64-element item of K and takes R rows per stage.
+// Launch plan of the warp-autonomous streaming GEMV:
+//  * lanes per row (lpr): the width in {32, 16, 8, 4} that wastes the fewest lanes on the row's
+//    items, subject to one warp batch of rows fitting a stage of <= 32 KB;
+//  * stage = the largest multiple of the warp batch within 32 KB;
+//  * 148 CTAs (one per SM, so the kernel launched next can sit beside it and prefetch) unless the
+//    matrix is long enough to want more warps streaming per SM, then 2 per SM.
 GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     GemvPlan pl{};
     const int blk_elems = (wt == WT_Q6K) ? 256 : 32;
@@ -99,64 +102,65 @@ GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas) {
     if (K <= 0 || Mv <= 0 || K % 64 != 0 || K % blk_elems != 0) return pl;
     const int I = K / 64;
     const int rowB = (K / blk_elems) * blk_bytes;
-    const int max_cons = GEMV_MAX_NT - 32;
-    if (I > max_cons) return pl;
-    int P = 256 / I;
-    if (P < 1) P = 1;
-    if (P > 16) P = 16;
-    if ((P * I + 31) / 32 * 32 > max_cons) P = max_cons / I;
-    if (P < 1) return pl;
-    // rows per thread per stage (independent dot products in flight): as many as keep a stage
-    // within 28 KB, at most GEMV_MAX_R
-    int R = 28672 / (P * rowB);
-    if (R < 1) R = 1;
-    if (R > GEMV_MAX_R) R = GEMV_MAX_R;
-    int S = P * R;
-    if (dual && (S & 1)) {
-        if (R < GEMV_MAX_R) ++R;
-        else --R;
-        S = P * R;
-        if (S & 1 || S < 2) {
-            R = 2;
-            S = P * 2;
+    const int RB = gemv_rows_per_group(dual);
+    const int rows_per_unit = dual ? 2 : 1;
+    const int stage_cap = 32768;
+    int best_lpr = 0;
+    double best_eff = -1.0;
+    for (int lpr = 32; lpr >= 4; lpr >>= 1) {
+        const int BR = (32 / lpr) * RB;
+        if ((long long)BR * rows_per_unit * rowB > stage_cap && lpr != 32) continue;
+        const int passes = (I + lpr - 1) / lpr;
+        const double eff = (double)I / (double)(passes * lpr);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best_lpr = lpr;
         }
     }
+    if (!best_lpr) return pl;
+    const int BR = (32 / best_lpr) * RB;
+    int mult = stage_cap / (BR * rows_per_unit * rowB);
+    if (mult < 1) mult = 1;
+    int S = BR * mult;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = device_sms(dev);
     int G = max_ctas > 0 ? max_ctas : sms;
+    if (max_ctas <= 0) {
+        const int stages_one = ((Mv + sms - 1) / sms + S - 1) / S;
+        if (stages_one > 8) G = 2 * sms;
+    }
     if (G > Mv) G = Mv;
-    const int step = dual ? S / 2 : S;
     const int rows_cta = (Mv + G - 1) / G;
-    const int stages_cta = (rows_cta + step - 1) / step;
-    const int stage_bytes = ((S * rowB + GEMV_STAGE_SLACK + 127) / 128) * 128;
+    if (S > rows_cta) S = ((rows_cta + BR - 1) / BR) * BR;
+    const int stages_cta = (rows_cta + S - 1) / S;
+    const int SR = S * rows_per_unit;
+    const int stage_bytes = ((SR * rowB + GEMV_STAGE_SLACK + 127) / 128) * 128;
     const int budget = std::min(device_smem_optin(dev) - 1024, 112 * 1024);
     int ring = 8;
     if (ring > stages_cta) ring = stages_cta;
-    while (ring > 1 && (int)gemv_smem_layout(ring, stage_bytes, S, I).total > budget) --ring;
-    if ((int)gemv_smem_layout(ring, stage_bytes, S, I).total > budget) return pl;
+    while (ring > 1 && (int)gemv_smem_layout(ring, stage_bytes, SR, I).total > budget) --ring;
+    if ((int)gemv_smem_layout(ring, stage_bytes, SR, I).total > budget) return pl;
     pl.ok = 1;
     pl.I = I;
     pl.rowB = rowB;
-    pl.P = P;
-    pl.R = R;
+    pl.S = S;
+    pl.lpr = best_lpr;
     pl.ring = ring;
     pl.stage_bytes = stage_bytes;
-    pl.nt_cons = (P * I + 31) / 32 * 32;
-    pl.block = pl.nt_cons + 32;
+    pl.block = GEMV_MAX_NT;
     pl.grid = G;
-    pl.smem = (int)gemv_smem_layout(ring, stage_bytes, S, I).total;
+    pl.smem = (int)gemv_smem_layout(ring, stage_bytes, SR, I).total;
     return pl;
 }
 
 void fill_plan(GemvArgs& a, const GemvPlan& pl) {
     a.I = pl.I;
     a.rowB = pl.rowB;
-    a.P = pl.P;
-    a.R = pl.R;
+    a.S = pl.S;
+    a.lpr = pl.lpr;
     a.ring = pl.ring;
     a.stage_bytes = pl.stage_bytes;
-    a.nt_cons = pl.nt_cons;
 }
 
 template <int WT, int XM, int EPI>

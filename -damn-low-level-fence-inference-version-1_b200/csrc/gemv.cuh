@@ -39,9 +39,9 @@ enum : int { WT_Q6K = 0, WT_Q80 = 1 };
 enum : int { X_F16 = 0, X_F32 = 1, X_F32_R16 = 2, X_NORM = 3, X_NORM_R16 = 4 };
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_LMHEAD = 3 };
 
-constexpr int GEMV_MAX_NT = 320;  // consumer threads + one producer warp; two CTAs fit on an SM
+constexpr int GEMV_NW = 8;                        // consumer warps per CTA
+constexpr int GEMV_MAX_NT = GEMV_NW * 32 + 32;    // + one producer warp; two CTAs fit on an SM
 constexpr int GEMV_MAX_SEG = 3;
-constexpr int GEMV_MAX_R = 4;  // rows per consumer thread per stage
 constexpr int GEMV_STAGE_SLACK = 256;  // per-stage bytes: <= 3 pieces x (30 B alignment + 31 B padding) + over-read
 
 struct GemvSeg {
@@ -67,11 +67,10 @@ struct GemvArgs {
     int K;
     int rowB;         // bytes per row
     int I;            // items (64 elements) per row
-    int P;            // row slots of consumer threads (threads = P * I)
-    int R;            // rows each consumer thread handles per stage (stage = P * R rows)
+    int S;            // virtual rows per stage (dual: gate/up pairs)
+    int lpr;          // lanes per row: a warp works on 32/lpr row groups at once
     int ring;         // stages in the shared-memory ring
     int stage_bytes;  // bytes per ring slot (multiple of 128)
-    int nt_cons;      // consumer threads (multiple of 32)
     // x source
     const void* x;
     const float* norm_w;
@@ -485,59 +484,66 @@ __device__ __forceinline__ void load_slice(uint32_t rec, XSlice<WT>& s) {
 }
 
 // Shared-memory carve-up (all regions 16-byte aligned); the host plan uses the same function.
+// SR = rows per stage slot (dual: 2 x pairs).
 struct GemvSmem {
-    uint32_t red, xq, rowtab, rowinfo, bars, misc, total;
+    uint32_t xq, rowtab, rowinfo, bars, misc, total;
 };
-__host__ __device__ inline GemvSmem gemv_smem_layout(int ring, int stage_bytes, int S, int I) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int ring, int stage_bytes, int SR, int I) {
     auto r16 = [](uint32_t x) { return (x + 15u) & ~15u; };
     GemvSmem L;
-    L.red = (uint32_t)ring * (uint32_t)stage_bytes;
-    L.xq = L.red + r16(8u * S * I);
+    L.xq = (uint32_t)ring * (uint32_t)stage_bytes;
     L.rowtab = L.xq + (uint32_t)I * XQ_WORDS * 4u;
-    L.rowinfo = L.rowtab + r16(4u * ring * S);
-    L.bars = L.rowinfo + r16(4u * ring * S);
+    L.rowinfo = L.rowtab + r16(4u * ring * SR);
+    L.bars = L.rowinfo + r16(4u * ring * SR);
     L.misc = L.bars + r16(16u * ring);
     L.total = L.misc + 512u;
     return L;
 }
 
+// Rows (dual: pairs) each lane group takes per batch: two independent rows share one x load;
+// in dual mode the gate and up rows of a pair already share it.
+__host__ __device__ inline int gemv_rows_per_group(int dual) { return dual ? 1 : 2; }
+
+// One warp-autonomous streaming GEMV. Per CTA: one producer warp streams the CTA's contiguous rows
+// through a ring of shared-memory stages (1-D TMA bulk copies on mbarriers); GEMV_NW consumer
+// warps each take whole batches of rows (lane group of `lpr` lanes per row, each lane a strided
+// subset of the row's 64-element items, shuffle reduction inside the group) and release every
+// stage independently — no CTA-wide barrier in the steady state.
 template <int WT, int XM, int EPI>
 __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    const int ncons_warps = a.nt_cons >> 5;
-    const bool is_producer = (tid >= a.nt_cons);
-    const int P = a.P, I = a.I, R = a.R, S = a.P * a.R;  // S = rows per stage
+    constexpr int NT_CONS = GEMV_NW * 32;
+    const bool is_producer = (tid >= NT_CONS);
+    const int I = a.I, S = a.S;
+    const int SR = a.dual ? 2 * S : S;
 
-    const GemvSmem SL = gemv_smem_layout(a.ring, a.stage_bytes, S, I);
-    uint8_t* ring = smem;
-    float* red = reinterpret_cast<float*>(smem + SL.red);
+    const GemvSmem SL = gemv_smem_layout(a.ring, a.stage_bytes, SR, I);
     const uint32_t smem_sa = smem_u32(smem);  // shared-window address of the dynamic allocation
     const uint32_t xq_sa = smem_sa + SL.xq;
-    uint32_t* rowtab = reinterpret_cast<uint32_t*>(smem + SL.rowtab);   // [ring][P] byte offset of each row
-    int* rowinfo = reinterpret_cast<int*>(smem + SL.rowinfo);            // [ring][P] (tensor << 28) | row
+    uint8_t* ring = smem;
+    uint32_t* rowtab = reinterpret_cast<uint32_t*>(smem + SL.rowtab);  // [ring][SR] byte offset of each row
+    int* rowinfo = reinterpret_cast<int*>(smem + SL.rowinfo);           // [ring][SR] (tensor << 28) | row
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
     uint64_t* empty = full + a.ring;
-    float* misc = reinterpret_cast<float*>(smem + SL.misc);  // [32] block reduction scratch
+    float* misc = reinterpret_cast<float*>(smem + SL.misc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
-    float* warp_best_v = misc + 40;                        // [32]
-    int* warp_best_i = reinterpret_cast<int*>(misc + 72);  // [32]
+    float* warp_best_v = misc + 40;                        // [GEMV_NW]
+    int* warp_best_i = reinterpret_cast<int*>(misc + 72);  // [GEMV_NW]
 
-    // ---- CTA row range (virtual rows)
+    // ---- CTA range of virtual rows (dual: pairs)
     const int G = gridDim.x;
     const int c = blockIdx.x;
     const int v_begin = (int)(((long long)a.Mv * c) / G);
     const int v_end = (int)(((long long)a.Mv * (c + 1)) / G);
-    const int rows_cta = v_end - v_begin;
-    const int step = a.dual ? S / 2 : S;  // virtual rows per stage (dual: gate/up pairs)
-    const int nstages = (rows_cta + step - 1) / step;
+    const int nstages = (v_end - v_begin + S - 1) / S;
 
     if (tid == 0) {
         for (int s = 0; s < a.ring; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], ncons_warps);
+            mbar_init(&empty[s], GEMV_NW);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -562,8 +568,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
             }
-            const int va = v_begin + s * step;
-            const int n = min(step, v_end - va);
+            const int va = v_begin + s * S;
+            const int n = min(S, v_end - va);
             StageGeo geo;
             stage_geo(a, va, n, geo);
             const int rows_in_stage = a.dual ? 2 * n : n;
@@ -579,8 +585,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
                         first = geo.p[j].first_row;
                         r0 = geo.p[j].seg_row0;
                     }
-                rowtab[slot * S + rr] = (uint32_t)slot * a.stage_bytes + off + delta + (uint32_t)(rr - first) * a.rowB;
-                rowinfo[slot * S + rr] = (k << 28) | (r0 + rr - first);
+                rowtab[slot * SR + rr] = (uint32_t)slot * a.stage_bytes + off + delta + (uint32_t)(rr - first) * a.rowB;
+                rowinfo[slot * SR + rr] = (k << 28) | (r0 + rr - first);
             }
             __syncwarp();
             if (lane == 0) {
@@ -613,62 +619,46 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
     // ================= consumers
     pdl_wait();  // x, residual and epilogue targets come from the previous kernel
 
-    const int p = tid / I;         // row slot within a stage
-    const int item = tid - p * I;  // fixed K slice of this thread
-    const bool active = (p < P);   // threads beyond P*I only help with barriers/reductions
-
-    // ---- prologue: x of every item quantised once per CTA (threads of row slot 0)
+    // ---- prologue: x of every item quantised once per CTA into shared memory
     float rms = 1.f;
     if (XM == X_NORM || XM == X_NORM_R16) {
+        const float* x = static_cast<const float*>(a.x);
         float ss = 0.f;
-        if (p == 0) {
-            const float* x = static_cast<const float*>(a.x);
-            int base[4];
-            if (WT == WT_Q6K) {
-                const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
+        for (int i = tid * 16; i < a.K; i += NT_CONS * 16) {
+            const float4* q4 = reinterpret_cast<const float4*>(x + i);
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) base[cc] = b * 256 + h * 128 + cc * 32 + l16 * 16;
-            } else {
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) base[cc] = item * 64 + cc * 16;
-            }
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const float4* q4 = reinterpret_cast<const float4*>(x + base[cc]);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float4 f = q4[k];
-                    ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
-                }
+            for (int k = 0; k < 4; ++k) {
+                const float4 f = q4[k];
+                ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
             }
         }
         ss = warp_sum(ss);
         if (lane == 0) misc[warp] = ss;
-        named_bar_sync(1, a.nt_cons);
+        named_bar_sync(1, NT_CONS);
         float tot = 0.f;
-        for (int w = 0; w < ncons_warps; ++w) tot += misc[w];
+#pragma unroll
+        for (int w = 0; w < GEMV_NW; ++w) tot += misc[w];
         rms = rsqrtf(tot / (float)a.K + a.eps);
     }
-    if (p == 0) {
+    for (int it = tid; it < I; it += NT_CONS) {
         XSlice<WT> t;
-        make_slice<WT, XM>(a, item, rms, t);
-        store_slice<WT>(xq_sa + item * XQ_WORDS * 4, t);
+        make_slice<WT, XM>(a, it, rms, t);
+        store_slice<WT>(xq_sa + it * XQ_WORDS * 4, t);
     }
-    named_bar_sync(1, a.nt_cons);
-    XSlice<WT> xs;
-    if (active) load_slice<WT>(xq_sa + item * XQ_WORDS * 4, xs);
+    named_bar_sync(1, NT_CONS);
 
-    const int item_off = (WT == WT_Q6K) ? (item >> 2) * 210 : item * 68;
+    constexpr int RBM = 2;  // max rows per lane group per batch
+    const int RB = gemv_rows_per_group(a.dual);
+    const int lpr = a.lpr;
+    const int grp = lane / lpr, sub = lane - grp * lpr;
+    const int BR = (32 / lpr) * RB;  // rows (pairs) per warp batch
     float best_v = 0.f;
     int best_i = -1;
-    int buf = 0;
 
     for (int s = 0; s < nstages; ++s) {
         const int slot = s % a.ring;
-        const int va = v_begin + s * step;
-        const int n = min(step, v_end - va);
-        const int rows_in_stage = a.dual ? 2 * n : n;
-        const int nred = a.dual ? n : rows_in_stage;
+        const int va = v_begin + s * S;
+        const int n = min(S, v_end - va);
 
         bool ok = !*abort_flag;
         if (ok) {
@@ -681,77 +671,94 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
                 ok = false;
             }
         }
-        // this thread's R rows of the stage: p, p + P, ..., independent dot products (ILP)
-        float part[GEMV_MAX_R];
+        const int nbatch = ok ? (n + BR - 1) / BR : 0;
+        for (int b = warp; b < nbatch; b += GEMV_NW) {
+            // rows of this lane group: b*BR + grp*RB + j
+            uint32_t ra[RBM], rb2[RBM];
+            bool valid[RBM];
 #pragma unroll
-        for (int j = 0; j < GEMV_MAX_R; ++j) {
-            part[j] = 0.f;
-            const int rs = p + P * j;
-            if (j < R && ok && active && rs < rows_in_stage)
-                part[j] = item_dot<WT>(smem_sa + rowtab[slot * S + rs] + item_off, item, xs);
-        }
-        // rows this warp reduces below (warp, warp + nw, ...): lane j keeps the tensor/row of the
-        // j-th one, read before the slot is released
-        int myinfo = 0;
-        if (ok && warp + lane * ncons_warps < nred) myinfo = rowinfo[slot * S + warp + lane * ncons_warps];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (active) {
-#pragma unroll
-            for (int j = 0; j < GEMV_MAX_R; ++j)
-                if (j < R) red[(buf * S + p + P * j) * I + item] = part[j];
-        }
-        named_bar_sync(1, a.nt_cons);
-
-        // ---- reduce rows and run the epilogue (fixed order -> deterministic)
-        for (int r = warp, q = 0; r < nred; r += ncons_warps, ++q) {
-            const int info = __shfl_sync(0xffffffffu, myinfo, q);
-            const float* rr = red + (buf * S + r) * I;
-            float sum = 0.f;
-            for (int j = lane; j < I; j += 32) sum += rr[j];
-            sum = warp_sum(sum);
-            float sum2 = 0.f;
-            if (a.dual) {
-                const float* r2 = red + (buf * S + r + n) * I;
-                for (int j = lane; j < I; j += 32) sum2 += r2[j];
-                sum2 = warp_sum(sum2);
+            for (int j = 0; j < RBM; ++j) {
+                const int rr = b * BR + grp * RB + j;
+                valid[j] = (j < RB) && rr < n;
+                ra[j] = valid[j] ? smem_sa + rowtab[slot * SR + rr] : smem_sa;
+                rb2[j] = (valid[j] && a.dual) ? smem_sa + rowtab[slot * SR + n + rr] : smem_sa;
             }
-            if (lane == 0 && ok) {
-                const int row = info & 0x0FFFFFFF;
-                if (EPI == EPI_SWIGLU) {
-                    const float o = silu_mul(sum, sum2);
-                    if (a.act_f16) reinterpret_cast<__half*>(a.act)[row] = __float2half_rn(o);
-                    else reinterpret_cast<float*>(a.act)[row] = o;
-                } else if (EPI == EPI_STORE) {
-                    const int sgi = info >> 28;
-                    float* yk = sgi == 0 ? a.seg[0].y : (sgi == 1 ? a.seg[1].y : a.seg[2].y);
-                    const float* bk = sgi == 0 ? a.seg[0].bias : (sgi == 1 ? a.seg[1].bias : a.seg[2].bias);
-                    yk[row] = bk ? sum + bk[row] : sum;
-                } else if (EPI == EPI_RESID) {
-                    a.resid[row] = sum + a.resid[row];
-                } else if (EPI == EPI_LMHEAD) {
-                    a.logits[row] = sum;
-                    if (argmax_better(sum, row, best_v, best_i)) {
-                        best_v = sum;
-                        best_i = row;
+            float acc[RBM], acc2[RBM];
+#pragma unroll
+            for (int j = 0; j < RBM; ++j) acc[j] = acc2[j] = 0.f;
+            for (int it = sub; it < I; it += lpr) {
+                XSlice<WT> xs;
+                load_slice<WT>(xq_sa + it * XQ_WORDS * 4, xs);
+                const uint32_t io = (WT == WT_Q6K) ? (uint32_t)(it >> 2) * 210u : (uint32_t)it * 68u;
+#pragma unroll
+                for (int j = 0; j < RBM; ++j) {
+                    if (valid[j]) {
+                        acc[j] += item_dot<WT>(ra[j] + io, it, xs);
+                        if (a.dual) acc2[j] += item_dot<WT>(rb2[j] + io, it, xs);
+                    }
+                }
+            }
+            // reduce inside the lane group (fixed xor order -> deterministic)
+#pragma unroll
+            for (int j = 0; j < RBM; ++j) {
+                for (int o = lpr >> 1; o > 0; o >>= 1) {
+                    acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+                    acc2[j] += __shfl_xor_sync(0xffffffffu, acc2[j], o);
+                }
+            }
+            if (sub == 0) {
+#pragma unroll
+                for (int j = 0; j < RBM; ++j) {
+                    if (!valid[j]) continue;
+                    const int rr = b * BR + grp * RB + j;
+                    const int info = rowinfo[slot * SR + rr];
+                    const int row = info & 0x0FFFFFFF;
+                    const float sum = acc[j];
+                    if (EPI == EPI_SWIGLU) {
+                        const float o = silu_mul(sum, acc2[j]);
+                        if (a.act_f16) reinterpret_cast<__half*>(a.act)[row] = __float2half_rn(o);
+                        else reinterpret_cast<float*>(a.act)[row] = o;
+                    } else if (EPI == EPI_STORE) {
+                        const int sgi = info >> 28;
+                        float* yk = sgi == 0 ? a.seg[0].y : (sgi == 1 ? a.seg[1].y : a.seg[2].y);
+                        const float* bk = sgi == 0 ? a.seg[0].bias : (sgi == 1 ? a.seg[1].bias : a.seg[2].bias);
+                        yk[row] = bk ? sum + bk[row] : sum;
+                    } else if (EPI == EPI_RESID) {
+                        a.resid[row] = sum + a.resid[row];
+                    } else if (EPI == EPI_LMHEAD) {
+                        a.logits[row] = sum;
+                        if (argmax_better(sum, row, best_v, best_i)) {
+                            best_v = sum;
+                            best_i = row;
+                        }
                     }
                 }
             }
         }
-        buf ^= 1;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
     }
 
     if (EPI == EPI_LMHEAD) {
-        // CTA best -> global; the last CTA to arrive reduces all CTAs and advances the state.
+        // lane -> warp -> CTA best; the last CTA to arrive reduces all CTAs and advances the state
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (oi >= 0 && argmax_better(ov, oi, best_v, best_i)) {
+                best_v = ov;
+                best_i = oi;
+            }
+        }
         if (lane == 0) {
             warp_best_v[warp] = best_v;
             warp_best_i[warp] = best_i;
         }
-        named_bar_sync(1, a.nt_cons);
+        named_bar_sync(1, NT_CONS);
         if (tid == 0) {
             float bv = 0.f;
             int bi = -1;
-            for (int w = 0; w < ncons_warps; ++w)
+            for (int w = 0; w < GEMV_NW; ++w)
                 if (warp_best_i[w] >= 0 && argmax_better(warp_best_v[w], warp_best_i[w], bv, bi)) {
                     bv = warp_best_v[w];
                     bi = warp_best_i[w];
@@ -799,7 +806,7 @@ __global__ void gemv_q8_0_simple_kernel(const uint8_t* __restrict__ W, const flo
 struct GemvPlan {
     int ok;
     int grid, block, smem;
-    int P, R, ring, stage_bytes, I, rowB, nt_cons;
+    int S, lpr, ring, stage_bytes, I, rowB;
 };
 
 }  // namespace fence
