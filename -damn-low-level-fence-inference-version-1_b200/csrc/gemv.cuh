@@ -671,8 +671,13 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
                 ok = false;
             }
         }
+        // batches are dealt to warps round-robin over the CTA's whole row range (a stage may hold
+        // fewer batches than there are warps)
         const int nbatch = ok ? (n + BR - 1) / BR : 0;
-        for (int b = warp; b < nbatch; b += GEMV_NW) {
+        const int gb0 = s * (S / BR);  // global index of this stage's first batch
+        int b = warp - gb0 % GEMV_NW;
+        if (b < 0) b += GEMV_NW;
+        for (; b < nbatch; b += GEMV_NW) {
             // rows of this lane group: b*BR + grp*RB + j
             uint32_t ra[RBM], rb2[RBM];
             bool valid[RBM];
