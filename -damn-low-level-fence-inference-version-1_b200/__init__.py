@@ -16,8 +16,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libfence_b200.so")
 
 FENCE_LAUNCH_PDL = 1
-FENCE_KV_BF16 = 0
-FENCE_KV_F16 = 1
+FENCE_KV_F16 = 0
+FENCE_KV_BF16 = 1
 GGML_Q8_0 = 8
 GGML_Q6_K = 14
 
@@ -194,7 +194,7 @@ def synth_blocks(ggml_type: int, n_blocks: int, seed: int, stream: int = 0, d: f
 class Model:
     """The reference's Qwen3Model API over the engine handle."""
 
-    def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_BF16, device: int = 0,
+    def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
                  use_graph: bool = True, verbose: bool = False):
         L = lib()
         o = LoadOpts()

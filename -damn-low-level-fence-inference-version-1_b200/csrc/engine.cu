@@ -271,7 +271,7 @@ void free_model(fence_model* m) {
 extern "C" void fence_load_opts_default(fence_load_opts* o) {
     std::memset(o, 0, sizeof *o);
     o->max_ctx = 4096;
-    o->kv_dtype = FENCE_KV_BF16;
+    o->kv_dtype = FENCE_KV_F16;
     o->device = 0;
     o->use_graph = 1;
     o->verbose = 0;

@@ -7,7 +7,7 @@
 // way; the reference's BPE merges and chat templates are not rebuilt. Harness flags on top:
 //   --tokens 1,2,3   prompt given as token ids (skips text encoding)
 //   --seed N         sampler seed (the reference seeds from random_device)
-//   --kv f16|bf16    KV-cache element type (default bf16)
+//   --kv f16|bf16    KV-cache element type (default f16, the reference cache type)
 //   --no-graph       launch kernels one by one instead of replaying the captured step
 #include <chrono>
 #include <cstdio>
@@ -39,7 +39,7 @@ void print_usage(const char* prog) {
     printf("Harness options:\n");
     printf("  --tokens LIST      Comma-separated prompt token ids\n");
     printf("  --seed N           Sampler seed\n");
-    printf("  --kv f16|bf16      KV cache type (default bf16)\n");
+    printf("  --kv f16|bf16      KV cache type (default f16, the reference cache type)\n");
     printf("  --no-graph         Do not replay a captured CUDA graph\n");
 }
 
@@ -136,7 +136,7 @@ struct Vocab {
 
 int main(int argc, char** argv) {
     printf("Fence Inference Engine (B200 / sm_100a)\n\n");
-    std::string model_path, prompt, system_prompt = "You are a helpful assistant.", tokens_arg, kv = "bf16";
+    std::string model_path, prompt, system_prompt = "You are a helpful assistant.", tokens_arg, kv = "f16";
     int max_tokens = 512, max_ctx = 4096, top_k = 50;
     float temp = 0.7f, top_p = 0.8f, rep = 1.15f;
     bool debug = false, graph = true;
@@ -203,7 +203,7 @@ int main(int argc, char** argv) {
     fence_load_opts o;
     fence_load_opts_default(&o);
     o.max_ctx = max_ctx;
-    o.kv_dtype = (kv == "f16") ? FENCE_KV_F16 : FENCE_KV_BF16;
+    o.kv_dtype = (kv == "bf16") ? FENCE_KV_BF16 : FENCE_KV_F16;
     o.use_graph = graph ? 1 : 0;
     o.verbose = 1;
     fence_model* m = fence_model_load(model_path.c_str(), &o);

@@ -114,9 +114,12 @@ def model_bytes_per_token(cfg):
     return int(cfg.weight_bytes)
 
 
-def measure_gemv_roofline(fb, torch, copies=32, launches=256):
+def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
     """Config-0 Q6_K GEMV (4096x4096) through the drop-in C-ABI, rotating over `copies` weight
-    copies (> L2) so every launch streams from HBM; CUDA events on the launching stream."""
+    copies (> L2) so every launch streams from HBM; CUDA events on the launching stream. With
+    pdl=True the launches use FENCE_LAUNCH_PDL (weights are never written), so each GEMV starts
+    streaming while the previous one drains, as inside the decode step."""
+    fb.lib().fence_set_launch_flags(fb.FENCE_LAUNCH_PDL if pdl else 0)
     M = K = 4096
     nblk = M * K // 256
     W = np.frombuffer(fb.synth_blocks(fb.GGML_Q6_K, nblk, seed=0), np.uint8)
@@ -138,6 +141,7 @@ def measure_gemv_roofline(fb, torch, copies=32, launches=256):
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / launches
+    fb.lib().fence_set_launch_flags(0)
     del dW
     return ms
 
@@ -194,9 +198,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="qwen3-4b")
-    ap.add_argument("--kv", default="bf16", choices=["bf16", "f16"])
+    ap.add_argument("--kv", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--tmp", default=None, help="directory for the synthetic GGUF (default: /dev/shm if roomy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="decode", choices=["decode", "gemv"],
+                    help="gemv: only the config-0 Q6_K GEMV roofline measurement (small; used for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -216,6 +222,13 @@ def main():
 
     import torch
     torch.cuda.set_device(local)
+    if args.mode == "gemv":
+        fb = _load_pkg()
+        peak, peak_kind = hbm_peak()
+        ms = measure_gemv_roofline(fb, torch, copies=16, launches=max(args.steps, 1), pdl=True)
+        print(json.dumps({"metric": "gemv_q6k_config0_GBps", "value": round(CONFIG0_BYTES / (ms * 1e-3) / 1e9, 1),
+                          "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "peak": peak, "peak_kind": peak_kind}))
+        return
     dist = None
     if world > 1:
         import datetime
@@ -276,7 +289,8 @@ def main():
         model.close()
 
     peak, peak_kind = hbm_peak()
-    gemv_ms = measure_gemv_roofline(fb, torch)
+    gemv_ms = measure_gemv_roofline(fb, torch, pdl=True)
+    gemv_ms_serial = measure_gemv_roofline(fb, torch, pdl=False)
     achieved = CONFIG0_BYTES / (gemv_ms * 1e-3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -301,7 +315,9 @@ def main():
                    "l2": "weights larger than L2 (no flush needed)"},
         "roofline": {"bound": "hbm", "kernel": "gemv_q6k 4096x4096 (config 0)", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic_from_profiles(), "us_per_launch": round(gemv_ms * 1e3, 3)},
+                     "traffic": traffic_from_profiles(), "us_per_launch": round(gemv_ms * 1e3, 3),
+                     "us_per_launch_serialized": round(gemv_ms_serial * 1e3, 3),
+                     "algorithmic_bytes_per_launch": CONFIG0_BYTES},
         "step_roofline": {"weight_bytes_per_token": step_bytes,
                           "achieved_gbs": round(step_bytes * tok_s / 1e9, 1),
                           "frac": round(step_bytes * tok_s / 1e9 / peak, 4)},

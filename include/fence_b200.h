@@ -174,12 +174,12 @@ typedef struct fence_config {
     size_t weight_bytes;    /* bytes of weights streamed per decode token (this rank)        */
 } fence_config;
 
-#define FENCE_KV_BF16 0
-#define FENCE_KV_F16  1
+#define FENCE_KV_F16  0
+#define FENCE_KV_BF16 1
 
 typedef struct fence_load_opts {
     int max_ctx;        /* context length to allocate (reference default 4096)            */
-    int kv_dtype;       /* FENCE_KV_BF16 (default) or FENCE_KV_F16 (reference numerics)   */
+    int kv_dtype;       /* FENCE_KV_F16 (default, the reference cache type) or FENCE_KV_BF16 */
     int device;         /* CUDA device ordinal                                            */
     int use_graph;      /* capture the token step in a CUDA graph (default 1)             */
     int verbose;        /* print the reference's load banner                              */

@@ -56,7 +56,7 @@ int oracle_argmax(const float* x, int n);
 
 /* ---- full model (src/model/qwen3.cu:116-341) ---- */
 typedef struct oracle_model oracle_model;
-/* kv_bf16: 0 = fp16 cache (reference), 1 = bf16 (engine default). */
+/* kv_bf16: 0 = fp16 cache (reference), 1 = bf16 (engine option). */
 oracle_model* oracle_model_open(const char* path, int max_ctx, int kv_bf16, int nthreads);
 void oracle_model_close(oracle_model* m);
 /* dims[0..9] = layers, embed, ff, heads, kv_heads, head_dim, vocab, max_ctx, linear_type, qk_norm */
