@@ -89,6 +89,8 @@ SIGNATURES = [
     ("fence_gqa_attention", ctypes.c_int,
      [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     ("fence_argmax", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_gqa_attention_static", ctypes.c_int,
+     [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("fence_load_opts_default", None, [ctypes.POINTER(LoadOpts)]),
     ("fence_model_load", _vp, [ctypes.c_char_p, ctypes.POINTER(LoadOpts)]),
     ("fence_model_free", None, [_vp]),

@@ -48,6 +48,7 @@ typedef struct CUstream_st* fence_stream_t;
 #define FENCE_E_DEVICE_WAIT (-5)  /* a device-side bounded wait expired (kernel gave up)       */
 #define FENCE_E_IO          (-6)  /* file could not be opened / written                       */
 #define FENCE_E_NOMEM       (-7)  /* device or host allocation failed                         */
+#define FENCE_E_SCRATCH     (-8)  /* request exceeds a fixed static scratch (see *_static)    */
 
 /* Thread-local text of the last error raised by any fence_* call on this thread ("" if none). */
 const char* fence_last_error(void);
@@ -149,6 +150,20 @@ int fence_gqa_attention(float* attn_out, const float* q, const uint16_t* k_cache
  * (i mod 256) has the smallest 8-bit reversal wins, then the smallest index; NaN and values
  * <= -1e30 never win; 0 when nothing qualifies. Replaces argmax, src/kernels/ops.cuh:501-505. */
 int fence_argmax(const float* x, int* result, int n, fence_stream_t stream);
+
+/* No counterpart in the reference. fence_gqa_attention without score_buf, for callers that cannot
+ * allocate at the call site (a foreign-language binding handed only the operands, or a per-token
+ * host loop that must not call the device-synchronising cudaMalloc). Allocates nothing: the
+ * split-context partials live in a per-device static array of FENCE_ATTN_STATIC_FLOATS floats
+ * (2 MiB). Same split and same results as fence_gqa_attention; a call that needs more than the
+ * array (n_q_heads * chunks * (head_dim + 2) floats, chunks as in fence_gqa_attention) returns
+ * FENCE_E_SCRATCH without launching. The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress) and must come before any stream capture. Calls that overlap in time on
+ * one device race on the shared array: order them on one stream. */
+#define FENCE_ATTN_STATIC_FLOATS 524288
+int fence_gqa_attention_static(float* attn_out, const float* q, const uint16_t* k_cache,
+                               const uint16_t* v_cache, int head_dim, int n_q_heads, int n_kv_heads,
+                               int seq_len, int max_ctx, fence_stream_t stream);
 
 /* =====================================================================================
  * 2. Engine — the reference's Qwen3Model (src/model/qwen3.h:115-155) as a C handle.

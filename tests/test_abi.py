@@ -47,6 +47,11 @@ def test_dropin_argument_errors_are_host_side(fb):
     assert L.fence_gqa_attention(1, 2, 16, 16, 96, 8, 2, 10, 4096, 5, None) == -4  # head_dim 96
     assert L.fence_store_kv(1, 2, 3, 4, 4096, 1024, 4096, None) == -1  # pos out of range
     assert L.fence_argmax(None, None, 10, None) == -1
+    # the static-scratch attention variant checks its arguments and its scratch bound on the host
+    assert L.fence_gqa_attention_static(1, 2, 3, 4, 128, 32, 5, 10, 4096, None) == -1
+    assert L.fence_gqa_attention_static(1, 2, 16, 16, 96, 8, 2, 10, 4096, None) == -4
+    assert L.fence_gqa_attention_static(1, 2, 16, 16, 128, 64, 8, 8320, 8320, None) == -8  # 64 chunks
+    assert "static scratch" in fb.last_error()
 
 
 def test_model_load_rejects_bad_files_on_host(fb, tmp_path):
