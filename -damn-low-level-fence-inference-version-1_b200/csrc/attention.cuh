@@ -73,10 +73,13 @@ struct AttnArgs {
     unsigned int* counter;  // [Hkv] arrival counters, zero between launches
 };
 
-// Fused-mode split of the context: one chunk up to 256 positions (no merge step at all), then
-// ceil(seq_len / 256) chunks (at most nchunk), each a multiple of 16 positions.
+// Fused-mode split of the context: chunks of 64 positions (one CTA each, a single shared-memory
+// tile: the per-CTA work is a latency chain, so spreading the context over more CTAs is what
+// shortens it), at most nchunk chunks (then longer ones), each a multiple of 16 positions. Up to
+// 64 positions there is one chunk and no merge step.
+constexpr int ATTN_CHUNK = 64;
 __device__ __forceinline__ int attn_chunk_len(int seq_len, int nchunk) {
-    int n = (seq_len + 255) / 256;
+    int n = (seq_len + ATTN_CHUNK - 1) / ATTN_CHUNK;
     if (n > nchunk) n = nchunk;
     if (n < 1) n = 1;
     int c = (seq_len + n - 1) / n;
@@ -217,13 +220,20 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
             }
             __syncwarp();
             if (g == G) {
-                // round to the cache type, store the new row (global) and into its tile slot
+                // round to the cache type, store the new row (global) and into its tile slot; the
+                // new v values are loaded before any store (the stores could otherwise alias them
+                // and serialise every load behind the previous store)
                 const int r = pos - t0;
                 KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
                 KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
-                for (int d = lane; d < HD; d += 32) {
+                float vn[HD / 32];
+#pragma unroll
+                for (int i = 0; i < HD / 32; ++i) vn[i] = a.v_new[(long long)h * HD + lane + 32 * i];
+#pragma unroll
+                for (int i = 0; i < HD / 32; ++i) {
+                    const int d = lane + 32 * i;
                     const KVT kq = C::from(v[d]);
-                    const KVT vq = C::from(a.v_new[(long long)h * HD + d]);
+                    const KVT vq = C::from(vn[i]);
                     kw[d] = kq;
                     vw[d] = vq;
                     if (r < ATTN_CMAX) {  // in the first tile; a later tile re-reads the row from global
@@ -268,23 +278,23 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
                     kf[4] = f2.x; kf[5] = f2.y; kf[6] = f3.x; kf[7] = f3.y;
 #pragma unroll
                     for (int g = 0; g < ATTN_MAX_G; ++g) {
-                        if (g < G) {
-                            const float4 qa = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC);
-                            const float4 qb = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC + 4);
-                            acc[g] = fmaf(qa.x, kf[0], acc[g]);
-                            acc[g] = fmaf(qa.y, kf[1], acc[g]);
-                            acc[g] = fmaf(qa.z, kf[2], acc[g]);
-                            acc[g] = fmaf(qa.w, kf[3], acc[g]);
-                            acc[g] = fmaf(qb.x, kf[4], acc[g]);
-                            acc[g] = fmaf(qb.y, kf[5], acc[g]);
-                            acc[g] = fmaf(qb.z, kf[6], acc[g]);
-                            acc[g] = fmaf(qb.w, kf[7], acc[g]);
-                        }
+                        if (g >= G) break;  // uniform: no predicated work for absent heads
+                        const float4 qa = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC);
+                        const float4 qb = *reinterpret_cast<const float4*>(sq + g * HD + ch * EPC + 4);
+                        acc[g] = fmaf(qa.x, kf[0], acc[g]);
+                        acc[g] = fmaf(qa.y, kf[1], acc[g]);
+                        acc[g] = fmaf(qa.z, kf[2], acc[g]);
+                        acc[g] = fmaf(qa.w, kf[3], acc[g]);
+                        acc[g] = fmaf(qb.x, kf[4], acc[g]);
+                        acc[g] = fmaf(qb.y, kf[5], acc[g]);
+                        acc[g] = fmaf(qb.z, kf[6], acc[g]);
+                        acc[g] = fmaf(qb.w, kf[7], acc[g]);
                     }
                 }
             }
 #pragma unroll
             for (int g = 0; g < ATTN_MAX_G; ++g) {
+                if (g >= G) break;
                 acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
                 acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
             }
@@ -389,20 +399,40 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         __syncthreads();
         if (*sflag) {
             __threadfence();
+            // merge in two steps: (1) the chunks' max / exp-sum per head -> per-chunk scale factors
+            // in shared memory (reusing the score buffer), (2) each output element adds its chunks'
+            // partial outputs in chunk order (independent loads, deterministic). The partials are
+            // read from L2: other CTAs wrote them before their counter increment.
             const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
+            float* fsc = ss;           // [G][n_active] chunk max, then scale factor; [G] 1/L after
+            float* fls = sq;           // [G][n_active] chunk exp-sums (q is no longer needed)
+            for (int i = tid; i < G * n_active; i += ATTN_THREADS) {
+                const int g = i / n_active, cc = i - g * n_active;
+                const float* pr = hb + ((long long)cc * G + g) * part_stride;
+                fsc[i] = __ldcg(pr + HD);
+                fls[i] = __ldcg(pr + HD + 1);
+            }
+            __syncthreads();
+            if (tid < G) {
+                const int g = tid;
+                float M = -INFINITY;
+                for (int cc = 0; cc < n_active; ++cc) M = fmaxf(M, fsc[g * n_active + cc]);
+                float L = 0.f;
+                for (int cc = 0; cc < n_active; ++cc) {
+                    const float f = expf(fsc[g * n_active + cc] - M);
+                    L += fls[g * n_active + cc] * f;
+                    fsc[g * n_active + cc] = f;
+                }
+                fsc[G * n_active + g] = 1.0f / L;
+            }
+            __syncthreads();
             for (int pidx = tid; pidx < G * HD; pidx += ATTN_THREADS) {
                 const int g = pidx / HD, d = pidx - g * HD;
-                float M = -INFINITY;
+                float O = 0.f;
+#pragma unroll 8
                 for (int cc = 0; cc < n_active; ++cc)
-                    M = fmaxf(M, ((volatile const float*)hb)[((long long)cc * G + g) * part_stride + HD]);
-                float L = 0.f, O = 0.f;
-                for (int cc = 0; cc < n_active; ++cc) {
-                    const volatile float* pr = hb + ((long long)cc * G + g) * part_stride;
-                    const float f = expf(pr[HD] - M);
-                    L += pr[HD + 1] * f;
-                    O += pr[d] * f;
-                }
-                a.out[(long long)(qh0 + g) * HD + d] = O / L;
+                    O += __ldcg(hb + ((long long)cc * G + g) * part_stride + d) * fsc[g * n_active + cc];
+                a.out[(long long)(qh0 + g) * HD + d] = O * fsc[G * n_active + g];
             }
             if (tid == 0) a.counter[h] = 0u;
         }

@@ -25,14 +25,17 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "gguf.h"
+#include "rgemv.cuh"
 #include "host.h"
 
 namespace fence {
 
-GemvPlan plan_gemv(int wt, int K, int Mv, int dual, int max_ctas);
-void fill_plan(GemvArgs& a, const GemvPlan& pl);
-template <int WT, int XM, int EPI>
-cudaError_t launch_gemv(const GemvArgs& a, const GemvPlan& pl, cudaStream_t st, bool pdl);
+size_t rmat_bytes(int wt, long long rows, int K);
+RMat rmat_carve(int wt, long long rows, int K, uint8_t* base);
+cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
+                      int dst_stride, cudaStream_t st);
+RGemvPlan plan_rgemv(RGemvArgs& a, int sms, int smem_budget);
+cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
                         float top_p, int top_k, float rep_penalty, float min_p, bool dynamic_temp,
                         std::mt19937& rng);
@@ -45,9 +48,15 @@ struct LayerW {
     const float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
 };
 
+// One GEMV phase of the token step over repacked weights.
+struct RPhase {
+    RGemvArgs a;
+    RGemvPlan p;
+    int xm, epi;
+};
+
 struct LayerLaunch {
-    GemvArgs qkv, o, gu, down;
-    GemvPlan pqkv, po, pgu, pdown;
+    RPhase qkv, o, gu, down;  // QKV fused into one matrix, gate/up rows interleaved
     AttnArgs attn;
 };
 
@@ -81,8 +90,9 @@ struct fence_model {
     int h_state_n = 0;
     int* h_token = nullptr;          // pinned
     std::vector<LayerLaunch> launches;
-    GemvArgs lm;
-    GemvPlan plm{};
+    RPhase lm{};
+    uint8_t* rarena = nullptr;      // repacked linears (rgemv.cuh layouts)
+    float* qkv_bias = nullptr;      // fused q|k|v bias when the model has any
     int attn_nchunk = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
@@ -95,24 +105,6 @@ namespace {
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 int wtype_id(GGMLType t) { return (int)t; }
-
-// ---- one launch of the GEMV template selected by weight type / modes
-cudaError_t gemv_dispatch(int gtype, int xm, int epi, const GemvArgs& a, const GemvPlan& pl, cudaStream_t st) {
-#define CASE(WT, XM, EPI) \
-    if (wt == WT && xm == XM && epi == EPI) return launch_gemv<WT, XM, EPI>(a, pl, st, true);
-    const int wt = gtype == 14 ? WT_Q6K : WT_Q80;
-    CASE(WT_Q6K, X_NORM_R16, EPI_STORE)
-    CASE(WT_Q80, X_NORM, EPI_STORE)
-    CASE(WT_Q6K, X_F32_R16, EPI_RESID)
-    CASE(WT_Q80, X_F32, EPI_RESID)
-    CASE(WT_Q6K, X_NORM_R16, EPI_SWIGLU)
-    CASE(WT_Q80, X_NORM, EPI_SWIGLU)
-    CASE(WT_Q6K, X_F16, EPI_RESID)
-    CASE(WT_Q80, X_NORM, EPI_LMHEAD)
-    CASE(WT_Q6K, X_NORM, EPI_LMHEAD)
-#undef CASE
-    return cudaErrorInvalidValue;
-}
 
 __global__ void embed_state_kernel(float* __restrict__ out, const uint8_t* __restrict__ W,
                                    const DecodeState* __restrict__ st, int dim) {
@@ -157,15 +149,14 @@ int enqueue_step(fence_model* m) {
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         const LayerLaunch& L = m->launches[l];
-        const int q6 = 14;
-        FENCE_CUDA_TRY(gemv_dispatch(w.t_qkv, w.t_qkv == q6 ? X_NORM_R16 : X_NORM, EPI_STORE, L.qkv, L.pqkv, st));
+        FENCE_CUDA_TRY(rgemv_dispatch(L.qkv.xm, L.qkv.epi, L.qkv.a, L.qkv.p, st));
         if (c.kv_dtype == FENCE_KV_F16) FENCE_CUDA_TRY(launch_attn<__half>(L.attn, m->attn_nchunk, c.n_kv_heads, st));
         else FENCE_CUDA_TRY(launch_attn<__nv_bfloat16>(L.attn, m->attn_nchunk, c.n_kv_heads, st));
-        FENCE_CUDA_TRY(gemv_dispatch(w.t_o, w.t_o == q6 ? X_F32_R16 : X_F32, EPI_RESID, L.o, L.po, st));
-        FENCE_CUDA_TRY(gemv_dispatch(w.t_gu, w.t_gu == q6 ? X_NORM_R16 : X_NORM, EPI_SWIGLU, L.gu, L.pgu, st));
-        FENCE_CUDA_TRY(gemv_dispatch(w.t_down, w.t_down == q6 ? X_F16 : X_F32, EPI_RESID, L.down, L.pdown, st));
+        FENCE_CUDA_TRY(rgemv_dispatch(L.o.xm, L.o.epi, L.o.a, L.o.p, st));
+        FENCE_CUDA_TRY(rgemv_dispatch(L.gu.xm, L.gu.epi, L.gu.a, L.gu.p, st));
+        FENCE_CUDA_TRY(rgemv_dispatch(L.down.xm, L.down.epi, L.down.a, L.down.p, st));
     }
-    FENCE_CUDA_TRY(gemv_dispatch(c.embd_type, X_NORM, EPI_LMHEAD, m->lm, m->plm, st));
+    FENCE_CUDA_TRY(rgemv_dispatch(m->lm.xm, m->lm.epi, m->lm.a, m->lm.p, st));
     return FENCE_OK;
 }
 
@@ -258,6 +249,8 @@ void free_model(fence_model* m) {
     cudaFree(m->state);
     cudaFree(m->token_log);
     cudaFree(m->rope);
+    cudaFree(m->rarena);
+    cudaFree(m->qkv_bias);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -498,7 +491,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
 
     const int HD = c.head_dim, G = c.n_heads / c.n_kv_heads;
     const size_t kv_elems = (size_t)c.n_layers * c.n_kv_heads * c.max_ctx * HD;
-    m->attn_nchunk = std::max(32, (c.max_ctx + ATTN_CMAX - 1) / ATTN_CMAX);
+    // chunks per KV head: 64-position chunks up to 120 (the merge keeps G x chunks scale factors in
+    // the CTA's score buffer); longer contexts get longer chunks
+    m->attn_nchunk = std::min(120, std::max(32, (c.max_ctx + ATTN_CHUNK - 1) / ATTN_CHUNK));
     bool ok = cudaMalloc(&m->kcache, kv_elems * 2) == cudaSuccess && cudaMalloc(&m->vcache, kv_elems * 2) == cudaSuccess &&
               cudaMemset(m->kcache, 0, kv_elems * 2) == cudaSuccess && cudaMemset(m->vcache, 0, kv_elems * 2) == cudaSuccess &&
               cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qd + 2 * kvd) * 4) == cudaSuccess &&
@@ -531,68 +526,101 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
             return bail(FENCE_E_NOMEM, "model_load: rope table upload failed");
     }
 
-    // ---- per-layer launch arguments
+    // ---- repacked linears (rgemv.cuh): one fused QKV matrix and one gate/up-interleaved matrix per
+    // layer, O, down and the tied LM head, rewritten once on the device from the uploaded blocks
+    auto wt_of = [](int t) { return t == 14 ? WT_Q6K : WT_Q80; };
+    const long long QKVR = (long long)(qd + 2 * kvd);
+    size_t rbytes = rmat_bytes(WT_Q80, c.vocab_size, (int)H);
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerW& w = m->layers[l];
+        rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) + rmat_bytes(wt_of(w.t_o), (long long)H, (int)qd) +
+                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)F, (int)H) + rmat_bytes(wt_of(w.t_down), (long long)H, (int)F);
+    }
+    if (qd % 256 || H % 256 || F % 256) {
+        // Q8_0 rows only need 64-element items; Q6_K super-blocks need 256
+        for (int l = 0; l < c.n_layers; ++l) {
+            const LayerW& w = m->layers[l];
+            if ((w.t_qkv == 14 && H % 256) || (w.t_o == 14 && qd % 256) || (w.t_gu == 14 && H % 256) ||
+                (w.t_down == 14 && F % 256) || qd % 64 || F % 64)
+                return bail(FENCE_E_UNSUPPORTED, "model_load: linear input width not a multiple of the block size");
+        }
+    }
+    if (cudaMalloc(&m->rarena, rbytes) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: repacked arena allocation failed");
+    int sms = 0, smem_sm = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->dev);
+    cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, m->dev);
+    // two CTAs share an SM (a phase and the next, under programmatic dependent launch)
+    const int smem_budget = smem_sm / 2 - 2048;
+    uint8_t* rp = m->rarena;
+    auto carve = [&](int wt, long long rows, int K) {
+        RMat r = rmat_carve(wt, rows, K, rp);
+        rp += rmat_bytes(wt, rows, K);
+        return r;
+    };
+    bool any_bias = false;
+    for (const LayerW& w : m->layers) any_bias = any_bias || w.q_bias || w.k_bias || w.v_bias;
+    if (any_bias) {
+        if (cudaMalloc(&m->qkv_bias, (size_t)c.n_layers * QKVR * 4) != cudaSuccess ||
+            cudaMemset(m->qkv_bias, 0, (size_t)c.n_layers * QKVR * 4) != cudaSuccess)
+            return bail(FENCE_E_NOMEM, "model_load: bias allocation failed");
+    }
+    cudaStream_t st = m->stream;
+    auto fill = [&](int wt, const uint8_t* src, long long rows, int K, const RMat& r, long long row0, int stride) {
+        return rmat_fill(wt, src, rows, K, r, row0, stride, st) == cudaSuccess;
+    };
+    auto phase = [&](RPhase& ph, const RMat& r, int wt, int K, int Mv, int dual, int xm, int epi) -> bool {
+        ph = RPhase{};
+        ph.a.w = r;
+        ph.a.wt = wt;
+        ph.a.I = K / 64;
+        ph.a.Mv = Mv;
+        ph.a.dual = dual;
+        ph.xm = xm;
+        ph.epi = epi;
+        ph.p = plan_rgemv(ph.a, sms, smem_budget);
+        return ph.p.ok != 0;
+    };
+
     m->launches.resize(c.n_layers);
     const size_t kv_layer = (size_t)c.n_kv_heads * c.max_ctx * HD;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
-        const int wq = w.t_qkv == 14 ? WT_Q6K : WT_Q80, wo = w.t_o == 14 ? WT_Q6K : WT_Q80,
-                  wg = w.t_gu == 14 ? WT_Q6K : WT_Q80, wd = w.t_down == 14 ? WT_Q6K : WT_Q80;
-        // QKV
-        L.pqkv = plan_gemv(wq, (int)H, (int)(qd + 2 * kvd), 0, 0);
-        L.po = plan_gemv(wo, (int)qd, (int)H, 0, 0);
-        L.pgu = plan_gemv(wg, (int)H, (int)F, 1, 0);
-        L.pdown = plan_gemv(wd, (int)F, (int)H, 0, 0);
-        if (!L.pqkv.ok || !L.po.ok || !L.pgu.ok || !L.pdown.ok)
+        const int wq = wt_of(w.t_qkv), wo = wt_of(w.t_o), wg = wt_of(w.t_gu), wd = wt_of(w.t_down);
+        const RMat rq = carve(wq, QKVR, (int)H), ro = carve(wo, (long long)H, (int)qd),
+                   rg = carve(wg, 2 * (long long)F, (int)H), rd = carve(wd, (long long)H, (int)F);
+        if (!fill(wq, w.q, (long long)qd, (int)H, rq, 0, 1) || !fill(wq, w.k, (long long)kvd, (int)H, rq, (long long)qd, 1) ||
+            !fill(wq, w.v, (long long)kvd, (int)H, rq, (long long)(qd + kvd), 1) ||
+            !fill(wo, w.o, (long long)H, (int)qd, ro, 0, 1) || !fill(wg, w.gate, (long long)F, (int)H, rg, 0, 2) ||
+            !fill(wg, w.up, (long long)F, (int)H, rg, 1, 2) || !fill(wd, w.down, (long long)H, (int)F, rd, 0, 1))
+            return bail(FENCE_E_NOMEM, "model_load: repacking failed");
+        float* bias = nullptr;
+        if (any_bias) {
+            bias = m->qkv_bias + (size_t)l * QKVR;
+            if ((w.q_bias && cudaMemcpy(bias, w.q_bias, qd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
+                (w.k_bias && cudaMemcpy(bias + qd, w.k_bias, kvd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
+                (w.v_bias && cudaMemcpy(bias + qd + kvd, w.v_bias, kvd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess))
+                return bail(FENCE_E_NOMEM, "model_load: bias upload failed");
+        }
+        if (!phase(L.qkv, rq, wq, (int)H, (int)QKVR, 0, wq == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_STORE) ||
+            !phase(L.o, ro, wo, (int)qd, (int)H, 0, wo == WT_Q6K ? X_F32_R16 : X_F32, EPI_RESID) ||
+            !phase(L.gu, rg, wg, (int)H, (int)F, 1, wg == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_SWIGLU) ||
+            !phase(L.down, rd, wd, (int)F, (int)H, 0, wd == WT_Q6K ? X_F16 : X_F32, EPI_RESID))
             return bail(FENCE_E_UNSUPPORTED, "model_load: a layer shape does not fit the streaming GEMV");
-        GemvArgs a{};
-        a.nseg = 3;
-        a.seg[0] = GemvSeg{w.q, (int)qd, m->qkv, w.q_bias};
-        a.seg[1] = GemvSeg{w.k, (int)kvd, m->qkv + qd, w.k_bias};
-        a.seg[2] = GemvSeg{w.v, (int)kvd, m->qkv + qd + kvd, w.v_bias};
-        a.Mv = (int)(qd + 2 * kvd);
-        a.K = (int)H;
-        a.x = m->hidden;
-        a.norm_w = w.attn_norm;
-        a.eps = c.rms_eps;
-        fill_plan(a, L.pqkv);
-        L.qkv = a;
-        // O + residual
-        a = GemvArgs{};
-        a.nseg = 1;
-        a.seg[0] = GemvSeg{w.o, (int)H, nullptr, nullptr};
-        a.Mv = (int)H;
-        a.K = (int)qd;
-        a.x = m->attn_out;
-        a.resid = m->hidden;
-        fill_plan(a, L.po);
-        L.o = a;
-        // gate/up + SwiGLU
-        a = GemvArgs{};
-        a.nseg = 2;
-        a.dual = 1;
-        a.seg[0] = GemvSeg{w.gate, (int)F, nullptr, nullptr};
-        a.seg[1] = GemvSeg{w.up, (int)F, nullptr, nullptr};
-        a.Mv = (int)F;
-        a.K = (int)H;
-        a.x = m->hidden;
-        a.norm_w = w.ffn_norm;
-        a.eps = c.rms_eps;
-        a.act = m->act;
-        a.act_f16 = (w.t_down == 14) ? 1 : 0;
-        fill_plan(a, L.pgu);
-        L.gu = a;
-        // down + residual
-        a = GemvArgs{};
-        a.nseg = 1;
-        a.seg[0] = GemvSeg{w.down, (int)H, nullptr, nullptr};
-        a.Mv = (int)H;
-        a.K = (int)F;
-        a.x = m->act;
-        a.resid = m->hidden;
-        fill_plan(a, L.pdown);
-        L.down = a;
+        L.qkv.a.x = m->hidden;
+        L.qkv.a.norm_w = w.attn_norm;
+        L.qkv.a.eps = c.rms_eps;
+        L.qkv.a.y = m->qkv;  // [q | k | v], the fused matrix's row order
+        L.qkv.a.bias = bias;
+        L.o.a.x = m->attn_out;
+        L.o.a.resid = m->hidden;
+        L.gu.a.x = m->hidden;
+        L.gu.a.norm_w = w.ffn_norm;
+        L.gu.a.eps = c.rms_eps;
+        L.gu.a.act = m->act;
+        L.gu.a.act_f16 = (w.t_down == 14) ? 1 : 0;  // the reference rounds the down input to fp16
+        L.down.a.x = m->act;
+        L.down.a.resid = m->hidden;
         // attention
         AttnArgs at{};
         at.q = m->qkv;
@@ -616,19 +644,15 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         at.out = m->attn_out;
         at.counter = m->counters;
         L.attn = at;
-        (void)wo;
-        (void)wd;
-        (void)wg;
     }
     // LM head: tied token_embd (the reference ignores output.weight, qwen3.cu:180-212,261)
-    m->plm = plan_gemv(WT_Q80, (int)H, c.vocab_size, 0, 0);
-    if (!m->plm.ok || m->plm.grid > 4096) return bail(FENCE_E_UNSUPPORTED, "model_load: LM head shape not supported");
     {
-        GemvArgs a{};
-        a.nseg = 1;
-        a.seg[0] = GemvSeg{m->tok_embd, c.vocab_size, nullptr, nullptr};
-        a.Mv = c.vocab_size;
-        a.K = (int)H;
+        const RMat rl = carve(WT_Q80, c.vocab_size, (int)H);
+        if (!fill(WT_Q80, m->tok_embd, c.vocab_size, (int)H, rl, 0, 1))
+            return bail(FENCE_E_NOMEM, "model_load: repacking failed");
+        if (!phase(m->lm, rl, WT_Q80, (int)H, c.vocab_size, 0, X_NORM, EPI_LMHEAD) || m->lm.p.grid > 4096)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: LM head shape not supported");
+        RGemvArgs& a = m->lm.a;
         a.x = m->hidden;
         a.norm_w = m->out_norm;
         a.eps = c.rms_eps;
@@ -639,8 +663,6 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         a.state = m->state;
         a.token_log = m->token_log;
         a.token_log_cap = m->token_log_cap;
-        fill_plan(a, m->plm);
-        m->lm = a;
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: device error during setup");
     if (opts.use_graph) {

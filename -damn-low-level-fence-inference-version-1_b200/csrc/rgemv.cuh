@@ -1,0 +1,650 @@
+// rgemv.cuh — the engine's streaming GEMV over REPACKED weights (sm_100a).
+//
+// The drop-in launchers read the reference's GGUF blocks as they are (gemv.cuh), whose Q6_K
+// super-blocks are 210 bytes long and so sit at 2-byte alignment in shared memory; every 16-byte
+// load then costs five 4-byte loads and four funnel shifts, and the access pattern hits few banks.
+// The engine owns its weights, so at load time it rewrites every linear once into an aligned,
+// bank-friendly layout with the SAME bytes per weight (repack kernels in rgemv.cu):
+//
+//   Q6_K  (K/256 super-blocks of 210 B per row; item = 64 weights = (super-block j, half h, l16))
+//     q[row][item][48]  ql[64h+16*l16 .. +16] | ql[64h+32+16*l16 .. +16] | qh[32h+16*l16 .. +16]
+//     s[row][item][4]   int8 scales of the item's four 16-element columns: sc[8h + 2c + l16]
+//     d[row][K/256]     fp16 super-block scale d
+//   Q8_0  (K/32 blocks of 34 B per row; item = 64 weights = blocks 2i, 2i+1)
+//     q[row][item][64]  the item's 64 int8 quants in four 16-byte chunks; chunk k is stored at
+//                       position k ^ ((item >> 1) & 3), so the 8 lanes of a quarter warp reading
+//                       position p of 8 consecutive items hit 8 different 16-byte bank groups
+//     d[row][item][2]   fp16 d of block 2i, then of block 2i+1
+//
+// The arithmetic per item is the drop-in kernels' (gemv.cuh item_dot) operation for operation:
+// the integer dot products are exact and the float expression is the same, so the engine's
+// results do not depend on the layout.
+//
+// Kernel (one CTA per SM, 7 consumer warps + 1 producer warp, so that the next phase's kernel fits
+// beside it on the SM and streams its weights under programmatic dependent launch):
+//  * producer: streams the CTA's rows in stages of R rows (3 bulk copies per stage: q, s, d slices)
+//    into a ring of shared-memory slots guarded by mbarriers;
+//  * consumers: quantise x once per CTA, then every stage is worked on by ALL consumer lanes: lane
+//    gl owns one (row, item) of the stage — the same item for the whole kernel, its x held in
+//    registers; a row longer than the lanes is split into equal parts — and a segmented shuffle
+//    reduction sums each row part inside a warp; the first lane of each segment stores that
+//    per-warp piece in shared memory. Nothing else (no atomics, no global traffic) sits in the
+//    stage loop: after the last stage one thread per row adds the row's pieces in a fixed order
+//    (deterministic) and runs the fused epilogue with coalesced global accesses.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace fence {
+
+constexpr int RG_NW = 7;                 // consumer warps
+constexpr int RG_NT = RG_NW * 32 + 32;   // + producer warp
+constexpr int RG_NL = RG_NW * 32;        // consumer lanes
+constexpr int RG_MAX_R = 64;             // row slots per stage
+constexpr int RG_MAX_RING = 12;
+
+// Repacked matrix (see the layout above). Arrays are padded by 64 bytes so stage copies rounded up
+// to 16 bytes stay inside the allocation.
+struct RMat {
+    const uint8_t* q;
+    const uint8_t* s;  // Q6_K only
+    const uint8_t* d;
+    int rows;
+};
+
+struct RGemvArgs {
+    RMat w;
+    int wt;
+    int I;            // items (64 weights) per row
+    int np;           // parts per row (rows longer than the consumer lanes are split in np equal parts)
+    int R;            // rows per stage (dual: even; rows 2p, 2p+1 are gate/up of pair p)
+    int dual;
+    int Mv;           // virtual rows (dual: gate/up pairs)
+    int ring;         // slots in the ring
+    int slot_bytes;
+    int mp;           // max per-warp pieces of one row's reduction
+    int rows_cta;     // max rows (dual: 2 x pairs) of one CTA
+    // x source
+    const void* x;
+    const float* norm_w;
+    float eps;
+    // epilogues
+    float* y;            // EPI_STORE (row-indexed)
+    const float* bias;   // EPI_STORE, optional
+    float* resid;        // EPI_RESID
+    void* act;           // EPI_SWIGLU (pair-indexed)
+    int act_f16;
+    float* logits;       // EPI_LMHEAD
+    float* cta_val;
+    int* cta_idx;
+    unsigned int* counter;
+    DecodeState* state;
+    int* token_log;
+    int token_log_cap;
+};
+
+// Launch plan (host).
+struct RGemvPlan {
+    int ok;
+    int grid, block, smem;
+};
+
+__host__ __device__ inline int rg_qbytes(int wt) { return wt == WT_Q6K ? 48 : 64; }
+__host__ __device__ inline int rg_dbytes_row(int wt, int I) { return wt == WT_Q6K ? I / 2 : I * 4; }
+__host__ __device__ inline int rg_sbytes_row(int wt, int I) { return wt == WT_Q6K ? I * 4 : 0; }
+
+// Shared-memory layout of one slot: [q | s | d] each 16-aligned, d copied from a 16-aligned source
+// below its first row (the offset of that row inside the copy is recomputed by the consumers).
+struct RSlot {
+    uint32_t s_off, d_off, bytes;
+};
+__host__ __device__ inline RSlot rg_slot(int wt, int I, int R) {
+    RSlot L;
+    const uint32_t qb = (uint32_t)R * I * rg_qbytes(wt);
+    const uint32_t sb = (uint32_t)R * rg_sbytes_row(wt, I);
+    const uint32_t db = (uint32_t)R * rg_dbytes_row(wt, I);
+    L.s_off = (qb + 15u) & ~15u;
+    L.d_off = (L.s_off + sb + 15u) & ~15u;
+    L.bytes = (L.d_off + db + 16u + 15u) & ~15u;  // + up to 15 bytes of d alignment slack
+    return L;
+}
+
+struct RGSmem {
+    uint32_t xq, acc, bars, misc, total;
+};
+__host__ __device__ inline RGSmem rg_smem_layout(int ring, int slot_bytes, int I, int rows_cta, int mp) {
+    auto r16 = [](uint32_t x) { return (x + 15u) & ~15u; };
+    RGSmem L;
+    L.xq = (uint32_t)ring * (uint32_t)slot_bytes;
+    L.acc = L.xq + r16((uint32_t)I * XQ_WORDS * 4u);
+    L.bars = L.acc + r16(4u * (uint32_t)rows_cta * (uint32_t)mp);
+    L.misc = L.bars + r16(16u * ring);
+    L.total = L.misc + 512u;
+    return L;
+}
+
+// Per-warp pieces of row slot rs's reduction (np parts of ip items, lanes rs*np*ip ..).
+__host__ __device__ inline int rg_part_pieces(int rs, int pt, int np, int ip) {
+    const int lo = (rs * np + pt) * ip;
+    return ((lo + ip - 1) >> 5) - (lo >> 5) + 1;
+}
+__host__ __device__ inline int rg_row_pieces(int rs, int np, int ip) {
+    int n = 0;
+    for (int pt = 0; pt < np; ++pt) n += rg_part_pieces(rs, pt, np, ip);
+    return n;
+}
+
+// ---------------------------------------------------------------------------------------------
+// x: one 40-word record per item in shared memory, built by a group of lanes.
+//   Q6_K: xh[16] | xl[16] | corr[4] | xs | 0 0 0 ; word 4c+k = elements 4k..4k+3 of column c
+//   Q8_0: xh[16] | xl[16] | 0 0 0 0 | xs0 | xs1 | 0 0 ; word w = elements 4w..4w+3 of the item
+// Q6_K records are built by 4 lanes (lane q: column q), Q8_0 records by 2 lanes (lane q: block q).
+// The arithmetic is make_slice's (gemv.cuh) element for element; the group's amax is an exact max.
+template <int WT>
+__device__ __forceinline__ int rg_task_base(int item, int q) {
+    if (WT == WT_Q6K) {
+        const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
+        return b * 256 + h * 128 + q * 32 + l16 * 16;
+    }
+    return item * 64 + q * 32;
+}
+
+// Raw x values of one record-building task (Q6_K: 16 values of column q; Q8_0: 32 of block q).
+template <int WT, int XM>
+__device__ __forceinline__ void rg_load_task(const void* xsrc, int base, float (&v)[(WT == WT_Q6K) ? 16 : 32]) {
+    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    if (XM == X_F16) {
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xsrc) + base);
+#pragma unroll
+        for (int c = 0; c < NV / 8; ++c) {
+            const uint4 u = p[c];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[c * 8 + 2 * k] = half_bits_to_float(w[k]);
+                v[c * 8 + 2 * k + 1] = half_bits_to_float(w[k] >> 16);
+            }
+        }
+    } else {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(xsrc) + base);
+#pragma unroll
+        for (int c = 0; c < NV / 4; ++c) {
+            const float4 f = p[c];
+            v[4 * c] = f.x;
+            v[4 * c + 1] = f.y;
+            v[4 * c + 2] = f.z;
+            v[4 * c + 3] = f.w;
+        }
+    }
+}
+
+// Normalise / round the task's values as make_slice does (gemv.cuh), quantise them with the
+// item's scale (a max over the lane group: exact) and store the task's words of the record.
+// All lanes of the warp call this (shuffles); lanes with active == false store nothing.
+template <int WT, int XM>
+__device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 32], const float (&w)[(WT == WT_Q6K) ? 16 : 32],
+                                               int q, float rms, uint32_t rec, bool active) {
+    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    if (XM == X_NORM || XM == X_NORM_R16) {  // w[i] * x[i] * rms, the reference's order (ops.cuh:43)
+#pragma unroll
+        for (int e = 0; e < NV; ++e) v[e] = (v[e] * w[e]) * rms;
+    }
+    if (XM == X_F32_R16 || XM == X_NORM_R16) {
+#pragma unroll
+        for (int e = 0; e < NV; ++e) v[e] = round_f16(v[e]);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int e = 0; e < NV; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    if (WT == WT_Q6K) {  // one scale per item: max over its 4 columns
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    }
+    float inv;
+    const float xs = quant_scale(amax, inv);
+    if (!active) return;
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < NV / 4; ++k) {
+        uint32_t hw = 0u, lw = 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int qv = __float2int_rn(v[4 * k + j] * inv);
+            sum += qv;
+            uint32_t hb, lb;
+            split16(qv, hb, lb);
+            hw |= hb << (8 * j);
+            lw |= lb << (8 * j);
+        }
+        const uint32_t wi = (WT == WT_Q6K) ? (uint32_t)(4 * q + k) : (uint32_t)(8 * q + k);
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 4u * wi), "r"(hw) : "memory");
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 64u + 4u * wi), "r"(lw) : "memory");
+    }
+    if (WT == WT_Q6K) {
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 128u + 4u * q), "r"(-32 * sum) : "memory");
+        if (q == 0)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rec + 144u), "r"(__float_as_uint(xs)),
+                         "r"(0u), "r"(0u), "r"(0u) : "memory");
+    } else {
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 144u + 4u * q), "r"(__float_as_uint(xs)) : "memory");
+        if (q == 0)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rec + 128u), "r"(0u), "r"(0u), "r"(0u),
+                         "r"(0u) : "memory");
+        else
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(rec + 152u), "r"(0u), "r"(0u) : "memory");
+    }
+}
+
+// Per-lane x of its item, in the order its weight loads deliver them.
+struct RX {
+    uint32_t xh[16], xl[16];
+    int corr[4];     // Q6_K: -32 * sum of the column's quantised x
+    float xsA, xsB;  // Q6_K: xsA; Q8_0: scale of the block in chunk slots 0-1 / 2-3
+    uint32_t dsel;   // Q8_0: byte_perm selector of slot pair 0-1's d (0x10 or 0x32)
+};
+
+template <int WT>
+__device__ __forceinline__ void rg_load_x(uint32_t rec, int item, RX& x) {
+    if (WT == WT_Q6K) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 a = lds128(rec + 16u * k), b = lds128(rec + 64u + 16u * k);
+            x.xh[4 * k] = a.x; x.xh[4 * k + 1] = a.y; x.xh[4 * k + 2] = a.z; x.xh[4 * k + 3] = a.w;
+            x.xl[4 * k] = b.x; x.xl[4 * k + 1] = b.y; x.xl[4 * k + 2] = b.z; x.xl[4 * k + 3] = b.w;
+        }
+        const uint4 c = lds128(rec + 128u);
+        x.corr[0] = (int)c.x; x.corr[1] = (int)c.y; x.corr[2] = (int)c.z; x.corr[3] = (int)c.w;
+        x.xsA = __uint_as_float(lds32(rec + 144u));
+        x.xsB = 0.f;
+        x.dsel = 0u;
+    } else {
+        // weight chunk slot p holds chunk p ^ f: give slot p the x words of that chunk
+        const uint32_t f = (uint32_t)(item >> 1) & 3u;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t k = (uint32_t)p ^ f;
+            const uint4 a = lds128(rec + 16u * k), b = lds128(rec + 64u + 16u * k);
+            x.xh[4 * p] = a.x; x.xh[4 * p + 1] = a.y; x.xh[4 * p + 2] = a.z; x.xh[4 * p + 3] = a.w;
+            x.xl[4 * p] = b.x; x.xl[4 * p + 1] = b.y; x.xl[4 * p + 2] = b.z; x.xl[4 * p + 3] = b.w;
+        }
+        const float xs0 = __uint_as_float(lds32(rec + 144u)), xs1 = __uint_as_float(lds32(rec + 148u));
+        const bool swap = f >= 2u;  // slots 0-1 then hold block 1
+        x.xsA = swap ? xs1 : xs0;
+        x.xsB = swap ? xs0 : xs1;
+        x.dsel = swap ? 0x3232u : 0x1010u;
+        x.corr[0] = x.corr[1] = x.corr[2] = x.corr[3] = 0;
+    }
+}
+
+// 64-weight item dot of repacked weights: q, s, d are 32-bit shared addresses of the item's record,
+// its scale word (Q6_K) and its d (Q6_K: the super-block's fp16; Q8_0: the item's two fp16).
+template <int WT>
+__device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d, const RX& x) {
+    if (WT == WT_Q6K) {
+        const uint4 A = lds128(q), B = lds128(q + 16u), H = lds128(q + 32u);
+        const uint32_t sc = lds32(s);
+        const uint32_t dbits = lds_u16(d);
+        const uint32_t ql0[4] = {A.x, A.y, A.z, A.w}, ql1[4] = {B.x, B.y, B.z, B.w}, qh[4] = {H.x, H.y, H.z, H.w};
+        int hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
+        int lo0 = x.corr[0], lo1 = x.corr[1], lo2 = x.corr[2], lo3 = x.corr[3];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t qm = qh[k] & 0x33333333u;  // crumbs of columns 0 (bits 0-1) and 2 (bits 4-5)
+            const uint32_t qn = qh[k] & 0xCCCCCCCCu;  // crumbs of columns 1 (bits 2-3) and 3 (bits 6-7)
+            const uint32_t q0 = (ql0[k] & 0x0F0F0F0Fu) | ((qm << 4) & 0xF0F0F0F0u);
+            const uint32_t q1 = (ql1[k] & 0x0F0F0F0Fu) | ((qn << 2) & 0xF0F0F0F0u);
+            const uint32_t q2 = ((ql0[k] >> 4) & 0x0F0F0F0Fu) | (qm & 0xF0F0F0F0u);
+            const uint32_t q3 = ((ql1[k] >> 4) & 0x0F0F0F0Fu) | ((qn >> 2) & 0xF0F0F0F0u);
+            hi0 = dp4a_us(q0, x.xh[0 * 4 + k], hi0);
+            lo0 = dp4a_uu(q0, x.xl[0 * 4 + k], lo0);
+            hi1 = dp4a_us(q1, x.xh[1 * 4 + k], hi1);
+            lo1 = dp4a_uu(q1, x.xl[1 * 4 + k], lo1);
+            hi2 = dp4a_us(q2, x.xh[2 * 4 + k], hi2);
+            lo2 = dp4a_uu(q2, x.xl[2 * 4 + k], lo2);
+            hi3 = dp4a_us(q3, x.xh[3 * 4 + k], hi3);
+            lo3 = dp4a_uu(q3, x.xl[3 * 4 + k], lo3);
+        }
+        const int sc0 = (int)(sc << 24) >> 24, sc1 = (int)(sc << 16) >> 24;
+        const int sc2 = (int)(sc << 8) >> 24, sc3 = (int)sc >> 24;
+        const float t = (float)((hi0 * 256 + lo0) * sc0) + (float)((hi1 * 256 + lo1) * sc1) +
+                        (float)((hi2 * 256 + lo2) * sc2) + (float)((hi3 * 256 + lo3) * sc3);
+        return t * (half_bits_to_float(dbits) * x.xsA);
+    } else {
+        int hiA = 0, loA = 0, hiB = 0, loB = 0;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint4 w = lds128(q + 16u * p);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                if (p < 2) {
+                    hiA = dp4a_ss(ww[m], x.xh[4 * p + m], hiA);
+                    loA = dp4a_su(ww[m], x.xl[4 * p + m], loA);
+                } else {
+                    hiB = dp4a_ss(ww[m], x.xh[4 * p + m], hiB);
+                    loB = dp4a_su(ww[m], x.xl[4 * p + m], loB);
+                }
+            }
+        }
+        const uint32_t dd = lds32(d);
+        const float dA = half_bits_to_float(__byte_perm(dd, 0u, x.dsel));
+        const float dB = half_bits_to_float(__byte_perm(dd, 0u, x.dsel ^ 0x2222u));
+        return (float)(hiA * 256 + loA) * (dA * x.xsA) + (float)(hiB * 256 + loB) * (dB * x.xsB);
+    }
+}
+
+// Epilogue of one finished row (or gate/up pair).
+template <int EPI>
+__device__ __forceinline__ void rg_epilogue(const RGemvArgs& a, int row, float sum, float sum2, float& best_v,
+                                            int& best_i) {
+    if (EPI == EPI_SWIGLU) {
+        const float o = silu_mul(sum, sum2);
+        if (a.act_f16) reinterpret_cast<__half*>(a.act)[row] = __float2half_rn(o);
+        else reinterpret_cast<float*>(a.act)[row] = o;
+    } else if (EPI == EPI_STORE) {
+        a.y[row] = a.bias ? sum + a.bias[row] : sum;
+    } else if (EPI == EPI_RESID) {
+        a.resid[row] = sum + a.resid[row];
+    } else {
+        a.logits[row] = sum;
+        if (argmax_better(sum, row, best_v, best_i)) {
+            best_v = sum;
+            best_i = row;
+        }
+    }
+}
+
+template <int WT, int XM, int EPI>
+__global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__ RGemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool is_producer = tid >= RG_NL;
+    const int I = a.I, R = a.R, ring = a.ring;
+    const bool dual = a.dual != 0;
+    const int S = dual ? R / 2 : R;  // virtual rows per stage
+    const RGSmem SL = rg_smem_layout(ring, a.slot_bytes, I, a.rows_cta, a.mp);
+    const RSlot SS = rg_slot(WT, I, R);
+    const uint32_t smem_sa = smem_u32(smem);
+    const uint32_t xq_sa = smem_sa + SL.xq;
+    float* acc = reinterpret_cast<float*>(smem + SL.acc);  // [rows of the CTA][mp] reduction pieces
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
+    uint64_t* empty = full + ring;
+    float* misc = reinterpret_cast<float*>(smem + SL.misc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
+    float* warp_best_v = misc + 40;
+    int* warp_best_i = reinterpret_cast<int*>(misc + 72);
+
+    const int G = gridDim.x, c = blockIdx.x;
+    const int v_begin = (int)(((long long)a.Mv * c) / G), v_end = (int)(((long long)a.Mv * (c + 1)) / G);
+    const int nstages = (v_end - v_begin + S - 1) / S;
+    const int qb = rg_qbytes(WT), sbr = rg_sbytes_row(WT, I), dbr = rg_dbytes_row(WT, I);
+
+    if (tid == 0) {
+        for (int s = 0; s < ring; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], RG_NW);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) pdl_launch_dependents();
+
+    if (is_producer) {
+        // ================= producer: weights never depend on the previous kernel, so it streams
+        // before griddepcontrol.wait
+        if (lane == 0) {
+            for (int s = 0; s < nstages; ++s) {
+                const int slot = s % ring;
+                if (s >= ring) {
+                    bool ok = false;
+                    for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                        if (mbar_try_wait(&empty[slot], ((s / ring) - 1) & 1)) { ok = true; break; }
+                    if (!ok) {
+                        if (!*abort_flag) set_device_error(-5);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+                const int v0 = v_begin + s * S;
+                const int nv = min(S, v_end - v0);
+                const long long row0 = dual ? 2ll * v0 : v0;
+                const uint32_t nrows = dual ? 2u * nv : (uint32_t)nv;
+                uint8_t* dst = smem + (size_t)slot * a.slot_bytes;
+                const uint32_t qbytes = nrows * (uint32_t)I * qb;
+                const uint32_t sbytes = nrows * (uint32_t)sbr;
+                const uint64_t d0 = (uint64_t)row0 * dbr;
+                const uint64_t d0a = d0 & ~uint64_t(15);
+                const uint32_t dbytes = ((uint32_t)(d0 - d0a) + nrows * (uint32_t)dbr + 15u) & ~15u;
+                mbar_arrive_expect_tx(&full[slot], qbytes + sbytes + dbytes);
+                bulk_g2s(dst, a.w.q + (uint64_t)row0 * I * qb, qbytes, &full[slot]);
+                if (sbytes) bulk_g2s(dst + SS.s_off, a.w.s + (uint64_t)row0 * sbr, sbytes, &full[slot]);
+                bulk_g2s(dst + SS.d_off, a.w.d + d0a, dbytes, &full[slot]);
+            }
+        }
+        __syncwarp();
+        pdl_wait();
+        return;
+    }
+
+    // ================= consumers
+    constexpr int NT = RG_NL;
+    constexpr int LPI = (WT == WT_Q6K) ? 4 : 2;  // lanes per x record
+    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    constexpr bool NORM = (XM == X_NORM || XM == X_NORM_R16);
+    const int ntask = I * LPI;
+    // norm weights do not depend on the previous kernel: fetch them before the wait
+    constexpr int PASSES = (WT == WT_Q6K) ? 2 : 1;  // task passes kept in registers (more re-read x)
+    float wv[PASSES][NV];
+    if (NORM) {
+#pragma unroll
+        for (int ps = 0; ps < PASSES; ++ps) {
+            const int idx = ps * NT + tid;
+            const int base = idx < ntask ? rg_task_base<WT>(idx / LPI, idx % LPI) : 0;
+            const float4* p = reinterpret_cast<const float4*>(a.norm_w + base);
+#pragma unroll
+            for (int cc = 0; cc < NV / 4; ++cc) {
+                const float4 f = p[cc];
+                wv[ps][4 * cc] = f.x;
+                wv[ps][4 * cc + 1] = f.y;
+                wv[ps][4 * cc + 2] = f.z;
+                wv[ps][4 * cc + 3] = f.w;
+            }
+        }
+    }
+    pdl_wait();  // x, residual and epilogue targets come from the previous kernel
+
+    // ---- x prologue: load (sum of squares for RMSNorm), quantise once per CTA into shared memory
+    {
+        float xv[PASSES][NV];
+        float ss = 0.f;
+#pragma unroll
+        for (int ps = 0; ps < PASSES; ++ps) {
+            const int idx = ps * NT + tid;
+            const int base = idx < ntask ? rg_task_base<WT>(idx / LPI, idx % LPI) : 0;
+            rg_load_task<WT, XM>(a.x, base, xv[ps]);
+            if (NORM && idx < ntask) {
+#pragma unroll
+                for (int e = 0; e < NV; ++e) ss += xv[ps][e] * xv[ps][e];
+            }
+        }
+        float rms = 1.f;
+        if (NORM) {
+            for (int b0 = PASSES * NT + tid; b0 < ntask; b0 += NT) {  // beyond the register passes
+                float t[NV];
+                rg_load_task<WT, XM>(a.x, rg_task_base<WT>(b0 / LPI, b0 % LPI), t);
+#pragma unroll
+                for (int e = 0; e < NV; ++e) ss += t[e] * t[e];
+            }
+            ss = warp_sum(ss);
+            if (lane == 0) misc[warp] = ss;
+            named_bar_sync(1, NT);
+            float tot = 0.f;
+#pragma unroll
+            for (int w = 0; w < RG_NW; ++w) tot += misc[w];
+            rms = rsqrtf(tot / (float)(I * 64) + a.eps);
+        }
+        // quantise: register passes (static index), then any remaining tasks straight from memory;
+        // trip counts are warp-uniform (shuffles inside)
+#pragma unroll
+        for (int ps = 0; ps < PASSES; ++ps) {
+            const int b0 = ps * NT + warp * 32;
+            if (b0 < ntask) {
+                const int idx = b0 + lane;
+                const bool active = idx < ntask;
+                const int item = active ? idx / LPI : 0, q = idx % LPI;
+                rg_quant_store<WT, XM>(xv[ps], wv[ps], q, rms, xq_sa + item * XQ_WORDS * 4, active);
+            }
+        }
+        for (int b0 = PASSES * NT + warp * 32; b0 < ntask; b0 += NT) {
+            const int idx = b0 + lane;
+            const bool active = idx < ntask;
+            const int item = active ? idx / LPI : 0, q = idx % LPI;
+            float t[NV], tw[NV];
+            const int base = active ? rg_task_base<WT>(item, q) : 0;
+            rg_load_task<WT, XM>(a.x, base, t);
+            if (NORM) {
+                const float4* p = reinterpret_cast<const float4*>(a.norm_w + base);
+#pragma unroll
+                for (int cc = 0; cc < NV / 4; ++cc) {
+                    const float4 f = p[cc];
+                    tw[4 * cc] = f.x;
+                    tw[4 * cc + 1] = f.y;
+                    tw[4 * cc + 2] = f.z;
+                    tw[4 * cc + 3] = f.w;
+                }
+            }
+            rg_quant_store<WT, XM>(t, tw, q, rms, xq_sa + item * XQ_WORDS * 4, active);
+        }
+    }
+    named_bar_sync(1, NT);
+
+    // ---- lane <-> (slot, item): slot = (row of the stage, part of the row), IP items per part
+    const int NP = a.np, IP = I / NP, MP = a.mp;
+    const int sl = tid / IP, itp = tid - sl * IP;
+    const int rs = sl / NP, pt = sl - rs * NP, it = pt * IP + itp;
+    const bool lane_on = rs < R;
+    RX x;
+    if (lane_on) rg_load_x<WT>(xq_sa + it * XQ_WORDS * 4, it, x);
+    const int slot_lo = sl * IP;
+    const int seg_hi = min(slot_lo + IP - 1 - warp * 32, 31);
+    const bool head = lane == max(slot_lo - warp * 32, 0);
+    int pidx = warp - (slot_lo >> 5);  // this segment's piece index in its row's reduction
+    for (int p2 = 0; p2 < pt; ++p2) pidx += rg_part_pieces(rs, p2, NP, IP);
+    const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
+    const uint32_t s_off = SS.s_off + (uint32_t)(rs * I + it) * 4u;
+    const uint32_t d_off = SS.d_off + (WT == WT_Q6K ? (uint32_t)(rs * (I / 4) + (it >> 2)) * 2u
+                                                     : (uint32_t)(rs * I + it) * 4u);
+    const long long row_begin = dual ? 2ll * v_begin : v_begin;
+
+    for (int s = 0; s < nstages; ++s) {
+        const int slot = s % ring;
+        const int v0 = v_begin + s * S;
+        const int nv = min(S, v_end - v0);
+        const long long row0 = dual ? 2ll * v0 : v0;
+        const int nrows = dual ? 2 * nv : nv;
+        bool ok = !*abort_flag;
+        if (ok) {
+            bool got = false;
+            for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
+                if (mbar_try_wait(&full[slot], (s / ring) & 1)) { got = true; break; }
+            if (!got) {
+                if (!*abort_flag) set_device_error(-5);
+                *abort_flag = 1;
+                ok = false;
+            }
+        }
+        const bool on = ok && lane_on && rs < nrows;
+        float v = 0.f;
+        if (on) {
+            const uint32_t base = smem_sa + (uint32_t)slot * a.slot_bytes;
+            const uint32_t ddelta = (uint32_t)(((uint64_t)row0 * dbr) & 15u);
+            v = rg_item_dot<WT>(base + q_off, base + s_off, base + d_off + ddelta, x);
+        }
+        // segmented reduction: lanes of one row part inside this warp, fixed tree (deterministic)
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float t = __shfl_down_sync(0xffffffffu, v, o);
+            if (lane + o <= seg_hi) v += t;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the slot's bytes are no longer read
+        if (on && head) acc[(size_t)(row0 - row_begin + rs) * MP + pidx] = v;
+    }
+    named_bar_sync(1, NT);  // every piece of every row is in shared memory
+
+    // ---- epilogues, one thread per row (pair): pieces added in part, then warp order
+    auto row_sum = [&](int rl) {
+        const int r_s = rl % R;
+        const int n = rg_row_pieces(r_s, NP, IP);
+        float t = 0.f;
+        for (int k = 0; k < n; ++k) t += acc[(size_t)rl * MP + k];
+        return t;
+    };
+    float best_v = 0.f;
+    int best_i = -1;
+    const int nvr = v_end - v_begin;
+    for (int vr = tid; vr < nvr; vr += NT) {
+        if (dual) {
+            rg_epilogue<EPI>(a, v_begin + vr, row_sum(2 * vr), row_sum(2 * vr + 1), best_v, best_i);
+        } else {
+            rg_epilogue<EPI>(a, v_begin + vr, row_sum(vr), 0.f, best_v, best_i);
+        }
+    }
+
+    if (EPI == EPI_LMHEAD) {
+        // thread -> warp -> CTA best; the last CTA to arrive reduces all CTAs and advances the state
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (oi >= 0 && argmax_better(ov, oi, best_v, best_i)) {
+                best_v = ov;
+                best_i = oi;
+            }
+        }
+        if (lane == 0) {
+            warp_best_v[warp] = best_v;
+            warp_best_i[warp] = best_i;
+        }
+        named_bar_sync(1, NT);
+        if (tid == 0) {
+            float bv = 0.f;
+            int bi = -1;
+            for (int w = 0; w < RG_NW; ++w)
+                if (warp_best_i[w] >= 0 && argmax_better(warp_best_v[w], warp_best_i[w], bv, bi)) {
+                    bv = warp_best_v[w];
+                    bi = warp_best_i[w];
+                }
+            a.cta_val[c] = bv;
+            a.cta_idx[c] = bi;
+            __threadfence();
+            const unsigned int prev = atomicAdd(a.counter, 1u);
+            if (prev == (unsigned)G - 1) {
+                __threadfence();
+                float gv = 0.f;
+                int gi = -1;
+                for (int k = 0; k < G; ++k) {
+                    const int ik = ((volatile int*)a.cta_idx)[k];
+                    const float vk = ((volatile float*)a.cta_val)[k];
+                    if (ik >= 0 && argmax_better(vk, ik, gv, gi)) {
+                        gv = vk;
+                        gi = ik;
+                    }
+                }
+                if (gi < 0) gi = 0;
+                if (a.state) {
+                    DecodeState* st = a.state;
+                    st->token = gi;
+                    st->pos = st->pos + 1;
+                    if (a.token_log && st->step < a.token_log_cap) a.token_log[st->step] = gi;
+                    st->step = st->step + 1;
+                }
+                *a.counter = 0u;
+            }
+        }
+    }
+}
+
+}  // namespace fence
