@@ -48,7 +48,7 @@ class LoadOpts(ctypes.Structure):
     _fields_ = [
         ("max_ctx", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("device", ctypes.c_int),
         ("use_graph", ctypes.c_int), ("verbose", ctypes.c_int), ("tp_rank", ctypes.c_int),
-        ("tp_size", ctypes.c_int), ("nccl_comm", ctypes.c_void_p),
+        ("tp_size", ctypes.c_int), ("nccl_comm", ctypes.c_void_p), ("step_kernel", ctypes.c_int),
     ]
 
 
@@ -89,6 +89,7 @@ SIGNATURES = [
     ("fence_gqa_attention", ctypes.c_int,
      [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     ("fence_argmax", ctypes.c_int, [_vp, _vp, ctypes.c_int, _vp]),
+    ("fence_step_trace", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp]),
     ("fence_gqa_attention_static", ctypes.c_int,
      [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("fence_load_opts_default", None, [ctypes.POINTER(LoadOpts)]),
@@ -164,6 +165,13 @@ CONFIGS = {
     "tiny-q8": dict(arch=b"llama", n_layers=2, embed_dim=512, ff_dim=1024, n_heads=8, n_kv_heads=2,
                     head_dim=128, vocab_size=2048, rope_freq_base=5e5, rms_eps=1e-5,
                     linear_type=GGML_Q8_0, qk_norm=0),
+    # wide test models: K = 4096 rows (64 items) for QKV, O, gate/up and the LM head
+    "wide-q6k": dict(arch=b"qwen3", n_layers=2, embed_dim=4096, ff_dim=1024, n_heads=32, n_kv_heads=8,
+                     head_dim=128, vocab_size=2048, rope_freq_base=1e6, rms_eps=1e-6,
+                     linear_type=GGML_Q6_K, qk_norm=1),
+    "wide-q8": dict(arch=b"llama", n_layers=2, embed_dim=4096, ff_dim=1024, n_heads=32, n_kv_heads=8,
+                    head_dim=128, vocab_size=2048, rope_freq_base=5e5, rms_eps=1e-5,
+                    linear_type=GGML_Q8_0, qk_norm=0),
 }
 
 
@@ -197,11 +205,12 @@ class Model:
     """The reference's Qwen3Model API over the engine handle."""
 
     def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
-                 use_graph: bool = True, verbose: bool = False):
+                 use_graph: bool = True, verbose: bool = False, step_kernel: bool = True):
         L = lib()
         o = LoadOpts()
         L.fence_load_opts_default(ctypes.byref(o))
         o.max_ctx, o.kv_dtype, o.device, o.use_graph, o.verbose = max_ctx, kv_dtype, device, int(use_graph), int(verbose)
+        o.step_kernel = int(step_kernel)
         h = L.fence_model_load(path.encode(), ctypes.byref(o))
         if not h:
             raise FenceError(f"model load failed: {last_error()}")
@@ -270,3 +279,14 @@ class Model:
         ms = ctypes.c_float(0)
         check(lib().fence_time_decode(self._h, token, pos, n_steps, ctypes.byref(ms)), "time_decode")
         return ms.value
+
+    def step_trace(self, token: int, pos: int):
+        """One traced token step (persistent step kernel): array [n_ctas, n_phases, 8]: globaltimer ns
+        at phase start, x ready, stages done, end; consumer and producer ring-wait cycles."""
+        import numpy as np
+        nph, nct = ctypes.c_int(0), ctypes.c_int(0)
+        cap = 4096 * 1024
+        buf = np.zeros(cap, np.uint64)
+        check(lib().fence_step_trace(self._h, token, pos, buf.ctypes.data, cap, ctypes.byref(nph), ctypes.byref(nct)),
+              "step_trace")
+        return buf[: nct.value * nph.value * 8].reshape(nct.value, nph.value, 8)

@@ -25,7 +25,7 @@
 namespace fence {
 
 constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_CMAX = 128;  // positions per shared-memory tile
+constexpr int ATTN_CMAX = 64;   // positions per shared-memory tile (one fused-mode chunk)
 constexpr int ATTN_MAX_G = 8;   // query heads per KV head supported
 constexpr int ATTN_TPP = 4;     // threads per position in the score pass (each owns a quarter of head_dim)
 
@@ -110,8 +110,13 @@ __device__ __forceinline__ void head_rope_warp(float* v, const float2* cs, int l
     __syncwarp();
 }
 
-template <typename KVT, int HD, bool FUSED>
-__global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid_constant__ AttnArgs a) {
+// One (KV head h, context chunk c) unit, run by threads 0 .. ATTN_THREADS-1 of the calling CTA,
+// which synchronise on named barrier bar_id. STANDALONE: a kernel of its own (programmatic dependent
+// launch around the loads that depend on the previous kernel); otherwise a phase of the persistent
+// step kernel, whose grid barrier already orders it after the QKV phase.
+template <typename KVT, int HD, bool FUSED, bool STANDALONE>
+__device__ __forceinline__ void attn_chunk(const AttnArgs& a, int h, int c, uint8_t* sm, int bar_id,
+                                           int known_pos = -1) {
     using C = KVConv<KVT>;
     constexpr int CH = HD * (int)sizeof(KVT) / 16;  // 16-byte chunks per row
     constexpr int EPC = 16 / (int)sizeof(KVT);      // elements per chunk
@@ -119,7 +124,6 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     constexpr int KP = (ATTN_MAX_G * HD / 2 + ATTN_THREADS - 1) / ATTN_THREADS;  // PV pairs per thread
     constexpr int NW = ATTN_THREADS / 32;
     static_assert(CH >= 8 && CH % ATTN_TPP == 0, "head_dim too small for the swizzle");
-    extern __shared__ __align__(128) uint8_t sm[];
     KVT* sk = reinterpret_cast<KVT*>(sm);
     KVT* sv = sk + ATTN_CMAX * HD;
     float* sq = reinterpret_cast<float*>(sv + ATTN_CMAX * HD);  // [G][HD]
@@ -134,11 +138,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     int* sflag = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int h = blockIdx.y;
     const int G = a.n_q_heads / a.n_kv_heads;
     int seq_len, pos, clen;
     if (FUSED) {
-        pos = a.state->pos;  // written by the previous token step, independent of this step's GEMVs
+        // written by the previous token step, independent of this step's GEMVs (the step kernel
+        // reads it once and passes it in)
+        pos = known_pos >= 0 ? known_pos : a.state->pos;
         seq_len = pos + 1;
         clen = attn_chunk_len(seq_len, a.nchunk);
     } else {
@@ -147,9 +152,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         clen = a.chunk_fixed;
     }
     const int n_active = (seq_len + clen - 1) / clen;
-    const int c = blockIdx.x;
     if (c >= n_active) {
-        if (tid == 0) pdl_launch_dependents();
+        if (STANDALONE && tid == 0) pdl_launch_dependents();
         return;
     }
     const int t0 = c * clen;
@@ -189,15 +193,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         smax[tid] = -INFINITY;
         ssum[tid] = 0.f;
     }
-    if (tid == 0) pdl_launch_dependents();
-    pdl_wait();
+    if (STANDALONE) {
+        if (tid == 0) pdl_launch_dependents();
+        pdl_wait();
+    }
 
     // ---- q of the G heads (and the new K/V row) from the QKV GEMV
     const int qh0 = h * G;
     for (int i = tid; i < G * HD; i += ATTN_THREADS) sq[i] = a.q[(long long)qh0 * HD + i];
     if (owns_new)
         for (int d = tid; d < HD; d += ATTN_THREADS) skn[d] = a.k_new[(long long)h * HD + d];
-    __syncthreads();
+    named_bar_sync(bar_id, ATTN_THREADS);
     if (FUSED) {
         // q/k RMSNorm (w * x * rms) then NeoX rotation, warp per head; one more warp for the new k
         for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
@@ -257,7 +263,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
         const int nt = te - ts;
         if (ts != t0) stage_tile(ts, te);
         cp_async_wait_all();
-        __syncthreads();
+        named_bar_sync(bar_id, ATTN_THREADS);
 
         // ---- scores: ATTN_TPP threads per position, each over CPQ chunks, then a shuffle sum
         for (int base = 0; base < nt; base += ATTN_THREADS / ATTN_TPP) {
@@ -304,7 +310,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
                     if (g < G) ss[g * ATTN_CMAX + r] = acc[g] * scale;
             }
         }
-        __syncthreads();
+        named_bar_sync(bar_id, ATTN_THREADS);
 
         // ---- online softmax statistics per head (warp per head)
         for (int g = warp; g < G; g += NW) {
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
                 smax[g] = m_new;
             }
         }
-        __syncthreads();
+        named_bar_sync(bar_id, ATTN_THREADS);
 
         // ---- P.V accumulate: thread <-> (head, dim pair)
 #pragma unroll
@@ -352,7 +358,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
                 o[k][1] = o1;
             }
         }
-        __syncthreads();  // before the next tile overwrites sk/sv/ss
+        named_bar_sync(bar_id, ATTN_THREADS);  // before the next tile overwrites sk/sv/ss
     }
 
     const int part_stride = HD + 2;
@@ -391,12 +397,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
     if (FUSED) {
         // ---- last CTA of this KV head merges all chunks
         __threadfence();
-        __syncthreads();
+        named_bar_sync(bar_id, ATTN_THREADS);
         if (tid == 0) {
             const unsigned prev = atomicAdd(&a.counter[h], 1u);
             *sflag = (prev == (unsigned)n_active - 1) ? 1 : 0;
         }
-        __syncthreads();
+        named_bar_sync(bar_id, ATTN_THREADS);
         if (*sflag) {
             __threadfence();
             // merge in two steps: (1) the chunks' max / exp-sum per head -> per-chunk scale factors
@@ -404,15 +410,17 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
             // partial outputs in chunk order (independent loads, deterministic). The partials are
             // read from L2: other CTAs wrote them before their counter increment.
             const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
-            float* fsc = ss;           // [G][n_active] chunk max, then scale factor; [G] 1/L after
-            float* fls = sq;           // [G][n_active] chunk exp-sums (q is no longer needed)
+            // the K tile and q are no longer needed: [G][n_active] chunk max (then scale factor) and
+            // [G] 1/L in the K tile (>= 4096 floats), [G][n_active] exp-sums in q (1024 floats)
+            float* fsc = reinterpret_cast<float*>(sk);
+            float* fls = sq;
             for (int i = tid; i < G * n_active; i += ATTN_THREADS) {
                 const int g = i / n_active, cc = i - g * n_active;
                 const float* pr = hb + ((long long)cc * G + g) * part_stride;
                 fsc[i] = __ldcg(pr + HD);
                 fls[i] = __ldcg(pr + HD + 1);
             }
-            __syncthreads();
+            named_bar_sync(bar_id, ATTN_THREADS);
             if (tid < G) {
                 const int g = tid;
                 float M = -INFINITY;
@@ -425,7 +433,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
                 }
                 fsc[G * n_active + g] = 1.0f / L;
             }
-            __syncthreads();
+            named_bar_sync(bar_id, ATTN_THREADS);
             for (int pidx = tid; pidx < G * HD; pidx += ATTN_THREADS) {
                 const int g = pidx / HD, d = pidx - g * HD;
                 float O = 0.f;
@@ -437,6 +445,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid
             if (tid == 0) a.counter[h] = 0u;
         }
     }
+}
+
+template <typename KVT, int HD, bool FUSED>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_partial_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    attn_chunk<KVT, HD, FUSED, true>(a, blockIdx.y, blockIdx.x, sm, 0);
 }
 
 // Drop-in merge: one CTA per query head, thread per dimension.

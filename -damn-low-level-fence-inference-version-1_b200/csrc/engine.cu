@@ -26,6 +26,7 @@
 #include "gemv.cuh"
 #include "gguf.h"
 #include "rgemv.cuh"
+#include "step.cuh"
 #include "host.h"
 
 namespace fence {
@@ -92,6 +93,13 @@ struct fence_model {
     std::vector<LayerLaunch> launches;
     RPhase lm{};
     uint8_t* rarena = nullptr;      // repacked linears (rgemv.cuh layouts)
+    // persistent token-step kernel (step.cuh)
+    int use_step = 0;
+    std::vector<SPhase> h_phases;
+    SPhase* d_phases = nullptr;
+    unsigned long long* d_bar = nullptr;
+    StepArgs sargs{};
+    StepPlan splan{};
     float* qkv_bias = nullptr;      // fused q|k|v bias when the model has any
     int attn_nchunk = 0;
     cudaGraph_t graph = nullptr;
@@ -144,6 +152,11 @@ cudaError_t launch_attn(const AttnArgs& a, int nchunk, int nkv, cudaStream_t st)
 int enqueue_step(fence_model* m) {
     const fence_config& c = m->cfg;
     cudaStream_t st = m->stream;
+    if (m->use_step) {
+        if (c.kv_dtype == FENCE_KV_F16) FENCE_CUDA_TRY(launch_step<__half>(m->sargs, m->splan, st));
+        else FENCE_CUDA_TRY(launch_step<__nv_bfloat16>(m->sargs, m->splan, st));
+        return FENCE_OK;
+    }
     embed_state_kernel<<<(c.embed_dim + 255) / 256, 256, 0, st>>>(m->hidden, m->tok_embd, m->state, c.embed_dim);
     FENCE_CUDA_TRY(cudaGetLastError());
     for (int l = 0; l < c.n_layers; ++l) {
@@ -223,6 +236,63 @@ bool check_vec(const GGUFTensorInfo* t, uint64_t n, std::string& err) {
     return true;
 }
 
+// The token step as the persistent kernel's phase list, from the per-phase launch arguments.
+int build_step_phases(fence_model* m) {
+    const fence_config& c = m->cfg;
+    std::vector<SPhase>& ph = m->h_phases;
+    ph.clear();
+    auto gemv = [&](const RPhase& r) {
+        SPhase p{};
+        p.kind = SP_GEMV;
+        p.g = r.a;
+        p.xm = r.xm;
+        p.epi = r.epi;
+        return p;
+    };
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerLaunch& L = m->launches[l];
+        SPhase q = gemv(L.qkv);
+        if (l == 0) {  // the token embedding is folded into the first phase's prologue
+            q.embed = 1;
+            q.embd = m->tok_embd;
+            q.hidden_out = m->hidden;
+        }
+        ph.push_back(q);
+        SPhase at{};
+        at.kind = SP_ATTN;
+        at.at = L.attn;
+        ph.push_back(at);
+        ph.push_back(gemv(L.o));
+        ph.push_back(gemv(L.gu));
+        ph.push_back(gemv(L.down));
+    }
+    ph.push_back(gemv(m->lm));
+    std::string err;
+    m->splan = plan_step(ph, m->dev, err);
+    if (!m->splan.ok) return set_error(FENCE_E_UNSUPPORTED, "%s", err.c_str());
+    if (m->splan.grid > 4096) return set_error(FENCE_E_UNSUPPORTED, "step kernel: more than 4096 SMs");
+    FENCE_CUDA_TRY(cudaMalloc(&m->d_phases, ph.size() * sizeof(SPhase)));
+    FENCE_CUDA_TRY(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(SPhase), cudaMemcpyHostToDevice));
+    FENCE_CUDA_TRY(cudaMalloc(&m->d_bar, sizeof(unsigned long long)));
+    FENCE_CUDA_TRY(cudaMemset(m->d_bar, 0, sizeof(unsigned long long)));
+    StepArgs& A = m->sargs;
+    A = StepArgs{};
+    A.ph = m->d_phases;
+    A.nph = (int)ph.size();
+    A.ring = m->splan.ring;
+    A.slot_bytes = m->splan.slot_bytes;
+    A.scratch_bytes = m->splan.scratch_bytes;
+    A.acc_floats = m->splan.acc_floats;
+    A.bar = m->d_bar;
+    A.state = m->state;
+    A.cta_val = m->lm_val;
+    A.cta_idx = m->lm_idx;
+    A.token_log = m->token_log;
+    A.token_log_cap = m->token_log_cap;
+    m->use_step = 1;
+    return FENCE_OK;
+}
+
 void free_model(fence_model* m) {
     if (!m) return;
     if (!m->stream) {  // failed before any device work
@@ -251,6 +321,8 @@ void free_model(fence_model* m) {
     cudaFree(m->rope);
     cudaFree(m->rarena);
     cudaFree(m->qkv_bias);
+    cudaFree(m->d_phases);
+    cudaFree(m->d_bar);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -270,6 +342,7 @@ extern "C" void fence_load_opts_default(fence_load_opts* o) {
     o->verbose = 0;
     o->tp_rank = 0;
     o->tp_size = 1;
+    o->step_kernel = 1;
 }
 
 extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts* opts_in) {
@@ -664,6 +737,10 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         a.token_log = m->token_log;
         a.token_log_cap = m->token_log_cap;
     }
+    if (opts.step_kernel) {
+        const int rc = build_step_phases(m);
+        if (rc != FENCE_OK) return bail(rc, std::string("model_load: ") + fence_last_error());
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: device error during setup");
     if (opts.use_graph) {
         const int rc = capture_graph(m);
@@ -675,6 +752,37 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
 }
 
 extern "C" void fence_model_free(fence_model* m) { free_model(m); }
+
+extern "C" int fence_step_trace(fence_model* m, int token, int pos, unsigned long long* host_out, int cap,
+                                int* n_phases, int* n_ctas) {
+    if (!m || !host_out) return set_error(FENCE_E_ARG, "step_trace: null argument");
+    if (!m->use_step) return set_error(FENCE_E_UNSUPPORTED, "step_trace: the model was loaded without the step kernel");
+    if (token < 0 || token >= m->cfg.vocab_size || pos < 0 || pos >= m->cfg.max_ctx)
+        return set_error(FENCE_E_ARG, "step_trace: token %d / pos %d out of range", token, pos);
+    const int NPH = m->sargs.nph, G = m->splan.grid;
+    if (n_phases) *n_phases = NPH;
+    if (n_ctas) *n_ctas = G;
+    const size_t n = (size_t)G * NPH * SK_TRACE;
+    if ((size_t)cap < n) return set_error(FENCE_E_ARG, "step_trace: needs %zu entries, got %d", n, cap);
+    cudaSetDevice(m->dev);
+    unsigned long long* d = nullptr;
+    FENCE_CUDA_TRY(cudaMalloc(&d, n * sizeof(unsigned long long)));
+    int rc = cuda_status(cudaMemsetAsync(d, 0, n * sizeof(unsigned long long), m->stream), "step_trace: clear");
+    if (rc == FENCE_OK) rc = set_state(m, token, pos, 0);
+    if (rc == FENCE_OK) {
+        StepArgs a = m->sargs;
+        a.trace = d;
+        const cudaError_t e = (m->cfg.kv_dtype == FENCE_KV_F16) ? launch_step<__half>(a, m->splan, m->stream)
+                                                                : launch_step<__nv_bfloat16>(a, m->splan, m->stream);
+        rc = cuda_status(e, "step_trace: launch");
+    }
+    if (rc == FENCE_OK) rc = cuda_status(cudaStreamSynchronize(m->stream), "step_trace");
+    if (rc == FENCE_OK)
+        rc = cuda_status(cudaMemcpy(host_out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
+                         "step_trace: copy");
+    cudaFree(d);
+    return rc;
+}
 
 extern "C" int fence_model_config(const fence_model* m, fence_config* out) {
     if (!m || !out) return set_error(FENCE_E_ARG, "model_config: null argument");

@@ -2,6 +2,7 @@
 // device error word) and every kernel live in one module, so no relocatable device code is needed.
 #include "gemv.cu"
 #include "rgemv.cu"
+#include "step.cu"
 #include "ops.cu"
 #include "attention_static.cu"
 #include "engine.cu"

@@ -277,25 +277,51 @@ __device__ __forceinline__ void rg_load_x(uint32_t rec, int item, RX& x) {
     }
 }
 
-// 64-weight item dot of repacked weights: q, s, d are 32-bit shared addresses of the item's record,
-// its scale word (Q6_K) and its d (Q6_K: the super-block's fp16; Q8_0: the item's two fp16).
+// The words of one item a lane needs from a stage: Q6_K ql0 | ql1 | qh (12 words), its scale word
+// and the super-block d; Q8_0 the 4 quant chunks (16 words) and the item's two d.
+struct RW {
+    uint32_t w[16];
+    uint32_t sc, d;
+};
+
+// Loads an item's words: q, s, d are 32-bit shared addresses of the item's record, its scale word
+// (Q6_K) and its d (Q6_K: the super-block's fp16; Q8_0: the item's two fp16).
 template <int WT>
-__device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d, const RX& x) {
+__device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d, RW& r) {
     if (WT == WT_Q6K) {
-        const uint4 A = lds128(q), B = lds128(q + 16u), H = lds128(q + 32u);
-        const uint32_t sc = lds32(s);
-        const uint32_t dbits = lds_u16(d);
-        const uint32_t ql0[4] = {A.x, A.y, A.z, A.w}, ql1[4] = {B.x, B.y, B.z, B.w}, qh[4] = {H.x, H.y, H.z, H.w};
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const uint4 u = lds128(q + 16u * k);
+            r.w[4 * k] = u.x; r.w[4 * k + 1] = u.y; r.w[4 * k + 2] = u.z; r.w[4 * k + 3] = u.w;
+        }
+        r.sc = lds32(s);
+        r.d = lds_u16(d);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 u = lds128(q + 16u * k);
+            r.w[4 * k] = u.x; r.w[4 * k + 1] = u.y; r.w[4 * k + 2] = u.z; r.w[4 * k + 3] = u.w;
+        }
+        r.sc = 0u;
+        r.d = lds32(d);
+    }
+}
+
+// 64-weight item dot of loaded words with the lane's x.
+template <int WT>
+__device__ __forceinline__ float rg_item_compute(const RW& r, const RX& x) {
+    if (WT == WT_Q6K) {
         int hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
         int lo0 = x.corr[0], lo1 = x.corr[1], lo2 = x.corr[2], lo3 = x.corr[3];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const uint32_t qm = qh[k] & 0x33333333u;  // crumbs of columns 0 (bits 0-1) and 2 (bits 4-5)
-            const uint32_t qn = qh[k] & 0xCCCCCCCCu;  // crumbs of columns 1 (bits 2-3) and 3 (bits 6-7)
-            const uint32_t q0 = (ql0[k] & 0x0F0F0F0Fu) | ((qm << 4) & 0xF0F0F0F0u);
-            const uint32_t q1 = (ql1[k] & 0x0F0F0F0Fu) | ((qn << 2) & 0xF0F0F0F0u);
-            const uint32_t q2 = ((ql0[k] >> 4) & 0x0F0F0F0Fu) | (qm & 0xF0F0F0F0u);
-            const uint32_t q3 = ((ql1[k] >> 4) & 0x0F0F0F0Fu) | ((qn >> 2) & 0xF0F0F0F0u);
+            const uint32_t ql0 = r.w[k], ql1 = r.w[4 + k], qh = r.w[8 + k];
+            const uint32_t qm = qh & 0x33333333u;  // crumbs of columns 0 (bits 0-1) and 2 (bits 4-5)
+            const uint32_t qn = qh & 0xCCCCCCCCu;  // crumbs of columns 1 (bits 2-3) and 3 (bits 6-7)
+            const uint32_t q0 = (ql0 & 0x0F0F0F0Fu) | ((qm << 4) & 0xF0F0F0F0u);
+            const uint32_t q1 = (ql1 & 0x0F0F0F0Fu) | ((qn << 2) & 0xF0F0F0F0u);
+            const uint32_t q2 = ((ql0 >> 4) & 0x0F0F0F0Fu) | (qm & 0xF0F0F0F0u);
+            const uint32_t q3 = ((ql1 >> 4) & 0x0F0F0F0Fu) | ((qn >> 2) & 0xF0F0F0F0u);
             hi0 = dp4a_us(q0, x.xh[0 * 4 + k], hi0);
             lo0 = dp4a_uu(q0, x.xl[0 * 4 + k], lo0);
             hi1 = dp4a_us(q1, x.xh[1 * 4 + k], hi1);
@@ -305,33 +331,36 @@ __device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d,
             hi3 = dp4a_us(q3, x.xh[3 * 4 + k], hi3);
             lo3 = dp4a_uu(q3, x.xl[3 * 4 + k], lo3);
         }
+        const uint32_t sc = r.sc;
         const int sc0 = (int)(sc << 24) >> 24, sc1 = (int)(sc << 16) >> 24;
         const int sc2 = (int)(sc << 8) >> 24, sc3 = (int)sc >> 24;
         const float t = (float)((hi0 * 256 + lo0) * sc0) + (float)((hi1 * 256 + lo1) * sc1) +
                         (float)((hi2 * 256 + lo2) * sc2) + (float)((hi3 * 256 + lo3) * sc3);
-        return t * (half_bits_to_float(dbits) * x.xsA);
+        return t * (half_bits_to_float(r.d) * x.xsA);
     } else {
         int hiA = 0, loA = 0, hiB = 0, loB = 0;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const uint4 w = lds128(q + 16u * p);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                if (p < 2) {
-                    hiA = dp4a_ss(ww[m], x.xh[4 * p + m], hiA);
-                    loA = dp4a_su(ww[m], x.xl[4 * p + m], loA);
-                } else {
-                    hiB = dp4a_ss(ww[m], x.xh[4 * p + m], hiB);
-                    loB = dp4a_su(ww[m], x.xl[4 * p + m], loB);
-                }
+        for (int m = 0; m < 16; ++m) {
+            if (m < 8) {
+                hiA = dp4a_ss(r.w[m], x.xh[m], hiA);
+                loA = dp4a_su(r.w[m], x.xl[m], loA);
+            } else {
+                hiB = dp4a_ss(r.w[m], x.xh[m], hiB);
+                loB = dp4a_su(r.w[m], x.xl[m], loB);
             }
         }
-        const uint32_t dd = lds32(d);
-        const float dA = half_bits_to_float(__byte_perm(dd, 0u, x.dsel));
-        const float dB = half_bits_to_float(__byte_perm(dd, 0u, x.dsel ^ 0x2222u));
+        const float dA = half_bits_to_float(__byte_perm(r.d, 0u, x.dsel));
+        const float dB = half_bits_to_float(__byte_perm(r.d, 0u, x.dsel ^ 0x2222u));
         return (float)(hiA * 256 + loA) * (dA * x.xsA) + (float)(hiB * 256 + loB) * (dB * x.xsB);
     }
+}
+
+// 64-weight item dot of repacked weights straight from shared memory.
+template <int WT>
+__device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d, const RX& x) {
+    RW r;
+    rg_item_load<WT>(q, s, d, r);
+    return rg_item_compute<WT>(r, x);
 }
 
 // Epilogue of one finished row (or gate/up pair).

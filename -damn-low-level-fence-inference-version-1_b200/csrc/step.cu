@@ -1,0 +1,104 @@
+// step.cu — planning and cooperative launch of the persistent token-step kernel (step.cuh).
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "host.h"
+#include "step.cuh"
+
+namespace fence {
+
+struct StepPlan {
+    int ok = 0;
+    int grid = 0, block = SK_NT, smem = 0;
+    int ring = 0, slot_bytes = 0, scratch_bytes = 0, acc_floats = 0;
+};
+
+// Geometry of one GEMV phase for SK_NL consumer lanes (stages of R actual rows).
+static bool plan_step_gemv(RGemvArgs& g, int grid, std::string& err) {
+    const int I = g.I;
+    if (I <= 0 || g.Mv <= 0) {
+        err = "step kernel: empty GEMV phase";
+        return false;
+    }
+    int np = (I + SK_NL - 1) / SK_NL;
+    while (np <= I && I % np) ++np;
+    const int IP = I / np;
+    int R = std::min((SK_NL / IP) / np, SK_MAX_R);
+    const int vcta = (g.Mv + grid - 1) / grid;
+    const int rows_cta = vcta * (g.dual ? 2 : 1);
+    R = std::max(1, std::min(R, rows_cta));
+    int mp = 1;
+    for (int r = 0; r < R; ++r) mp = std::max(mp, rg_row_pieces(r, np, IP));
+    g.np = np;
+    g.R = R;
+    g.mp = mp;
+    g.rows_cta = rows_cta;
+    g.ring = 0;
+    g.slot_bytes = (int)((rg_slot(g.wt, I, R).bytes + 127u) & ~127u);
+    return true;
+}
+
+static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err) {
+    StepPlan P;
+    int sms = 0, optin = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const int grid = sms;
+    int scratch = attn_smem_bytes<__half, 128>();  // same size for bf16
+    int slot = 0, accf = 0;
+    for (SPhase& ph : phases) {
+        if (ph.kind != SP_GEMV) continue;
+        if (!plan_step_gemv(ph.g, grid, err)) return P;
+        slot = std::max(slot, ph.g.slot_bytes);
+        accf = std::max(accf, ph.g.rows_cta * ph.g.mp);
+        int need = ph.g.I * XQ_WORDS * 4;
+        if (ph.embed) need += ph.g.I * 64 * 4;  // fp32 embedding row after the x records
+        scratch = std::max(scratch, need);
+    }
+    P.scratch_bytes = (scratch + 15) / 16 * 16;
+    P.acc_floats = accf;
+    P.slot_bytes = slot;
+    int ring = 8;
+    while (ring > 2 && (int)sk_smem_layout(ring, slot, P.scratch_bytes, accf).total > optin) --ring;
+    if ((int)sk_smem_layout(ring, slot, P.scratch_bytes, accf).total > optin) {
+        err = "step kernel: the shared-memory plan does not fit";
+        return P;
+    }
+    P.ring = ring;
+    P.smem = (int)sk_smem_layout(ring, slot, P.scratch_bytes, accf).total;
+    P.grid = grid;
+    P.ok = 1;
+    return P;
+}
+
+template <typename KVT>
+static cudaError_t launch_step(const StepArgs& a, const StepPlan& P, cudaStream_t st) {
+    auto kern = step_kernel<KVT>;
+    static int smem_set[64] = {};  // per device: largest dynamic smem enabled so far
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (smem_set[dev] < P.smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P.smem);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, P.block, P.smem);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+        smem_set[dev] = P.smem;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(P.grid);
+    cfg.blockDim = dim3(P.block);
+    cfg.dynamicSmemBytes = P.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the phase counter needs it
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+}  // namespace fence

@@ -1,0 +1,555 @@
+// step.cuh — the whole batch-1 token step (reference: Qwen3Model::forward,
+// src/model/qwen3.cu:241-341) as ONE persistent kernel on B200.
+//
+// A token is ~180 dependent phases (per layer: QKV, attention, O + residual, gate/up + SwiGLU,
+// down + residual; then the LM head), each only a few MB of weights. As separate kernels every
+// phase pays launch, DRAM ramp-up, drain and the completion hand-off. Here the weights of ALL
+// phases stream through one shared-memory ring per SM — weights never depend on activations — and
+// the consumer warps run the phases in order, separated by a grid-wide phase counter.
+//
+//  * grid: one CTA per SM (cooperative launch: all CTAs co-resident, which the counter needs);
+//    block: SK_NW consumer warps + 1 producer warp (16 warps: 128 registers each).
+//  * producer warp (lane 0): walks every GEMV phase's rows of this CTA in order and streams them
+//    (rgemv.cuh repacked layout: q, s, d slices of R rows per stage, 1-D bulk copies, no
+//    multicast) into the ring; it only ever waits for free slots.
+//  * consumers, per GEMV phase (the rgemv.cuh design with 480 lanes): norm weights fetched before
+//    the phase wait; wait for the counter; x quantised once per CTA into shared memory; every stage
+//    worked on by all lanes (lane <-> (row, item), x in registers, segmented shuffle reduction,
+//    one shared-memory piece per (row, warp)); after the last stage one thread per row adds the
+//    pieces in a fixed order and runs the fused epilogue; then the CTA counts itself done.
+//  * attention phase: (KV head, 64-position chunk) units over the CTAs, each run by 256 threads
+//    with attention.cuh's chunk body (q/k RMSNorm, RoPE, KV store, online softmax, last-unit merge).
+//  * LM head: logits + argmax; the CTA that completes the step last reduces the argmax and
+//    advances the device decode state (token, pos, step).
+//
+// Counter protocol: every CTA adds 1 after each phase and 1 after publishing its argmax, so a step
+// adds (n_phases + 1) * G. A CTA takes the step's base as the counter at kernel start rounded down
+// to that multiple (no CTA can be a whole step ahead within one launch); phase k may start once the
+// counter reaches base + k * G. Every wait is bounded; on expiry the device error word is set and
+// the CTA stops waiting (its results are then invalid, but the kernel ends).
+#pragma once
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "rgemv.cuh"
+
+namespace fence {
+
+constexpr int SK_NW = 15;                 // consumer warps
+constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
+constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
+constexpr int SK_MAX_R = 64;              // rows per stage
+constexpr uint32_t SK_BAR_SPINS = 1u << 20;
+constexpr int SK_WAIT_ERR = -5;           // FENCE_E_DEVICE_WAIT in the device error word
+
+enum : int { SP_GEMV = 0, SP_ATTN = 1 };
+constexpr int SK_TRACE = 8;  // trace words per CTA and phase
+
+struct __align__(16) SPhase {
+    int kind;
+    RGemvArgs g;      // GEMV: matrix, geometry (I, np, R, mp, rows_cta), x, epilogue targets
+    int xm, epi;
+    int embed;        // first phase: x = dequantised token_embd row of state->token
+    const uint8_t* embd;
+    float* hidden_out;
+    AttnArgs at;      // attention
+};
+
+struct StepArgs {
+    const SPhase* ph;
+    int nph;
+    int ring, slot_bytes;
+    int scratch_bytes;   // union: x records (+ embedding row) / attention tile
+    int acc_floats;      // reduction pieces of the largest phase
+    unsigned long long* bar;
+    DecodeState* state;
+    float* cta_val;
+    int* cta_idx;
+    int* token_log;
+    int token_log_cap;
+    // optional trace, null = off: [G][nph][SK_TRACE] per CTA: globaltimer ns at the phase start
+    // (after the counter wait), when x is quantised (GEMV) / the first unit is done (attention),
+    // when the last stage is consumed, and at the end (before the count); SM cycles the consumers
+    // waited for filled slots and cycles the producer waited for free slots
+    unsigned long long* trace;
+};
+
+constexpr uint32_t SK_DESC = (sizeof(SPhase) + 15u) & ~15u;  // one phase descriptor in shared memory
+static_assert(sizeof(SPhase) % 16 == 0 && alignof(SPhase) == 16, "descriptors are copied in 16-byte words");
+constexpr int SK_RPRE = SK_NL;                               // prefetched residual rows per CTA
+
+struct SKSmem {
+    uint32_t scratch, acc, desc, rpre, bars, misc, total;
+};
+__host__ __device__ inline SKSmem sk_smem_layout(int ring, int slot_bytes, int scratch_bytes, int acc_floats) {
+    auto r16 = [](uint32_t x) { return (x + 15u) & ~15u; };
+    SKSmem L;
+    L.scratch = (uint32_t)ring * (uint32_t)slot_bytes;
+    L.acc = L.scratch + r16((uint32_t)scratch_bytes);
+    L.desc = L.acc + r16(4u * (uint32_t)acc_floats);
+    L.rpre = L.desc + 2u * SK_DESC;
+    L.bars = L.rpre + r16(4u * SK_RPRE);
+    L.misc = L.bars + r16(16u * ring);
+    L.total = L.misc + 512u;
+    return L;
+}
+
+// Copies phase descriptor k from global to a shared-memory buffer (consumer warp w, lanes 0..).
+__device__ __forceinline__ void sk_fetch_desc(const SPhase* src, uint8_t* dst, int lane) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+    for (int i = lane; i < (int)(sizeof(SPhase) / 16); i += 32) d4[i] = s4[i];
+    if (lane == 0 && sizeof(SPhase) % 16) {
+        const uint8_t* sb = reinterpret_cast<const uint8_t*>(src);
+        for (uint32_t b = sizeof(SPhase) / 16 * 16; b < sizeof(SPhase); ++b) dst[b] = sb[b];
+    }
+}
+
+__device__ __forceinline__ unsigned long long sk_ld_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long sk_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Row range of this CTA in a GEMV phase: virtual rows (dual: gate/up pairs) and actual rows.
+struct SKRows {
+    int v_begin, v_end;
+    long long r_begin, r_end;
+};
+__device__ __forceinline__ SKRows sk_rows(const RGemvArgs& g, int c, int G) {
+    SKRows r;
+    r.v_begin = (int)(((long long)g.Mv * c) / G);
+    r.v_end = (int)(((long long)g.Mv * (c + 1)) / G);
+    r.r_begin = g.dual ? 2ll * r.v_begin : r.v_begin;
+    r.r_end = g.dual ? 2ll * r.v_end : r.v_end;
+    return r;
+}
+
+// ---- x prologue of a GEMV phase (consumers): records of all items in shared memory.
+template <int WT, int XM>
+__device__ __forceinline__ void sk_quantise(const void* xsrc, const float* norm_w, float eps, int I, uint32_t xq_sa,
+                                            float* misc) {
+    constexpr int NT = SK_NL;
+    constexpr int LPI = (WT == WT_Q6K) ? 4 : 2;
+    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    constexpr bool NORM = (XM == X_NORM || XM == X_NORM_R16);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ntask = I * LPI;
+    float xv[NV], wv[NV];
+    const bool mine = tid < ntask;  // one register pass; further tasks re-read x below
+    const int base0 = mine ? rg_task_base<WT>(tid / LPI, tid % LPI) : 0;
+    rg_load_task<WT, XM>(xsrc, base0, xv);
+    float rms = 1.f;
+    if (NORM) {
+        const float4* p = reinterpret_cast<const float4*>(norm_w + base0);
+#pragma unroll
+        for (int cc = 0; cc < NV / 4; ++cc) {
+            const float4 f = p[cc];
+            wv[4 * cc] = f.x;
+            wv[4 * cc + 1] = f.y;
+            wv[4 * cc + 2] = f.z;
+            wv[4 * cc + 3] = f.w;
+        }
+        float ss = 0.f;
+        if (mine) {
+#pragma unroll
+            for (int e = 0; e < NV; ++e) ss += xv[e] * xv[e];
+        }
+        for (int b = NT + tid; b < ntask; b += NT) {
+            float t[NV];
+            rg_load_task<WT, XM>(xsrc, rg_task_base<WT>(b / LPI, b % LPI), t);
+#pragma unroll
+            for (int e = 0; e < NV; ++e) ss += t[e] * t[e];
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) misc[warp] = ss;
+        named_bar_sync(1, NT);
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < SK_NW; ++w) tot += misc[w];
+        rms = rsqrtf(tot / (float)(I * 64) + eps);
+    }
+    if (warp * 32 < ntask) {  // warp-uniform (shuffles inside)
+        const int item = mine ? tid / LPI : 0;
+        rg_quant_store<WT, XM>(xv, wv, tid % LPI, rms, xq_sa + item * XQ_WORDS * 4, mine);
+    }
+    for (int b0 = NT + warp * 32; b0 < ntask; b0 += NT) {
+        const int idx = b0 + lane;
+        const bool active = idx < ntask;
+        const int item = active ? idx / LPI : 0, q = idx % LPI;
+        const int base = active ? rg_task_base<WT>(item, q) : 0;
+        float t[NV], tw[NV];
+        rg_load_task<WT, XM>(xsrc, base, t);
+        if (NORM) {
+            const float4* p = reinterpret_cast<const float4*>(norm_w + base);
+#pragma unroll
+            for (int cc = 0; cc < NV / 4; ++cc) {
+                const float4 f = p[cc];
+                tw[4 * cc] = f.x;
+                tw[4 * cc + 1] = f.y;
+                tw[4 * cc + 2] = f.z;
+                tw[4 * cc + 3] = f.w;
+            }
+        }
+        rg_quant_store<WT, XM>(t, tw, q, rms, xq_sa + item * XQ_WORDS * 4, active);
+    }
+    named_bar_sync(1, NT);  // records complete; misc free again
+}
+
+// Out of line: the prologue's register use stays out of the stage loop's allocation.
+template <int WT>
+__device__ __noinline__ void sk_quantise_xm(int xm, const void* xsrc, const float* norm_w, float eps, int I,
+                                               uint32_t xq_sa, float* misc) {
+    switch (xm) {
+        case X_F16: sk_quantise<WT, X_F16>(xsrc, norm_w, eps, I, xq_sa, misc); break;
+        case X_F32: sk_quantise<WT, X_F32>(xsrc, norm_w, eps, I, xq_sa, misc); break;
+        case X_F32_R16: sk_quantise<WT, X_F32_R16>(xsrc, norm_w, eps, I, xq_sa, misc); break;
+        case X_NORM: sk_quantise<WT, X_NORM>(xsrc, norm_w, eps, I, xq_sa, misc); break;
+        default: sk_quantise<WT, X_NORM_R16>(xsrc, norm_w, eps, I, xq_sa, misc); break;
+    }
+}
+
+// ---- the stage loop of a GEMV phase (consumers), one loop for both weight types: only the item
+// dot branches on the (phase-uniform) type. Returns the ring stages consumed.
+__device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& rr, uint32_t use, int ring,
+                                              int slot_bytes, uint32_t smem_sa, uint32_t xq_sa, float* acc,
+                                              uint64_t* full, uint64_t* empty, volatile int* abort_flag,
+                                              unsigned long long& wait_cycles, bool timing) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool q6 = g.wt == WT_Q6K;
+    const int I = g.I, NP = g.np, IP = I / NP, R = g.R, MP = g.mp;
+    const int qb = rg_qbytes(g.wt), dbr = rg_dbytes_row(g.wt, I);
+    const RSlot SS = rg_slot(g.wt, I, R);
+    const int sl = tid / IP, itp = tid - sl * IP;
+    const int rs = sl / NP, pt = sl - rs * NP, it = pt * IP + itp;
+    const bool lane_on = rs < R;
+    RX x;
+    if (lane_on) {
+        if (q6) rg_load_x<WT_Q6K>(xq_sa + it * XQ_WORDS * 4, it, x);
+        else rg_load_x<WT_Q80>(xq_sa + it * XQ_WORDS * 4, it, x);
+    }
+    const int slot_lo = sl * IP;
+    const int seg_hi = min(slot_lo + IP - 1 - warp * 32, 31);
+    const bool head = lane == max(slot_lo - warp * 32, 0);
+    int pidx = warp - (slot_lo >> 5);
+    for (int p2 = 0; p2 < pt; ++p2) pidx += rg_part_pieces(rs, p2, NP, IP);
+    const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
+    const uint32_t s_off = SS.s_off + (uint32_t)(rs * I + it) * 4u;
+    const uint32_t d_off = SS.d_off + (q6 ? (uint32_t)(rs * (I / 4) + (it >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
+    const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
+    const uint32_t ring_u = (uint32_t)ring;
+    for (int s = 0; s < nstages; ++s, ++use) {
+        const uint32_t slot = use % ring_u;
+        const long long row0 = rr.r_begin + (long long)s * R;
+        const int nrows = (int)min((long long)R, rr.r_end - row0);
+        bool ok = !*abort_flag;
+        if (ok) {
+            const long long w0 = timing ? clock64() : 0;
+            bool got = false;
+            for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
+                if (mbar_try_wait(&full[slot], (use / ring_u) & 1)) { got = true; break; }
+            if (timing) wait_cycles += (unsigned long long)(clock64() - w0);
+            if (!got) {
+                if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                *abort_flag = 1;
+                ok = false;
+            }
+        }
+        const bool on = ok && lane_on && rs < nrows;
+        float v = 0.f;
+        if (on) {
+            const uint32_t base = smem_sa + slot * (uint32_t)slot_bytes;
+            const uint32_t ddelta = (uint32_t)(((uint64_t)row0 * dbr) & 15u);
+            if (q6) v = rg_item_dot<WT_Q6K>(base + q_off, base + s_off, base + d_off + ddelta, x);
+            else v = rg_item_dot<WT_Q80>(base + q_off, base + s_off, base + d_off + ddelta, x);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float t = __shfl_down_sync(0xffffffffu, v, o);
+            if (lane + o <= seg_hi) v += t;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (on && head) acc[(size_t)(row0 - rr.r_begin + rs) * MP + pidx] = v;
+    }
+    return use;
+}
+
+// One attention unit by threads 0..ATTN_THREADS-1, out of line (its registers stay out of the GEMV
+// loops' allocation).
+template <typename KVT>
+__device__ __noinline__ void sk_attn_unit(const AttnArgs& at, int h, int c, uint8_t* scratch, int pos) {
+    attn_chunk<KVT, 128, true, false>(at, h, c, scratch, 2, pos);
+}
+
+// Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
+// prefetched at the phase start (rows up to SK_RPRE).
+__device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
+                                             const float* rpre, float& best_v, int& best_i) {
+    const int NP = g.np, IP = g.I / g.np, R = g.R, MP = g.mp;
+    auto row_sum = [&](int rl) {
+        const int n = rg_row_pieces(rl % R, NP, IP);
+        float t = 0.f;
+        for (int k = 0; k < n; ++k) t += acc[(size_t)rl * MP + k];
+        return t;
+    };
+    const int nvr = rr.v_end - rr.v_begin;
+    for (int vr = threadIdx.x; vr < nvr; vr += SK_NL) {
+        const int row = rr.v_begin + vr;
+        if (epi == EPI_SWIGLU) {
+            const float o = silu_mul(row_sum(2 * vr), row_sum(2 * vr + 1));
+            if (g.act_f16) reinterpret_cast<__half*>(g.act)[row] = __float2half_rn(o);
+            else reinterpret_cast<float*>(g.act)[row] = o;
+        } else {
+            const float sum = row_sum(vr);
+            if (epi == EPI_STORE) {
+                g.y[row] = g.bias ? sum + g.bias[row] : sum;
+            } else if (epi == EPI_RESID) {
+                g.resid[row] = sum + (vr < SK_RPRE ? rpre[vr] : g.resid[row]);
+            } else {
+                g.logits[row] = sum;
+                if (argmax_better(sum, row, best_v, best_i)) {
+                    best_v = sum;
+                    best_i = row;
+                }
+            }
+        }
+    }
+}
+
+template <typename KVT>
+__global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ StepArgs A) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NT = SK_NL;
+    const bool is_producer = tid >= NT;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int ring = A.ring, NPH = A.nph;
+    const SKSmem SL = sk_smem_layout(ring, A.slot_bytes, A.scratch_bytes, A.acc_floats);
+    const uint32_t smem_sa = smem_u32(smem);
+    uint8_t* scratch = smem + SL.scratch;
+    const uint32_t xq_sa = smem_sa + SL.scratch;
+    float* acc = reinterpret_cast<float*>(smem + SL.acc);
+    uint8_t* desc = smem + SL.desc;  // [2] phase descriptors: phase k in buffer k & 1
+    float* rpre = reinterpret_cast<float*>(smem + SL.rpre);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SL.bars);
+    uint64_t* empty = full + ring;
+    float* misc = reinterpret_cast<float*>(smem + SL.misc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
+    float* warp_best_v = misc + 40;
+    int* warp_best_i = reinterpret_cast<int*>(misc + 72);
+
+    if (tid == 0) {
+        for (int s = 0; s < ring; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], SK_NW);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const unsigned long long per_step = (unsigned long long)(NPH + 1) * (unsigned long long)G;
+    const unsigned long long base = (sk_ld_acquire(A.bar) / per_step) * per_step;
+
+    if (is_producer) {
+        // ================= producer (lane 0): stream every GEMV phase's rows of this CTA
+        if (lane == 0) {
+            uint32_t use = 0;
+            for (int k = 0; k < NPH && !*abort_flag; ++k) {
+                const SPhase& ph = A.ph[k];
+                if (ph.kind != SP_GEMV) continue;
+                const RGemvArgs& g = ph.g;
+                const SKRows rr = sk_rows(g, c, G);
+                const int I = g.I, R = g.R;
+                const int qb = rg_qbytes(g.wt), sbr = rg_sbytes_row(g.wt, I), dbr = rg_dbytes_row(g.wt, I);
+                const RSlot SS = rg_slot(g.wt, I, R);
+                const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
+                unsigned long long pwait = 0;
+                bool stop = false;
+                for (int s = 0; s < nstages; ++s, ++use) {
+                    const int slot = use % ring;
+                    if (use >= (uint32_t)ring) {
+                        const long long w0 = A.trace ? clock64() : 0;
+                        bool ok = false;
+                        for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                            if (mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1)) { ok = true; break; }
+                        if (A.trace) pwait += (unsigned long long)(clock64() - w0);
+                        if (!ok) {
+                            if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                            *abort_flag = 1;
+                            stop = true;
+                            break;
+                        }
+                    }
+                    const long long row0 = rr.r_begin + (long long)s * R;
+                    const uint32_t nrows = (uint32_t)min((long long)R, rr.r_end - row0);
+                    uint8_t* dst = smem + (size_t)slot * A.slot_bytes;
+                    const uint32_t qbytes = nrows * (uint32_t)I * qb;
+                    const uint32_t sbytes = nrows * (uint32_t)sbr;
+                    const uint64_t d0 = (uint64_t)row0 * dbr;
+                    const uint64_t d0a = d0 & ~uint64_t(15);
+                    const uint32_t dbytes = ((uint32_t)(d0 - d0a) + nrows * (uint32_t)dbr + 15u) & ~15u;
+                    mbar_arrive_expect_tx(&full[slot], qbytes + sbytes + dbytes);
+                    bulk_g2s(dst, g.w.q + (uint64_t)row0 * I * qb, qbytes, &full[slot]);
+                    if (sbytes) bulk_g2s(dst + SS.s_off, g.w.s + (uint64_t)row0 * sbr, sbytes, &full[slot]);
+                    bulk_g2s(dst + SS.d_off, g.w.d + d0a, dbytes, &full[slot]);
+                }
+                if (A.trace) A.trace[((size_t)c * NPH + k) * SK_TRACE + 5] = pwait;
+                if (stop) break;
+            }
+            // leave no bulk copy in flight (immediately true on the normal path, where the
+            // consumers waited for every stage); bounded
+            const uint32_t first = use > (uint32_t)ring ? use - ring : 0u;
+            for (uint32_t u = first; u < use; ++u)
+                for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS; ++it)
+                    if (mbar_try_wait(&full[u % ring], (u / ring) & 1)) break;
+        }
+        return;
+    }
+
+    // ================= consumers
+    uint32_t use = 0;
+    float best_v = 0.f;
+    int best_i = -1;
+    const int pos = A.state->pos;  // fixed for the whole step (advanced only at its very end)
+    if (warp == 0) sk_fetch_desc(&A.ph[0], desc, lane);
+    named_bar_sync(1, NT);
+    for (int k = 0; k < NPH; ++k) {
+        const SPhase& ph = *reinterpret_cast<const SPhase*>(desc + (k & 1) * SK_DESC);
+        // the next phase's descriptor, read while this phase runs (ordered by the phase-end barrier)
+        if (warp == SK_NW - 1 && k + 1 < NPH) sk_fetch_desc(&A.ph[k + 1], desc + ((k + 1) & 1) * SK_DESC, lane);
+        if (k > 0) {  // wait until every CTA has finished phase k-1
+            if (tid == 0) {
+                // acquire: the other CTAs' phase k-1 writes (released by their counts) become
+                // visible to this thread and, through the CTA barrier below, to the whole CTA
+                const unsigned long long target = base + (unsigned long long)k * G;
+                bool ok = false;
+                for (uint32_t it = 0; it < SK_BAR_SPINS && !*abort_flag; ++it)
+                    if (sk_ld_acquire(A.bar) >= target) { ok = true; break; }
+                if (!ok) {
+                    if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                    *abort_flag = 1;
+                }
+            }
+            named_bar_sync(1, NT);
+        }
+        if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE] = sk_ns();
+        unsigned long long wcyc = 0;
+        if (ph.kind == SP_GEMV) {
+            const RGemvArgs& g = ph.g;
+            const SKRows rr = sk_rows(g, c, G);
+            const void* xsrc = g.x;
+            if (ph.epi == EPI_RESID) {  // residual rows, needed only by the epilogue: fetch them now
+                const int nvr = rr.v_end - rr.v_begin;
+                if (tid < nvr && tid < SK_RPRE) cp_async4(rpre + tid, g.resid + rr.v_begin + tid);
+                cp_async_commit();
+            }
+            if (ph.embed) {
+                // hidden = dequant(token_embd[token]) (gemv_q8_0.cuh:24-36) into shared memory after
+                // the x records; CTA 0 also stores it as the residual stream
+                const int K = g.I * 64;
+                float* ebuf = reinterpret_cast<float*>(scratch + A.scratch_bytes) - K;
+                const uint8_t* row = ph.embd + (size_t)A.state->token * (K / 32) * 34;
+                for (int i = tid; i < K; i += NT) {
+                    const uint8_t* blk = row + (i / 32) * 34;
+                    const float v = half_bits_to_float(blk[0] | (blk[1] << 8)) * (float)(int8_t)blk[2 + (i & 31)];
+                    ebuf[i] = v;
+                    if (c == 0) ph.hidden_out[i] = v;
+                }
+                named_bar_sync(1, NT);
+                xsrc = ebuf;
+            }
+            if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
+            else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
+            if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
+            use = sk_stages(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag, wcyc,
+                            A.trace != nullptr);
+            named_bar_sync(1, NT);  // every piece of every row is in shared memory
+            if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 2] = sk_ns();
+            if (ph.epi == EPI_RESID) {
+                cp_async_wait_all();
+                named_bar_sync(1, NT);
+            }
+            if (!*abort_flag) sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i);
+        } else if (!*abort_flag) {
+            const AttnArgs& at = ph.at;
+            const int seq = pos + 1;
+            const int clen = attn_chunk_len(seq, at.nchunk);
+            const int nch = (seq + clen - 1) / clen;
+            const int units = at.n_kv_heads * nch;
+            for (int u = c; u < units; u += G) {
+                if (tid < ATTN_THREADS)
+                    sk_attn_unit<KVT>(at, u / nch, u % nch, scratch, pos);
+                named_bar_sync(1, NT);  // the next unit reuses the scratch
+                if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
+            }
+        }
+        // ---- this CTA is done with phase k
+        named_bar_sync(1, NT);
+        if (tid == 0) {
+            if (A.trace) {
+                A.trace[((size_t)c * NPH + k) * SK_TRACE + 3] = sk_ns();
+                A.trace[((size_t)c * NPH + k) * SK_TRACE + 4] = wcyc;
+            }
+            // release (cumulative): every consumer write of this CTA, ordered before by the CTA
+            // barrier, is visible before the count
+            asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(A.bar), "l"(1ull) : "memory");
+        }
+    }
+
+    // ---- argmax of the LM head: thread -> warp -> CTA -> (last CTA of the step) global
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (oi >= 0 && argmax_better(ov, oi, best_v, best_i)) {
+            best_v = ov;
+            best_i = oi;
+        }
+    }
+    if (lane == 0) {
+        warp_best_v[warp] = best_v;
+        warp_best_i[warp] = best_i;
+    }
+    named_bar_sync(1, NT);
+    if (tid == 0) {
+        float bv = 0.f;
+        int bi = -1;
+        for (int w = 0; w < SK_NW; ++w)
+            if (warp_best_i[w] >= 0 && argmax_better(warp_best_v[w], warp_best_i[w], bv, bi)) {
+                bv = warp_best_v[w];
+                bi = warp_best_i[w];
+            }
+        A.cta_val[c] = bv;
+        A.cta_idx[c] = bi;
+        __threadfence();
+        const unsigned long long prev = atomicAdd(A.bar, 1ull);
+        if (prev == base + per_step - 1ull) {  // the last CTA: every CTA's best is visible
+            __threadfence();
+            float gv = 0.f;
+            int gi = -1;
+            for (int kk = 0; kk < G; ++kk) {
+                const int ik = ((volatile int*)A.cta_idx)[kk];
+                const float vk = ((volatile float*)A.cta_val)[kk];
+                if (ik >= 0 && argmax_better(vk, ik, gv, gi)) {
+                    gv = vk;
+                    gi = ik;
+                }
+            }
+            if (gi < 0) gi = 0;
+            DecodeState* st = A.state;
+            st->token = gi;
+            st->pos = st->pos + 1;
+            if (A.token_log && st->step < A.token_log_cap) A.token_log[st->step] = gi;
+            st->step = st->step + 1;
+        }
+    }
+}
+
+}  // namespace fence

@@ -201,6 +201,9 @@ typedef struct fence_load_opts {
     /* tensor parallel: rank `tp_rank` of `tp_size`; nccl_comm is an ncclComm_t or NULL */
     int tp_rank, tp_size;
     void* nccl_comm;
+    /* 1 (default): the whole token step is one persistent kernel (weights of all phases stream
+     * continuously, phases separated by a grid-wide counter); 0: one kernel per phase            */
+    int step_kernel;
 } fence_load_opts;
 
 /* Fills *opts with defaults (max_ctx 4096, bf16 KV, device 0, graphs on, single rank). */
@@ -245,6 +248,16 @@ int fence_copy_logits(fence_model* m, float* host_out);
 
 /* Times n_steps device-resident decode steps with CUDA events on the engine's stream; *ms = total. */
 int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms);
+/* No counterpart in the reference (diagnostic). Runs one token step (token at pos) of a model
+ * loaded with the persistent step kernel, eagerly, with phase tracing on, and copies the trace to
+ * host_out: [n_ctas][n_phases][8] per CTA: globaltimer nanoseconds at the phase start (after the
+ * grid-counter wait), when x is quantised (attention: when the CTA's first unit is done), when the
+ * last weight stage is consumed, and at the end (before the CTA counts itself done); SM clock
+ * cycles the consumers waited for filled ring slots, cycles the producer waited for free slots;
+ * two reserved words. cap = capacity of host_out in entries (>= n_ctas * n_phases * 8).
+ * Allocates a device buffer for the trace. */
+int fence_step_trace(fence_model* m, int token, int pos, unsigned long long* host_out, int cap,
+                     int* n_phases, int* n_ctas);
 
 /* =====================================================================================
  * 3. Synthetic GGUF writer (seeded, counter-based, byte-reproducible).

@@ -1,5 +1,6 @@
 """The decode engine (fused kernels, CUDA graph) against the CPU oracle's restatement of the
-reference forward (src/model/qwen3.cu:241-341) on seeded synthetic GGUF models."""
+reference forward (src/model/qwen3.cu:241-341) on seeded synthetic GGUF models. Both token-step
+implementations are covered: the persistent step kernel (default) and one kernel per phase."""
 import numpy as np
 import pytest
 
@@ -12,15 +13,15 @@ LOGIT_ATOL = 2e-3  # engine vs fp64 oracle on the tiny models (north-star bound 
 def models(fb, tmp_path_factory):
     d = tmp_path_factory.mktemp("models")
     out = {}
-    for cfg in ["tiny-q6k", "tiny-q8"]:
+    for cfg in ["tiny-q6k", "tiny-q8", "wide-q6k", "wide-q8"]:
         p = str(d / f"{cfg}.gguf")
         fb.synth_write(p, cfg, seed=21)
         out[cfg] = p
     return out
 
 
-def run_teacher(fb, orc, path, kv, tokens, max_ctx=256, graph=True):
-    eng = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, use_graph=graph)
+def run_teacher(fb, orc, path, kv, tokens, max_ctx=256, graph=True, step=True):
+    eng = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, use_graph=graph, step_kernel=step)
     ora = orc.OracleModel(path, max_ctx=max_ctx, kv_bf16=(kv == fb.FENCE_KV_BF16), threads=8)
     diffs, ids_e, ids_o, margins = [], [], [], []
     for pos, tok in enumerate(tokens):
@@ -37,23 +38,25 @@ def run_teacher(fb, orc, path, kv, tokens, max_ctx=256, graph=True):
     return np.array(diffs), ids_e, ids_o, margins
 
 
+@pytest.mark.parametrize("step", [True, False])
 @pytest.mark.parametrize("cfg", ["tiny-q6k", "tiny-q8"])
 @pytest.mark.parametrize("kv", [0, 1])
-def test_engine_matches_oracle_teacher_forced(fb, orc, models, cfg, kv):
+def test_engine_matches_oracle_teacher_forced(fb, orc, models, cfg, kv, step):
     tokens = list(np.random.default_rng(1).integers(0, 2048, 40))
-    diffs, ids_e, ids_o, margins = run_teacher(fb, orc, models[cfg], kv, tokens)
+    diffs, ids_e, ids_o, margins = run_teacher(fb, orc, models[cfg], kv, tokens, step=step)
     assert diffs.max() < LOGIT_ATOL, diffs
     for e, o, m in zip(ids_e, ids_o, margins):
         if m > 2 * LOGIT_ATOL:
             assert e == o
 
 
-def test_graph_and_eager_are_identical(fb, models):
+@pytest.mark.parametrize("step", [True, False])
+def test_graph_and_eager_are_identical(fb, models, step):
     p = models["tiny-q6k"]
     toks = [5, 9, 1000, 3, 77, 2047, 0]
     outs = []
     for graph in (True, False):
-        m = fb.Model(p, max_ctx=64, use_graph=graph)
+        m = fb.Model(p, max_ctx=64, use_graph=graph, step_kernel=step)
         for pos, t in enumerate(toks):
             m.forward(t, pos)
         outs.append(m.logits())
@@ -99,10 +102,11 @@ def test_nucleus_sampling_seeded(fb, models):
     m.close()
 
 
-def test_long_context_positions(fb, orc, models):
-    """Positions beyond one attention tile and chunk (adaptive chunk length) stay exact-range."""
+@pytest.mark.parametrize("step", [True, False])
+def test_long_context_positions(fb, orc, models, step):
+    """Positions over many attention chunks (multi-chunk merge) stay within the bound."""
     p = models["tiny-q6k"]
-    eng = fb.Model(p, max_ctx=1024, kv_dtype=fb.FENCE_KV_F16)
+    eng = fb.Model(p, max_ctx=1024, kv_dtype=fb.FENCE_KV_F16, step_kernel=step)
     ora = orc.OracleModel(p, max_ctx=1024, kv_bf16=False, threads=8)
     rng = np.random.default_rng(3)
     worst = 0.0
@@ -115,3 +119,33 @@ def test_long_context_positions(fb, orc, models):
     eng.close()
     ora.close()
     assert worst < LOGIT_ATOL
+
+
+@pytest.mark.parametrize("step", [True, False])
+@pytest.mark.parametrize("cfg", ["wide-q6k", "wide-q8"])
+def test_wide_rows_match_oracle(fb, orc, models, cfg, step):
+    """K = 4096 phases (64 items per row: rows spanning several warps of the reduction)."""
+    tokens = list(np.random.default_rng(2).integers(0, 2048, 12))
+    diffs, ids_e, ids_o, margins = run_teacher(fb, orc, models[cfg], fb.FENCE_KV_F16, tokens, step=step)
+    assert diffs.max() < LOGIT_ATOL, diffs
+    for e, o, m in zip(ids_e, ids_o, margins):
+        if m > 2 * LOGIT_ATOL:
+            assert e == o
+
+
+@pytest.mark.parametrize("cfg", ["tiny-q6k", "tiny-q8", "wide-q6k"])
+def test_step_kernel_matches_phase_kernels(fb, models, cfg):
+    """The two step implementations quantise the same activations and compute the same integer dots;
+    they differ only in how the per-warp partial sums are grouped, and through the fp16 KV cache an
+    occasional one-ulp rounding difference carries into later tokens."""
+    toks = list(np.random.default_rng(5).integers(0, 2048, 24))
+    outs = []
+    for step in (True, False):
+        m = fb.Model(models[cfg], max_ctx=128, step_kernel=step)
+        logs = []
+        for pos, t in enumerate(toks):
+            m.forward(int(t), pos)
+            logs.append(m.logits())
+        outs.append(np.stack(logs))
+        m.close()
+    np.testing.assert_allclose(outs[0], outs[1], rtol=0, atol=1e-3)
