@@ -281,11 +281,290 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
     return use;
 }
 
-// One attention unit by threads 0..ATTN_THREADS-1, out of line (its registers stay out of the GEMV
-// loops' allocation).
+// One attention unit of the step kernel (KV head h, context chunk c of clen positions), run by
+// threads 0..ATTN_THREADS-1 (named barrier 2). The semantics are attention.cuh's fused chunk
+// (q/k RMSNorm, NeoX RoPE, KV store of the new row, softmax(q.K^T / sqrt(hd)) V in fp32, reference
+// src/kernels/ops.cuh:66-177,320-443); the schedule is cut for latency:
+//  * every load (K/V rows, q, new k/v, norm weights, RoPE row) goes out as one batch of 16-byte
+//    async copies (the producer warp already pulled this CTA's K/V rows into L2);
+//  * scores: 8 threads per position, each holding 16 dims of one head's q in registers;
+//  * P.V: 4 independent accumulator chains per output pair;
+//  * the unit writes its chunk's unnormalised output, max and exp-sum to the partials; the last
+//    unit of the KV head to arrive (arrival counter) merges the head's chunks, so attention is a
+//    single phase; for a single chunk the unit writes the normalised output itself.
 template <typename KVT>
-__device__ __noinline__ void sk_attn_unit(const AttnArgs& at, int h, int c, uint8_t* scratch, int pos) {
-    attn_chunk<KVT, 128, true, false>(at, h, c, scratch, 2, pos);
+__device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
+                                          uint8_t* sm) {
+    using C = KVConv<KVT>;
+    constexpr int HD = 128, CH = HD * (int)sizeof(KVT) / 16, EPC = 16 / (int)sizeof(KVT);
+    constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX, TPP = 8;
+    static_assert(CH == 16 && TILE == 64 && NT == 256, "unit geometry");
+    KVT* sk = reinterpret_cast<KVT*>(sm);
+    KVT* sv = sk + TILE * HD;
+    float* sq = reinterpret_cast<float*>(sv + TILE * HD);  // [G][HD]
+    float* ss = sq + ATTN_MAX_G * HD;                       // [G][TILE]
+    float* skn = ss + ATTN_MAX_G * TILE;                    // [HD] new k
+    float* svn = skn + HD;                                  // [HD] new v
+    float* sqw = svn + HD;
+    float* skw = sqw + HD;
+    float2* srope = reinterpret_cast<float2*>(skw + HD);    // [HD/2]
+    float* smax = reinterpret_cast<float*>(srope + HD / 2);
+    float* ssum = smax + ATTN_MAX_G;
+    float* sresc = ssum + ATTN_MAX_G;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.n_q_heads / a.n_kv_heads;
+    const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
+    const bool owns_new = pos >= t0 && pos < t1;
+    const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
+    const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
+    auto stage_tile = [&](int ts, int te) {  // rows [ts, te) except pos -> smem rows, chunk ^ (row & 7)
+        for (int idx = tid; idx < (te - ts) * CH; idx += NT) {
+            const int r = idx >> 4, ch = idx & 15;
+            const int t = ts + r;
+            if (t == pos) continue;  // produced below
+            const int pch = ch ^ (r & 7);
+            cp_async16(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16,
+                       reinterpret_cast<const uint8_t*>(kb + (long long)t * a.stride_t) + ch * 16);
+            cp_async16(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16,
+                       reinterpret_cast<const uint8_t*>(vb + (long long)t * a.stride_t) + ch * 16);
+        }
+    };
+    // ---- one batch of loads
+    stage_tile(t0, min(t0 + TILE, t1));
+    const int qh0 = h * G;
+    for (int i = tid; i < G * (HD / 4); i += NT) cp_async16(sq + 4 * i, a.q + (long long)qh0 * HD + 4 * i);
+    if (tid < HD / 4) {
+        const int i = tid;
+        if (owns_new) {
+            cp_async16(skn + 4 * i, a.k_new + (long long)h * HD + 4 * i);
+            cp_async16(svn + 4 * i, a.v_new + (long long)h * HD + 4 * i);
+        }
+        if (a.q_norm_w) cp_async16(sqw + 4 * i, a.q_norm_w + 4 * i);
+        if (a.k_norm_w) cp_async16(skw + 4 * i, a.k_norm_w + 4 * i);
+        // RoPE row: HD/2 (cos, sin) pairs = HD/4 chunks of 16 bytes
+        cp_async16(reinterpret_cast<float*>(srope) + 4 * i, reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
+    }
+    cp_async_commit();
+    if (tid < ATTN_MAX_G) {
+        smax[tid] = -INFINITY;
+        ssum[tid] = 0.f;
+    }
+    cp_async_wait_all();
+    named_bar_sync(2, NT);
+    // ---- q/k RMSNorm (w * x * rms) and NeoX rotation, a warp per head; the new K/V row
+    for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
+        float* v = (g < G) ? sq + g * HD : skn;
+        const float* nw = (g < G) ? a.q_norm_w : a.k_norm_w;
+        const float* w = (g < G) ? sqw : skw;
+        float x4[HD / 32];
+#pragma unroll
+        for (int i = 0; i < HD / 32; ++i) x4[i] = v[lane + 32 * i];
+        if (nw) {
+            float s2 = 0.f;
+#pragma unroll
+            for (int i = 0; i < HD / 32; ++i) s2 += x4[i] * x4[i];
+            s2 = warp_sum(s2);
+            const float r = rsqrtf(s2 / (float)HD + a.eps);
+#pragma unroll
+            for (int i = 0; i < HD / 32; ++i) x4[i] = w[lane + 32 * i] * x4[i] * r;
+        }
+        // rotation pairs (j, j + 64): lane holds j = lane, lane + 32 and their partners
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const float2 t = srope[lane + 32 * i];
+            const float x0 = x4[i], x1 = x4[i + 2];
+            x4[i] = x0 * t.x - x1 * t.y;
+            x4[i + 2] = x0 * t.y + x1 * t.x;
+        }
+#pragma unroll
+        for (int i = 0; i < HD / 32; ++i) v[lane + 32 * i] = x4[i];
+        if (g == G) {  // round to the cache type, store the row (global) and into its tile slot
+            const int r = pos - t0;
+            KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+            KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
+#pragma unroll
+            for (int i = 0; i < HD / 32; ++i) {
+                const int d = lane + 32 * i;
+                const KVT kq = C::from(x4[i]);
+                const KVT vq = C::from(svn[d]);
+                kw[d] = kq;
+                vw[d] = vq;
+                if (r < TILE) {
+                    const int pch = (d / EPC) ^ (r & 7);
+                    reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16)[d % EPC] = kq;
+                    reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16)[d % EPC] = vq;
+                }
+            }
+        }
+    }
+    named_bar_sync(2, NT);
+
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int sp = tid & (TPP - 1);  // dims [8 sp, 8 sp + 8) and [64 + 8 sp, 64 + 8 sp + 8)
+    // P.V: thread <-> (head, dim pair) items tid and tid + NT; 4 independent chains each
+    constexpr int KP = (ATTN_MAX_G * HD / 2 + NT - 1) / NT;
+    float o[KP][4][2];
+#pragma unroll
+    for (int k = 0; k < KP; ++k)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[k][j][0] = o[k][j][1] = 0.f;
+    for (int ts = t0; ts < t1; ts += TILE) {
+        const int te = min(ts + TILE, t1), nt = te - ts;
+        if (ts != t0) {
+            stage_tile(ts, te);
+            cp_async_commit();
+            cp_async_wait_all();
+            named_bar_sync(2, NT);
+        }
+        // ---- scores, one head at a time with its q slice in registers (more heads per pass raise
+        //      the unit's register demand, which the call then costs the whole kernel in spills)
+        for (int g = 0; g < G; ++g) {
+            float qv[16];
+            const float* qs = sq + g * HD;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                qv[e] = qs[8 * sp + e];
+                qv[8 + e] = qs[64 + 8 * sp + e];
+            }
+#pragma unroll
+            for (int pass = 0; pass < 2; ++pass) {
+                const int r = pass * 32 + (tid >> 3);
+                float acc = 0.f;
+                if (r < nt) {
+                    const uint8_t* krow = reinterpret_cast<const uint8_t*>(sk + r * HD);
+                    const uint4 wa = *reinterpret_cast<const uint4*>(krow + ((sp ^ (r & 7)) * 16));
+                    const uint4 wb = *reinterpret_cast<const uint4*>(krow + (((sp + 8) ^ (r & 7)) * 16));
+                    const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 kf = C::pair(w[e]);
+                        acc = fmaf(qv[2 * e], kf.x, acc);
+                        acc = fmaf(qv[2 * e + 1], kf.y, acc);
+                    }
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                if (r < nt && sp == 0) ss[g * TILE + r] = acc * scale;
+            }
+        }
+        named_bar_sync(2, NT);
+        // ---- online softmax statistics, a warp per head
+        for (int g = warp; g < G; g += NW) {
+            const float s0 = lane < nt ? ss[g * TILE + lane] : -INFINITY;
+            const float s1 = lane + 32 < nt ? ss[g * TILE + lane + 32] : -INFINITY;
+            const float m = warp_max(fmaxf(s0, s1));
+            const float m_old = smax[g];
+            const float m_new = fmaxf(m_old, m);
+            const float e0 = lane < nt ? expf(s0 - m_new) : 0.f;
+            const float e1 = lane + 32 < nt ? expf(s1 - m_new) : 0.f;
+            if (lane < nt) ss[g * TILE + lane] = e0;
+            if (lane + 32 < nt) ss[g * TILE + lane + 32] = e1;
+            const float l = warp_sum(e0 + e1);
+            if (lane == 0) {
+                const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                sresc[g] = f;
+                ssum[g] = ssum[g] * f + l;
+                smax[g] = m_new;
+            }
+        }
+        named_bar_sync(2, NT);
+        // ---- P.V
+#pragma unroll
+        for (int k = 0; k < KP; ++k) {
+            const int pidx = tid + k * NT;
+            if (pidx < G * (HD / 2)) {
+                const int g = pidx / (HD / 2);
+                const int d = 2 * (pidx - g * (HD / 2));
+                const int ch = d / EPC, within = d % EPC;
+                const float f = sresc[g];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    o[k][j][0] *= f;
+                    o[k][j][1] *= f;
+                }
+                const float* pg = ss + g * TILE;
+                for (int r = 0; r < nt; r += 4) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int rr = r + j;
+                        if (rr < nt) {
+                            const uint32_t w = *reinterpret_cast<const uint32_t*>(
+                                reinterpret_cast<const uint8_t*>(sv + rr * HD) + ((ch ^ (rr & 7)) * 16) + within * sizeof(KVT));
+                            const float2 vv = C::pair(w);
+                            o[k][j][0] = fmaf(pg[rr], vv.x, o[k][j][0]);
+                            o[k][j][1] = fmaf(pg[rr], vv.y, o[k][j][1]);
+                        }
+                    }
+                }
+            }
+        }
+        named_bar_sync(2, NT);  // before the next tile (or unit) reuses the scratch
+    }
+    // ---- output (single chunk) or this chunk's partials
+    const int part_stride = HD + 2;
+    float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * part_stride;
+#pragma unroll
+    for (int k = 0; k < KP; ++k) {
+        const int pidx = tid + k * NT;
+        if (pidx < G * (HD / 2)) {
+            const int g = pidx / (HD / 2);
+            const int d = 2 * (pidx - g * (HD / 2));
+            const float s0 = (o[k][0][0] + o[k][1][0]) + (o[k][2][0] + o[k][3][0]);
+            const float s1 = (o[k][0][1] + o[k][1][1]) + (o[k][2][1] + o[k][3][1]);
+            if (n_active == 1) {
+                const float inv = 1.0f / ssum[g];
+                a.out[(long long)(qh0 + g) * HD + d] = s0 * inv;
+                a.out[(long long)(qh0 + g) * HD + d + 1] = s1 * inv;
+            } else {
+                pbase[g * part_stride + d] = s0;
+                pbase[g * part_stride + d + 1] = s1;
+            }
+        }
+    }
+    if (n_active == 1) return;
+    if (tid < G) {
+        pbase[tid * part_stride + HD] = smax[tid];
+        pbase[tid * part_stride + HD + 1] = ssum[tid];
+    }
+    // ---- the last unit of KV head h to finish merges its chunks: output (query head qh0 + g, dim
+    //      d) = sum_c o_c w_c with w_c = e^(m_c - M) / sum_c' l_c' e^(m_c' - M), M = max_c m_c; the
+    //      weights first (a warp per head), then every output's sum over the chunks in chunk order
+    //      with independent loads (deterministic whichever unit merges)
+    int* last = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
+    __threadfence();  // this thread's partials are visible before the unit's arrival
+    named_bar_sync(2, NT);
+    if (tid == 0) *last = atomicAdd(&a.counter[h], 1u) == (unsigned)(n_active - 1);
+    named_bar_sync(2, NT);
+    if (!*last) return;
+    __threadfence();
+    const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
+    float* wc = sq;  // [n_active][G] chunk weights (q is no longer needed)
+    for (int g = warp; g < G; g += NW) {
+        float m = -INFINITY;
+        for (int cc = lane; cc < n_active; cc += 32) m = fmaxf(m, __ldcg(hb + ((long long)cc * G + g) * part_stride + HD));
+        m = warp_max(m);
+        float l = 0.f;
+        for (int cc = lane; cc < n_active; cc += 32) {
+            const float* pr = hb + ((long long)cc * G + g) * part_stride;
+            const float e = expf(__ldcg(pr + HD) - m);
+            wc[cc * G + g] = e;
+            l += __ldcg(pr + HD + 1) * e;
+        }
+        l = warp_sum(l);
+        const float inv = 1.0f / l;
+        for (int cc = lane; cc < n_active; cc += 32) wc[cc * G + g] *= inv;
+    }
+    named_bar_sync(2, NT);
+    for (int i = tid; i < G * HD; i += NT) {
+        const int g = i / HD, d = i - g * HD;
+        const float* po = hb + (long long)g * part_stride + d;
+        float O = 0.f;
+#pragma unroll 8
+        for (int cc = 0; cc < n_active; ++cc) O = fmaf(__ldcg(po + (long long)cc * G * part_stride), wc[cc * G + g], O);
+        a.out[(long long)(qh0 + g) * HD + d] = O;
+    }
+    if (tid == 0) a.counter[h] = 0u;  // every unit of head h has arrived: reset for the next layer
 }
 
 // Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
@@ -361,8 +640,23 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         // ================= producer (lane 0): stream every GEMV phase's rows of this CTA
         if (lane == 0) {
             uint32_t use = 0;
+            const int ppos = A.state->pos;
             for (int k = 0; k < NPH && !*abort_flag; ++k) {
                 const SPhase& ph = A.ph[k];
+                if (ph.kind == SP_ATTN) {
+                    // pull this CTA's K/V rows of the coming attention phase into L2
+                    const AttnArgs& at = ph.at;
+                    const int seq = ppos + 1;
+                    const int clen = attn_chunk_len(seq, at.nchunk);
+                    const int nch = (seq + clen - 1) / clen;
+                    for (int u = c; u < at.n_kv_heads * nch; u += G) {
+                        const int h = u / nch, t0 = (u % nch) * clen, t1 = min(t0 + clen, seq);
+                        const size_t off = ((size_t)h * at.stride_h + (size_t)t0 * at.stride_t) * sizeof(KVT);
+                        const uint32_t bytes = (uint32_t)((t1 - t0) * at.stride_t * sizeof(KVT));
+                        bulk_prefetch_l2(static_cast<const uint8_t*>(at.kc) + off, bytes);
+                        bulk_prefetch_l2(static_cast<const uint8_t*>(at.vc) + off, bytes);
+                    }
+                }
                 if (ph.kind != SP_GEMV) continue;
                 const RGemvArgs& g = ph.g;
                 const SKRows rr = sk_rows(g, c, G);
@@ -484,8 +778,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             const int nch = (seq + clen - 1) / clen;
             const int units = at.n_kv_heads * nch;
             for (int u = c; u < units; u += G) {
-                if (tid < ATTN_THREADS)
-                    sk_attn_unit<KVT>(at, u / nch, u % nch, scratch, pos);
+                if (tid < ATTN_THREADS) sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch);
                 named_bar_sync(1, NT);  // the next unit reuses the scratch
                 if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
             }

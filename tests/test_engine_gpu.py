@@ -136,8 +136,9 @@ def test_wide_rows_match_oracle(fb, orc, models, cfg, step):
 @pytest.mark.parametrize("cfg", ["tiny-q6k", "tiny-q8", "wide-q6k"])
 def test_step_kernel_matches_phase_kernels(fb, models, cfg):
     """The two step implementations quantise the same activations and compute the same integer dots;
-    they differ only in how the per-warp partial sums are grouped, and through the fp16 KV cache an
-    occasional one-ulp rounding difference carries into later tokens."""
+    they group the GEMV partial sums and the attention score / P.V sums differently, and through the
+    fp16 KV cache an occasional one-ulp rounding difference carries into later tokens. Each is held
+    to LOGIT_ATOL against the oracle above; here they are held to the same bound against each other."""
     toks = list(np.random.default_rng(5).integers(0, 2048, 24))
     outs = []
     for step in (True, False):
@@ -148,4 +149,4 @@ def test_step_kernel_matches_phase_kernels(fb, models, cfg):
             logs.append(m.logits())
         outs.append(np.stack(logs))
         m.close()
-    np.testing.assert_allclose(outs[0], outs[1], rtol=0, atol=1e-3)
+    np.testing.assert_allclose(outs[0], outs[1], rtol=0, atol=LOGIT_ATOL)
