@@ -45,9 +45,7 @@ static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     const int grid = sms;
-    // attention unit: K and V tiles, q, scores, new k / v, norm weights, RoPE row, softmax state
-    int scratch = 2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 + 4 * 128 * 4 +
-                  64 * 8 + 3 * ATTN_MAX_G * 4 + 64;
+    int scratch = sk_attn_scratch_bytes();
     int slot = 0, accf = 0;
     for (SPhase& ph : phases) {
         if (ph.kind != SP_GEMV) continue;

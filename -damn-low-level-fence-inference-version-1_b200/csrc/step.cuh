@@ -281,14 +281,69 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
     return use;
 }
 
+// mma.sync m16n8k16 on KVT operands (f16 or bf16) with fp32 accumulators. Only rows 0..7 of A are
+// used (at most ATTN_MAX_G = 8 query heads per KV head), so A's rows 8..15 registers are zero.
+template <typename KVT>
+struct SKMma;
+template <>
+struct SKMma<__half> {
+    static __device__ __forceinline__ uint32_t pack(float x, float y) {
+        const __half2 h = __floats2half2_rn(x, y);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+    static __device__ __forceinline__ void mma(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+    }
+};
+template <>
+struct SKMma<__nv_bfloat16> {
+    static __device__ __forceinline__ uint32_t pack(float x, float y) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+    static __device__ __forceinline__ void mma(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+    }
+};
+
+// Positions per attention unit of the step kernel: spread the context of each KV head over the
+// CTAs available to it (ctas / n_kv_heads), in whole 64-position tiles, and never more chunks
+// than the partials hold (nchunk).
+__host__ __device__ __forceinline__ int sk_attn_clen(int seq, int nchunk, int ctas, int n_kv_heads) {
+    const int per_head = ctas / n_kv_heads > 1 ? ctas / n_kv_heads : 1;
+    int clen = (seq + per_head - 1) / per_head;
+    const int cmin = (seq + nchunk - 1) / nchunk;
+    if (clen < cmin) clen = cmin;
+    return (clen + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
+}
+
+// Shared memory of one attention unit (sk_attn_unit's carve-up): K and V tiles, fp32 q, scores,
+// new k / v, norm weights, RoPE row, softmax state, merge flag, q as (high, remainder) pairs.
+constexpr int sk_attn_scratch_bytes() {
+    return 2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 + 4 * 128 * 4 + 64 * 8 +
+           3 * ATTN_MAX_G * 4 + 16 + 2 * ATTN_MAX_G * 64 * 4;
+}
+
 // One attention unit of the step kernel (KV head h, context chunk c of clen positions), run by
 // threads 0..ATTN_THREADS-1 (named barrier 2). The semantics are attention.cuh's fused chunk
 // (q/k RMSNorm, NeoX RoPE, KV store of the new row, softmax(q.K^T / sqrt(hd)) V in fp32, reference
 // src/kernels/ops.cuh:66-177,320-443); the schedule is cut for latency:
-//  * every load (K/V rows, q, new k/v, norm weights, RoPE row) goes out as one batch of 16-byte
-//    async copies (the producer warp already pulled this CTA's K/V rows into L2);
-//  * scores: 8 threads per position, each holding 16 dims of one head's q in registers;
-//  * P.V: 4 independent accumulator chains per output pair;
+//  * the context is walked in 64-position tiles; the first tile's K/V rows and every small input
+//    (q, new k/v, norm weights, RoPE row) go out as one batch of 16-byte async copies, and the
+//    next tile's K rows load while this tile's softmax and P.V run, its V rows while the next
+//    scores run (the producer warp already pulled the unit's K/V rows into L2);
+//  * q.K^T and P.V run on the tensor cores (mma.sync m16n8k16, fp32 accumulators): the query
+//    heads are the rows of A, and the fp32 operand (q, or the softmax weights P) is split into
+//    a KVT high part and a KVT remainder, two products summed, so it keeps ~22 (f16) or ~16
+//    (bf16) bits while K and V enter exactly as cached;
 //  * the unit writes its chunk's unnormalised output, max and exp-sum to the partials; the last
 //    unit of the KV head to arrive (arrival counter) merges the head's chunks, so attention is a
 //    single phase; for a single chunk the unit writes the normalised output itself.
@@ -296,14 +351,15 @@ template <typename KVT>
 __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
                                           uint8_t* sm) {
     using C = KVConv<KVT>;
+    using M = SKMma<KVT>;
     constexpr int HD = 128, CH = HD * (int)sizeof(KVT) / 16, EPC = 16 / (int)sizeof(KVT);
-    constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX, TPP = 8;
-    static_assert(CH == 16 && TILE == 64 && NT == 256, "unit geometry");
+    constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX;
+    static_assert(CH == 16 && TILE == 64 && NT == 256 && NW == 8 && ATTN_MAX_G <= 8, "unit geometry");
     KVT* sk = reinterpret_cast<KVT*>(sm);
     KVT* sv = sk + TILE * HD;
-    float* sq = reinterpret_cast<float*>(sv + TILE * HD);  // [G][HD]
-    float* ss = sq + ATTN_MAX_G * HD;                       // [G][TILE]
-    float* skn = ss + ATTN_MAX_G * TILE;                    // [HD] new k
+    float* sq = reinterpret_cast<float*>(sv + TILE * HD);  // [G][HD] fp32 q, later the merge weights
+    float* ss = sq + ATTN_MAX_G * HD;                       // [G][TILE] scores, then P
+    float* skn = ss + ATTN_MAX_G * TILE;                    // [HD] new k (rotated, cache-rounded)
     float* svn = skn + HD;                                  // [HD] new v
     float* sqw = svn + HD;
     float* skw = sqw + HD;
@@ -311,26 +367,43 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     float* smax = reinterpret_cast<float*>(srope + HD / 2);
     float* ssum = smax + ATTN_MAX_G;
     float* sresc = ssum + ATTN_MAX_G;
+    int* last = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
+    uint32_t* sqa = reinterpret_cast<uint32_t*>(last + 4);  // [2][G][HD/2] q high / remainder pairs
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.n_q_heads / a.n_kv_heads;
     const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
     const bool owns_new = pos >= t0 && pos < t1;
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
     const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
-    auto stage_tile = [&](int ts, int te) {  // rows [ts, te) except pos -> smem rows, chunk ^ (row & 7)
+    // rows [ts, te) except pos -> tile rows, 16-byte chunk ch of row r at chunk ch ^ (r & 7)
+    auto stage = [&](KVT* dst, const KVT* src, int ts, int te) {
         for (int idx = tid; idx < (te - ts) * CH; idx += NT) {
             const int r = idx >> 4, ch = idx & 15;
             const int t = ts + r;
-            if (t == pos) continue;  // produced below
-            const int pch = ch ^ (r & 7);
-            cp_async16(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16,
-                       reinterpret_cast<const uint8_t*>(kb + (long long)t * a.stride_t) + ch * 16);
-            cp_async16(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16,
-                       reinterpret_cast<const uint8_t*>(vb + (long long)t * a.stride_t) + ch * 16);
+            if (t == pos) continue;  // produced by this unit
+            cp_async16(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16),
+                       reinterpret_cast<const uint8_t*>(src + (long long)t * a.stride_t) + ch * 16);
         }
     };
-    // ---- one batch of loads
-    stage_tile(t0, min(t0 + TILE, t1));
+    // the new row (cache-rounded floats) into its tile slot, when pos lies in [ts, ts + TILE)
+    auto put_new = [&](KVT* dst, const float* row, int ts) {
+        const int r = pos - ts;
+        if (r < 0 || r >= TILE || tid >= HD) return;
+        const int d = tid;
+        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(dst + r * HD) + (((d / EPC) ^ (r & 7)) * 16))[d % EPC] =
+            C::from(row[d]);
+    };
+    // rows [n, round16(n)) of a partial tile: zero, so that P.V's last k-step reads finite values
+    auto zero_tail = [&](KVT* dst, int n) {
+        const int n16 = (n + 15) & ~15;
+        for (int idx = tid; idx < (n16 - n) * CH; idx += NT) {
+            const int r = n + (idx >> 4), ch = idx & 15;
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16)) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+    };
+
+    // ---- first batch: small inputs + K rows of tile 0 (group 1), V rows of tile 0 (group 2)
     const int qh0 = h * G;
     for (int i = tid; i < G * (HD / 4); i += NT) cp_async16(sq + 4 * i, a.q + (long long)qh0 * HD + 4 * i);
     if (tid < HD / 4) {
@@ -342,18 +415,22 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         if (a.q_norm_w) cp_async16(sqw + 4 * i, a.q_norm_w + 4 * i);
         if (a.k_norm_w) cp_async16(skw + 4 * i, a.k_norm_w + 4 * i);
         // RoPE row: HD/2 (cos, sin) pairs = HD/4 chunks of 16 bytes
-        cp_async16(reinterpret_cast<float*>(srope) + 4 * i, reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
+        cp_async16(reinterpret_cast<float*>(srope) + 4 * i,
+                   reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
     }
+    stage(sk, kb, t0, min(t0 + TILE, t1));
+    cp_async_commit();
+    stage(sv, vb, t0, min(t0 + TILE, t1));
     cp_async_commit();
     if (tid < ATTN_MAX_G) {
         smax[tid] = -INFINITY;
         ssum[tid] = 0.f;
     }
-    cp_async_wait_all();
+    cp_async_wait_group<1>();
     named_bar_sync(2, NT);
     // ---- q/k RMSNorm (w * x * rms) and NeoX rotation, a warp per head; the new K/V row
     for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
-        float* v = (g < G) ? sq + g * HD : skn;
+        const float* v = (g < G) ? sq + g * HD : skn;
         const float* nw = (g < G) ? a.q_norm_w : a.k_norm_w;
         const float* w = (g < G) ? sqw : skw;
         float x4[HD / 32];
@@ -376,80 +453,76 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             x4[i] = x0 * t.x - x1 * t.y;
             x4[i + 2] = x0 * t.y + x1 * t.x;
         }
+        __syncwarp();
+        if (g < G) {  // q as (high, remainder) pairs: element pair (2j, 2j + 1) in word j
 #pragma unroll
-        for (int i = 0; i < HD / 32; ++i) v[lane + 32 * i] = x4[i];
-        if (g == G) {  // round to the cache type, store the row (global) and into its tile slot
-            const int r = pos - t0;
+            for (int i = 0; i < HD / 32; ++i) {
+                const float hi = M::round(x4[i]);
+                const float lo = x4[i] - hi;
+                const float hi_n = __shfl_down_sync(0xffffffffu, hi, 1);
+                const float lo_n = __shfl_down_sync(0xffffffffu, lo, 1);
+                if ((lane & 1) == 0) {
+                    const int j = (lane + 32 * i) >> 1;
+                    sqa[g * (HD / 2) + j] = M::pack(hi, hi_n);
+                    sqa[(ATTN_MAX_G + g) * (HD / 2) + j] = M::pack(lo, lo_n);
+                }
+            }
+        } else {  // round to the cache type and store the row (the tiles take it from skn / svn)
             KVT* kw = reinterpret_cast<KVT*>(a.kc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
             KVT* vw = reinterpret_cast<KVT*>(a.vc_w) + (long long)h * a.stride_h + (long long)pos * a.stride_t;
 #pragma unroll
             for (int i = 0; i < HD / 32; ++i) {
                 const int d = lane + 32 * i;
                 const KVT kq = C::from(x4[i]);
-                const KVT vq = C::from(svn[d]);
                 kw[d] = kq;
-                vw[d] = vq;
-                if (r < TILE) {
-                    const int pch = (d / EPC) ^ (r & 7);
-                    reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sk + r * HD) + pch * 16)[d % EPC] = kq;
-                    reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(sv + r * HD) + pch * 16)[d % EPC] = vq;
-                }
+                vw[d] = C::from(svn[d]);
+                skn[d] = C::to(kq);
             }
         }
     }
     named_bar_sync(2, NT);
+    put_new(sk, skn, t0);
 
     const float scale = 1.0f / sqrtf((float)HD);
-    const int sp = tid & (TPP - 1);  // dims [8 sp, 8 sp + 8) and [64 + 8 sp, 64 + 8 sp + 8)
-    // P.V: thread <-> (head, dim pair) items tid and tid + NT; 4 independent chains each
-    constexpr int KP = (ATTN_MAX_G * HD / 2 + NT - 1) / NT;
-    float o[KP][4][2];
-#pragma unroll
-    for (int k = 0; k < KP; ++k)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[k][j][0] = o[k][j][1] = 0.f;
+    const int gr = lane >> 2, q4 = lane & 3;  // fragment row (query head) and column pair
+    float oh[2][4] = {}, ol[2][4] = {};        // P.V accumulators: dims 16 warp + 8 j + 2 q4 + {0, 1}
     for (int ts = t0; ts < t1; ts += TILE) {
-        const int te = min(ts + TILE, t1), nt = te - ts;
+        const int nt = min(ts + TILE, t1) - ts;
+        const bool more = ts + TILE < t1;
         if (ts != t0) {
-            stage_tile(ts, te);
-            cp_async_commit();
-            cp_async_wait_all();
-            named_bar_sync(2, NT);
+            cp_async_wait_group<1>();  // K rows of this tile (its V rows may still be in flight)
+            put_new(sk, skn, ts);
         }
-        // ---- scores, one head at a time with its q slice in registers (more heads per pass raise
-        //      the unit's register demand, which the call then costs the whole kernel in spills)
-        for (int g = 0; g < G; ++g) {
-            float qv[16];
-            const float* qs = sq + g * HD;
+        named_bar_sync(2, NT);
+        // ---- scores: warp w -> positions 8w .. 8w + 7 of the tile, 8 k-steps of 16 dims
+        if (8 * warp < nt) {
+            float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
+            const int r = 8 * warp + gr;  // B column = tile row
+            const uint32_t* krow = reinterpret_cast<const uint32_t*>(sk + r * HD);
+            const uint32_t* qa = sqa + gr * (HD / 2);
+            const bool live = gr < G;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                qv[e] = qs[8 * sp + e];
-                qv[8 + e] = qs[64 + 8 * sp + e];
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint32_t b0 = krow[(((2 * ks) ^ (r & 7)) << 2) + q4];
+                const uint32_t b1 = krow[(((2 * ks + 1) ^ (r & 7)) << 2) + q4];
+                const uint32_t ah0 = live ? qa[8 * ks + q4] : 0u, ah2 = live ? qa[8 * ks + 4 + q4] : 0u;
+                const uint32_t al0 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + q4] : 0u;
+                const uint32_t al2 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + 4 + q4] : 0u;
+                M::mma(dh, ah0, ah2, b0, b1);
+                M::mma(dl, al0, al2, b0, b1);
             }
-#pragma unroll
-            for (int pass = 0; pass < 2; ++pass) {
-                const int r = pass * 32 + (tid >> 3);
-                float acc = 0.f;
-                if (r < nt) {
-                    const uint8_t* krow = reinterpret_cast<const uint8_t*>(sk + r * HD);
-                    const uint4 wa = *reinterpret_cast<const uint4*>(krow + ((sp ^ (r & 7)) * 16));
-                    const uint4 wb = *reinterpret_cast<const uint4*>(krow + (((sp + 8) ^ (r & 7)) * 16));
-                    const uint32_t w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 kf = C::pair(w[e]);
-                        acc = fmaf(qv[2 * e], kf.x, acc);
-                        acc = fmaf(qv[2 * e + 1], kf.y, acc);
-                    }
-                }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                if (r < nt && sp == 0) ss[g * TILE + r] = acc * scale;
+            if (live) {  // d[0], d[1]: head gr, tile rows 8 warp + 2 q4 + {0, 1}
+                const int col = 8 * warp + 2 * q4;
+                if (col < nt) ss[gr * TILE + col] = (dh[0] + dl[0]) * scale;
+                if (col + 1 < nt) ss[gr * TILE + col + 1] = (dh[1] + dl[1]) * scale;
             }
         }
         named_bar_sync(2, NT);
-        // ---- online softmax statistics, a warp per head
+        if (more) {  // the K tile is free: next tile's K rows
+            stage(sk, kb, ts + TILE, min(ts + 2 * TILE, t1));
+            cp_async_commit();
+        }
+        // ---- online softmax statistics, a warp per head; P (zero beyond nt) back into ss
         for (int g = warp; g < G; g += NW) {
             const float s0 = lane < nt ? ss[g * TILE + lane] : -INFINITY;
             const float s1 = lane + 32 < nt ? ss[g * TILE + lane + 32] : -INFINITY;
@@ -458,8 +531,8 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             const float m_new = fmaxf(m_old, m);
             const float e0 = lane < nt ? expf(s0 - m_new) : 0.f;
             const float e1 = lane + 32 < nt ? expf(s1 - m_new) : 0.f;
-            if (lane < nt) ss[g * TILE + lane] = e0;
-            if (lane + 32 < nt) ss[g * TILE + lane + 32] = e1;
+            ss[g * TILE + lane] = e0;
+            ss[g * TILE + lane + 32] = e1;
             const float l = warp_sum(e0 + e1);
             if (lane == 0) {
                 const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
@@ -468,57 +541,62 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
                 smax[g] = m_new;
             }
         }
+        if (more) cp_async_wait_group<1>();  // V rows of this tile (next K rows may be in flight)
+        else cp_async_wait_group<0>();
+        put_new(sv, svn, ts);
+        if (nt < TILE) zero_tail(sv, nt);
         named_bar_sync(2, NT);
-        // ---- P.V
+        // ---- P.V: warp w -> dims 16w .. 16w + 15 (two n-tiles), k-steps of 16 positions
+        {
+            const float f = gr < G ? sresc[gr] : 0.f;
 #pragma unroll
-        for (int k = 0; k < KP; ++k) {
-            const int pidx = tid + k * NT;
-            if (pidx < G * (HD / 2)) {
-                const int g = pidx / (HD / 2);
-                const int d = 2 * (pidx - g * (HD / 2));
-                const int ch = d / EPC, within = d % EPC;
-                const float f = sresc[g];
+            for (int j = 0; j < 2; ++j)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    o[k][j][0] *= f;
-                    o[k][j][1] *= f;
+                for (int e = 0; e < 4; ++e) {
+                    oh[j][e] *= f;
+                    ol[j][e] *= f;
                 }
-                const float* pg = ss + g * TILE;
-                for (int r = 0; r < nt; r += 4) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int rr = r + j;
-                        if (rr < nt) {
-                            const uint32_t w = *reinterpret_cast<const uint32_t*>(
-                                reinterpret_cast<const uint8_t*>(sv + rr * HD) + ((ch ^ (rr & 7)) * 16) + within * sizeof(KVT));
-                            const float2 vv = C::pair(w);
-                            o[k][j][0] = fmaf(pg[rr], vv.x, o[k][j][0]);
-                            o[k][j][1] = fmaf(pg[rr], vv.y, o[k][j][1]);
-                        }
-                    }
-                }
+            const float* prow = ss + gr * TILE;
+            const bool live = gr < G;
+            // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
+            const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lch = 2 * warp + (lane >> 4);
+            for (int ks = 0; ks < (nt + 15) / 16; ++ks) {
+                const int r = 16 * ks + lr;
+                const uint32_t addr = smem_u32(reinterpret_cast<uint8_t*>(sv + r * HD) + ((lch ^ (r & 7)) * 16));
+                uint32_t b[4];
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                             : "r"(addr));
+                const float2 p0 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 2 * q4) : make_float2(0.f, 0.f);
+                const float2 p2 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 8 + 2 * q4) : make_float2(0.f, 0.f);
+                const float h0x = M::round(p0.x), h0y = M::round(p0.y), h2x = M::round(p2.x), h2y = M::round(p2.y);
+                const uint32_t ah0 = M::pack(h0x, h0y), ah2 = M::pack(h2x, h2y);
+                const uint32_t al0 = M::pack(p0.x - h0x, p0.y - h0y), al2 = M::pack(p2.x - h2x, p2.y - h2y);
+                M::mma(oh[0], ah0, ah2, b[0], b[1]);
+                M::mma(ol[0], al0, al2, b[0], b[1]);
+                M::mma(oh[1], ah0, ah2, b[2], b[3]);
+                M::mma(ol[1], al0, al2, b[2], b[3]);
             }
         }
-        named_bar_sync(2, NT);  // before the next tile (or unit) reuses the scratch
+        named_bar_sync(2, NT);  // V tile and ss are free
+        if (more) {
+            stage(sv, vb, ts + TILE, min(ts + 2 * TILE, t1));
+            cp_async_commit();
+        }
     }
-    // ---- output (single chunk) or this chunk's partials
+    // ---- output (single chunk) or this chunk's partials: head gr, dims 16 warp + 8 j + 2 q4 + {0, 1}
     const int part_stride = HD + 2;
     float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * part_stride;
+    if (gr < G) {
+        const float inv = n_active == 1 ? 1.0f / ssum[gr] : 1.0f;
 #pragma unroll
-    for (int k = 0; k < KP; ++k) {
-        const int pidx = tid + k * NT;
-        if (pidx < G * (HD / 2)) {
-            const int g = pidx / (HD / 2);
-            const int d = 2 * (pidx - g * (HD / 2));
-            const float s0 = (o[k][0][0] + o[k][1][0]) + (o[k][2][0] + o[k][3][0]);
-            const float s1 = (o[k][0][1] + o[k][1][1]) + (o[k][2][1] + o[k][3][1]);
-            if (n_active == 1) {
-                const float inv = 1.0f / ssum[g];
-                a.out[(long long)(qh0 + g) * HD + d] = s0 * inv;
-                a.out[(long long)(qh0 + g) * HD + d + 1] = s1 * inv;
-            } else {
-                pbase[g * part_stride + d] = s0;
-                pbase[g * part_stride + d + 1] = s1;
+        for (int j = 0; j < 2; ++j) {
+            const int d = 16 * warp + 8 * j + 2 * q4;
+            const float2 o = make_float2((oh[j][0] + ol[j][0]) * inv, (oh[j][1] + ol[j][1]) * inv);
+            if (n_active == 1) *reinterpret_cast<float2*>(a.out + (long long)(qh0 + gr) * HD + d) = o;
+            else {
+                pbase[gr * part_stride + d] = o.x;
+                pbase[gr * part_stride + d + 1] = o.y;
             }
         }
     }
@@ -531,7 +609,6 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     //      d) = sum_c o_c w_c with w_c = e^(m_c - M) / sum_c' l_c' e^(m_c' - M), M = max_c m_c; the
     //      weights first (a warp per head), then every output's sum over the chunks in chunk order
     //      with independent loads (deterministic whichever unit merges)
-    int* last = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
     __threadfence();  // this thread's partials are visible before the unit's arrival
     named_bar_sync(2, NT);
     if (tid == 0) *last = atomicAdd(&a.counter[h], 1u) == (unsigned)(n_active - 1);
@@ -539,7 +616,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     if (!*last) return;
     __threadfence();
     const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
-    float* wc = sq;  // [n_active][G] chunk weights (q is no longer needed)
+    float* wc = sq;  // [n_active][G] chunk weights (n_active <= nchunk <= 120 < HD)
     for (int g = warp; g < G; g += NW) {
         float m = -INFINITY;
         for (int cc = lane; cc < n_active; cc += 32) m = fmaxf(m, __ldcg(hb + ((long long)cc * G + g) * part_stride + HD));
@@ -647,7 +724,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                     // pull this CTA's K/V rows of the coming attention phase into L2
                     const AttnArgs& at = ph.at;
                     const int seq = ppos + 1;
-                    const int clen = attn_chunk_len(seq, at.nchunk);
+                    const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads);
                     const int nch = (seq + clen - 1) / clen;
                     for (int u = c; u < at.n_kv_heads * nch; u += G) {
                         const int h = u / nch, t0 = (u % nch) * clen, t1 = min(t0 + clen, seq);
@@ -774,7 +851,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         } else if (!*abort_flag) {
             const AttnArgs& at = ph.at;
             const int seq = pos + 1;
-            const int clen = attn_chunk_len(seq, at.nchunk);
+            const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads);
             const int nch = (seq + clen - 1) / clen;
             const int units = at.n_kv_heads * nch;
             for (int u = c; u < units; u += G) {

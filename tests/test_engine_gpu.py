@@ -17,6 +17,10 @@ def models(fb, tmp_path_factory):
         p = str(d / f"{cfg}.gguf")
         fb.synth_write(p, cfg, seed=21)
         out[cfg] = p
+    # eight KV heads of one query head each: long contexts split into multi-tile attention units
+    p = str(d / "kv8.gguf")
+    fb.synth_write(p, "tiny-q6k", seed=23, n_layers=1, embed_dim=1024, n_heads=8, n_kv_heads=8)
+    out["kv8"] = p
     return out
 
 
@@ -115,6 +119,28 @@ def test_long_context_positions(fb, orc, models, step):
         eng.forward(t, pos)
         lo = ora.forward(t, pos)
         if pos % 50 == 49 or pos == 599:
+            worst = max(worst, float(np.max(np.abs(eng.logits() - lo))))
+    eng.close()
+    ora.close()
+    assert worst < LOGIT_ATOL
+
+
+@pytest.mark.parametrize("kv,n_pos", [("f16", 2400), ("bf16", 1300)])
+def test_multi_tile_attention_units(fb, orc, models, kv, n_pos):
+    """Eight KV heads share the 148 CTAs, so past ~1150 positions each attention unit of the step
+    kernel walks several 64-position tiles (next tile's K / V loads in flight during this one's
+    softmax and P.V): 2 tiles per unit from 1153, 3 from 2305 positions."""
+    kvt = fb.FENCE_KV_F16 if kv == "f16" else fb.FENCE_KV_BF16
+    p = models["kv8"]
+    eng = fb.Model(p, max_ctx=2560, kv_dtype=kvt, step_kernel=True)
+    ora = orc.OracleModel(p, max_ctx=2560, kv_bf16=(kv == "bf16"), threads=8)
+    rng = np.random.default_rng(4)
+    worst = 0.0
+    for pos in range(n_pos):
+        t = int(rng.integers(0, 2048))
+        eng.forward(t, pos)
+        lo = ora.forward(t, pos)
+        if pos % 100 == 99 or pos == n_pos - 1:
             worst = max(worst, float(np.max(np.abs(eng.logits() - lo))))
     eng.close()
     ora.close()
