@@ -3,6 +3,11 @@ on B200, plus the standalone Q6_K GEMV HBM bandwidth (config 0) as the roofline 
 kernel, and the CPU baseline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
+                  [--prompt P] [--layers L]
+
+--prompt sets the prefill length (default: the config's own, 128 / 4000 / 512 for configs 1 / 2 / 3);
+--layers cuts the model to L layers for small ncu captures only (the line then names the layer
+count and is not a measurement of the config).
 
 One JSON line is printed by rank 0. A step is one decode token (batch 1). Inputs are synthetic
 (seeded random-init GGUF of the config's exact shapes; no checkpoints exist offline). With N > 1,
@@ -28,7 +33,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 from __graft_entry__ import _load_pkg  # noqa: E402
 
-PROMPT_LEN = 128
+PROMPT_LEN = {"qwen3-4b": 128, "llama3-8b-q8": 4000, "qwen3-14b": 512}
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 CONFIG0_BYTES = 4096 * 16 * 210 + 4096 * 2 + 4096 * 4  # W + fp16 x + fp32 y = 13,787,136
@@ -104,9 +109,12 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def synth_model(fb, config, tmp):
+def synth_model(fb, config, tmp, layers=0):
     path = os.path.join(tmp, f"{config}.gguf")
-    fb.synth_write(path, config, seed=2024)
+    if layers > 0:
+        fb.synth_write(path, config, seed=2024, n_layers=layers)
+    else:
+        fb.synth_write(path, config, seed=2024)
     return path
 
 
@@ -198,6 +206,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="qwen3-4b")
+    ap.add_argument("--prompt", type=int, default=None, help="prefill tokens (default: the config's own)")
+    ap.add_argument("--layers", type=int, default=0, help="cut the model to this many layers (ncu captures)")
     ap.add_argument("--kv", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--tmp", default=None, help="directory for the synthetic GGUF (default: /dev/shm if roomy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -205,6 +215,8 @@ def main():
                     help="gemv: only the config-0 Q6_K GEMV roofline measurement (small; used for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.prompt is None:
+        args.prompt = PROMPT_LEN.get(args.config, 128)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -239,20 +251,20 @@ def main():
     fb = _load_pkg()
     with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
         # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
-        path = synth_model(fb, args.config, tmp)
+        path = synth_model(fb, args.config, tmp, args.layers)
         kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
-        total_pos = PROMPT_LEN + args.warmup + args.steps + 8
+        total_pos = args.prompt + args.warmup + args.steps + 8
         max_ctx = max(4096, total_pos)
         model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local)
         cfg = model.config
         rng = np.random.default_rng(7 + rank)
-        prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, PROMPT_LEN)]
+        prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, args.prompt)]
         # prefill (token by token, as the reference) — untimed
         d = None
         for pos, t in enumerate(prompt):
             d = model.forward(t, pos)
         first = model.sample_greedy(d)
-        pos = PROMPT_LEN
+        pos = args.prompt
         # warm-up decode steps (device-resident chain)
         warm_ids = model.decode_greedy(first, pos, args.warmup)
         pos += args.warmup
@@ -308,8 +320,9 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint16",
         "data": "synthetic (seeded random-init GGUF, config shapes)",
-        "config": {"workload": f"{args.config} batch-1 greedy decode, {PROMPT_LEN} prompt tokens, positions "
-                               f"{PROMPT_LEN + args.warmup}..{PROMPT_LEN + args.warmup + args.steps - 1}",
+        "config": {"workload": f"{args.config} batch-1 greedy decode, {args.prompt} prompt tokens, positions "
+                               f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}"
+                               + (f" ({args.layers}-layer cut for profiling, not the config)" if args.layers else ""),
                    "model": args.config, "kv_cache": args.kv, "global_batch": world, "seq_len": total_pos,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "weights larger than L2 (no flush needed)"},
