@@ -240,8 +240,8 @@ __device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 
 struct RX {
     uint32_t xh[16], xl[16];
     int corr[4];     // Q6_K: -32 * sum of the column's quantised x
-    float xsA, xsB;  // Q6_K: xsA; Q8_0: scale of the block in chunk slots 0-1 / 2-3
-    uint32_t dsel;   // Q8_0: byte_perm selector of slot pair 0-1's d (0x10 or 0x32)
+    float xsA, xsB;  // Q6_K: xsA; Q8_0: scale of block 0 (chunks 0-1) / block 1 (chunks 2-3)
+    uint32_t sw;     // Q8_0: byte offset of chunk k in the item record is (16 k) ^ sw
 };
 
 template <int WT>
@@ -257,22 +257,20 @@ __device__ __forceinline__ void rg_load_x(uint32_t rec, int item, RX& x) {
         x.corr[0] = (int)c.x; x.corr[1] = (int)c.y; x.corr[2] = (int)c.z; x.corr[3] = (int)c.w;
         x.xsA = __uint_as_float(lds32(rec + 144u));
         x.xsB = 0.f;
-        x.dsel = 0u;
+        x.sw = 0u;
     } else {
-        // weight chunk slot p holds chunk p ^ f: give slot p the x words of that chunk
-        const uint32_t f = (uint32_t)(item >> 1) & 3u;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const uint32_t k = (uint32_t)p ^ f;
+        for (int k = 0; k < 4; ++k) {
             const uint4 a = lds128(rec + 16u * k), b = lds128(rec + 64u + 16u * k);
-            x.xh[4 * p] = a.x; x.xh[4 * p + 1] = a.y; x.xh[4 * p + 2] = a.z; x.xh[4 * p + 3] = a.w;
-            x.xl[4 * p] = b.x; x.xl[4 * p + 1] = b.y; x.xl[4 * p + 2] = b.z; x.xl[4 * p + 3] = b.w;
+            x.xh[4 * k] = a.x; x.xh[4 * k + 1] = a.y; x.xh[4 * k + 2] = a.z; x.xh[4 * k + 3] = a.w;
+            x.xl[4 * k] = b.x; x.xl[4 * k + 1] = b.y; x.xl[4 * k + 2] = b.z; x.xl[4 * k + 3] = b.w;
         }
-        const float xs0 = __uint_as_float(lds32(rec + 144u)), xs1 = __uint_as_float(lds32(rec + 148u));
-        const bool swap = f >= 2u;  // slots 0-1 then hold block 1
-        x.xsA = swap ? xs1 : xs0;
-        x.xsB = swap ? xs0 : xs1;
-        x.dsel = swap ? 0x3232u : 0x1010u;
+        x.xsA = __uint_as_float(lds32(rec + 144u));
+        x.xsB = __uint_as_float(lds32(rec + 148u));
+        // the repack stores chunk k of item i at slot k ^ ((i >> 1) & 3): reading chunk k there, the
+        // eight lanes of a quarter-warp (consecutive items, 64-byte records) hit eight different
+        // 16-byte bank groups
+        x.sw = ((uint32_t)(item >> 1) & 3u) << 4;
         x.corr[0] = x.corr[1] = x.corr[2] = x.corr[3] = 0;
     }
 }
@@ -287,7 +285,7 @@ struct RW {
 // Loads an item's words: q, s, d are 32-bit shared addresses of the item's record, its scale word
 // (Q6_K) and its d (Q6_K: the super-block's fp16; Q8_0: the item's two fp16).
 template <int WT>
-__device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d, RW& r) {
+__device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d, uint32_t sw, RW& r) {
     if (WT == WT_Q6K) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
@@ -299,7 +297,7 @@ __device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d,
     } else {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const uint4 u = lds128(q + 16u * k);
+            const uint4 u = lds128(q + ((16u * k) ^ sw));
             r.w[4 * k] = u.x; r.w[4 * k + 1] = u.y; r.w[4 * k + 2] = u.z; r.w[4 * k + 3] = u.w;
         }
         r.sc = 0u;
@@ -349,8 +347,8 @@ __device__ __forceinline__ float rg_item_compute(const RW& r, const RX& x) {
                 loB = dp4a_su(r.w[m], x.xl[m], loB);
             }
         }
-        const float dA = half_bits_to_float(__byte_perm(r.d, 0u, x.dsel));
-        const float dB = half_bits_to_float(__byte_perm(r.d, 0u, x.dsel ^ 0x2222u));
+        const float dA = half_bits_to_float(r.d & 0xffffu);
+        const float dB = half_bits_to_float(r.d >> 16);
         return (float)(hiA * 256 + loA) * (dA * x.xsA) + (float)(hiB * 256 + loB) * (dB * x.xsB);
     }
 }
@@ -359,7 +357,7 @@ __device__ __forceinline__ float rg_item_compute(const RW& r, const RX& x) {
 template <int WT>
 __device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d, const RX& x) {
     RW r;
-    rg_item_load<WT>(q, s, d, r);
+    rg_item_load<WT>(q, s, d, x.sw, r);
     return rg_item_compute<WT>(r, x);
 }
 
