@@ -110,6 +110,13 @@ struct fence_model {
 
 namespace {
 
+int step_attn_solo() {
+#ifdef FENCE_TUNE_ENV
+    if (const char* e = getenv("FENCE_ATTN_SOLO")) return atoi(e);
+#endif
+    return kStepAttnSolo;
+}
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 int wtype_id(GGMLType t) { return (int)t; }
@@ -280,6 +287,7 @@ int build_step_phases(fence_model* m) {
     A.ph = m->d_phases;
     A.nph = (int)ph.size();
     A.ring = m->splan.ring;
+    A.attn_solo = step_attn_solo();
     A.slot_bytes = m->splan.slot_bytes;
     A.scratch_bytes = m->splan.scratch_bytes;
     A.acc_floats = m->splan.acc_floats;
@@ -571,7 +579,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
               cudaMemset(m->kcache, 0, kv_elems * 2) == cudaSuccess && cudaMemset(m->vcache, 0, kv_elems * 2) == cudaSuccess &&
               cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qd + 2 * kvd) * 4) == cudaSuccess &&
               cudaMalloc(&m->attn_out, qd * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
-              cudaMalloc(&m->attn_part, (size_t)c.n_kv_heads * m->attn_nchunk * G * (HD + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_part, (size_t)c.n_kv_heads * m->attn_nchunk * G * SK_PART_STRIDE * 4) == cudaSuccess &&
               cudaMalloc(&m->act, F * 4) == cudaSuccess &&
               cudaMalloc(&m->counters, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&
               cudaMemset(m->counters, 0, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&

@@ -17,8 +17,10 @@
 //    worked on by all lanes (lane <-> (row, item), x in registers, segmented shuffle reduction,
 //    one shared-memory piece per (row, warp)); after the last stage one thread per row adds the
 //    pieces in a fixed order and runs the fused epilogue; then the CTA counts itself done.
-//  * attention phase: (KV head, 64-position chunk) units over the CTAs, each run by 256 threads
-//    with attention.cuh's chunk body (q/k RMSNorm, RoPE, KV store, online softmax, last-unit merge).
+//  * attention phase: (KV head, context chunk) units over the CTAs, each run by 256 threads (q/k
+//    RMSNorm, RoPE, KV store, q.K^T and P.V on mma.sync, online softmax over 64-position tiles);
+//    a unit's first tile is loaded across the phase change, and the last unit of each KV head
+//    merges its chunks.
 //  * LM head: logits + argmax; the CTA that completes the step last reduces the argmax and
 //    advances the device decode state (token, pos, step).
 //
@@ -41,6 +43,7 @@ constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
 constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
 constexpr int SK_MAX_R = 64;              // rows per stage
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
+constexpr int kStepAttnSolo = 128;  // StepArgs::attn_solo used by the engine (a two-tile walk beats split + merge)
 constexpr int SK_WAIT_ERR = -5;           // FENCE_E_DEVICE_WAIT in the device error word
 
 enum : int { SP_GEMV = 0, SP_ATTN = 1 };
@@ -60,6 +63,7 @@ struct StepArgs {
     const SPhase* ph;
     int nph;
     int ring, slot_bytes;
+    int attn_solo;       // contexts up to this many positions: one attention unit per KV head
     int scratch_bytes;   // union: x records (+ embedding row) / attention tile
     int acc_floats;      // reduction pieces of the largest phase
     unsigned long long* bar;
@@ -314,10 +318,12 @@ struct SKMma<__nv_bfloat16> {
     }
 };
 
-// Positions per attention unit of the step kernel: spread the context of each KV head over the
-// CTAs available to it (ctas / n_kv_heads), in whole 64-position tiles, and never more chunks
-// than the partials hold (nchunk).
-__host__ __device__ __forceinline__ int sk_attn_clen(int seq, int nchunk, int ctas, int n_kv_heads) {
+// Positions per attention unit of the step kernel: up to `solo` positions one unit per KV head
+// walks the whole context (no merge); beyond, the context of each KV head is spread over the CTAs
+// available to it (ctas / n_kv_heads), in whole 64-position tiles, never more chunks than the
+// partials hold (nchunk).
+__host__ __device__ __forceinline__ int sk_attn_clen(int seq, int nchunk, int ctas, int n_kv_heads, int solo) {
+    if (seq <= solo) return (seq + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
     const int per_head = ctas / n_kv_heads > 1 ? ctas / n_kv_heads : 1;
     int clen = (seq + per_head - 1) / per_head;
     const int cmin = (seq + nchunk - 1) / nchunk;
@@ -325,8 +331,16 @@ __host__ __device__ __forceinline__ int sk_attn_clen(int seq, int nchunk, int ct
     return (clen + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
 }
 
+// Floats per (KV head, chunk, query head) record of the step kernel's attention partials: 128
+// unnormalised outputs, the max and the exp-sum, padded so that every record is 16-byte aligned.
+constexpr int SK_PART_STRIDE = 132;
+// Partial records the merging unit stages at a time: the K/V tiles, q, scores and the four
+// 128-float rows after them (40,960 bytes of the unit's scratch).
+constexpr int SK_MERGE_RECS = (2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 +
+                               4 * 128 * 4) / (SK_PART_STRIDE * 4);
+
 // Shared memory of one attention unit (sk_attn_unit's carve-up): K and V tiles, fp32 q, scores,
-// new k / v, norm weights, RoPE row, softmax state, merge flag, q as (high, remainder) pairs.
+// new k / v, norm weights, RoPE row, softmax state, padding, q as (high, remainder) pairs.
 constexpr int sk_attn_scratch_bytes() {
     return 2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 + 4 * 128 * 4 + 64 * 8 +
            3 * ATTN_MAX_G * 4 + 16 + 2 * ATTN_MAX_G * 64 * 4;
@@ -349,7 +363,7 @@ constexpr int sk_attn_scratch_bytes() {
 //    single phase; for a single chunk the unit writes the normalised output itself.
 template <typename KVT>
 __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
-                                          uint8_t* sm) {
+                                          uint8_t* sm, bool pre) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
     constexpr int HD = 128, CH = HD * (int)sizeof(KVT) / 16, EPC = 16 / (int)sizeof(KVT);
@@ -367,8 +381,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     float* smax = reinterpret_cast<float*>(srope + HD / 2);
     float* ssum = smax + ATTN_MAX_G;
     float* sresc = ssum + ATTN_MAX_G;
-    int* last = reinterpret_cast<int*>(sresc + ATTN_MAX_G);
-    uint32_t* sqa = reinterpret_cast<uint32_t*>(last + 4);  // [2][G][HD/2] q high / remainder pairs
+    uint32_t* sqa = reinterpret_cast<uint32_t*>(sresc + ATTN_MAX_G + 4);  // [2][G][HD/2] q high / remainder pairs
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.n_q_heads / a.n_kv_heads;
     const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
@@ -403,7 +416,8 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         }
     };
 
-    // ---- first batch: small inputs + K rows of tile 0 (group 1), V rows of tile 0 (group 2)
+    // ---- first batch: small inputs + K rows of tile 0 (group 1), V rows of tile 0 (group 2); with
+    //      pre, tile 0's K and V rows went out as one earlier group (sk_attn_prefetch_tile0)
     const int qh0 = h * G;
     for (int i = tid; i < G * (HD / 4); i += NT) cp_async16(sq + 4 * i, a.q + (long long)qh0 * HD + 4 * i);
     if (tid < HD / 4) {
@@ -418,9 +432,9 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         cp_async16(reinterpret_cast<float*>(srope) + 4 * i,
                    reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
     }
-    stage(sk, kb, t0, min(t0 + TILE, t1));
+    if (!pre) stage(sk, kb, t0, min(t0 + TILE, t1));  // pre: tile 0 is in flight already
     cp_async_commit();
-    stage(sv, vb, t0, min(t0 + TILE, t1));
+    if (!pre) stage(sv, vb, t0, min(t0 + TILE, t1));
     cp_async_commit();
     if (tid < ATTN_MAX_G) {
         smax[tid] = -INFINITY;
@@ -585,8 +599,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         }
     }
     // ---- output (single chunk) or this chunk's partials: head gr, dims 16 warp + 8 j + 2 q4 + {0, 1}
-    const int part_stride = HD + 2;
-    float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * part_stride;
+    float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * SK_PART_STRIDE;
     if (gr < G) {
         const float inv = n_active == 1 ? 1.0f / ssum[gr] : 1.0f;
 #pragma unroll
@@ -594,54 +607,91 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             const int d = 16 * warp + 8 * j + 2 * q4;
             const float2 o = make_float2((oh[j][0] + ol[j][0]) * inv, (oh[j][1] + ol[j][1]) * inv);
             if (n_active == 1) *reinterpret_cast<float2*>(a.out + (long long)(qh0 + gr) * HD + d) = o;
-            else {
-                pbase[gr * part_stride + d] = o.x;
-                pbase[gr * part_stride + d + 1] = o.y;
-            }
+            else *reinterpret_cast<float2*>(pbase + gr * SK_PART_STRIDE + d) = o;
         }
     }
     if (n_active == 1) return;
-    if (tid < G) {
-        pbase[tid * part_stride + HD] = smax[tid];
-        pbase[tid * part_stride + HD + 1] = ssum[tid];
+    if (tid < G) *reinterpret_cast<float2*>(pbase + tid * SK_PART_STRIDE + HD) = make_float2(smax[tid], ssum[tid]);
+    // ---- the last unit of KV head h to arrive merges the head's chunks: output (query head
+    //      qh0 + g, dim d) = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M), one pass in chunk order
+    //      with a running rescale (deterministic whichever unit merges). The arrival is one
+    //      acq_rel atomic after the CTA barrier (cumulative release of the unit's partials); the
+    //      last unit stages the head's partial records in shared memory with one batch of async
+    //      copies per SK_MERGE_RECS records.
+    named_bar_sync(2, NT);
+    int* flag = reinterpret_cast<int*>(sresc + ATTN_MAX_G);  // outside the staging area
+    if (tid == 0) {
+        unsigned old;
+        asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counter + h) : "memory");
+        *flag = old == (unsigned)(n_active - 1);
     }
-    // ---- the last unit of KV head h to finish merges its chunks: output (query head qh0 + g, dim
-    //      d) = sum_c o_c w_c with w_c = e^(m_c - M) / sum_c' l_c' e^(m_c' - M), M = max_c m_c; the
-    //      weights first (a warp per head), then every output's sum over the chunks in chunk order
-    //      with independent loads (deterministic whichever unit merges)
-    __threadfence();  // this thread's partials are visible before the unit's arrival
     named_bar_sync(2, NT);
-    if (tid == 0) *last = atomicAdd(&a.counter[h], 1u) == (unsigned)(n_active - 1);
-    named_bar_sync(2, NT);
-    if (!*last) return;
-    __threadfence();
-    const float* hb = a.part + ((long long)h * a.nchunk * G) * part_stride;
-    float* wc = sq;  // [n_active][G] chunk weights (n_active <= nchunk <= 120 < HD)
-    for (int g = warp; g < G; g += NW) {
-        float m = -INFINITY;
-        for (int cc = lane; cc < n_active; cc += 32) m = fmaxf(m, __ldcg(hb + ((long long)cc * G + g) * part_stride + HD));
-        m = warp_max(m);
-        float l = 0.f;
-        for (int cc = lane; cc < n_active; cc += 32) {
-            const float* pr = hb + ((long long)cc * G + g) * part_stride;
-            const float e = expf(__ldcg(pr + HD) - m);
-            wc[cc * G + g] = e;
-            l += __ldcg(pr + HD + 1) * e;
+    if (!*flag) return;
+    constexpr int RS = SK_PART_STRIDE, NO = ATTN_MAX_G * HD / NT;  // outputs per thread (<= 4)
+    float* sp = reinterpret_cast<float*>(sm);                     // [batch][G][RS] staged records
+    const float* hb = a.part + (long long)h * a.nchunk * G * RS;
+    const int per_batch = SK_MERGE_RECS / G;
+    float Mx[NO], Lx[NO], Ox[NO];
+#pragma unroll
+    for (int j = 0; j < NO; ++j) {
+        Mx[j] = -INFINITY;
+        Lx[j] = 0.f;
+        Ox[j] = 0.f;
+    }
+    for (int cb = 0; cb < n_active; cb += per_batch) {
+        const int nb = min(per_batch, n_active - cb);
+        const int n16 = nb * G * (RS / 4);  // 16-byte pieces of nb chunks' records
+        const float* src = hb + (long long)cb * G * RS;
+        for (int i = tid; i < n16; i += NT) cp_async16(sp + 4 * i, src + 4 * i);
+        cp_async_commit();
+        cp_async_wait_group<0>();
+        named_bar_sync(2, NT);
+#pragma unroll
+        for (int j = 0; j < NO; ++j) {
+            const int i = tid + j * NT, g = i / HD, d = i - g * HD;
+            if (g < G) {
+                for (int cc = 0; cc < nb; ++cc) {
+                    const float* pr = sp + (cc * G + g) * RS;
+                    const float mc = pr[HD], lc = pr[HD + 1], oc = pr[d];
+                    const float Mn = fmaxf(Mx[j], mc);
+                    const float f1 = (Mx[j] == -INFINITY) ? 0.f : expf(Mx[j] - Mn), f2 = expf(mc - Mn);
+                    Lx[j] = Lx[j] * f1 + lc * f2;
+                    Ox[j] = Ox[j] * f1 + oc * f2;
+                    Mx[j] = Mn;
+                }
+            }
         }
-        l = warp_sum(l);
-        const float inv = 1.0f / l;
-        for (int cc = lane; cc < n_active; cc += 32) wc[cc * G + g] *= inv;
+        named_bar_sync(2, NT);  // the next batch overwrites the staging area
     }
-    named_bar_sync(2, NT);
-    for (int i = tid; i < G * HD; i += NT) {
-        const int g = i / HD, d = i - g * HD;
-        const float* po = hb + (long long)g * part_stride + d;
-        float O = 0.f;
-#pragma unroll 8
-        for (int cc = 0; cc < n_active; ++cc) O = fmaf(__ldcg(po + (long long)cc * G * part_stride), wc[cc * G + g], O);
-        a.out[(long long)(qh0 + g) * HD + d] = O;
+#pragma unroll
+    for (int j = 0; j < NO; ++j) {
+        const int i = tid + j * NT, g = i / HD;
+        if (g < G) a.out[(long long)qh0 * HD + i] = Ox[j] / Lx[j];
     }
-    if (tid == 0) a.counter[h] = 0u;  // every unit of head h has arrived: reset for the next layer
+    if (tid == 0) a.counter[h] = 0u;  // every unit of head h has arrived: zero for the next layer
+}
+
+// Issues the K and V rows of tile 0 of attention unit (h, c) as one cp.async group (threads
+// 0..ATTN_THREADS-1, the unit's own threads, which later wait for it): run at the end of the
+// phase before attention, so the rows load across the phase change. The cache rows before pos
+// are not written by that phase; the row at pos is skipped, as the unit produces it.
+template <typename KVT>
+__device__ __forceinline__ void sk_attn_prefetch_tile0(const AttnArgs& a, int h, int c, int clen, int pos,
+                                                       uint8_t* sm) {
+    constexpr int HD = 128, CH = 16, TILE = ATTN_CMAX;
+    KVT* sk = reinterpret_cast<KVT*>(sm);
+    KVT* sv = sk + TILE * HD;
+    const int t0 = c * clen, te = min(min(t0 + clen, pos + 1), t0 + TILE);
+    const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
+    const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
+    for (int idx = threadIdx.x; idx < (te - t0) * CH; idx += ATTN_THREADS) {
+        const int r = idx >> 4, ch = idx & 15, t = t0 + r;
+        if (t == pos) continue;
+        const uint32_t so = (uint32_t)r * HD * sizeof(KVT) + ((ch ^ (r & 7)) * 16);
+        cp_async16(reinterpret_cast<uint8_t*>(sk) + so, reinterpret_cast<const uint8_t*>(kb + (long long)t * a.stride_t) + ch * 16);
+        cp_async16(reinterpret_cast<uint8_t*>(sv) + so, reinterpret_cast<const uint8_t*>(vb + (long long)t * a.stride_t) + ch * 16);
+    }
+    cp_async_commit();
 }
 
 // Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
@@ -724,7 +774,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                     // pull this CTA's K/V rows of the coming attention phase into L2
                     const AttnArgs& at = ph.at;
                     const int seq = ppos + 1;
-                    const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads);
+                    const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads, A.attn_solo);
                     const int nch = (seq + clen - 1) / clen;
                     for (int u = c; u < at.n_kv_heads * nch; u += G) {
                         const int h = u / nch, t0 = (u % nch) * clen, t1 = min(t0 + clen, seq);
@@ -791,6 +841,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     const int pos = A.state->pos;  // fixed for the whole step (advanced only at its very end)
     if (warp == 0) sk_fetch_desc(&A.ph[0], desc, lane);
     named_bar_sync(1, NT);
+    bool attn_pre = false;  // this thread issued tile 0 of its CTA's first attention unit
     for (int k = 0; k < NPH; ++k) {
         const SPhase& ph = *reinterpret_cast<const SPhase*>(desc + (k & 1) * SK_DESC);
         // the next phase's descriptor, read while this phase runs (ordered by the phase-end barrier)
@@ -848,14 +899,30 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 named_bar_sync(1, NT);
             }
             if (!*abort_flag) sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i);
+            // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
+            // records are dead; the next descriptor was fetched at this phase's start)
+            if (k + 1 < NPH && tid < ATTN_THREADS) {
+                const SPhase& nx = *reinterpret_cast<const SPhase*>(desc + ((k + 1) & 1) * SK_DESC);
+                if (nx.kind == SP_ATTN) {
+                    const int seq = pos + 1;
+                    const int clen = sk_attn_clen(seq, nx.at.nchunk, G, nx.at.n_kv_heads, A.attn_solo);
+                    const int nch = (seq + clen - 1) / clen;
+                    if (c < nx.at.n_kv_heads * nch) {
+                        sk_attn_prefetch_tile0<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch);
+                        attn_pre = true;
+                    }
+                }
+            }
         } else if (!*abort_flag) {
             const AttnArgs& at = ph.at;
             const int seq = pos + 1;
-            const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads);
+            const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads, A.attn_solo);
             const int nch = (seq + clen - 1) / clen;
             const int units = at.n_kv_heads * nch;
             for (int u = c; u < units; u += G) {
-                if (tid < ATTN_THREADS) sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch);
+                // the first unit's tile 0 may have been issued at the end of the previous phase
+                if (tid < ATTN_THREADS) sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre);
+                attn_pre = false;
                 named_bar_sync(1, NT);  // the next unit reuses the scratch
                 if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
             }
