@@ -1,6 +1,7 @@
 """Benchmark: batch-1 greedy decode tokens/s of the Qwen3-4B-shaped Q6_K model
-on B200, plus the standalone Q6_K GEMV HBM bandwidth (config 0) as the roofline of the dominant
-kernel, and the CPU baseline.
+on B200. The roofline object is the step kernel's (one launch per token: the dominant and only
+kernel of the decode loop) against measured HBM bandwidth; the drop-in config-0 Q6_K GEMV is
+reported beside it (gemv_config0), with the CPU baseline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
                   [--prompt P] [--layers L]
@@ -47,16 +48,38 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profiles():
-    """Per-launch DRAM bytes of the config-0 Q6_K GEMV from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "gemv_q6k_config0.md")
+def traffic_from_profiles(name, key="traffic_bytes_per_launch"):
+    """A per-launch DRAM byte count recorded in a committed ncu summary under profiles/, if any."""
+    p = os.path.join(ROOT, "profiles", name)
     try:
         for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 return int(line.split(":")[1].strip())
-    except OSError:
+    except (OSError, ValueError):
         pass
     return None
+
+
+def traffic_ratio_from_profiles(name):
+    """DRAM bytes / algorithmic bytes of one step-kernel launch, from a committed ncu summary of a
+    smaller cut of the same config (the traffic scales with the bytes streamed)."""
+    try:
+        for line in open(os.path.join(ROOT, "profiles", name)):
+            if line.startswith("traffic_ratio:"):
+                return float(line.split(":")[1].strip())
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def step_algorithmic_bytes(cfg, positions):
+    """Bytes one decode token must move (the roofline numerator): every weight streamed once
+    (layer linears + the tied LM head, weight_bytes), the token's embedding row, and the K and V
+    rows of the context read by attention (fp16), averaged over the timed positions."""
+    kv_dim = cfg.n_kv_heads * cfg.head_dim
+    embed_row = cfg.embed_dim // 32 * 34
+    kv = sum(2 * cfg.n_layers * (p + 1) * kv_dim * 2 for p in positions) / max(1, len(positions))
+    return int(cfg.weight_bytes + embed_row + kv)
 
 
 class ClockSampler:
@@ -116,10 +139,6 @@ def synth_model(fb, config, tmp, layers=0):
     else:
         fb.synth_write(path, config, seed=2024)
     return path
-
-
-def model_bytes_per_token(cfg):
-    return int(cfg.weight_bytes)
 
 
 def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
@@ -297,7 +316,7 @@ def main():
             nxt = model.sample_greedy(dl)
         e2e_s = time.perf_counter() - t0
         e2e_val = e2e_steps / e2e_s * world
-        step_bytes = model_bytes_per_token(cfg)
+        step_bytes = step_algorithmic_bytes(cfg, range(pos - args.steps, pos))
         model.close()
 
     peak, peak_kind = hbm_peak()
@@ -314,7 +333,11 @@ def main():
         cpu = {"value": round(n / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
                "sample": f"{n} decode tokens of {args.config} at positions 0..{n - 1} through the oracle port "
                          f"(oracle/fence_oracle.c, fp64) on {threads} host threads, ~20 s"}
-    launches_per_step = 1 + 5 * cfg.n_layers + 1
+    launches_per_step = 1  # the persistent step kernel: one launch per token
+    step_us = ms / args.steps * 1e3
+    step_gbs = step_bytes / (step_us * 1e-6) / 1e9
+    ratio = traffic_ratio_from_profiles(f"step_kernel_{args.config.replace('-', '_')}.md")
+    step_traffic = int(ratio * step_bytes) if ratio else None
     line = {
         "metric": "decode_tokens_per_s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
@@ -326,14 +349,18 @@ def main():
                    "model": args.config, "kv_cache": args.kv, "global_batch": world, "seq_len": total_pos,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "weights larger than L2 (no flush needed)"},
-        "roofline": {"bound": "hbm", "kernel": "gemv_q6k 4096x4096 (config 0)", "achieved": round(achieved, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic_from_profiles(), "us_per_launch": round(gemv_ms * 1e3, 3),
-                     "us_per_launch_serialized": round(gemv_ms_serial * 1e3, 3),
-                     "algorithmic_bytes_per_launch": CONFIG0_BYTES},
-        "step_roofline": {"weight_bytes_per_token": step_bytes,
-                          "achieved_gbs": round(step_bytes * tok_s / 1e9, 1),
-                          "frac": round(step_bytes * tok_s / 1e9 / peak, 4)},
+        "roofline": {"bound": "hbm", "kernel": "step_kernel (one launch = one whole token step)",
+                     "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind,
+                     "traffic": step_traffic, "us_per_launch": round(step_us, 2),
+                     "algorithmic_bytes_per_launch": step_bytes},
+        "gemv_config0": {"kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "traffic": traffic_from_profiles("gemv_q6k_config0.md"),
+                         "us_per_launch": round(gemv_ms * 1e3, 3),
+                         "us_per_launch_serialized": round(gemv_ms_serial * 1e3, 3),
+                         "algorithmic_bytes_per_launch": CONFIG0_BYTES},
         "e2e": {"value": round(e2e_val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),

@@ -206,7 +206,7 @@ typedef struct fence_load_opts {
     int step_kernel;
 } fence_load_opts;
 
-/* Fills *opts with defaults (max_ctx 4096, bf16 KV, device 0, graphs on, single rank). */
+/* Fills *opts with defaults (max_ctx 4096, fp16 KV, device 0, graphs on, single rank, step kernel). */
 void fence_load_opts_default(fence_load_opts* opts);
 
 /* Qwen3Model::load (src/model/qwen3.cu:116-228): mmap the GGUF, read the config from its metadata
