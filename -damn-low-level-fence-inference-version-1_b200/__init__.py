@@ -30,6 +30,9 @@ class FenceError(RuntimeError):
     """A fence_* call returned a non-zero status."""
 
 
+FENCE_TP_HANDLE_BYTES = 64
+
+
 class Config(ctypes.Structure):
     _fields_ = [
         ("n_layers", ctypes.c_int), ("embed_dim", ctypes.c_int), ("ff_dim", ctypes.c_int),
@@ -106,6 +109,8 @@ SIGNATURES = [
     ("fence_decode_greedy", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_int_p]),
     ("fence_copy_logits", ctypes.c_int, [_vp, _c_float_p]),
     ("fence_time_decode", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_float_p]),
+    ("fence_tp_handle", ctypes.c_int, [_vp, _vp, ctypes.c_int]),
+    ("fence_tp_connect", ctypes.c_int, [_vp, _vp, ctypes.c_int]),
     ("fence_synth_spec_default", None, [ctypes.POINTER(SynthSpec)]),
     ("fence_synth_write_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), ctypes.c_int]),
     ("fence_synth_fill_blocks", ctypes.c_int,
@@ -205,12 +210,14 @@ class Model:
     """The reference's Qwen3Model API over the engine handle."""
 
     def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
-                 use_graph: bool = True, verbose: bool = False, step_kernel: bool = True):
+                 use_graph: bool = True, verbose: bool = False, step_kernel: bool = True,
+                 tp_rank: int = 0, tp_size: int = 1):
         L = lib()
         o = LoadOpts()
         L.fence_load_opts_default(ctypes.byref(o))
         o.max_ctx, o.kv_dtype, o.device, o.use_graph, o.verbose = max_ctx, kv_dtype, device, int(use_graph), int(verbose)
         o.step_kernel = int(step_kernel)
+        o.tp_rank, o.tp_size = tp_rank, tp_size
         h = L.fence_model_load(path.encode(), ctypes.byref(o))
         if not h:
             raise FenceError(f"model load failed: {last_error()}")
@@ -236,9 +243,26 @@ class Model:
             raise FenceError(f"forward failed: {last_error()}")
         return p
 
+    def vocab_shard(self):
+        """(first row, rows) of this rank's LM-head vocabulary shard ((0, vocab) without TP)."""
+        V, n, r = self.config.vocab_size, max(1, self.config.tp_size), self.config.tp_rank
+        per = (V + n - 1) // n
+        return r * per, min(V, (r + 1) * per) - r * per
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-buffer handle, to give every other rank (tensor parallel)."""
+        buf = ctypes.create_string_buffer(FENCE_TP_HANDLE_BYTES)
+        check(lib().fence_tp_handle(self._h, buf, FENCE_TP_HANDLE_BYTES), "tp_handle")
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """Maps every rank's exchange buffer (handles in rank order) and builds the step."""
+        blob = b"".join(handles)
+        check(lib().fence_tp_connect(self._h, blob, len(handles)), "tp_connect")
+
     def logits(self):
         import numpy as np
-        out = np.empty(self.config.vocab_size, dtype=np.float32)
+        out = np.empty(self.vocab_shard()[1], dtype=np.float32)
         check(lib().fence_copy_logits(self._h, out.ctypes.data_as(_c_float_p)), "copy_logits")
         return out
 

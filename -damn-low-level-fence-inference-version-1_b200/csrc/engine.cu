@@ -34,7 +34,7 @@ namespace fence {
 size_t rmat_bytes(int wt, long long rows, int K);
 RMat rmat_carve(int wt, long long rows, int K, uint8_t* base);
 cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
-                      int dst_stride, cudaStream_t st);
+                      int dst_stride, cudaStream_t st, int src_K = 0);
 RGemvPlan plan_rgemv(RGemvArgs& a, int sms, int smem_budget);
 cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
@@ -102,6 +102,13 @@ struct fence_model {
     StepPlan splan{};
     float* qkv_bias = nullptr;      // fused q|k|v bias when the model has any
     int attn_nchunk = 0;
+    // tensor parallel (tp_n > 1): this rank's shard; the exchange buffer is shared with the peers
+    int tp_n = 1, tp_rank = 0, vocab0 = 0, vocab_n = 0;
+    float* hidden_b = nullptr;      // residual stream after the odd reductions
+    uint8_t* xbuf = nullptr;        // this rank's exchange buffer (sk_xb_bytes)
+    uint8_t* xpeer[SK_TP_MAX] = {};  // every rank's exchange buffer as mapped here (own = xbuf)
+    unsigned long long* tp_launch = nullptr;
+    int tp_connected = 0;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
     std::mt19937 rng{0x5eed};
@@ -181,6 +188,8 @@ int enqueue_step(fence_model* m) {
 }
 
 int run_step(fence_model* m) {
+    if (m->tp_n > 1 && !m->tp_connected)
+        return set_error(FENCE_E_ARG, "tensor-parallel model: call fence_tp_connect on every rank first");
     if (m->gexec) return cuda_status(cudaGraphLaunch(m->gexec, m->stream), "graph launch");
     return enqueue_step(m);
 }
@@ -256,6 +265,21 @@ int build_step_phases(fence_model* m) {
         p.epi = r.epi;
         return p;
     };
+    // tensor parallel: reduction 2l after o_proj, 2l+1 after down; the residual stream alternates
+    // between hidden (read by even reductions) and hidden_b (odd)
+    const bool tp = m->tp_n > 1;
+    auto tp_sum = [&](SPhase& p, int red) {
+        if (!tp || red < 0) return;
+        p.tp_sum = 1;
+        p.red_idx = red;
+        p.hin = (red & 1) ? m->hidden_b : m->hidden;
+        p.hout = (red & 1) ? m->hidden : m->hidden_b;
+    };
+    auto tp_red = [&](SPhase& p, int red) {
+        if (!tp) return;
+        p.tp_red = 1;
+        p.red_idx = red;
+    };
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerLaunch& L = m->launches[l];
         SPhase q = gemv(L.qkv);
@@ -264,16 +288,23 @@ int build_step_phases(fence_model* m) {
             q.embd = m->tok_embd;
             q.hidden_out = m->hidden;
         }
+        tp_sum(q, 2 * l - 1);
         ph.push_back(q);
         SPhase at{};
         at.kind = SP_ATTN;
         at.at = L.attn;
         ph.push_back(at);
-        ph.push_back(gemv(L.o));
-        ph.push_back(gemv(L.gu));
-        ph.push_back(gemv(L.down));
+        SPhase o = gemv(L.o), gu = gemv(L.gu), dn = gemv(L.down);
+        tp_red(o, 2 * l);
+        tp_sum(gu, 2 * l);
+        tp_red(dn, 2 * l + 1);
+        ph.push_back(o);
+        ph.push_back(gu);
+        ph.push_back(dn);
     }
-    ph.push_back(gemv(m->lm));
+    SPhase lm = gemv(m->lm);
+    tp_sum(lm, 2 * c.n_layers - 1);
+    ph.push_back(lm);
     std::string err;
     m->splan = plan_step(ph, m->dev, err);
     if (!m->splan.ok) return set_error(FENCE_E_UNSUPPORTED, "%s", err.c_str());
@@ -297,6 +328,17 @@ int build_step_phases(fence_model* m) {
     A.cta_idx = m->lm_idx;
     A.token_log = m->token_log;
     A.token_log_cap = m->token_log_cap;
+    if (tp) {
+        A.tp_n = m->tp_n;
+        A.tp_rank = m->tp_rank;
+        A.tp_h = c.embed_dim;
+        A.n_red = 2 * c.n_layers;
+        A.vocab0 = m->vocab0;
+        for (int p = 0; p < m->tp_n; ++p) A.xb[p] = m->xpeer[p];
+        A.launch = m->tp_launch;
+    } else {
+        A.tp_n = 1;
+    }
     m->use_step = 1;
     return FENCE_OK;
 }
@@ -331,6 +373,11 @@ void free_model(fence_model* m) {
     cudaFree(m->qkv_bias);
     cudaFree(m->d_phases);
     cudaFree(m->d_bar);
+    for (int p = 0; p < m->tp_n; ++p)
+        if (p != m->tp_rank && m->xpeer[p]) cudaIpcCloseMemHandle(m->xpeer[p]);
+    cudaFree(m->xbuf);
+    cudaFree(m->hidden_b);
+    cudaFree(m->tp_launch);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -361,8 +408,13 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         set_error(FENCE_E_ARG, "model_load: null path");
         return nullptr;
     }
-    if (opts.tp_size > 1) {
-        set_error(FENCE_E_UNSUPPORTED, "model_load: tensor parallel loading is not built in this library");
+    if (opts.tp_size > 1 && (opts.tp_size > SK_TP_MAX || opts.tp_rank < 0 || opts.tp_rank >= opts.tp_size)) {
+        set_error(FENCE_E_ARG, "model_load: tp_rank %d / tp_size %d (at most %d ranks)", opts.tp_rank, opts.tp_size,
+                  SK_TP_MAX);
+        return nullptr;
+    }
+    if (opts.tp_size > 1 && !opts.step_kernel) {
+        set_error(FENCE_E_UNSUPPORTED, "model_load: tensor parallel decode runs in the step kernel (step_kernel = 1)");
         return nullptr;
     }
     fence_model* m = new fence_model();
@@ -427,8 +479,8 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     c.min_p = 0.05f;
     c.dynamic_temp = 1;
     c.kv_dtype = opts.kv_dtype;
-    c.tp_rank = 0;
-    c.tp_size = 1;
+    c.tp_rank = opts.tp_size > 1 ? opts.tp_rank : 0;
+    c.tp_size = opts.tp_size > 1 ? opts.tp_size : 1;
     c.embd_type = (int)embd->type;
 
     if (c.n_layers <= 0 || c.embed_dim <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads)
@@ -446,6 +498,19 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
 
     const uint64_t H = c.embed_dim, F = c.ff_dim, qd = (uint64_t)c.n_heads * c.head_dim,
                    kvd = (uint64_t)c.n_kv_heads * c.head_dim;
+    // ---- this rank's shard (Megatron split, tp_size ranks): q/k/v rows by heads and gate/up rows by
+    // FFN rows (column-parallel, no exchange), o_proj and down by input columns (row-parallel: each
+    // rank's partial rows are summed over the ranks), the tied LM head by vocabulary rows
+    const int TPN = c.tp_size, TPR = c.tp_rank;
+    if (TPN > 1 && (c.n_heads % TPN || c.n_kv_heads % TPN || c.ff_dim % TPN))
+        return bail(FENCE_E_UNSUPPORTED, "model_load: heads / FFN rows do not split evenly over tp_size ranks");
+    const uint64_t qdl = qd / TPN, kvdl = kvd / TPN, Fl = F / TPN;
+    const int Hq_l = c.n_heads / TPN, Hkv_l = c.n_kv_heads / TPN;
+    const int Vl = (c.vocab_size + TPN - 1) / TPN, v0 = TPR * Vl, vn = std::min(c.vocab_size, v0 + Vl) - v0;
+    m->tp_n = TPN;
+    m->tp_rank = TPR;
+    m->vocab0 = v0;
+    m->vocab_n = vn;
 
     // ---- collect and validate tensors, lay out the device arena
     struct Up {
@@ -571,18 +636,18 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     }
 
     const int HD = c.head_dim, G = c.n_heads / c.n_kv_heads;
-    const size_t kv_elems = (size_t)c.n_layers * c.n_kv_heads * c.max_ctx * HD;
+    const size_t kv_elems = (size_t)c.n_layers * Hkv_l * c.max_ctx * HD;
     // chunks per KV head: 64-position chunks up to 120 (the merge keeps G x chunks scale factors in
     // the CTA's score buffer); longer contexts get longer chunks
     m->attn_nchunk = std::min(120, std::max(32, (c.max_ctx + ATTN_CHUNK - 1) / ATTN_CHUNK));
     bool ok = cudaMalloc(&m->kcache, kv_elems * 2) == cudaSuccess && cudaMalloc(&m->vcache, kv_elems * 2) == cudaSuccess &&
               cudaMemset(m->kcache, 0, kv_elems * 2) == cudaSuccess && cudaMemset(m->vcache, 0, kv_elems * 2) == cudaSuccess &&
-              cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qd + 2 * kvd) * 4) == cudaSuccess &&
-              cudaMalloc(&m->attn_out, qd * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)c.vocab_size * 4) == cudaSuccess &&
-              cudaMalloc(&m->attn_part, (size_t)c.n_kv_heads * m->attn_nchunk * G * SK_PART_STRIDE * 4) == cudaSuccess &&
-              cudaMalloc(&m->act, F * 4) == cudaSuccess &&
-              cudaMalloc(&m->counters, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&
-              cudaMemset(m->counters, 0, (c.n_kv_heads + 1) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qdl + 2 * kvdl) * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_out, qdl * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)vn * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_part, (size_t)Hkv_l * m->attn_nchunk * G * SK_PART_STRIDE * 4) == cudaSuccess &&
+              cudaMalloc(&m->act, Fl * 4) == cudaSuccess &&
+              cudaMalloc(&m->counters, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&
+              cudaMemset(m->counters, 0, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&
               cudaMalloc(&m->lm_val, 4096 * 4) == cudaSuccess && cudaMalloc(&m->lm_idx, 4096 * 4) == cudaSuccess &&
               cudaMalloc(&m->state, sizeof(DecodeState)) == cudaSuccess &&
               cudaMemset(m->state, 0, sizeof(DecodeState)) == cudaSuccess &&
@@ -590,6 +655,13 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
               cudaMallocHost(&m->h_state, 64 * sizeof(DecodeState)) == cudaSuccess &&
               cudaMallocHost(&m->h_token, 64 * sizeof(int)) == cudaSuccess;
     if (!ok) return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
+    if (TPN > 1) {
+        const size_t xb = sk_xb_bytes(TPN, (int)H);
+        if (cudaMalloc(&m->hidden_b, H * 4) != cudaSuccess || cudaMalloc(&m->xbuf, xb) != cudaSuccess ||
+            cudaMemset(m->xbuf, 0, xb) != cudaSuccess || cudaMalloc(&m->tp_launch, 8) != cudaSuccess ||
+            cudaMemset(m->tp_launch, 0, 8) != cudaSuccess)
+            return bail(FENCE_E_NOMEM, "model_load: exchange buffer allocation failed");
+    }
     m->h_state_n = 64;
     m->token_log_cap = std::max(c.max_ctx, 4096);
     if (cudaMalloc(&m->token_log, m->token_log_cap * sizeof(int)) != cudaSuccess)
@@ -610,22 +682,27 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     // ---- repacked linears (rgemv.cuh): one fused QKV matrix and one gate/up-interleaved matrix per
     // layer, O, down and the tied LM head, rewritten once on the device from the uploaded blocks
     auto wt_of = [](int t) { return t == 14 ? WT_Q6K : WT_Q80; };
-    const long long QKVR = (long long)(qd + 2 * kvd);
-    size_t rbytes = rmat_bytes(WT_Q80, c.vocab_size, (int)H);
+    const long long QKVR = (long long)(qdl + 2 * kvdl);
+    size_t rbytes = rmat_bytes(WT_Q80, vn, (int)H);
+    size_t shard_bytes = (size_t)vn * (H / 32) * 34;  // LM-head shard (+ the layers' shards below)
+    auto raw_row = [](int t, uint64_t K) { return t == 14 ? K / 256 * 210 : K / 32 * 34; };
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
-        rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) + rmat_bytes(wt_of(w.t_o), (long long)H, (int)qd) +
-                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)F, (int)H) + rmat_bytes(wt_of(w.t_down), (long long)H, (int)F);
+        rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) + rmat_bytes(wt_of(w.t_o), (long long)H, (int)qdl) +
+                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)Fl, (int)H) + rmat_bytes(wt_of(w.t_down), (long long)H, (int)Fl);
+        shard_bytes += QKVR * raw_row(w.t_qkv, H) + H * raw_row(w.t_o, qdl) + 2 * Fl * raw_row(w.t_gu, H) +
+                       H * raw_row(w.t_down, Fl);
     }
-    if (qd % 256 || H % 256 || F % 256) {
-        // Q8_0 rows only need 64-element items; Q6_K super-blocks need 256
-        for (int l = 0; l < c.n_layers; ++l) {
-            const LayerW& w = m->layers[l];
-            if ((w.t_qkv == 14 && H % 256) || (w.t_o == 14 && qd % 256) || (w.t_gu == 14 && H % 256) ||
-                (w.t_down == 14 && F % 256) || qd % 64 || F % 64)
-                return bail(FENCE_E_UNSUPPORTED, "model_load: linear input width not a multiple of the block size");
-        }
+    // Q8_0 rows only need 64-element items; Q6_K super-blocks need 256 (a rank's column slice too)
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerW& w = m->layers[l];
+        if ((w.t_qkv == 14 && H % 256) || (w.t_o == 14 && qdl % 256) || (w.t_gu == 14 && H % 256) ||
+            (w.t_down == 14 && Fl % 256) || qdl % 64 || Fl % 64 || H % 64)
+            return bail(FENCE_E_UNSUPPORTED, TPN > 1 ? "model_load: a rank's o_proj / down column slice is not a whole "
+                                                       "number of quant blocks (choose another tp_size)"
+                                                     : "model_load: linear input width not a multiple of the block size");
     }
+    if (TPN > 1) c.weight_bytes = shard_bytes;
     if (cudaMalloc(&m->rarena, rbytes) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: repacked arena allocation failed");
     int sms = 0, smem_sm = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->dev);
@@ -663,30 +740,37 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     };
 
     m->launches.resize(c.n_layers);
-    const size_t kv_layer = (size_t)c.n_kv_heads * c.max_ctx * HD;
+    const size_t kv_layer = (size_t)Hkv_l * c.max_ctx * HD;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
         const int wq = wt_of(w.t_qkv), wo = wt_of(w.t_o), wg = wt_of(w.t_gu), wd = wt_of(w.t_down);
-        const RMat rq = carve(wq, QKVR, (int)H), ro = carve(wo, (long long)H, (int)qd),
-                   rg = carve(wg, 2 * (long long)F, (int)H), rd = carve(wd, (long long)H, (int)F);
-        if (!fill(wq, w.q, (long long)qd, (int)H, rq, 0, 1) || !fill(wq, w.k, (long long)kvd, (int)H, rq, (long long)qd, 1) ||
-            !fill(wq, w.v, (long long)kvd, (int)H, rq, (long long)(qd + kvd), 1) ||
-            !fill(wo, w.o, (long long)H, (int)qd, ro, 0, 1) || !fill(wg, w.gate, (long long)F, (int)H, rg, 0, 2) ||
-            !fill(wg, w.up, (long long)F, (int)H, rg, 1, 2) || !fill(wd, w.down, (long long)H, (int)F, rd, 0, 1))
+        const RMat rq = carve(wq, QKVR, (int)H), ro = carve(wo, (long long)H, (int)qdl),
+                   rg = carve(wg, 2 * (long long)Fl, (int)H), rd = carve(wd, (long long)H, (int)Fl);
+        // this rank's rows (q/k/v heads, FFN rows) and input columns (o_proj, down)
+        const uint64_t rq_b = raw_row(w.t_qkv, H), rg_b = raw_row(w.t_gu, H);
+        const uint8_t* o_src = w.o + raw_row(w.t_o, TPR * qdl);
+        const uint8_t* d_src = w.down + raw_row(w.t_down, TPR * Fl);
+        if (!fill(wq, w.q + TPR * qdl * rq_b, (long long)qdl, (int)H, rq, 0, 1) ||
+            !fill(wq, w.k + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)qdl, 1) ||
+            !fill(wq, w.v + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)(qdl + kvdl), 1) ||
+            rmat_fill(wo, o_src, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd) != cudaSuccess ||
+            !fill(wg, w.gate + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 0, 2) ||
+            !fill(wg, w.up + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 1, 2) ||
+            rmat_fill(wd, d_src, (long long)H, (int)Fl, rd, 0, 1, st, (int)F) != cudaSuccess)
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
         float* bias = nullptr;
         if (any_bias) {
             bias = m->qkv_bias + (size_t)l * QKVR;
-            if ((w.q_bias && cudaMemcpy(bias, w.q_bias, qd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
-                (w.k_bias && cudaMemcpy(bias + qd, w.k_bias, kvd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
-                (w.v_bias && cudaMemcpy(bias + qd + kvd, w.v_bias, kvd * 4, cudaMemcpyDeviceToDevice) != cudaSuccess))
+            if ((w.q_bias && cudaMemcpy(bias, w.q_bias + TPR * qdl, qdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
+                (w.k_bias && cudaMemcpy(bias + qdl, w.k_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
+                (w.v_bias && cudaMemcpy(bias + qdl + kvdl, w.v_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess))
                 return bail(FENCE_E_NOMEM, "model_load: bias upload failed");
         }
         if (!phase(L.qkv, rq, wq, (int)H, (int)QKVR, 0, wq == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_STORE) ||
-            !phase(L.o, ro, wo, (int)qd, (int)H, 0, wo == WT_Q6K ? X_F32_R16 : X_F32, EPI_RESID) ||
-            !phase(L.gu, rg, wg, (int)H, (int)F, 1, wg == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_SWIGLU) ||
-            !phase(L.down, rd, wd, (int)F, (int)H, 0, wd == WT_Q6K ? X_F16 : X_F32, EPI_RESID))
+            !phase(L.o, ro, wo, (int)qdl, (int)H, 0, wo == WT_Q6K ? X_F32_R16 : X_F32, EPI_RESID) ||
+            !phase(L.gu, rg, wg, (int)H, (int)Fl, 1, wg == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_SWIGLU) ||
+            !phase(L.down, rd, wd, (int)Fl, (int)H, 0, wd == WT_Q6K ? X_F16 : X_F32, EPI_RESID))
             return bail(FENCE_E_UNSUPPORTED, "model_load: a layer shape does not fit the streaming GEMV");
         L.qkv.a.x = m->hidden;
         L.qkv.a.norm_w = w.attn_norm;
@@ -711,13 +795,13 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         at.vc_w = const_cast<void*>(at.vc);
         at.stride_t = HD;
         at.stride_h = (long long)c.max_ctx * HD;
-        at.n_q_heads = c.n_heads;
-        at.n_kv_heads = c.n_kv_heads;
+        at.n_q_heads = Hq_l;
+        at.n_kv_heads = Hkv_l;
         at.nchunk = m->attn_nchunk;
         at.part = m->attn_part;
         at.state = m->state;
-        at.k_new = m->qkv + qd;
-        at.v_new = m->qkv + qd + kvd;
+        at.k_new = m->qkv + qdl;
+        at.v_new = m->qkv + qdl + kvdl;
         at.q_norm_w = w.q_norm;
         at.k_norm_w = w.k_norm;
         at.eps = c.rms_eps;
@@ -728,10 +812,10 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     }
     // LM head: tied token_embd (the reference ignores output.weight, qwen3.cu:180-212,261)
     {
-        const RMat rl = carve(WT_Q80, c.vocab_size, (int)H);
-        if (!fill(WT_Q80, m->tok_embd, c.vocab_size, (int)H, rl, 0, 1))
+        const RMat rl = carve(WT_Q80, vn, (int)H);
+        if (!fill(WT_Q80, m->tok_embd + (size_t)v0 * (H / 32) * 34, vn, (int)H, rl, 0, 1))
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
-        if (!phase(m->lm, rl, WT_Q80, (int)H, c.vocab_size, 0, X_NORM, EPI_LMHEAD) || m->lm.p.grid > 4096)
+        if (!phase(m->lm, rl, WT_Q80, (int)H, vn, 0, X_NORM, EPI_LMHEAD) || m->lm.p.grid > 4096)
             return bail(FENCE_E_UNSUPPORTED, "model_load: LM head shape not supported");
         RGemvArgs& a = m->lm.a;
         a.x = m->hidden;
@@ -740,17 +824,17 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         a.logits = m->logits;
         a.cta_val = m->lm_val;
         a.cta_idx = m->lm_idx;
-        a.counter = m->counters + c.n_kv_heads;
+        a.counter = m->counters + Hkv_l;
         a.state = m->state;
         a.token_log = m->token_log;
         a.token_log_cap = m->token_log_cap;
     }
-    if (opts.step_kernel) {
+    if (opts.step_kernel && TPN == 1) {  // tensor parallel: once the ranks are connected (fence_tp_connect)
         const int rc = build_step_phases(m);
         if (rc != FENCE_OK) return bail(rc, std::string("model_load: ") + fence_last_error());
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: device error during setup");
-    if (opts.use_graph) {
+    if (opts.use_graph && TPN == 1) {
         const int rc = capture_graph(m);
         if (rc != FENCE_OK) return bail(rc, std::string("model_load: graph capture failed: ") + fence_last_error());
     }
@@ -848,6 +932,7 @@ extern "C" int fence_sample_nucleus(fence_model* m, const float* d_logits, const
     if (!m || !d_logits) return set_error(FENCE_E_ARG, "sample_nucleus: null argument");
     const fence_config& c = m->cfg;
     if (c.temperature <= 0.0f || c.top_k <= 1) return fence_sample_greedy(m, d_logits);
+    if (m->tp_n > 1) return set_error(FENCE_E_UNSUPPORTED, "sample_nucleus: a tensor-parallel rank holds a vocabulary shard");
     cudaSetDevice(m->dev);
     FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_logits.data(), d_logits, (size_t)c.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
     FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
@@ -919,10 +1004,53 @@ extern "C" int fence_time_decode(fence_model* m, int token, int pos, int n_steps
     return rc;
 }
 
+extern "C" int fence_tp_handle(fence_model* m, void* out, int cap) {
+    if (!m || !out || cap < FENCE_TP_HANDLE_BYTES) return set_error(FENCE_E_ARG, "tp_handle: bad arguments");
+    if (m->tp_n < 2) return set_error(FENCE_E_ARG, "tp_handle: the model was loaded with tp_size 1");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= FENCE_TP_HANDLE_BYTES, "handle size");
+    cudaSetDevice(m->dev);
+    cudaIpcMemHandle_t h;
+    FENCE_CUDA_TRY(cudaIpcGetMemHandle(&h, m->xbuf));
+    std::memset(out, 0, FENCE_TP_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof h);
+    return FENCE_OK;
+}
+
+extern "C" int fence_tp_connect(fence_model* m, const void* handles, int n_ranks) {
+    if (!m || !handles) return set_error(FENCE_E_ARG, "tp_connect: null argument");
+    if (m->tp_n < 2 || n_ranks != m->tp_n)
+        return set_error(FENCE_E_ARG, "tp_connect: %d handles for a model of tp_size %d", n_ranks, m->tp_n);
+    if (m->tp_connected) return set_error(FENCE_E_ARG, "tp_connect: already connected");
+    cudaSetDevice(m->dev);
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int p = 0; p < n_ranks; ++p) {
+        if (p == m->tp_rank) {
+            m->xpeer[p] = m->xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)p * FENCE_TP_HANDLE_BYTES, sizeof h);
+        void* ptr = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess)
+            return set_error((int)e, "tp_connect: rank %d's exchange buffer: %s", p, cudaGetErrorString(e));
+        m->xpeer[p] = static_cast<uint8_t*>(ptr);
+    }
+    int rc = build_step_phases(m);
+    if (rc != FENCE_OK) return rc;
+    FENCE_CUDA_TRY(cudaDeviceSynchronize());
+    if (m->opts.use_graph) {
+        rc = capture_graph(m);
+        if (rc != FENCE_OK) return rc;
+    }
+    m->tp_connected = 1;
+    return FENCE_OK;
+}
+
 extern "C" int fence_copy_logits(fence_model* m, float* host_out) {
     if (!m || !host_out) return set_error(FENCE_E_ARG, "copy_logits: null argument");
     cudaSetDevice(m->dev);
-    FENCE_CUDA_TRY(cudaMemcpyAsync(host_out, m->logits, (size_t)m->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+    FENCE_CUDA_TRY(cudaMemcpyAsync(host_out, m->logits, (size_t)m->vocab_n * 4, cudaMemcpyDeviceToHost, m->stream));
     FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
     return FENCE_OK;
 }

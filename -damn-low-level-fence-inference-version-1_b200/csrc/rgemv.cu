@@ -9,17 +9,19 @@ namespace fence {
 
 // ------------------------------------------------------------------ repack kernels (load time)
 // GGUF Q6_K rows (block_q6_K, src/kernels/q6k_types.h:27-32) -> q/s/d arrays; row r of the source
-// becomes row dst_row0 + r * dst_stride of the destination (fused QKV, interleaved gate/up).
-__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long rows, int nsb, uint8_t* __restrict__ q,
-                                  uint8_t* __restrict__ s, uint8_t* __restrict__ d, long long dst_row0,
-                                  int dst_stride) {
+// becomes row dst_row0 + r * dst_stride of the destination (fused QKV, interleaved gate/up). The
+// source rows are src_nsb blocks apart; the first nsb blocks from src of each are taken (a column
+// slice when src_nsb > nsb: a tensor-parallel shard of a row-parallel matrix).
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long rows, int nsb, int src_nsb,
+                                  uint8_t* __restrict__ q, uint8_t* __restrict__ s, uint8_t* __restrict__ d,
+                                  long long dst_row0, int dst_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const int I = nsb * 4;
     if (idx >= rows * I) return;
     const long long r = idx / I;
     const int it = (int)(idx - r * I);
     const int j = it >> 2, h = (it >> 1) & 1, l16 = it & 1;
-    const uint8_t* blk = src + ((size_t)r * nsb + j) * 210;
+    const uint8_t* blk = src + ((size_t)r * src_nsb + j) * 210;
     const long long dr = dst_row0 + r * dst_stride;
     uint8_t* qd = q + ((size_t)dr * I + it) * 48;
     for (int e = 0; e < 16; ++e) {
@@ -36,14 +38,16 @@ __global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long row
     }
 }
 
-// GGUF Q8_0 rows (block_q8_0, src/kernels/q8_0_types.h:11-14) -> swizzled q / d arrays.
-__global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long rows, int I, uint8_t* __restrict__ q,
-                                  uint8_t* __restrict__ d, long long dst_row0, int dst_stride) {
+// GGUF Q8_0 rows (block_q8_0, src/kernels/q8_0_types.h:11-14) -> swizzled q / d arrays; source
+// rows src_nb blocks apart, the first 2 I blocks from src of each taken.
+__global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long rows, int I, int src_nb,
+                                  uint8_t* __restrict__ q, uint8_t* __restrict__ d, long long dst_row0,
+                                  int dst_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * I) return;
     const long long r = idx / I;
     const int it = (int)(idx - r * I);
-    const uint8_t* b0 = src + ((size_t)r * 2 * I + 2 * it) * 34;
+    const uint8_t* b0 = src + ((size_t)r * src_nb + 2 * it) * 34;
     const uint8_t* b1 = b0 + 34;
     const long long dr = dst_row0 + r * dst_stride;
     uint8_t* qd = q + ((size_t)dr * I + it) * 64;
@@ -85,18 +89,20 @@ RMat rmat_carve(int wt, long long rows, int K, uint8_t* base) {
     return m;
 }
 
+// src_K: inputs per source row (K for whole rows; the full width for a column slice starting at src).
 cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
-                      int dst_stride, cudaStream_t st) {
+                      int dst_stride, cudaStream_t st, int src_K) {
     const int I = K / 64;
     const long long n = rows * I;
     const int threads = 256;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
+    if (src_K <= 0) src_K = K;
     if (wt == WT_Q6K)
-        repack_q6k_kernel<<<blocks, threads, 0, st>>>(src, rows, K / 256, const_cast<uint8_t*>(m.q),
+        repack_q6k_kernel<<<blocks, threads, 0, st>>>(src, rows, K / 256, src_K / 256, const_cast<uint8_t*>(m.q),
                                                       const_cast<uint8_t*>(m.s), const_cast<uint8_t*>(m.d), dst_row0,
                                                       dst_stride);
     else
-        repack_q80_kernel<<<blocks, threads, 0, st>>>(src, rows, I, const_cast<uint8_t*>(m.q),
+        repack_q80_kernel<<<blocks, threads, 0, st>>>(src, rows, I, src_K / 32, const_cast<uint8_t*>(m.q),
                                                       const_cast<uint8_t*>(m.d), dst_row0, dst_stride);
     return cudaGetLastError();
 }

@@ -53,7 +53,7 @@ static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err
         slot = std::max(slot, ph.g.slot_bytes);
         accf = std::max(accf, ph.g.rows_cta * ph.g.mp);
         int need = ph.g.I * XQ_WORDS * 4;
-        if (ph.embed) need += ph.g.I * 64 * 4;  // fp32 embedding row after the x records
+        if (ph.embed || ph.tp_sum) need += ph.g.I * 64 * 4;  // fp32 x row (embedding / reduced) after the records
         scratch = std::max(scratch, need);
     }
     P.scratch_bytes = (scratch + 15) / 16 * 16;

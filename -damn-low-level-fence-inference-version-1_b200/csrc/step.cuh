@@ -43,6 +43,13 @@ constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
 constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
 constexpr int SK_MAX_R = 64;              // rows per stage
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
+// Exchange buffer of one rank (tensor parallel): reduction counter, argmax counter, one argmax
+// (value bits | index << 32) per rank, then partials [2][tp_n][tp_h] fp32.
+constexpr int SK_TP_MAX = 8;
+constexpr uint32_t SK_XB_RCNT = 0, SK_XB_ACNT = 8, SK_XB_ARG = 256, SK_XB_PART = 1024;
+__host__ __device__ inline size_t sk_xb_bytes(int tp_n, int tp_h) {
+    return SK_XB_PART + (size_t)2 * tp_n * tp_h * 4;
+}
 constexpr int kStepAttnSolo = 128;  // StepArgs::attn_solo used by the engine (a two-tile walk beats split + merge)
 constexpr int SK_WAIT_ERR = -5;           // FENCE_E_DEVICE_WAIT in the device error word
 
@@ -57,6 +64,14 @@ struct __align__(16) SPhase {
     const uint8_t* embd;
     float* hidden_out;
     AttnArgs at;      // attention
+    // tensor parallel (StepArgs::tp_n > 1)
+    int tp_red;       // row-parallel matrix: the epilogue sends its partial rows to every rank's
+                      // exchange buffer (slot red_idx & 1) instead of adding the residual
+    int tp_sum;       // x prologue: x = hin + the ranks' partials of reduction red_idx, summed in
+                      // rank order (identical on every rank); this CTA's share of it goes to hout
+    int red_idx;      // the step's reduction this phase produces (tp_red) or consumes (tp_sum)
+    const float* hin;
+    float* hout;
 };
 
 struct StepArgs {
@@ -77,6 +92,14 @@ struct StepArgs {
     // when the last stage is consumed, and at the end (before the count); SM cycles the consumers
     // waited for filled slots and cycles the producer waited for free slots
     unsigned long long* trace;
+    // tensor parallel: tp_n ranks (one GPU each, one step kernel each), exchanging over NVLink
+    // through every rank's exchange buffer xb[p] (mapped into this process): SK_XB_* layout
+    int tp_n, tp_rank;
+    int tp_h;            // floats per rank per reduction (the hidden size)
+    int n_red;           // reductions per step (2 per layer)
+    int vocab0;          // first vocabulary row of this rank's LM-head shard
+    uint8_t* xb[SK_TP_MAX];
+    unsigned long long* launch;  // steps this rank has finished (read at the start, +1 at the end)
 };
 
 constexpr uint32_t SK_DESC = (sizeof(SPhase) + 15u) & ~15u;  // one phase descriptor in shared memory
@@ -114,6 +137,20 @@ __device__ __forceinline__ unsigned long long sk_ld_acquire(const unsigned long 
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ unsigned long long sk_ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// +v on a (possibly peer-mapped) counter, releasing this thread's earlier writes (and, after a CTA
+// barrier, the CTA's) to every GPU of the system
+__device__ __forceinline__ void sk_red_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Rank p's partials of reduction slot buf, as mapped here: [tp_n][tp_h]
+__device__ __forceinline__ float* sk_xpart(const StepArgs& A, int p, int buf) {
+    return reinterpret_cast<float*>(A.xb[p] + SK_XB_PART) + (size_t)buf * A.tp_n * A.tp_h;
 }
 __device__ __forceinline__ unsigned long long sk_ns() {
     unsigned long long t;
@@ -697,7 +734,8 @@ __device__ __forceinline__ void sk_attn_prefetch_tile0(const AttnArgs& a, int h,
 // Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
 // prefetched at the phase start (rows up to SK_RPRE).
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
-                                             const float* rpre, float& best_v, int& best_i) {
+                                             const float* rpre, float& best_v, int& best_i, const StepArgs& A,
+                                             const SPhase& ph) {
     const int NP = g.np, IP = g.I / g.np, R = g.R, MP = g.mp;
     auto row_sum = [&](int rl) {
         const int n = rg_row_pieces(rl % R, NP, IP);
@@ -716,6 +754,8 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
             const float sum = row_sum(vr);
             if (epi == EPI_STORE) {
                 g.y[row] = g.bias ? sum + g.bias[row] : sum;
+            } else if (epi == EPI_RESID && ph.tp_red) {  // partial row -> every rank (NVLink stores)
+                for (int p = 0; p < A.tp_n; ++p) sk_xpart(A, p, ph.red_idx & 1)[A.tp_rank * A.tp_h + row] = sum;
             } else if (epi == EPI_RESID) {
                 g.resid[row] = sum + (vr < SK_RPRE ? rpre[vr] : g.resid[row]);
             } else {
@@ -839,6 +879,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     float best_v = 0.f;
     int best_i = -1;
     const int pos = A.state->pos;  // fixed for the whole step (advanced only at its very end)
+    const unsigned long long launch0 = A.tp_n > 1 ? *reinterpret_cast<volatile unsigned long long*>(A.launch) : 0ull;
     if (warp == 0) sk_fetch_desc(&A.ph[0], desc, lane);
     named_bar_sync(1, NT);
     bool attn_pre = false;  // this thread issued tile 0 of its CTA's first attention unit
@@ -867,7 +908,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             const RGemvArgs& g = ph.g;
             const SKRows rr = sk_rows(g, c, G);
             const void* xsrc = g.x;
-            if (ph.epi == EPI_RESID) {  // residual rows, needed only by the epilogue: fetch them now
+            if (ph.epi == EPI_RESID && !ph.tp_red) {  // residual rows, needed only by the epilogue: fetch them now
                 const int nvr = rr.v_end - rr.v_begin;
                 if (tid < nvr && tid < SK_RPRE) cp_async4(rpre + tid, g.resid + rr.v_begin + tid);
                 cp_async_commit();
@@ -887,6 +928,36 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 named_bar_sync(1, NT);
                 xsrc = ebuf;
             }
+            if (ph.tp_sum) {
+                // every rank's partials of reduction red_idx have arrived (each of tp_n x G CTAs
+                // counts once per reduction on every rank's counter)
+                if (tid == 0) {
+                    const unsigned long long target =
+                        (launch0 * (unsigned long long)A.n_red + (unsigned long long)ph.red_idx + 1ull) *
+                        (unsigned long long)(A.tp_n * G);
+                    const unsigned long long* cnt = reinterpret_cast<const unsigned long long*>(A.xb[A.tp_rank] + SK_XB_RCNT);
+                    bool ok = false;
+                    for (uint32_t it = 0; it < SK_BAR_SPINS && !*abort_flag; ++it)
+                        if (sk_ld_acquire_sys(cnt) >= target) { ok = true; break; }
+                    if (!ok) {
+                        if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                        *abort_flag = 1;
+                    }
+                }
+                named_bar_sync(1, NT);
+                const int H = A.tp_h;
+                float* hbuf = reinterpret_cast<float*>(scratch + A.scratch_bytes) - H;
+                const float* parts = sk_xpart(A, A.tp_rank, ph.red_idx & 1);
+                const int h0 = (int)((long long)H * c / G), h1 = (int)((long long)H * (c + 1) / G);
+                for (int i = tid; i < H; i += NT) {
+                    float v = __ldcg(ph.hin + i);
+                    for (int p = 0; p < A.tp_n; ++p) v += __ldcg(parts + (size_t)p * H + i);
+                    hbuf[i] = v;
+                    if (i >= h0 && i < h1) ph.hout[i] = v;  // the residual stream, for the next reduction
+                }
+                named_bar_sync(1, NT);
+                xsrc = hbuf;
+            }
             if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
@@ -898,7 +969,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 cp_async_wait_all();
                 named_bar_sync(1, NT);
             }
-            if (!*abort_flag) sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i);
+            if (!*abort_flag) sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph);
             // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
             // records are dead; the next descriptor was fetched at this phase's start)
             if (k + 1 < NPH && tid < ATTN_THREADS) {
@@ -934,6 +1005,11 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 A.trace[((size_t)c * NPH + k) * SK_TRACE + 3] = sk_ns();
                 A.trace[((size_t)c * NPH + k) * SK_TRACE + 4] = wcyc;
             }
+            // tensor parallel: this CTA's partial rows (stored to every rank above) are released
+            // to the system before each rank's reduction counter counts them
+            if (ph.kind == SP_GEMV && ph.tp_red)
+                for (int p = 0; p < A.tp_n; ++p)
+                    sk_red_release_sys(reinterpret_cast<unsigned long long*>(A.xb[p] + SK_XB_RCNT), 1ull);
             // release (cumulative): every consumer write of this CTA, ordered before by the CTA
             // barrier, is visible before the count
             asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(A.bar), "l"(1ull) : "memory");
@@ -980,6 +1056,32 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 }
             }
             if (gi < 0) gi = 0;
+            if (A.tp_n > 1) {
+                // every rank's shard best (value, global vocabulary index) to every rank, then the
+                // best of them (greater value, then smaller index): the same id on every rank
+                gi += A.vocab0;
+                const unsigned long long pair = ((unsigned long long)(unsigned)gi << 32) | __float_as_uint(gv);
+                for (int p = 0; p < A.tp_n; ++p) {
+                    *reinterpret_cast<volatile unsigned long long*>(A.xb[p] + SK_XB_ARG + 8 * A.tp_rank) = pair;
+                    sk_red_release_sys(reinterpret_cast<unsigned long long*>(A.xb[p] + SK_XB_ACNT), 1ull);
+                }
+                const unsigned long long* acnt = reinterpret_cast<const unsigned long long*>(A.xb[A.tp_rank] + SK_XB_ACNT);
+                bool ok = false;
+                for (uint32_t it = 0; it < SK_BAR_SPINS; ++it)
+                    if (sk_ld_acquire_sys(acnt) >= (launch0 + 1ull) * (unsigned long long)A.tp_n) { ok = true; break; }
+                if (!ok) set_device_error(SK_WAIT_ERR);
+                for (int p = 0; p < A.tp_n; ++p) {
+                    const unsigned long long q =
+                        *reinterpret_cast<volatile const unsigned long long*>(A.xb[A.tp_rank] + SK_XB_ARG + 8 * p);
+                    const float qv = __uint_as_float((unsigned)q);
+                    const int qi = (int)(q >> 32);
+                    if (p == 0 || qv > gv || (qv == gv && qi < gi)) {
+                        gv = qv;
+                        gi = qi;
+                    }
+                }
+                *reinterpret_cast<volatile unsigned long long*>(A.launch) = launch0 + 1ull;
+            }
             DecodeState* st = A.state;
             st->token = gi;
             st->pos = st->pos + 1;

@@ -198,7 +198,8 @@ typedef struct fence_load_opts {
     int device;         /* CUDA device ordinal                                            */
     int use_graph;      /* capture the token step in a CUDA graph (default 1)             */
     int verbose;        /* print the reference's load banner                              */
-    /* tensor parallel: rank `tp_rank` of `tp_size`; nccl_comm is an ncclComm_t or NULL */
+    /* tensor parallel: rank `tp_rank` of `tp_size` (see fence_tp_connect); nccl_comm is unused
+     * (the ranks exchange inside the step kernel over NVLink peer memory) and must be NULL */
     int tp_rank, tp_size;
     void* nccl_comm;
     /* 1 (default): the whole token step is one persistent kernel (weights of all phases stream
@@ -243,8 +244,24 @@ int fence_generate(fence_model* m, const int* prompt, int n_prompt, int max_new_
  * the n_steps sampled ids are copied to out_tokens (host) at the end. */
 int fence_decode_greedy(fence_model* m, int token, int pos, int n_steps, int* out_tokens);
 
-/* Last logits / hidden state of the most recent step, copied to host (for parity tests). */
+/* Last logits of the most recent step, copied to host (for parity tests): vocab_size floats, or
+ * under tensor parallelism this rank's vocabulary shard (see fence_tp_connect). */
 int fence_copy_logits(fence_model* m, float* host_out);
+
+/* Tensor parallel (no counterpart in the reference, whose forward is single-GPU; the split is the
+ * Megatron one: q/k/v heads and gate/up rows per rank, o_proj and down by input columns with their
+ * partial rows summed over the ranks, the tied LM head by vocabulary rows). One process per GPU
+ * loads the same GGUF with opts.tp_rank / opts.tp_size (step_kernel = 1); every rank then passes
+ * its handle (FENCE_TP_HANDLE_BYTES, a CUDA IPC handle of its exchange buffer) to the others by
+ * any host channel, and fence_tp_connect(handles of ranks 0..tp_size-1 in rank order) maps the
+ * peers' buffers (NVLink P2P) and builds the step. The ranks must then call fence_forward /
+ * fence_time_decode / fence_decode_greedy in lockstep with the same arguments: each step kernel
+ * sends its partial rows to every rank and waits (bounded) for theirs. fence_forward returns this
+ * rank's vocabulary shard of the logits (rows [tp_rank * ceil(V / tp_size), ...)); the greedy id
+ * is the global one on every rank; fence_sample_nucleus is not available per shard. */
+#define FENCE_TP_HANDLE_BYTES 64
+int fence_tp_handle(fence_model* m, void* out, int cap);
+int fence_tp_connect(fence_model* m, const void* handles, int n_ranks);
 
 /* Times n_steps device-resident decode steps with CUDA events on the engine's stream; *ms = total. */
 int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms);

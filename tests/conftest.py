@@ -15,7 +15,8 @@ def load_pkg():
     """The binding module of libfence_b200.so (its directory name is not a Python identifier)."""
     if "fence_b200" in sys.modules:
         return sys.modules["fence_b200"]
-    spec = importlib.util.spec_from_file_location("fence_b200", os.path.join(PKG_DIR, "__init__.py"))
+    spec = importlib.util.spec_from_file_location("fence_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
     mod = importlib.util.module_from_spec(spec)
     sys.modules["fence_b200"] = mod
     spec.loader.exec_module(mod)

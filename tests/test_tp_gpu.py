@@ -1,0 +1,90 @@
+"""Tensor parallel on 2 GPUs (skipped with fewer): two ranks, one process each, decode the same
+tokens with the model split over them (heads / FFN rows / vocabulary rows per rank, o_proj and
+down partial rows exchanged over NVLink inside every step kernel), against the same model on one
+GPU. The two splits sum the row-parallel partials in a different order, so logits agree to the
+engine's tolerance, not bit for bit; the greedy id is the same on both ranks."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import load_pkg
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_ATOL = 2e-3  # as the engine-vs-oracle bound on the tiny models
+SHAPES = {
+    "tp-q6k": dict(config="tiny-q6k", n_layers=2, embed_dim=1024, ff_dim=2048, n_heads=8, n_kv_heads=4,
+                   vocab_size=2051),
+    "tp-q8": dict(config="tiny-q8", n_layers=2, embed_dim=1024, ff_dim=2048, n_heads=8, n_kv_heads=4,
+                  vocab_size=2051),
+}
+STEPS = 40
+
+
+def _gpus():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tokens():
+    return [int(t) for t in np.random.default_rng(11).integers(0, 2051, STEPS)]
+
+
+def _rank(rank, world, port, path, out_dir, use_graph):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        fb = load_pkg()
+        import fence_b200.tp as tp
+        m = fb.Model(path, max_ctx=256, device=rank, tp_rank=rank, tp_size=world, use_graph=use_graph)
+        tp.connect(m)
+        logits, ids = [], []
+        for pos, t in enumerate(_tokens()):
+            d = m.forward(t, pos)
+            logits.append(m.logits())
+            ids.append(m.sample_greedy(d))
+        dec = m.decode_greedy(ids[-1], STEPS, 24)  # device-resident chain, ranks in lockstep
+        v0, vn = m.vocab_shard()
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), logits=np.stack(logits), ids=np.array(ids),
+                 dec=np.array(dec), v0=v0, vn=vn)
+        m.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+@pytest.mark.parametrize("use_graph", [True, False])
+def test_tp2_matches_single_gpu(fb, tmp_path, shape, use_graph):
+    import torch.multiprocessing as mp
+    kw = dict(SHAPES[shape])
+    cfg = kw.pop("config")
+    path = str(tmp_path / f"{shape}.gguf")
+    fb.synth_write(path, cfg, seed=31, **kw)
+    mp.spawn(_rank, args=(2, _free_port(), path, str(tmp_path), use_graph), nprocs=2, join=True)
+    r = [np.load(tmp_path / f"r{k}.npz") for k in range(2)]
+    assert int(r[0]["v0"]) == 0 and int(r[1]["v0"]) == int(r[0]["vn"])
+    tp_logits = np.concatenate([r[0]["logits"], r[1]["logits"]], axis=1)
+    assert (r[0]["ids"] == r[1]["ids"]).all() and (r[0]["dec"] == r[1]["dec"]).all()
+    m = fb.Model(path, max_ctx=256, device=0)
+    ref, ref_ids = [], []
+    for pos, t in enumerate(_tokens()):
+        d = m.forward(t, pos)
+        ref.append(m.logits())
+        ref_ids.append(m.sample_greedy(d))
+    m.close()
+    ref = np.stack(ref)
+    assert tp_logits.shape == ref.shape
+    np.testing.assert_allclose(tp_logits, ref, rtol=0, atol=LOGIT_ATOL)
+    for k, (a, b) in enumerate(zip(r[0]["ids"], ref_ids)):
+        top2 = np.sort(ref[k])[-2:]
+        if top2[1] - top2[0] > 2 * LOGIT_ATOL:
+            assert a == b, (k, a, b)
