@@ -408,9 +408,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         set_error(FENCE_E_ARG, "model_load: null path");
         return nullptr;
     }
-    if (opts.tp_size > 1 && (opts.tp_size > SK_TP_MAX || opts.tp_rank < 0 || opts.tp_rank >= opts.tp_size)) {
-        set_error(FENCE_E_ARG, "model_load: tp_rank %d / tp_size %d (at most %d ranks)", opts.tp_rank, opts.tp_size,
-                  SK_TP_MAX);
+    if (opts.tp_size > 1 && ((opts.tp_size != 2 && opts.tp_size != 4 && opts.tp_size != 8) || opts.tp_rank < 0 ||
+                             opts.tp_rank >= opts.tp_size)) {
+        set_error(FENCE_E_ARG, "model_load: tp_rank %d / tp_size %d (tp_size 2, 4 or 8)", opts.tp_rank, opts.tp_size);
         return nullptr;
     }
     if (opts.tp_size > 1 && !opts.step_kernel) {
@@ -736,7 +736,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         ph.xm = xm;
         ph.epi = epi;
         ph.p = plan_rgemv(ph.a, sms, smem_budget);
-        return ph.p.ok != 0;
+        // the per-phase kernel's plan (its own 224-lane geometry) matters only without the step
+        // kernel, which plans every phase itself (plan_step)
+        return ph.p.ok != 0 || opts.step_kernel != 0;
     };
 
     m->launches.resize(c.n_layers);

@@ -43,12 +43,15 @@ constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
 constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
 constexpr int SK_MAX_R = 64;              // rows per stage
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
-// Exchange buffer of one rank (tensor parallel): reduction counter, argmax counter, one argmax
-// (value bits | index << 32) per rank, then partials [2][tp_n][tp_h] fp32.
+// Exchange buffer of one rank (tensor parallel): an argmax counter, one argmax (value bits |
+// index << 32) per rank, then partials [2][tp_h][tp_n] (a row's ranks adjacent), each a 64-bit
+// (value bits | tag << 32)
+// stored with one 8-byte access: the tag (the step's reduction number, never 0) tells a reader
+// that the value is this reduction's, so no fence or counter sits between the ranks' partials.
 constexpr int SK_TP_MAX = 8;
-constexpr uint32_t SK_XB_RCNT = 0, SK_XB_ACNT = 8, SK_XB_ARG = 256, SK_XB_PART = 1024;
+constexpr uint32_t SK_XB_ACNT = 8, SK_XB_ARG = 256, SK_XB_PART = 1024;
 __host__ __device__ inline size_t sk_xb_bytes(int tp_n, int tp_h) {
-    return SK_XB_PART + (size_t)2 * tp_n * tp_h * 4;
+    return SK_XB_PART + (size_t)2 * tp_n * tp_h * 8;
 }
 constexpr int kStepAttnSolo = 128;  // StepArgs::attn_solo used by the engine (a two-tile walk beats split + merge)
 constexpr int SK_WAIT_ERR = -5;           // FENCE_E_DEVICE_WAIT in the device error word
@@ -148,9 +151,21 @@ __device__ __forceinline__ unsigned long long sk_ld_acquire_sys(const unsigned l
 __device__ __forceinline__ void sk_red_release_sys(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Rank p's partials of reduction slot buf, as mapped here: [tp_n][tp_h]
-__device__ __forceinline__ float* sk_xpart(const StepArgs& A, int p, int buf) {
-    return reinterpret_cast<float*>(A.xb[p] + SK_XB_PART) + (size_t)buf * A.tp_n * A.tp_h;
+// Rank p's tagged partials of reduction slot buf, as mapped here: [tp_h][tp_n]
+__device__ __forceinline__ unsigned long long* sk_xpart(const StepArgs& A, int p, int buf) {
+    return reinterpret_cast<unsigned long long*>(A.xb[p] + SK_XB_PART) + (size_t)buf * A.tp_n * A.tp_h;
+}
+__device__ __forceinline__ void sk_st_sys64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long sk_ld_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// The tag of reduction red of the step counted launch0 (1-based, so a zeroed buffer never matches).
+__device__ __forceinline__ unsigned sk_red_tag(const StepArgs& A, unsigned long long launch0, int red) {
+    return (unsigned)(launch0 * (unsigned long long)A.n_red + (unsigned long long)red) + 1u;
 }
 __device__ __forceinline__ unsigned long long sk_ns() {
     unsigned long long t;
@@ -731,11 +746,37 @@ __device__ __forceinline__ void sk_attn_prefetch_tile0(const AttnArgs& a, int h,
     cp_async_commit();
 }
 
+// x of a phase after a tensor-parallel reduction: hbuf[i] = hin[i] + sum over ranks (rank order)
+// of the tagged partials of row i (adjacent in memory); rows [h0, h1) also to hout (this CTA's
+// share of the residual stream). A pass reads every row with no load depending on another (four
+// rows of a thread in flight together); passes repeat, bounded, until every tag matched.
+template <int N>
+__device__ __forceinline__ bool sk_tp_gather(const float* hin, float* hout, const unsigned long long* parts,
+                                             unsigned tag, float* hbuf, int H, int h0, int h1) {
+    for (uint32_t pass = 0; pass < SK_BAR_SPINS; ++pass) {
+        bool bad = false;
+#pragma unroll 4
+        for (int i = (int)threadIdx.x; i < H; i += SK_NL) {
+            float v = __ldcg(hin + i);
+#pragma unroll
+            for (int p = 0; p < N; ++p) {
+                const unsigned long long w = sk_ld_sys64(parts + (size_t)i * N + p);
+                bad |= (unsigned)(w >> 32) != tag;
+                v += __uint_as_float((unsigned)w);
+            }
+            hbuf[i] = v;
+            if (i >= h0 && i < h1) hout[i] = v;  // the residual stream, for the next reduction
+        }
+        if (!bad) return true;
+    }
+    return false;
+}
+
 // Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
 // prefetched at the phase start (rows up to SK_RPRE).
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
                                              const float* rpre, float& best_v, int& best_i, const StepArgs& A,
-                                             const SPhase& ph) {
+                                             const SPhase& ph, unsigned tag) {
     const int NP = g.np, IP = g.I / g.np, R = g.R, MP = g.mp;
     auto row_sum = [&](int rl) {
         const int n = rg_row_pieces(rl % R, NP, IP);
@@ -754,8 +795,9 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
             const float sum = row_sum(vr);
             if (epi == EPI_STORE) {
                 g.y[row] = g.bias ? sum + g.bias[row] : sum;
-            } else if (epi == EPI_RESID && ph.tp_red) {  // partial row -> every rank (NVLink stores)
-                for (int p = 0; p < A.tp_n; ++p) sk_xpart(A, p, ph.red_idx & 1)[A.tp_rank * A.tp_h + row] = sum;
+            } else if (epi == EPI_RESID && ph.tp_red) {  // tagged partial row -> every rank (NVLink stores)
+                const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(sum);
+                for (int p = 0; p < A.tp_n; ++p) sk_st_sys64(sk_xpart(A, p, ph.red_idx & 1) + (size_t)row * A.tp_n + A.tp_rank, v);
             } else if (epi == EPI_RESID) {
                 g.resid[row] = sum + (vr < SK_RPRE ? rpre[vr] : g.resid[row]);
             } else {
@@ -929,31 +971,22 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 xsrc = ebuf;
             }
             if (ph.tp_sum) {
-                // every rank's partials of reduction red_idx have arrived (each of tp_n x G CTAs
-                // counts once per reduction on every rank's counter)
-                if (tid == 0) {
-                    const unsigned long long target =
-                        (launch0 * (unsigned long long)A.n_red + (unsigned long long)ph.red_idx + 1ull) *
-                        (unsigned long long)(A.tp_n * G);
-                    const unsigned long long* cnt = reinterpret_cast<const unsigned long long*>(A.xb[A.tp_rank] + SK_XB_RCNT);
-                    bool ok = false;
-                    for (uint32_t it = 0; it < SK_BAR_SPINS && !*abort_flag; ++it)
-                        if (sk_ld_acquire_sys(cnt) >= target) { ok = true; break; }
-                    if (!ok) {
-                        if (!*abort_flag) set_device_error(SK_WAIT_ERR);
-                        *abort_flag = 1;
-                    }
-                }
-                named_bar_sync(1, NT);
+                // x = hin + every rank's partial of reduction red_idx, in rank order; a partial is
+                // used once its tag matches (bounded spin per element)
                 const int H = A.tp_h;
                 float* hbuf = reinterpret_cast<float*>(scratch + A.scratch_bytes) - H;
-                const float* parts = sk_xpart(A, A.tp_rank, ph.red_idx & 1);
+                const unsigned long long* parts = sk_xpart(A, A.tp_rank, ph.red_idx & 1);
+                const unsigned tag = sk_red_tag(A, launch0, ph.red_idx);
                 const int h0 = (int)((long long)H * c / G), h1 = (int)((long long)H * (c + 1) / G);
-                for (int i = tid; i < H; i += NT) {
-                    float v = __ldcg(ph.hin + i);
-                    for (int p = 0; p < A.tp_n; ++p) v += __ldcg(parts + (size_t)p * H + i);
-                    hbuf[i] = v;
-                    if (i >= h0 && i < h1) ph.hout[i] = v;  // the residual stream, for the next reduction
+                bool ok;
+                switch (A.tp_n) {
+                    case 2: ok = sk_tp_gather<2>(ph.hin, ph.hout, parts, tag, hbuf, H, h0, h1); break;
+                    case 4: ok = sk_tp_gather<4>(ph.hin, ph.hout, parts, tag, hbuf, H, h0, h1); break;
+                    default: ok = sk_tp_gather<8>(ph.hin, ph.hout, parts, tag, hbuf, H, h0, h1); break;
+                }
+                if (!ok) {
+                    set_device_error(SK_WAIT_ERR);
+                    *abort_flag = 1;
                 }
                 named_bar_sync(1, NT);
                 xsrc = hbuf;
@@ -969,7 +1002,9 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 cp_async_wait_all();
                 named_bar_sync(1, NT);
             }
-            if (!*abort_flag) sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph);
+            if (!*abort_flag)
+                sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph,
+                             ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
             // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
             // records are dead; the next descriptor was fetched at this phase's start)
             if (k + 1 < NPH && tid < ATTN_THREADS) {
@@ -1005,11 +1040,6 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 A.trace[((size_t)c * NPH + k) * SK_TRACE + 3] = sk_ns();
                 A.trace[((size_t)c * NPH + k) * SK_TRACE + 4] = wcyc;
             }
-            // tensor parallel: this CTA's partial rows (stored to every rank above) are released
-            // to the system before each rank's reduction counter counts them
-            if (ph.kind == SP_GEMV && ph.tp_red)
-                for (int p = 0; p < A.tp_n; ++p)
-                    sk_red_release_sys(reinterpret_cast<unsigned long long*>(A.xb[p] + SK_XB_RCNT), 1ull);
             // release (cumulative): every consumer write of this CTA, ordered before by the CTA
             // barrier, is visible before the count
             asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(A.bar), "l"(1ull) : "memory");

@@ -19,8 +19,8 @@ GGML_Q6_K, GGML_Q8_0 = 14, 8
 def shard_plan(n_heads: int, n_kv_heads: int, head_dim: int, ff_dim: int, vocab: int, rank: int, size: int,
                o_type: int = GGML_Q6_K, down_type: int = GGML_Q6_K) -> dict:
     """Rows / columns of one rank's shard; raises ValueError where the engine refuses to load."""
-    if not 0 <= rank < size or size > 8:
-        raise ValueError(f"rank {rank} of {size} (at most 8 ranks)")
+    if size not in (1, 2, 4, 8) or not 0 <= rank < size:
+        raise ValueError(f"rank {rank} of {size} (tp_size 1, 2, 4 or 8)")
     if n_heads % size or n_kv_heads % size or ff_dim % size:
         raise ValueError("heads / FFN rows do not split evenly")
     qd, kvd, F = n_heads * head_dim // size, n_kv_heads * head_dim // size, ff_dim // size

@@ -4,11 +4,13 @@ kernel of the decode loop) against measured HBM bandwidth; the drop-in config-0 
 reported beside it (gemv_config0), with the CPU baseline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
-                  [--prompt P] [--layers L]
+                  [--prompt P] [--layers L] [--tp]
 
 --prompt sets the prefill length (default: the config's own, 128 / 4000 / 512 for configs 1 / 2 / 3);
 --layers cuts the model to L layers for small ncu captures only (the line then names the layer
-count and is not a measurement of the config).
+count and is not a measurement of the config). --tp (with N > 1 ranks) splits ONE model over the
+ranks (tensor parallel, config 3: `--config qwen3-14b --tp`): value = that one sequence's tokens/s,
+scaling "strong"; without it the N ranks are independent replicas (configs 1 and 2).
 
 One JSON line is printed by rank 0. A step is one decode token (batch 1). Inputs are synthetic
 (seeded random-init GGUF of the config's exact shapes; no checkpoints exist offline). With N > 1,
@@ -227,6 +229,9 @@ def main():
     ap.add_argument("--config", default="qwen3-4b")
     ap.add_argument("--prompt", type=int, default=None, help="prefill tokens (default: the config's own)")
     ap.add_argument("--layers", type=int, default=0, help="cut the model to this many layers (ncu captures)")
+    ap.add_argument("--tp", action="store_true",
+                    help="with N > 1: one model split over the N ranks (tensor parallel, strong scaling) instead "
+                         "of N independent replicas (the default for configs 1 and 2)")
     ap.add_argument("--kv", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--tmp", default=None, help="directory for the synthetic GGUF (default: /dev/shm if roomy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -274,9 +279,15 @@ def main():
         kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
         total_pos = args.prompt + args.warmup + args.steps + 8
         max_ctx = max(4096, total_pos)
-        model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local)
+        tp = args.tp and world > 1
+        if tp:
+            model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world)
+            import fence_b200.tp as fbtp
+            fbtp.connect(model, dist.new_group(backend="gloo"))
+        else:
+            model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local)
         cfg = model.config
-        rng = np.random.default_rng(7 + rank)
+        rng = np.random.default_rng(7 if tp else 7 + rank)  # tensor parallel: every rank feeds the same tokens
         prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, args.prompt)]
         # prefill (token by token, as the reference) — untimed
         d = None
@@ -302,7 +313,7 @@ def main():
             dist.barrier()
         pos += args.steps
         tok_s = args.steps / (ms / 1e3)
-        value = tok_s * world
+        value = tok_s if tp else tok_s * world  # one sequence over all ranks / one per replica
 
         # e2e through the reference-facing API: forward(token, pos) from the host (16-byte state
         # H2D from pinned memory) + sample_greedy (4-byte id D2H + sync) every step
@@ -315,7 +326,7 @@ def main():
             dl = model.forward(nxt, e2e_pos + i)
             nxt = model.sample_greedy(dl)
         e2e_s = time.perf_counter() - t0
-        e2e_val = e2e_steps / e2e_s * world
+        e2e_val = e2e_steps / e2e_s * (1 if tp else world)
         step_bytes = step_algorithmic_bytes(cfg, range(pos - args.steps, pos))
         model.close()
 
@@ -341,13 +352,13 @@ def main():
     line = {
         "metric": "decode_tokens_per_s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint16",
+        "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8xint16",
         "data": "synthetic (seeded random-init GGUF, config shapes)",
         "config": {"workload": f"{args.config} batch-1 greedy decode, {args.prompt} prompt tokens, positions "
                                f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}"
                                + (f" ({args.layers}-layer cut for profiling, not the config)" if args.layers else ""),
                    "model": args.config, "kv_cache": args.kv, "global_batch": world, "seq_len": total_pos,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
                    "l2": "weights larger than L2 (no flush needed)"},
         "roofline": {"bound": "hbm", "kernel": "step_kernel (one launch = one whole token step)",
                      "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
