@@ -72,9 +72,9 @@ static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err
     return P;
 }
 
-template <typename KVT>
-static cudaError_t launch_step(const StepArgs& a, const StepPlan& P, cudaStream_t st) {
-    auto kern = step_kernel<KVT>;
+template <typename KVT, bool TP>
+static cudaError_t launch_step_k(const StepArgs& a, const StepPlan& P, cudaStream_t st) {
+    auto kern = step_kernel<KVT, TP>;
     static int smem_set[64] = {};  // per device: largest dynamic smem enabled so far
     int dev = 0;
     cudaGetDevice(&dev);
@@ -99,6 +99,11 @@ static cudaError_t launch_step(const StepArgs& a, const StepPlan& P, cudaStream_
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+template <typename KVT>
+static cudaError_t launch_step(const StepArgs& a, const StepPlan& P, cudaStream_t st) {
+    return a.tp_n > 1 ? launch_step_k<KVT, true>(a, P, st) : launch_step_k<KVT, false>(a, P, st);
 }
 
 }  // namespace fence

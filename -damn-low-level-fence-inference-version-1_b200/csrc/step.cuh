@@ -774,6 +774,7 @@ __device__ __forceinline__ bool sk_tp_gather(const float* hin, float* hout, cons
 
 // Epilogues of a GEMV phase, one consumer thread per virtual row; rpre holds the residual rows
 // prefetched at the phase start (rows up to SK_RPRE).
+template <bool TP>
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
                                              const float* rpre, float& best_v, int& best_i, const StepArgs& A,
                                              const SPhase& ph, unsigned tag) {
@@ -795,7 +796,7 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
             const float sum = row_sum(vr);
             if (epi == EPI_STORE) {
                 g.y[row] = g.bias ? sum + g.bias[row] : sum;
-            } else if (epi == EPI_RESID && ph.tp_red) {  // tagged partial row -> every rank (NVLink stores)
+            } else if (TP && epi == EPI_RESID && ph.tp_red) {  // tagged partial row -> every rank (NVLink stores)
                 const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(sum);
                 for (int p = 0; p < A.tp_n; ++p) sk_st_sys64(sk_xpart(A, p, ph.red_idx & 1) + (size_t)row * A.tp_n + A.tp_rank, v);
             } else if (epi == EPI_RESID) {
@@ -811,7 +812,8 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
     }
 }
 
-template <typename KVT>
+// TP: tensor-parallel build (StepArgs::tp_n > 1); the single-GPU build carries none of its code.
+template <typename KVT, bool TP>
 __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ StepArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -921,7 +923,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     float best_v = 0.f;
     int best_i = -1;
     const int pos = A.state->pos;  // fixed for the whole step (advanced only at its very end)
-    const unsigned long long launch0 = A.tp_n > 1 ? *reinterpret_cast<volatile unsigned long long*>(A.launch) : 0ull;
+    const unsigned long long launch0 = TP ? *reinterpret_cast<volatile unsigned long long*>(A.launch) : 0ull;
     if (warp == 0) sk_fetch_desc(&A.ph[0], desc, lane);
     named_bar_sync(1, NT);
     bool attn_pre = false;  // this thread issued tile 0 of its CTA's first attention unit
@@ -950,7 +952,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             const RGemvArgs& g = ph.g;
             const SKRows rr = sk_rows(g, c, G);
             const void* xsrc = g.x;
-            if (ph.epi == EPI_RESID && !ph.tp_red) {  // residual rows, needed only by the epilogue: fetch them now
+            if (ph.epi == EPI_RESID && !(TP && ph.tp_red)) {  // residual rows, needed only by the epilogue: fetch them now
                 const int nvr = rr.v_end - rr.v_begin;
                 if (tid < nvr && tid < SK_RPRE) cp_async4(rpre + tid, g.resid + rr.v_begin + tid);
                 cp_async_commit();
@@ -970,7 +972,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 named_bar_sync(1, NT);
                 xsrc = ebuf;
             }
-            if (ph.tp_sum) {
+            if (TP && ph.tp_sum) {
                 // x = hin + every rank's partial of reduction red_idx, in rank order; a partial is
                 // used once its tag matches (bounded spin per element)
                 const int H = A.tp_h;
@@ -1003,8 +1005,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 named_bar_sync(1, NT);
             }
             if (!*abort_flag)
-                sk_epilogues(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph,
-                             ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
+                sk_epilogues<TP>(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph,
+                                 TP && ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
             // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
             // records are dead; the next descriptor was fetched at this phase's start)
             if (k + 1 < NPH && tid < ATTN_THREADS) {
@@ -1086,7 +1088,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 }
             }
             if (gi < 0) gi = 0;
-            if (A.tp_n > 1) {
+            if (TP) {
                 // every rank's shard best (value, global vocabulary index) to every rank, then the
                 // best of them (greater value, then smaller index): the same id on every rank
                 gi += A.vocab0;
