@@ -273,17 +273,28 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     fb = _load_pkg()
+    tp = args.tp and world > 1
     with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
-        # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
-        path = synth_model(fb, args.config, tmp, args.layers)
+        if tp:
+            # one model file for all ranks: rank 0 writes it, the others read it (same host)
+            gloo = dist.new_group(backend="gloo")
+            box = [tmp]
+            dist.broadcast_object_list(box, src=0, group=gloo)
+            path = os.path.join(box[0], f"{args.config}.gguf")
+            if rank == 0:
+                synth_model(fb, args.config, box[0], args.layers)
+            dist.barrier(group=gloo)
+        else:
+            # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
+            path = synth_model(fb, args.config, tmp, args.layers)
         kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
         total_pos = args.prompt + args.warmup + args.steps + 8
         max_ctx = max(4096, total_pos)
-        tp = args.tp and world > 1
         if tp:
             model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world)
             import fence_b200.tp as fbtp
-            fbtp.connect(model, dist.new_group(backend="gloo"))
+            fbtp.connect(model, gloo)
+            dist.barrier(group=gloo)  # every rank has read the file before rank 0 removes it
         else:
             model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local)
         cfg = model.config
