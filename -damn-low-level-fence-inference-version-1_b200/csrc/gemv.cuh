@@ -558,7 +558,8 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
             if (s >= a.ring) {
                 int ok = 0;
                 if (lane == 0) {
-                    for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                    ok = mbar_try_wait(&empty[slot], ((s / a.ring) - 1) & 1) ? 1 : 0;
+                    for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
                         if (mbar_try_wait(&empty[slot], ((s / a.ring) - 1) & 1)) { ok = 1; break; }
                     if (!ok) {
                         if (!*abort_flag) set_device_error(-5);
@@ -660,15 +661,15 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
         const int va = v_begin + s * S;
         const int n = min(S, v_end - va);
 
-        bool ok = !*abort_flag;
-        if (ok) {
-            bool got = false;
+        // fast path: one try; the abort flag (a shared-memory load queued behind the weight
+        // loads) is read only when the slot is not full yet
+        bool ok = mbar_try_wait(&full[slot], (s / a.ring) & 1);
+        if (!ok && !*abort_flag) {
             for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
-                if (mbar_try_wait(&full[slot], (s / a.ring) & 1)) { got = true; break; }
-            if (!got) {
+                if (mbar_try_wait(&full[slot], (s / a.ring) & 1)) { ok = true; break; }
+            if (!ok) {
                 if (!*abort_flag) set_device_error(-5);
                 *abort_flag = 1;
-                ok = false;
             }
         }
         // batches are dealt to warps round-robin over the CTA's whole row range (a stage may hold

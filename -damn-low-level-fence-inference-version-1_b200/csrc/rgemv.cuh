@@ -425,8 +425,8 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
             for (int s = 0; s < nstages; ++s) {
                 const int slot = s % ring;
                 if (s >= ring) {
-                    bool ok = false;
-                    for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                    bool ok = mbar_try_wait(&empty[slot], ((s / ring) - 1) & 1);
+                    for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
                         if (mbar_try_wait(&empty[slot], ((s / ring) - 1) & 1)) { ok = true; break; }
                     if (!ok) {
                         if (!*abort_flag) set_device_error(-5);
@@ -571,15 +571,15 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
         const int nv = min(S, v_end - v0);
         const long long row0 = dual ? 2ll * v0 : v0;
         const int nrows = dual ? 2 * nv : nv;
-        bool ok = !*abort_flag;
-        if (ok) {
-            bool got = false;
+        // fast path: one try; the abort flag (a shared-memory load queued behind the weight
+        // loads) is read only when the slot is not full yet
+        bool ok = mbar_try_wait(&full[slot], (s / ring) & 1);
+        if (!ok && !*abort_flag) {
             for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
-                if (mbar_try_wait(&full[slot], (s / ring) & 1)) { got = true; break; }
-            if (!got) {
+                if (mbar_try_wait(&full[slot], (s / ring) & 1)) { ok = true; break; }
+            if (!ok) {
                 if (!*abort_flag) set_device_error(-5);
                 *abort_flag = 1;
-                ok = false;
             }
         }
         const bool on = ok && lane_on && rs < nrows;

@@ -300,21 +300,21 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
     const uint32_t d_off = SS.d_off + (q6 ? (uint32_t)(rs * (I / 4) + (it >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
     const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
     const uint32_t ring_u = (uint32_t)ring;
+    uint32_t slot = use % ring_u, par = (use / ring_u) & 1u;  // advanced incrementally below
     for (int s = 0; s < nstages; ++s, ++use) {
-        const uint32_t slot = use % ring_u;
         const long long row0 = rr.r_begin + (long long)s * R;
         const int nrows = (int)min((long long)R, rr.r_end - row0);
-        bool ok = !*abort_flag;
-        if (ok) {
+        // fast path: the slot is usually full already (one try; the abort flag, a shared-memory
+        // load queued behind the other warps' weight loads, is read only when it is not)
+        bool ok = mbar_try_wait(&full[slot], par);
+        if (!ok && !*abort_flag) {
             const long long w0 = timing ? clock64() : 0;
-            bool got = false;
             for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
-                if (mbar_try_wait(&full[slot], (use / ring_u) & 1)) { got = true; break; }
+                if (mbar_try_wait(&full[slot], par)) { ok = true; break; }
             if (timing) wait_cycles += (unsigned long long)(clock64() - w0);
-            if (!got) {
+            if (!ok) {
                 if (!*abort_flag) set_device_error(SK_WAIT_ERR);
                 *abort_flag = 1;
-                ok = false;
             }
         }
         const bool on = ok && lane_on && rs < nrows;
@@ -333,6 +333,10 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
         if (on && head) acc[(size_t)(row0 - rr.r_begin + rs) * MP + pidx] = v;
+        if (++slot == ring_u) {
+            slot = 0;
+            par ^= 1u;
+        }
     }
     return use;
 }
@@ -881,8 +885,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                     const int slot = use % ring;
                     if (use >= (uint32_t)ring) {
                         const long long w0 = A.trace ? clock64() : 0;
-                        bool ok = false;
-                        for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                        bool ok = mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1);
+                        for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
                             if (mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1)) { ok = true; break; }
                         if (A.trace) pwait += (unsigned long long)(clock64() - w0);
                         if (!ok) {
@@ -937,8 +941,10 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 // visible to this thread and, through the CTA barrier below, to the whole CTA
                 const unsigned long long target = base + (unsigned long long)k * G;
                 bool ok = false;
-                for (uint32_t it = 0; it < SK_BAR_SPINS && !*abort_flag; ++it)
+                for (uint32_t it = 0; it < SK_BAR_SPINS; ++it) {
                     if (sk_ld_acquire(A.bar) >= target) { ok = true; break; }
+                    if ((it & 63u) == 63u && *abort_flag) break;
+                }
                 if (!ok) {
                     if (!*abort_flag) set_device_error(SK_WAIT_ERR);
                     *abort_flag = 1;
