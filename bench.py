@@ -145,9 +145,10 @@ def synth_model(fb, config, tmp, layers=0):
 
 def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
     """Config-0 Q6_K GEMV (4096x4096) through the drop-in C-ABI, rotating over `copies` weight
-    copies (> L2) so every launch streams from HBM; CUDA events on the launching stream. With
-    pdl=True the launches use FENCE_LAUNCH_PDL (weights are never written), so each GEMV starts
-    streaming while the previous one drains, as inside the decode step."""
+    copies (> L2) so every launch streams from HBM: one launch per copy captured in a CUDA graph,
+    the graph replayed back to back; CUDA events on the replay stream. With pdl=True the launches
+    use FENCE_LAUNCH_PDL (weights are never written), so each GEMV starts streaming while the
+    previous one drains, as inside the decode step."""
     fb.lib().fence_set_launch_flags(fb.FENCE_LAUNCH_PDL if pdl else 0)
     M = K = 4096
     nblk = M * K // 256
@@ -157,21 +158,30 @@ def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
     x = np.random.default_rng(0).standard_normal(K).astype(np.float32).astype(np.float16).view(np.int16)
     dx = torch.from_numpy(x.copy()).cuda()
     dy = torch.empty(M, dtype=torch.float32, device="cuda")
-    st = torch.cuda.current_stream()
-    sptr = st.cuda_stream
     L = fb.lib()
-    for i in range(copies):  # warm-up
-        fb.check(L.fence_gemv_q6k(dW[i].data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, sptr))
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for i in range(copies):  # warm-up (and the kernel's shared-memory attribute) outside capture
+            fb.check(L.fence_gemv_q6k(dW[i].data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, st.cuda_stream))
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for i in range(launches):
-        L.fence_gemv_q6k(dW[i % copies].data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, sptr)
-    e1.record(st)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(copies):
+            fb.check(L.fence_gemv_q6k(dW[i].data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K,
+                                      torch.cuda.current_stream().cuda_stream))
+    reps = max(1, launches // copies)
+    with torch.cuda.stream(st):
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            g.replay()
+        e1.record(st)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / launches
+    ms = e0.elapsed_time(e1) / (reps * copies)
     fb.lib().fence_set_launch_flags(0)
-    del dW
+    del g, dW
     return ms
 
 
@@ -376,7 +386,7 @@ def main():
                      "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind,
                      "traffic": step_traffic, "us_per_launch": round(step_us, 2),
                      "algorithmic_bytes_per_launch": step_bytes},
-        "gemv_config0": {"kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches",
+        "gemv_config0": {"kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches in a CUDA graph",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
                          "traffic": traffic_from_profiles("gemv_q6k_config0.md"),
