@@ -298,7 +298,8 @@ def main():
             # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
             path = synth_model(fb, args.config, tmp, args.layers)
         kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
-        total_pos = args.prompt + args.warmup + args.steps + 8
+        e2e_steps = min(args.steps, max(16, args.steps // 2))
+        total_pos = args.prompt + args.warmup + args.steps + e2e_steps + 8
         max_ctx = max(4096, total_pos)
         if tp:
             model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world)
@@ -338,7 +339,6 @@ def main():
 
         # e2e through the reference-facing API: forward(token, pos) from the host (16-byte state
         # H2D from pinned memory) + sample_greedy (4-byte id D2H + sync) every step
-        e2e_steps = min(args.steps, max(16, args.steps // 2))
         e2e_pos = pos
         nxt = tok
         torch.cuda.synchronize()
