@@ -31,10 +31,10 @@
 
 namespace fence {
 
-size_t rmat_bytes(int wt, long long rows, int K);
-RMat rmat_carve(int wt, long long rows, int K, uint8_t* base);
+size_t rmat_bytes(int wt, long long rows, int K, int iph = 0);
+RMat rmat_carve(int wt, long long rows, int K, uint8_t* base, int iph = 0);
 cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
-                      int dst_stride, cudaStream_t st, int src_K = 0);
+                      int dst_stride, cudaStream_t st, int src_K = 0, int item0 = 0);
 RGemvPlan plan_rgemv(RGemvArgs& a, int sms, int smem_budget);
 cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
@@ -685,21 +685,25 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     const long long QKVR = (long long)(qdl + 2 * kvdl);
     size_t rbytes = rmat_bytes(WT_Q80, vn, (int)H);
     size_t shard_bytes = (size_t)vn * (H / 32) * 34;  // LM-head shard (+ the layers' shards below)
-    auto raw_row = [](int t, uint64_t K) { return t == 14 ? K / 256 * 210 : K / 32 * 34; };
+    auto raw_row = [](int t, uint64_t K) { return t == 14 ? (K * 210 + 255) / 256 : K / 32 * 34; };
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
-        rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) + rmat_bytes(wt_of(w.t_o), (long long)H, (int)qdl) +
-                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)Fl, (int)H) + rmat_bytes(wt_of(w.t_down), (long long)H, (int)Fl);
+        rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) +
+                  rmat_bytes(wt_of(w.t_o), (long long)H, (int)qdl, (int)((TPR * qdl / 64) & 3)) +
+                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)Fl, (int)H) +
+                  rmat_bytes(wt_of(w.t_down), (long long)H, (int)Fl, (int)((TPR * Fl / 64) & 3));
         shard_bytes += QKVR * raw_row(w.t_qkv, H) + H * raw_row(w.t_o, qdl) + 2 * Fl * raw_row(w.t_gu, H) +
                        H * raw_row(w.t_down, Fl);
     }
     // Q8_0 rows only need 64-element items; Q6_K super-blocks need 256 (a rank's column slice too)
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
-        if ((w.t_qkv == 14 && H % 256) || (w.t_o == 14 && qdl % 256) || (w.t_gu == 14 && H % 256) ||
-            (w.t_down == 14 && Fl % 256) || qdl % 64 || Fl % 64 || H % 64)
+        // (a rank's o_proj / down column slice needs whole 64-input items only: a Q6_K super-block
+        // cut between two ranks has its d in both ranks' rows)
+        if ((w.t_qkv == 14 && H % 256) || (w.t_o == 14 && qd % 256) || (w.t_gu == 14 && H % 256) ||
+            (w.t_down == 14 && F % 256) || qdl % 64 || Fl % 64 || H % 64)
             return bail(FENCE_E_UNSUPPORTED, TPN > 1 ? "model_load: a rank's o_proj / down column slice is not a whole "
-                                                       "number of quant blocks (choose another tp_size)"
+                                                       "number of 64-input items (choose another tp_size)"
                                                      : "model_load: linear input width not a multiple of the block size");
     }
     if (TPN > 1) c.weight_bytes = shard_bytes;
@@ -710,9 +714,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     // two CTAs share an SM (a phase and the next, under programmatic dependent launch)
     const int smem_budget = smem_sm / 2 - 2048;
     uint8_t* rp = m->rarena;
-    auto carve = [&](int wt, long long rows, int K) {
-        RMat r = rmat_carve(wt, rows, K, rp);
-        rp += rmat_bytes(wt, rows, K);
+    auto carve = [&](int wt, long long rows, int K, int iph) {
+        RMat r = rmat_carve(wt, rows, K, rp, iph);
+        rp += rmat_bytes(wt, rows, K, iph);
         return r;
     };
     bool any_bias = false;
@@ -747,19 +751,19 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
         const int wq = wt_of(w.t_qkv), wo = wt_of(w.t_o), wg = wt_of(w.t_gu), wd = wt_of(w.t_down);
-        const RMat rq = carve(wq, QKVR, (int)H), ro = carve(wo, (long long)H, (int)qdl),
-                   rg = carve(wg, 2 * (long long)Fl, (int)H), rd = carve(wd, (long long)H, (int)Fl);
+        const int o_item0 = (int)(TPR * qdl / 64), d_item0 = (int)(TPR * Fl / 64);
+        const RMat rq = carve(wq, QKVR, (int)H, 0), ro = carve(wo, (long long)H, (int)qdl, o_item0 & 3),
+                   rg = carve(wg, 2 * (long long)Fl, (int)H, 0), rd = carve(wd, (long long)H, (int)Fl, d_item0 & 3);
         // this rank's rows (q/k/v heads, FFN rows) and input columns (o_proj, down)
         const uint64_t rq_b = raw_row(w.t_qkv, H), rg_b = raw_row(w.t_gu, H);
-        const uint8_t* o_src = w.o + raw_row(w.t_o, TPR * qdl);
-        const uint8_t* d_src = w.down + raw_row(w.t_down, TPR * Fl);
+
         if (!fill(wq, w.q + TPR * qdl * rq_b, (long long)qdl, (int)H, rq, 0, 1) ||
             !fill(wq, w.k + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)qdl, 1) ||
             !fill(wq, w.v + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)(qdl + kvdl), 1) ||
-            rmat_fill(wo, o_src, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd) != cudaSuccess ||
+            rmat_fill(wo, w.o, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd, o_item0) != cudaSuccess ||
             !fill(wg, w.gate + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 0, 2) ||
             !fill(wg, w.up + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 1, 2) ||
-            rmat_fill(wd, d_src, (long long)H, (int)Fl, rd, 0, 1, st, (int)F) != cudaSuccess)
+            rmat_fill(wd, w.down, (long long)H, (int)Fl, rd, 0, 1, st, (int)F, d_item0) != cudaSuccess)
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
         float* bias = nullptr;
         if (any_bias) {
@@ -814,7 +818,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     }
     // LM head: tied token_embd (the reference ignores output.weight, qwen3.cu:180-212,261)
     {
-        const RMat rl = carve(WT_Q80, vn, (int)H);
+        const RMat rl = carve(WT_Q80, vn, (int)H, 0);
         if (!fill(WT_Q80, m->tok_embd + (size_t)v0 * (H / 32) * 34, vn, (int)H, rl, 0, 1))
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
         if (!phase(m->lm, rl, WT_Q80, (int)H, vn, 0, X_NORM, EPI_LMHEAD) || m->lm.p.grid > 4096)

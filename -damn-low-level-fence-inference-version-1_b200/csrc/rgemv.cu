@@ -10,17 +10,19 @@ namespace fence {
 // ------------------------------------------------------------------ repack kernels (load time)
 // GGUF Q6_K rows (block_q6_K, src/kernels/q6k_types.h:27-32) -> q/s/d arrays; row r of the source
 // becomes row dst_row0 + r * dst_stride of the destination (fused QKV, interleaved gate/up). The
-// source rows are src_nsb blocks apart; the first nsb blocks from src of each are taken (a column
-// slice when src_nsb > nsb: a tensor-parallel shard of a row-parallel matrix).
-__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long rows, int nsb, int src_nsb,
+// source rows are src_nsb blocks apart; items item0 .. item0 + I - 1 of each are taken (a column
+// slice, a tensor-parallel shard of a row-parallel matrix, when I < 4 src_nsb; it may start and
+// end inside a super-block, whose d is then repeated in each neighbour's rows).
+__global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long rows, int I, int src_nsb, int item0,
                                   uint8_t* __restrict__ q, uint8_t* __restrict__ s, uint8_t* __restrict__ d,
                                   long long dst_row0, int dst_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const int I = nsb * 4;
     if (idx >= rows * I) return;
     const long long r = idx / I;
     const int it = (int)(idx - r * I);
-    const int j = it >> 2, h = (it >> 1) & 1, l16 = it & 1;
+    const int gi = item0 + it;  // item index in the source row
+    const int j = gi >> 2, h = (gi >> 1) & 1, l16 = gi & 1;
+    const int nsb = (I + (item0 & 3) + 3) >> 2;  // d entries per destination row
     const uint8_t* blk = src + ((size_t)r * src_nsb + j) * 210;
     const long long dr = dst_row0 + r * dst_stride;
     uint8_t* qd = q + ((size_t)dr * I + it) * 48;
@@ -29,25 +31,25 @@ __global__ void repack_q6k_kernel(const uint8_t* __restrict__ src, long long row
         qd[16 + e] = blk[64 * h + 32 + 16 * l16 + e];
         qd[32 + e] = blk[128 + 32 * h + 16 * l16 + e];
     }
-    uint8_t* sd = s + ((size_t)dr * I + it) * 4;
+    uint8_t* sd = s + (size_t)dr * rg_sbytes_row(WT_Q6K, I) + (size_t)it * 4;
     for (int c = 0; c < 4; ++c) sd[c] = blk[192 + 8 * h + 2 * c + l16];
-    if (h == 0 && l16 == 0) {
-        uint8_t* dd = d + ((size_t)dr * nsb + j) * 2;
+    if ((gi & 3) == 0 || it == 0) {  // the first item of each super-block this row holds
+        uint8_t* dd = d + ((size_t)dr * nsb + (j - (item0 >> 2))) * 2;
         dd[0] = blk[208];
         dd[1] = blk[209];
     }
 }
 
 // GGUF Q8_0 rows (block_q8_0, src/kernels/q8_0_types.h:11-14) -> swizzled q / d arrays; source
-// rows src_nb blocks apart, the first 2 I blocks from src of each taken.
-__global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long rows, int I, int src_nb,
+// rows src_nb blocks apart, items item0 .. item0 + I - 1 (blocks 2 item0 ..) of each taken.
+__global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long rows, int I, int src_nb, int item0,
                                   uint8_t* __restrict__ q, uint8_t* __restrict__ d, long long dst_row0,
                                   int dst_stride) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * I) return;
     const long long r = idx / I;
     const int it = (int)(idx - r * I);
-    const uint8_t* b0 = src + ((size_t)r * src_nb + 2 * it) * 34;
+    const uint8_t* b0 = src + ((size_t)r * src_nb + 2 * (item0 + it)) * 34;
     const uint8_t* b1 = b0 + 34;
     const long long dr = dst_row0 + r * dst_stride;
     uint8_t* qd = q + ((size_t)dr * I + it) * 64;
@@ -64,16 +66,16 @@ __global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long row
     dd[3] = b1[1];
 }
 
-size_t rmat_bytes(int wt, long long rows, int K) {
+size_t rmat_bytes(int wt, long long rows, int K, int iph) {
     const int I = K / 64;
     auto pad = [](size_t x) { return (x + 64 + 255) / 256 * 256; };
-    size_t n = pad((size_t)rows * I * rg_qbytes(wt)) + pad((size_t)rows * rg_dbytes_row(wt, I));
+    size_t n = pad((size_t)rows * I * rg_qbytes(wt)) + pad((size_t)rows * rg_dbytes_row(wt, I, iph));
     if (wt == WT_Q6K) n += pad((size_t)rows * rg_sbytes_row(wt, I));
     return n;
 }
 
-// Carves an RMat of `rows` rows of K inputs out of base (rmat_bytes(wt, rows, K) bytes).
-RMat rmat_carve(int wt, long long rows, int K, uint8_t* base) {
+// Carves an RMat of `rows` rows of K inputs out of base (rmat_bytes(wt, rows, K, iph) bytes).
+RMat rmat_carve(int wt, long long rows, int K, uint8_t* base, int iph) {
     const int I = K / 64;
     auto pad = [](size_t x) { return (x + 64 + 255) / 256 * 256; };
     RMat m{};
@@ -86,23 +88,25 @@ RMat rmat_carve(int wt, long long rows, int K, uint8_t* base) {
     }
     m.d = p;
     m.rows = (int)rows;
+    m.iph = wt == WT_Q6K ? iph : 0;
     return m;
 }
 
-// src_K: inputs per source row (K for whole rows; the full width for a column slice starting at src).
+// src: the source rows' start; src_K: inputs per source row (0: K); item0: the first 64-input
+// item of each source row taken (a column slice when K < src_K).
 cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
-                      int dst_stride, cudaStream_t st, int src_K) {
+                      int dst_stride, cudaStream_t st, int src_K, int item0) {
     const int I = K / 64;
     const long long n = rows * I;
     const int threads = 256;
     const unsigned blocks = (unsigned)((n + threads - 1) / threads);
     if (src_K <= 0) src_K = K;
     if (wt == WT_Q6K)
-        repack_q6k_kernel<<<blocks, threads, 0, st>>>(src, rows, K / 256, src_K / 256, const_cast<uint8_t*>(m.q),
+        repack_q6k_kernel<<<blocks, threads, 0, st>>>(src, rows, I, src_K / 256, item0, const_cast<uint8_t*>(m.q),
                                                       const_cast<uint8_t*>(m.s), const_cast<uint8_t*>(m.d), dst_row0,
                                                       dst_stride);
     else
-        repack_q80_kernel<<<blocks, threads, 0, st>>>(src, rows, I, src_K / 32, const_cast<uint8_t*>(m.q),
+        repack_q80_kernel<<<blocks, threads, 0, st>>>(src, rows, I, src_K / 32, item0, const_cast<uint8_t*>(m.q),
                                                       const_cast<uint8_t*>(m.d), dst_row0, dst_stride);
     return cudaGetLastError();
 }
@@ -125,7 +129,7 @@ RGemvPlan plan_rgemv(RGemvArgs& a, int sms, int smem_budget) {
         const int rc = (int)(((long long)a.Mv + g - 1) / g) * (a.dual ? 2 : 1);
         if (R > rc) R = a.dual ? std::max(2, (rc + 1) & ~1) : std::max(1, rc);
     }
-    const int slot = (int)((rg_slot(a.wt, I, R).bytes + 127u) & ~127u);
+    const int slot = (int)((rg_slot(a.wt, I, R, a.w.iph).bytes + 127u) & ~127u);
     const int S = a.dual ? R / 2 : R;
     const int grid = std::min(sms, a.Mv);
     const int vcta = (a.Mv + grid - 1) / grid;  // max virtual rows of one CTA

@@ -51,6 +51,8 @@ struct RMat {
     const uint8_t* s;  // Q6_K only
     const uint8_t* d;
     int rows;
+    int iph;           // Q6_K column slice starting inside a super-block: its first item's index
+                       // within that super-block (0..3); local item i uses d entry (i + iph) / 4
 };
 
 struct RGemvArgs {
@@ -91,19 +93,23 @@ struct RGemvPlan {
 };
 
 __host__ __device__ inline int rg_qbytes(int wt) { return wt == WT_Q6K ? 48 : 64; }
-__host__ __device__ inline int rg_dbytes_row(int wt, int I) { return wt == WT_Q6K ? I / 2 : I * 4; }
-__host__ __device__ inline int rg_sbytes_row(int wt, int I) { return wt == WT_Q6K ? I * 4 : 0; }
+__host__ __device__ inline int rg_dbytes_row(int wt, int I, int iph = 0) {
+    return wt == WT_Q6K ? ((I + iph + 3) >> 2) * 2 : I * 4;
+}
+// Q6_K scale bytes of one row (4 per item), padded to 16 so that every row starts 16-byte aligned
+// for the bulk copies (a tensor-parallel column slice may hold a number of items not divisible by 4)
+__host__ __device__ inline int rg_sbytes_row(int wt, int I) { return wt == WT_Q6K ? (I * 4 + 15) & ~15 : 0; }
 
 // Shared-memory layout of one slot: [q | s | d] each 16-aligned, d copied from a 16-aligned source
 // below its first row (the offset of that row inside the copy is recomputed by the consumers).
 struct RSlot {
     uint32_t s_off, d_off, bytes;
 };
-__host__ __device__ inline RSlot rg_slot(int wt, int I, int R) {
+__host__ __device__ inline RSlot rg_slot(int wt, int I, int R, int iph = 0) {
     RSlot L;
     const uint32_t qb = (uint32_t)R * I * rg_qbytes(wt);
     const uint32_t sb = (uint32_t)R * rg_sbytes_row(wt, I);
-    const uint32_t db = (uint32_t)R * rg_dbytes_row(wt, I);
+    const uint32_t db = (uint32_t)R * rg_dbytes_row(wt, I, iph);
     L.s_off = (qb + 15u) & ~15u;
     L.d_off = (L.s_off + sb + 15u) & ~15u;
     L.bytes = (L.d_off + db + 16u + 15u) & ~15u;  // + up to 15 bytes of d alignment slack
@@ -391,7 +397,7 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
     const bool dual = a.dual != 0;
     const int S = dual ? R / 2 : R;  // virtual rows per stage
     const RGSmem SL = rg_smem_layout(ring, a.slot_bytes, I, a.rows_cta, a.mp);
-    const RSlot SS = rg_slot(WT, I, R);
+    const RSlot SS = rg_slot(WT, I, R, a.w.iph);
     const uint32_t smem_sa = smem_u32(smem);
     const uint32_t xq_sa = smem_sa + SL.xq;
     float* acc = reinterpret_cast<float*>(smem + SL.acc);  // [rows of the CTA][mp] reduction pieces
@@ -405,7 +411,7 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
     const int G = gridDim.x, c = blockIdx.x;
     const int v_begin = (int)(((long long)a.Mv * c) / G), v_end = (int)(((long long)a.Mv * (c + 1)) / G);
     const int nstages = (v_end - v_begin + S - 1) / S;
-    const int qb = rg_qbytes(WT), sbr = rg_sbytes_row(WT, I), dbr = rg_dbytes_row(WT, I);
+    const int qb = rg_qbytes(WT), sbr = rg_sbytes_row(WT, I), dbr = rg_dbytes_row(WT, I, a.w.iph);
 
     if (tid == 0) {
         for (int s = 0; s < ring; ++s) {
@@ -560,8 +566,9 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
     int pidx = warp - (slot_lo >> 5);  // this segment's piece index in its row's reduction
     for (int p2 = 0; p2 < pt; ++p2) pidx += rg_part_pieces(rs, p2, NP, IP);
     const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
-    const uint32_t s_off = SS.s_off + (uint32_t)(rs * I + it) * 4u;
-    const uint32_t d_off = SS.d_off + (WT == WT_Q6K ? (uint32_t)(rs * (I / 4) + (it >> 2)) * 2u
+    const uint32_t s_off = SS.s_off + (uint32_t)(rs * rg_sbytes_row(WT, I) + it * 4);
+    const int nsbl = rg_dbytes_row(WT, I, a.w.iph) / 2;  // Q6_K d entries per row
+    const uint32_t d_off = SS.d_off + (WT == WT_Q6K ? (uint32_t)(rs * nsbl + ((it + a.w.iph) >> 2)) * 2u
                                                      : (uint32_t)(rs * I + it) * 4u);
     const long long row_begin = dual ? 2ll * v_begin : v_begin;
 

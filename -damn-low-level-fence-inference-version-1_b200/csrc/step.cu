@@ -35,7 +35,7 @@ static bool plan_step_gemv(RGemvArgs& g, int grid, std::string& err) {
     g.mp = mp;
     g.rows_cta = rows_cta;
     g.ring = 0;
-    g.slot_bytes = (int)((rg_slot(g.wt, I, R).bytes + 127u) & ~127u);
+    g.slot_bytes = (int)((rg_slot(g.wt, I, R, g.w.iph).bytes + 127u) & ~127u);
     return true;
 }
 

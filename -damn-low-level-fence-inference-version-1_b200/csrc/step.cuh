@@ -280,8 +280,8 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool q6 = g.wt == WT_Q6K;
     const int I = g.I, NP = g.np, IP = I / NP, R = g.R, MP = g.mp;
-    const int qb = rg_qbytes(g.wt), dbr = rg_dbytes_row(g.wt, I);
-    const RSlot SS = rg_slot(g.wt, I, R);
+    const int qb = rg_qbytes(g.wt), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
+    const RSlot SS = rg_slot(g.wt, I, R, g.w.iph);
     const int sl = tid / IP, itp = tid - sl * IP;
     const int rs = sl / NP, pt = sl - rs * NP, it = pt * IP + itp;
     const bool lane_on = rs < R;
@@ -296,8 +296,9 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
     int pidx = warp - (slot_lo >> 5);
     for (int p2 = 0; p2 < pt; ++p2) pidx += rg_part_pieces(rs, p2, NP, IP);
     const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
-    const uint32_t s_off = SS.s_off + (uint32_t)(rs * I + it) * 4u;
-    const uint32_t d_off = SS.d_off + (q6 ? (uint32_t)(rs * (I / 4) + (it >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
+    const uint32_t s_off = SS.s_off + (uint32_t)(rs * rg_sbytes_row(g.wt, I) + it * 4);
+    const uint32_t d_off =
+        SS.d_off + (q6 ? (uint32_t)(rs * (dbr / 2) + ((it + g.w.iph) >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
     const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
     const uint32_t ring_u = (uint32_t)ring;
     uint32_t slot = use % ring_u, par = (use / ring_u) & 1u;  // advanced incrementally below
@@ -876,8 +877,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 const RGemvArgs& g = ph.g;
                 const SKRows rr = sk_rows(g, c, G);
                 const int I = g.I, R = g.R;
-                const int qb = rg_qbytes(g.wt), sbr = rg_sbytes_row(g.wt, I), dbr = rg_dbytes_row(g.wt, I);
-                const RSlot SS = rg_slot(g.wt, I, R);
+                const int qb = rg_qbytes(g.wt), sbr = rg_sbytes_row(g.wt, I), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
+                const RSlot SS = rg_slot(g.wt, I, R, g.w.iph);
                 const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
                 unsigned long long pwait = 0;
                 bool stop = false;

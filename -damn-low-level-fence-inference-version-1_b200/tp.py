@@ -24,9 +24,8 @@ def shard_plan(n_heads: int, n_kv_heads: int, head_dim: int, ff_dim: int, vocab:
     if n_heads % size or n_kv_heads % size or ff_dim % size:
         raise ValueError("heads / FFN rows do not split evenly")
     qd, kvd, F = n_heads * head_dim // size, n_kv_heads * head_dim // size, ff_dim // size
-    blk = {GGML_Q6_K: 256, GGML_Q8_0: 64}
-    if qd % blk[o_type] or F % blk[down_type]:
-        raise ValueError("a rank's o_proj / down column slice is not a whole number of quant blocks")
+    if qd % 64 or F % 64:  # whole 64-input items (a Q6_K super-block may be cut between two ranks)
+        raise ValueError("a rank's o_proj / down column slice is not a whole number of 64-input items")
     per = (vocab + size - 1) // size
     v0 = rank * per
     return {

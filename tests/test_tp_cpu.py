@@ -16,7 +16,7 @@ def tp():
     return t
 
 
-@pytest.mark.parametrize("size", [1, 2, 4])
+@pytest.mark.parametrize("size", [1, 2, 4, 8])
 def test_shards_cover_config3(size):
     t = tp()
     plans = [t.shard_plan(**CFG3, rank=r, size=size) for r in range(size)]
@@ -29,16 +29,18 @@ def test_shards_cover_config3(size):
             pos = b
         assert pos == total, key
     for p in plans:
-        assert (p["o_cols"][1] - p["o_cols"][0]) % 256 == 0 and (p["down_cols"][1] - p["down_cols"][0]) % 256 == 0
+        assert (p["o_cols"][1] - p["o_cols"][0]) % 64 == 0 and (p["down_cols"][1] - p["down_cols"][0]) % 64 == 0
         assert p["q_heads"] * size == 40 and p["kv_heads"] * size == 8
 
 
-def test_config3_eight_ranks_refused():
-    """640 o_proj columns per rank is 2.5 Q6_K super-blocks: the engine refuses, and so does the plan."""
-    with pytest.raises(ValueError, match="whole number of quant blocks"):
-        tp().shard_plan(**CFG3, rank=0, size=8)
-    # the same split with Q8_0 linears (64-element blocks) is fine
-    tp().shard_plan(**CFG3, rank=3, size=8, o_type=8, down_type=8)
+def test_config3_eight_ranks_cut_super_blocks():
+    """At 8 ranks a rank holds 640 o_proj columns (2.5 Q6_K super-blocks) and 2176 down columns
+    (8.5): the odd ranks start in the middle of a super-block (its d goes to both neighbours)."""
+    p1 = tp().shard_plan(**CFG3, rank=1, size=8)
+    assert p1["o_cols"] == (640, 1280) and (640 // 64) % 4 == 2
+    assert p1["down_cols"] == (2176, 4352) and (2176 // 64) % 4 == 2
+    with pytest.raises(ValueError, match="64-input items"):
+        tp().shard_plan(n_heads=8, n_kv_heads=8, head_dim=32, ff_dim=1024, vocab=100, rank=0, size=8)
 
 
 def test_uneven_vocab_and_bad_heads():

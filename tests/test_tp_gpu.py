@@ -19,6 +19,10 @@ SHAPES = {
                    vocab_size=2051),
     "tp-q8": dict(config="tiny-q8", n_layers=2, embed_dim=1024, ff_dim=2048, n_heads=8, n_kv_heads=4,
                   vocab_size=2051),
+    # rank 1's o_proj columns (384..767) and down columns (640..1279) start in the middle of a Q6_K
+    # super-block: its d is repeated in both ranks' rows
+    "tp-q6k-cut": dict(config="tiny-q6k", n_layers=2, embed_dim=512, ff_dim=1280, n_heads=6, n_kv_heads=2,
+                       vocab_size=2051),
 }
 STEPS = 40
 
