@@ -44,8 +44,8 @@ constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
 constexpr int SK_MAX_R = 64;              // rows per stage
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
 // Exchange buffer of one rank (tensor parallel): an argmax counter, one argmax (value bits |
-// index << 32) per rank, then partials [2][tp_h][tp_n] (a row's ranks adjacent), each a 64-bit
-// (value bits | tag << 32)
+// index << 32) per rank, then partials [2][tp_n][tp_h] (a rank's rows adjacent, so the writing
+// warps store 256 contiguous bytes per row block), each a 64-bit (value bits | tag << 32)
 // stored with one 8-byte access: the tag (the step's reduction number, never 0) tells a reader
 // that the value is this reduction's, so no fence or counter sits between the ranks' partials.
 constexpr int SK_TP_MAX = 8;
@@ -151,7 +151,7 @@ __device__ __forceinline__ unsigned long long sk_ld_acquire_sys(const unsigned l
 __device__ __forceinline__ void sk_red_release_sys(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Rank p's tagged partials of reduction slot buf, as mapped here: [tp_h][tp_n]
+// Rank p's tagged partials of reduction slot buf, as mapped here: [tp_n][tp_h]
 __device__ __forceinline__ unsigned long long* sk_xpart(const StepArgs& A, int p, int buf) {
     return reinterpret_cast<unsigned long long*>(A.xb[p] + SK_XB_PART) + (size_t)buf * A.tp_n * A.tp_h;
 }
@@ -752,9 +752,10 @@ __device__ __forceinline__ void sk_attn_prefetch_tile0(const AttnArgs& a, int h,
 }
 
 // x of a phase after a tensor-parallel reduction: hbuf[i] = hin[i] + sum over ranks (rank order)
-// of the tagged partials of row i (adjacent in memory); rows [h0, h1) also to hout (this CTA's
-// share of the residual stream). A pass reads every row with no load depending on another (four
-// rows of a thread in flight together); passes repeat, bounded, until every tag matched.
+// of the tagged partials of row i; rows [h0, h1) also to hout (this CTA's share of the residual
+// stream). A pass reads every row with no load depending on another (four rows of a thread in
+// flight together, each rank's rows coalesced across the warp); passes repeat, bounded, until
+// every tag matched.
 template <int N>
 __device__ __forceinline__ bool sk_tp_gather(const float* hin, float* hout, const unsigned long long* parts,
                                              unsigned tag, float* hbuf, int H, int h0, int h1) {
@@ -765,7 +766,7 @@ __device__ __forceinline__ bool sk_tp_gather(const float* hin, float* hout, cons
             float v = __ldcg(hin + i);
 #pragma unroll
             for (int p = 0; p < N; ++p) {
-                const unsigned long long w = sk_ld_sys64(parts + (size_t)i * N + p);
+                const unsigned long long w = sk_ld_sys64(parts + (size_t)p * H + i);
                 bad |= (unsigned)(w >> 32) != tag;
                 v += __uint_as_float((unsigned)w);
             }
@@ -803,7 +804,7 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
                 g.y[row] = g.bias ? sum + g.bias[row] : sum;
             } else if (TP && epi == EPI_RESID && ph.tp_red) {  // tagged partial row -> every rank (NVLink stores)
                 const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(sum);
-                for (int p = 0; p < A.tp_n; ++p) sk_st_sys64(sk_xpart(A, p, ph.red_idx & 1) + (size_t)row * A.tp_n + A.tp_rank, v);
+                for (int p = 0; p < A.tp_n; ++p) sk_st_sys64(sk_xpart(A, p, ph.red_idx & 1) + (size_t)A.tp_rank * A.tp_h + row, v);
             } else if (epi == EPI_RESID) {
                 g.resid[row] = sum + (vr < SK_RPRE ? rpre[vr] : g.resid[row]);
             } else {
