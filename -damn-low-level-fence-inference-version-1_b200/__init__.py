@@ -110,6 +110,11 @@ SIGNATURES = [
     ("fence_copy_logits", ctypes.c_int, [_vp, _c_float_p]),
     ("fence_time_decode", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _c_float_p]),
     ("fence_tp_handle", ctypes.c_int, [_vp, _vp, ctypes.c_int]),
+    ("fence_sample_scratch_bytes", ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    ("fence_sample_nucleus_device", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int]),
+    ("fence_sample_nucleus_dev", ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                                ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                                ctypes.c_double, _vp, ctypes.c_size_t, _vp, _vp]),
     ("fence_tp_connect", ctypes.c_int, [_vp, _vp, ctypes.c_int]),
     ("fence_synth_spec_default", None, [ctypes.POINTER(SynthSpec)]),
     ("fence_synth_write_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), ctypes.c_int]),
@@ -275,6 +280,14 @@ class Model:
     def sample_nucleus(self, d_logits: int, history) -> int:
         arr = (ctypes.c_int * len(history))(*history)
         r = lib().fence_sample_nucleus(self._h, d_logits, arr, len(history))
+        if r < 0:
+            raise FenceError(last_error())
+        return r
+
+    def sample_nucleus_device(self, d_logits: int, history) -> int:
+        """sample_nucleus with the sampling steps on the device (only the id comes back)."""
+        arr = (ctypes.c_int * max(1, len(history)))(*history)
+        r = lib().fence_sample_nucleus_device(self._h, d_logits, arr, len(history))
         if r < 0:
             raise FenceError(last_error())
         return r

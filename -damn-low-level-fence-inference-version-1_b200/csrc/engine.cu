@@ -109,6 +109,12 @@ struct fence_model {
     uint8_t* xpeer[SK_TP_MAX] = {};  // every rank's exchange buffer as mapped here (own = xbuf)
     unsigned long long* tp_launch = nullptr;
     int tp_connected = 0;
+    // device nucleus sampler (allocated on its first use)
+    void* samp_scratch = nullptr;
+    size_t samp_bytes = 0;
+    int* samp_hist = nullptr;
+    int samp_hist_cap = 0;
+    int* samp_out = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
     std::mt19937 rng{0x5eed};
@@ -378,6 +384,9 @@ void free_model(fence_model* m) {
     cudaFree(m->xbuf);
     cudaFree(m->hidden_b);
     cudaFree(m->tp_launch);
+    cudaFree(m->samp_scratch);
+    cudaFree(m->samp_hist);
+    cudaFree(m->samp_out);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -901,6 +910,44 @@ extern "C" int fence_set_seed(fence_model* m, uint64_t seed) {
     if (!m) return set_error(FENCE_E_ARG, "set_seed: null model");
     m->rng.seed((std::mt19937::result_type)(seed ^ (seed >> 32)));
     return FENCE_OK;
+}
+
+extern "C" int fence_sample_nucleus_device(fence_model* m, const float* d_logits, const int* history, int n_history) {
+    if (!m || !d_logits || n_history < 0 || (n_history > 0 && !history))
+        return set_error(FENCE_E_ARG, "sample_nucleus_device: bad arguments");
+    const fence_config& c = m->cfg;
+    if (c.temperature <= 0.0f || c.top_k <= 1) return fence_sample_greedy(m, d_logits);
+    if (m->tp_n > 1) return set_error(FENCE_E_UNSUPPORTED, "sample_nucleus_device: a tensor-parallel rank holds a vocabulary shard");
+    cudaSetDevice(m->dev);
+    const size_t need = fence_sample_scratch_bytes(c.vocab_size, c.top_k);
+    if (!need) return set_error(FENCE_E_UNSUPPORTED, "sample_nucleus_device: top_k %d (the device sampler takes 2..256)", c.top_k);
+    if (m->samp_bytes < need) {
+        cudaFree(m->samp_scratch);
+        m->samp_scratch = nullptr;
+        m->samp_bytes = 0;
+        FENCE_CUDA_TRY(cudaMalloc(&m->samp_scratch, need));
+        m->samp_bytes = need;
+    }
+    if (!m->samp_out) FENCE_CUDA_TRY(cudaMalloc(&m->samp_out, sizeof(int)));
+    if (n_history > m->samp_hist_cap) {
+        cudaFree(m->samp_hist);
+        m->samp_hist = nullptr;
+        m->samp_hist_cap = 0;
+        FENCE_CUDA_TRY(cudaMalloc(&m->samp_hist, (size_t)n_history * sizeof(int)));
+        m->samp_hist_cap = n_history;
+    }
+    if (n_history > 0)
+        FENCE_CUDA_TRY(cudaMemcpyAsync(m->samp_hist, history, (size_t)n_history * sizeof(int), cudaMemcpyHostToDevice,
+                                       m->stream));
+    // the one draw std::discrete_distribution makes (libstdc++: generate_canonical<double, 53>)
+    const double u = std::generate_canonical<double, 53>(m->rng);
+    int rc = fence_sample_nucleus_dev(d_logits, c.vocab_size, m->samp_hist, n_history, c.temperature, c.top_p, c.top_k,
+                                      c.repetition_penalty, c.min_p, c.dynamic_temp, u, m->samp_scratch, m->samp_bytes,
+                                      m->samp_out, m->stream);
+    if (rc) return rc;
+    FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_token, m->samp_out, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return *m->h_token;
 }
 
 extern "C" const float* fence_forward(fence_model* m, int token_id, int pos) {

@@ -5,4 +5,5 @@
 #include "step.cu"
 #include "ops.cu"
 #include "attention_static.cu"
+#include "sampler_dev.cu"
 #include "engine.cu"

@@ -151,6 +151,21 @@ int fence_gqa_attention(float* attn_out, const float* q, const uint16_t* k_cache
  * <= -1e30 never win; 0 when nothing qualifies. Replaces argmax, src/kernels/ops.cuh:501-505. */
 int fence_argmax(const float* x, int* result, int n, fence_stream_t stream);
 
+/* Qwen3Model::sample_nucleus (src/model/qwen3.cu:351-460) on the device: repetition penalty once
+ * per occurrence of a token in `history` (device ids), min-p cut, entropy-scaled temperature,
+ * softmax, top_k largest probabilities (ties to the smaller id), the shortest prefix reaching
+ * top_p, then the draw std::discrete_distribution makes, with the caller's uniform u in [0, 1)
+ * (the kept weights normalised and accumulated in double; the first id whose cumulative is >= u).
+ * Only the id (*out_id, device) leaves the device, where the reference copies the whole logits
+ * vector to the host and sorts it. top_k in 2..256 and temperature > 0 (greedy decoding is
+ * fence_argmax); history up to 65536 ids. Caller-owned scratch of fence_sample_scratch_bytes(vocab,
+ * top_k) bytes, 256-byte aligned; logits are not modified. Sums run in a fixed tree order, so a
+ * probability differs from the reference's sequential float sum in its last bits. */
+size_t fence_sample_scratch_bytes(int vocab, int top_k);
+int fence_sample_nucleus_dev(const float* logits, int vocab, const int* history, int n_history, float temperature,
+                             float top_p, int top_k, float rep_penalty, float min_p, int dynamic_temp, double u,
+                             void* scratch, size_t scratch_bytes, int* out_id, fence_stream_t stream);
+
 /* No counterpart in the reference. fence_gqa_attention without score_buf, for callers that cannot
  * allocate at the call site (a foreign-language binding handed only the operands, or a per-token
  * host loop that must not call the device-synchronising cudaMalloc). Allocates nothing: the
@@ -231,6 +246,11 @@ int fence_sample_greedy(fence_model* m, const float* d_logits);
  * the engine's seeded mt19937 (fence_set_seed) where the reference seeds from random_device. */
 int fence_sample_nucleus(fence_model* m, const float* d_logits, const int* history, int n_history);
 int fence_set_seed(fence_model* m, uint64_t seed);
+/* sample_nucleus with the sampling steps on the device (fence_sample_nucleus_dev) and only the id
+ * copied back: same parameters, same engine generator (one draw per call; the host path skips
+ * its draw when a single token survives top-p), top_k up to 256. The first call allocates its
+ * scratch. */
+int fence_sample_nucleus_device(fence_model* m, const float* d_logits, const int* history, int n_history);
 
 /* Qwen3Model::generate (qwen3.cu:463-519): token-by-token prefill of `prompt`, then up to
  * max_new_tokens sampled tokens, stopping at eos_id (pass -1 for no stop token) or max_ctx.

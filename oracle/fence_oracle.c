@@ -632,3 +632,96 @@ int oracle_forward(oracle_model* m, int token, int pos, float* logits) {
     for (int i = 0; i < m->V; ++i) logits[i] = (float)m->ybuf[i];
     return 0;
 }
+
+/* ---- sample_nucleus, src/model/qwen3.cu:351-460 (see the header) ---- */
+typedef struct {
+    float p;
+    int i;
+} oracle_pi;
+static int oracle_pi_desc(const void* a, const void* b) {
+    const oracle_pi* x = (const oracle_pi*)a;
+    const oracle_pi* y = (const oracle_pi*)b;
+    if (x->p != y->p) return x->p > y->p ? -1 : 1;
+    return x->i < y->i ? -1 : (x->i > y->i);
+}
+
+int oracle_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
+                          float top_p, int top_k, float rep_penalty, float min_p, int dynamic_temp, double u,
+                          double* cut_margin, double* u_margin) {
+    float* l = (float*)malloc(sizeof(float) * (size_t)vocab);
+    oracle_pi* probs = (oracle_pi*)malloc(sizeof(oracle_pi) * (size_t)vocab);
+    memcpy(l, logits, sizeof(float) * (size_t)vocab);
+    if (rep_penalty > 1.0f && n_history > 0) /* qwen3.cu:358-369: once per occurrence */
+        for (int h = 0; h < n_history; ++h) {
+            const int t = history[h];
+            if (t >= 0 && t < vocab) l[t] = l[t] > 0 ? l[t] / rep_penalty : l[t] * rep_penalty;
+        }
+    float mx = -1e30f;
+    for (int i = 0; i < vocab; ++i) mx = l[i] > mx ? l[i] : mx;
+    if (min_p > 0.0f) { /* qwen3.cu:376-384 */
+        const float thr = mx + logf(min_p);
+        for (int i = 0; i < vocab; ++i)
+            if (l[i] < thr) l[i] = -1e30f;
+    }
+    float temp = temperature;
+    if (dynamic_temp) { /* qwen3.cu:388-412 */
+        float dyn = 0.0f;
+        for (int i = 0; i < vocab; ++i)
+            if (l[i] > -1e20f) dyn += expf(l[i] - mx);
+        float ent = 0.0f;
+        for (int i = 0; i < vocab; ++i)
+            if (l[i] > -1e20f) {
+                const float pr = expf(l[i] - mx) / dyn;
+                if (pr > 1e-6f) ent -= pr * logf(pr);
+            }
+        float sc = ent / 2.0f;
+        sc = sc < 0.5f ? 0.5f : (sc > 2.0f ? 2.0f : sc);
+        temp *= sc;
+    }
+    float sum = 0.0f; /* qwen3.cu:414-426 */
+    for (int i = 0; i < vocab; ++i) {
+        if (l[i] < -1e20f) {
+            l[i] = 0.0f;
+            continue;
+        }
+        l[i] = expf((l[i] - mx) / temp);
+        sum += l[i];
+    }
+    for (int i = 0; i < vocab; ++i) {
+        probs[i].p = l[i] / sum;
+        probs[i].i = i;
+    }
+    qsort(probs, (size_t)vocab, sizeof(oracle_pi), oracle_pi_desc); /* qwen3.cu:428-436, ties: smaller id */
+    const int limit = top_k < vocab ? top_k : vocab;                  /* qwen3.cu:438-448 */
+    float cum = 0.0f;
+    int k = limit;
+    double cm = 1e30;
+    for (int i = 0; i < limit; ++i) {
+        cum += probs[i].p;
+        const double d = fabs((double)cum - (double)top_p);
+        if (d < cm) cm = d;
+        if (cum >= top_p) {
+            k = i + 1;
+            break;
+        }
+    }
+    double w = 0.0, acc = 0.0, um = 1e30;
+    for (int i = 0; i < k; ++i) w += probs[i].p;
+    int pick = k - 1;
+    for (int i = 0; i < k; ++i) { /* qwen3.cu:450-456: std::discrete_distribution (libstdc++: cumulative of the
+                                     normalised weights in double, last set to 1, first >= u) */
+        acc += probs[i].p / w;
+        const double c = i == k - 1 ? 1.0 : acc;
+        if (i < k - 1 && fabs(c - u) < um) um = fabs(c - u);
+        if (i < k - 1 && c >= u) {
+            pick = i;
+            break;
+        }
+    }
+    const int id = probs[pick].i;
+    if (cut_margin) *cut_margin = cm;
+    if (u_margin) *u_margin = um;
+    free(l);
+    free(probs);
+    return id;
+}

@@ -54,6 +54,19 @@ void oracle_attention(float* out, const float* q, const uint16_t* kc, const uint
 /* argmax, src/kernels/ops.cuh:467-499: strided scan + tree, ties to the smaller index mod 256 */
 int oracle_argmax(const float* x, int n);
 
+/* Qwen3Model::sample_nucleus, src/model/qwen3.cu:351-460, in the reference's float arithmetic
+ * (sequential sums, penalty once per history occurrence, min-p, entropy-scaled temperature,
+ * descending sort with ties to the smaller index, top-k then top-p) with the random draw made
+ * explicit: u in [0, 1) plays the part of the one generate_canonical<double> draw that
+ * std::discrete_distribution makes, and the id is the first kept entry whose cumulative
+ * normalised weight (double) is >= u (the last one if none). Returns the token id; *cut_margin
+ * (if not NULL) receives the distance of the top-p cumulative from top_p at the cut and *u_margin
+ * the distance of u from the nearest cumulative boundary, so a test can skip draws that rounding
+ * could move. */
+int oracle_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
+                          float top_p, int top_k, float rep_penalty, float min_p, int dynamic_temp, double u,
+                          double* cut_margin, double* u_margin);
+
 /* ---- full model (src/model/qwen3.cu:116-341) ---- */
 typedef struct oracle_model oracle_model;
 /* kv_bf16: 0 = fp16 cache (reference), 1 = bf16 (engine option). */

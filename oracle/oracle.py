@@ -46,6 +46,9 @@ def oracle() -> ctypes.CDLL:
             "oracle_attention": (None, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_long, ctypes.c_long,
                                         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
             "oracle_argmax": (ctypes.c_int, [_vp, ctypes.c_int]),
+            "oracle_sample_nucleus": (ctypes.c_int, [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_float,
+                                                     ctypes.c_float, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+                                                     ctypes.c_int, ctypes.c_double, _vp, _vp]),
             "oracle_model_open": (_vp, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
             "oracle_model_close": (None, [_vp]),
             "oracle_model_dims": (None, [_vp, _vp]),

@@ -165,3 +165,29 @@ def test_argmax_random_ties_match_python_restatement(orc):
         for _ in range(5):
             x = rng.integers(0, 4, n).astype(np.float32)  # many exact ties
             assert orc.argmax(x) == ref_argmax_py(x.tolist())
+
+
+def test_oracle_nucleus_known_answers(orc):
+    """Hand-checkable draws of the oracle's sample_nucleus (qwen3.cu:351-460) with explicit u."""
+    import ctypes
+    O = orc.oracle()
+
+    def draw(logits, hist, temp, top_p, top_k, rp, min_p, dyn, u):
+        l = np.asarray(logits, np.float32)
+        h = np.asarray(hist, np.int32)
+        hp = h.ctypes.data_as(ctypes.c_void_p) if h.size else None
+        return O.oracle_sample_nucleus(l.ctypes.data_as(ctypes.c_void_p), l.size, hp, h.size, temp, top_p, top_k,
+                                       rp, min_p, dyn, u, None, None)
+
+    # top_p reached by the first entry: always the argmax, whatever u
+    assert draw([0.0, 5.0, 1.0, 2.0], [], 1.0, 0.5, 4, 1.0, 0.0, 0, 0.99) == 1
+    # two kept entries with probabilities 1/(1+e^-1) and e^-1/(1+e^-1): u picks one or the other
+    p0 = 1.0 / (1.0 + np.exp(-1.0))
+    assert draw([1.0, 0.0, -9.0], [], 1.0, 0.99, 2, 1.0, 0.0, 0, p0 - 1e-3) == 0
+    assert draw([1.0, 0.0, -9.0], [], 1.0, 0.99, 2, 1.0, 0.0, 0, p0 + 1e-3) == 1
+    # penalty twice on id 0 (2.0 / 1.5 / 1.5 = 0.889 < 1.0): id 1 becomes the argmax
+    assert draw([2.0, 1.0, -9.0], [0, 0], 1.0, 0.1, 3, 1.5, 0.0, 0, 0.5) == 1
+    # a negative logit is multiplied: id 0 goes from -0.1 to -0.15, below id 1 at -0.12
+    assert draw([-0.1, -0.12, -9.0], [0], 1.0, 0.1, 3, 1.5, 0.0, 0, 0.5) == 1
+    # min-p drops everything more than log(1/min_p) below the max: only id 2 survives
+    assert draw([0.0, 1.0, 5.0], [], 1.0, 1.0, 3, 1.0, 0.05, 1, 0.999) == 2
