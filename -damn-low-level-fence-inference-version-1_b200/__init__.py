@@ -51,7 +51,7 @@ class LoadOpts(ctypes.Structure):
     _fields_ = [
         ("max_ctx", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("device", ctypes.c_int),
         ("use_graph", ctypes.c_int), ("verbose", ctypes.c_int), ("tp_rank", ctypes.c_int),
-        ("tp_size", ctypes.c_int), ("nccl_comm", ctypes.c_void_p), ("step_kernel", ctypes.c_int),
+        ("tp_size", ctypes.c_int), ("step_kernel", ctypes.c_int), ("wait_test_phase", ctypes.c_int),
     ]
 
 
@@ -216,13 +216,14 @@ class Model:
 
     def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
                  use_graph: bool = True, verbose: bool = False, step_kernel: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1):
+                 tp_rank: int = 0, tp_size: int = 1, wait_test_phase: int = -1):
         L = lib()
         o = LoadOpts()
         L.fence_load_opts_default(ctypes.byref(o))
         o.max_ctx, o.kv_dtype, o.device, o.use_graph, o.verbose = max_ctx, kv_dtype, device, int(use_graph), int(verbose)
         o.step_kernel = int(step_kernel)
         o.tp_rank, o.tp_size = tp_rank, tp_size
+        o.wait_test_phase = wait_test_phase  # test only: a step-kernel phase whose counter wait runs out
         h = L.fence_model_load(path.encode(), ctypes.byref(o))
         if not h:
             raise FenceError(f"model load failed: {last_error()}")

@@ -14,13 +14,15 @@
 //    n_q_heads * chunks * (head_dim + 2) floats when it splits the context into chunks > 1, with
 //    chunks = min(max_ctx / (head_dim + 2), ceil(seq_len / 64), 64) — the same split as
 //    fence_gqa_attention, so both entry points give identical results. Larger requests are
-//    rejected with FENCE_E_SCRATCH before anything is launched (the worst case, 64 chunks at
-//    head_dim 128, fits up to 63 query heads).
+//    rejected with FENCE_E_SCRATCH before anything is launched (the worst case, 64 chunks, fits
+//    up to 63 query heads at head_dim 128 and 31 at head_dim 256).
 //  * nothing in the scratch has to start at zero: every partial the merge kernel reads was written
 //    by the same call's first kernel, so no clearing is done or needed.
 //  * set-up: the first call on each device (with that device current) looks up the array's device
-//    address with cudaGetSymbolAddress and caches it; make that first call before any stream
-//    capture begins.
+//    address with cudaGetSymbolAddress and caches it per device ordinal; make that first call
+//    before any stream capture begins. The cache is not dropped by cudaDeviceReset (after which
+//    the module reloads and the array's address may change): a process that resets a device must
+//    not call this entry point on that device again.
 //  * one scratch per device: calls that overlap in time on the same device (different streams or
 //    host threads without ordering) race on the partials. Serialise them on one stream.
 #include <mutex>

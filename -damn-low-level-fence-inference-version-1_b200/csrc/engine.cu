@@ -90,6 +90,8 @@ struct fence_model {
     DecodeState* h_state = nullptr;  // pinned staging ring
     int h_state_n = 0;
     int* h_token = nullptr;          // pinned
+    DecodeState* h_out = nullptr;    // pinned: the device state after the last fence_forward
+    int fwd_valid = 0;               // h_out holds the state of the step that produced m->logits
     std::vector<LayerLaunch> launches;
     RPhase lm{};
     uint8_t* rarena = nullptr;      // repacked linears (rgemv.cuh layouts)
@@ -225,8 +227,24 @@ int set_state(fence_model* m, int token, int pos, int step) {
     hs->token = token;
     hs->pos = pos;
     hs->step = step;
-    hs->pad = 0;
+    hs->err = 0;
     FENCE_CUDA_TRY(cudaMemcpyAsync(m->state, hs, sizeof(DecodeState), cudaMemcpyHostToDevice, m->stream));
+    return FENCE_OK;
+}
+
+// Enqueues the copy of the device decode state into m->h_out (pinned), to be read after the next
+// stream synchronisation.
+int fetch_state(fence_model* m) {
+    FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_out, m->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, m->stream));
+    return FENCE_OK;
+}
+
+// After a synchronisation that followed fetch_state: FENCE_E_DEVICE_WAIT if a step gave up on a
+// bounded wait (its results are invalid).
+int state_status(fence_model* m, const char* what) {
+    if (m->h_out->err)
+        return set_error(FENCE_E_DEVICE_WAIT, "%s: a device-side bounded wait expired (device error %d); the step's "
+                         "results are invalid", what, m->h_out->err);
     return FENCE_OK;
 }
 
@@ -334,6 +352,7 @@ int build_step_phases(fence_model* m) {
     A.cta_idx = m->lm_idx;
     A.token_log = m->token_log;
     A.token_log_cap = m->token_log_cap;
+    A.stall_phase = (m->opts.wait_test_phase >= 0 && m->opts.wait_test_phase < A.nph) ? m->opts.wait_test_phase : -1;
     if (tp) {
         A.tp_n = m->tp_n;
         A.tp_rank = m->tp_rank;
@@ -389,6 +408,7 @@ void free_model(fence_model* m) {
     cudaFree(m->samp_out);
     if (m->h_state) cudaFreeHost(m->h_state);
     if (m->h_token) cudaFreeHost(m->h_token);
+    if (m->h_out) cudaFreeHost(m->h_out);
     if (m->stream) cudaStreamDestroy(m->stream);
     m->gguf.close();
     delete m;
@@ -407,6 +427,7 @@ extern "C" void fence_load_opts_default(fence_load_opts* o) {
     o->tp_rank = 0;
     o->tp_size = 1;
     o->step_kernel = 1;
+    o->wait_test_phase = -1;
 }
 
 extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts* opts_in) {
@@ -662,7 +683,8 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
               cudaMemset(m->state, 0, sizeof(DecodeState)) == cudaSuccess &&
               cudaMalloc(&m->rope, (size_t)c.max_ctx * (HD / 2) * sizeof(float2)) == cudaSuccess &&
               cudaMallocHost(&m->h_state, 64 * sizeof(DecodeState)) == cudaSuccess &&
-              cudaMallocHost(&m->h_token, 64 * sizeof(int)) == cudaSuccess;
+              cudaMallocHost(&m->h_token, 64 * sizeof(int)) == cudaSuccess &&
+              cudaMallocHost(&m->h_out, sizeof(DecodeState)) == cudaSuccess;
     if (!ok) return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
     if (TPN > 1) {
         const size_t xb = sk_xb_bytes(TPN, (int)H);
@@ -883,6 +905,7 @@ extern "C" int fence_step_trace(fence_model* m, int token, int pos, unsigned lon
                                                                 : launch_step<__nv_bfloat16>(a, m->splan, m->stream);
         rc = cuda_status(e, "step_trace: launch");
     }
+    m->fwd_valid = 0;
     if (rc == FENCE_OK) rc = cuda_status(cudaStreamSynchronize(m->stream), "step_trace");
     if (rc == FENCE_OK)
         rc = cuda_status(cudaMemcpy(host_out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost),
@@ -960,15 +983,20 @@ extern "C" const float* fence_forward(fence_model* m, int token_id, int pos) {
         return nullptr;
     }
     cudaSetDevice(m->dev);
+    m->fwd_valid = 0;
     if (set_state(m, token_id, pos, 0) != FENCE_OK) return nullptr;
     if (run_step(m) != FENCE_OK) return nullptr;
+    if (fetch_state(m) != FENCE_OK) return nullptr;
     if (cuda_status(cudaStreamSynchronize(m->stream), "forward") != FENCE_OK) return nullptr;
+    if (state_status(m, "forward") != FENCE_OK) return nullptr;
+    m->fwd_valid = 1;  // h_out->token is the greedy id of these logits
     return m->logits;
 }
 
 extern "C" int fence_sample_greedy(fence_model* m, const float* d_logits) {
     if (!m || !d_logits) return set_error(FENCE_E_ARG, "sample_greedy: null argument");
     cudaSetDevice(m->dev);
+    if (d_logits == m->logits && m->fwd_valid) return m->h_out->token;  // read back by fence_forward
     if (d_logits == m->logits) {
         // the LM head already reduced the argmax (reference tie order) into the decode state
         FENCE_CUDA_TRY(cudaMemcpyAsync(m->h_token, &m->state->token, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
@@ -998,6 +1026,7 @@ extern "C" int fence_generate(fence_model* m, const int* prompt, int n_prompt, i
     if (!m || !prompt || n_prompt <= 0 || !out || !n_out) return set_error(FENCE_E_ARG, "generate: bad arguments");
     if (n_prompt > m->cfg.max_ctx) return set_error(FENCE_E_ARG, "generate: prompt longer than max_ctx");
     cudaSetDevice(m->dev);
+    m->fwd_valid = 0;
     std::vector<int> output(prompt, prompt + n_prompt);
     // prefill, token by token as in the reference (qwen3.cu:478-481); no host sync between tokens
     for (int i = 0; i < n_prompt; ++i) {
@@ -1018,7 +1047,9 @@ extern "C" int fence_generate(fence_model* m, const int* prompt, int n_prompt, i
         if (rc) return rc;
         ++pos;
     }
+    if (const int fr = fetch_state(m)) return fr;
     FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    if (const int st = state_status(m, "generate")) return st;
     const int n = (int)std::min<size_t>(output.size(), (size_t)out_cap);
     std::copy(output.begin(), output.begin() + n, out);
     *n_out = (int)output.size();
@@ -1030,19 +1061,22 @@ extern "C" int fence_decode_greedy(fence_model* m, int token, int pos, int n_ste
     if (pos < 0 || pos + n_steps > m->cfg.max_ctx || n_steps > m->token_log_cap)
         return set_error(FENCE_E_ARG, "decode_greedy: positions [%d, %d) exceed max_ctx", pos, pos + n_steps);
     cudaSetDevice(m->dev);
+    m->fwd_valid = 0;
     int rc = set_state(m, token, pos, 0);
     if (rc) return rc;
     for (int s = 0; s < n_steps; ++s)
         if ((rc = run_step(m))) return rc;
     FENCE_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->token_log, (size_t)n_steps * sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    if ((rc = fetch_state(m))) return rc;
     FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
-    return FENCE_OK;
+    return state_status(m, "decode_greedy");
 }
 
 extern "C" int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms) {
     if (!m || !ms || n_steps <= 0) return set_error(FENCE_E_ARG, "time_decode: bad arguments");
     if (pos < 0 || pos + n_steps > m->cfg.max_ctx) return set_error(FENCE_E_ARG, "time_decode: positions exceed max_ctx");
     cudaSetDevice(m->dev);
+    m->fwd_valid = 0;
     cudaEvent_t e0, e1;
     FENCE_CUDA_TRY(cudaEventCreate(&e0));
     FENCE_CUDA_TRY(cudaEventCreate(&e1));
@@ -1052,6 +1086,9 @@ extern "C" int fence_time_decode(fence_model* m, int token, int pos, int n_steps
     if (!rc) rc = cuda_status(cudaEventRecord(e1, m->stream), "event record");
     if (!rc) rc = cuda_status(cudaEventSynchronize(e1), "event sync");
     if (!rc) rc = cuda_status(cudaEventElapsedTime(ms, e0, e1), "elapsed");
+    if (!rc) rc = fetch_state(m);
+    if (!rc) rc = cuda_status(cudaStreamSynchronize(m->stream), "time_decode");
+    if (!rc) rc = state_status(m, "time_decode");
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     return rc;

@@ -56,7 +56,7 @@ struct DecodeState {
     int token;
     int pos;
     int step;
-    int pad;
+    int err;  // the device error word as the step that wrote token saw it at its end (0 = ok)
 };
 
 struct GemvArgs {

@@ -674,6 +674,7 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
                     st->pos = st->pos + 1;
                     if (a.token_log && st->step < a.token_log_cap) a.token_log[st->step] = gi;
                     st->step = st->step + 1;
+                    st->err = *reinterpret_cast<volatile int*>(&g_device_error);
                 }
                 *a.counter = 0u;
             }

@@ -103,6 +103,7 @@ struct StepArgs {
     int vocab0;          // first vocabulary row of this rank's LM-head shard
     uint8_t* xb[SK_TP_MAX];
     unsigned long long* launch;  // steps this rank has finished (read at the start, +1 at the end)
+    int stall_phase;     // test only: this phase's counter wait gets an unreachable target (-1 = off)
 };
 
 constexpr uint32_t SK_DESC = (sizeof(SPhase) + 15u) & ~15u;  // one phase descriptor in shared memory
@@ -941,7 +942,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             if (tid == 0) {
                 // acquire: the other CTAs' phase k-1 writes (released by their counts) become
                 // visible to this thread and, through the CTA barrier below, to the whole CTA
-                const unsigned long long target = base + (unsigned long long)k * G;
+                const unsigned long long target =
+                    k == A.stall_phase ? ~0ull : base + (unsigned long long)k * G;
                 bool ok = false;
                 for (uint32_t it = 0; it < SK_BAR_SPINS; ++it) {
                     if (sk_ld_acquire(A.bar) >= target) { ok = true; break; }
@@ -1056,6 +1058,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         }
     }
 
+    cp_async_wait_all();  // an attention tile prefetch of a step that gave up is not left in flight
     // ---- argmax of the LM head: thread -> warp -> CTA -> (last CTA of the step) global
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1127,6 +1130,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             st->pos = st->pos + 1;
             if (A.token_log && st->step < A.token_log_cap) A.token_log[st->step] = gi;
             st->step = st->step + 1;
+            st->err = *reinterpret_cast<volatile int*>(&g_device_error);
         }
     }
 }

@@ -1,28 +1,42 @@
-"""Benchmark: batch-1 greedy decode tokens/s of the Qwen3-4B-shaped Q6_K model
-on B200. The roofline object is the step kernel's (one launch per token: the dominant and only
-kernel of the decode loop) against measured HBM bandwidth; the drop-in config-0 Q6_K GEMV is
-reported beside it (gemv_config0), with the CPU baseline.
+"""Benchmark: batch-1 greedy decode tokens/s on B200, BASELINE's north-star configuration.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config NAME]
-                  [--prompt P] [--layers L] [--tp]
+                  [--prompt P] [--layers L] [--replicas] [--repeats R] [--no-extras]
 
---prompt sets the prefill length (default: the config's own, 128 / 4000 / 512 for configs 1 / 2 / 3);
---layers cuts the model to L layers for small ncu captures only (the line then names the layer
-count and is not a measurement of the config). --tp (with N > 1 ranks) splits ONE model over the
-ranks (tensor parallel, config 3: `--config qwen3-14b --tp`): value = that one sequence's tokens/s,
-scaling "strong"; without it the N ranks are independent replicas (configs 1 and 2).
+Defaults: N = 1 runs config 2 (`llama3-8b-q8`: Llama-3.1-8B shape, every linear Q8_0, KV cache
+prefilled with 4000 positions, decode at max-ctx 4096) — the largest single-GPU configuration and
+the one the north star's >= 70 % roofline target is stated on. N > 1 (one process per GPU under
+torchrun) runs config 3 (`qwen3-14b`) tensor parallel over the N ranks: ONE sequence split across
+the GPUs (strong scaling; value = that sequence's tokens/s); `--replicas` instead runs N independent
+copies of the config (weak scaling, no data-path collective).
 
-One JSON line is printed by rank 0. A step is one decode token (batch 1). Inputs are synthetic
-(seeded random-init GGUF of the config's exact shapes; no checkpoints exist offline). With N > 1,
-every rank decodes its own replica (weak scaling, no data-path collective); the value is the sum
-over ranks of tokens / max-over-ranks time.
+A step is one decode token (batch 1). Inputs are synthetic: a seeded random-init GGUF with the
+config's exact shapes and weight distributions (no checkpoints exist offline); the prompt is
+uniform-random token ids, prefilled token by token (untimed). The timed region is K device-resident
+decode steps (one step-kernel launch each, CUDA events on the engine's stream), bracketed by a
+barrier and synchronisations; it is repeated R times at the same positions (R chosen so the timed
+regions span >= 1.5 s for the clock samples) and the median repeat, max over ranks, is reported.
 
---impl reference times the reference's algorithm on the host cores (the oracle port of the token
-loop, oracle/fence_oracle.c, all threads), on the same config; only rank 0 runs it.
+The line carries, besides the contract keys: `roofline` (the step kernel: algorithmic bytes per
+launch = every weight byte once + the embedding row + the K/V rows read, against the measured HBM
+copy bandwidth), `e2e` (the same decode through fence_forward + fence_sample_greedy from the host),
+`cpu_baseline` (the reference's own scalar Q6_K dequant-dot GEMV, tests/test_gemv_q6k.cu:117-128,
+on config 0 on the host cores, 1 thread and all threads), `cpu_port_decode` (the CPU restatement of
+the token loop at the same positions), and with N = 1 the extra keys `gemv_config0` (the drop-in
+Q6_K GEMV on config 0), `config1` (Qwen3-4B shape, with the reference's own CUDA forward on this
+B200 beside it) and `config3_tp1` (config 3 on one GPU: the base of the N > 1 strong-scaling runs).
+
+--impl reference times the reference's algorithm for the path on the host cores: the CPU
+restatement of the token loop (oracle/fence_oracle.c; the reference has no CPU forward of its own,
+only the per-GEMV host oracle reported in cpu_baseline), all threads, same config and positions,
+a bounded number of tokens; only rank 0 runs it. It writes its model file with oracle/libsynth.so
+and never loads the product library.
 """
 import argparse
 import json
+import math
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -38,8 +52,10 @@ from __graft_entry__ import _load_pkg  # noqa: E402
 
 PROMPT_LEN = {"qwen3-4b": 128, "llama3-8b-q8": 4000, "qwen3-14b": 512}
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
 CONFIG0_BYTES = 4096 * 16 * 210 + 4096 * 2 + 4096 * 4  # W + fp16 x + fp32 y = 13,787,136
+MIN_TIMED_S = 1.5
 
 
 def hbm_peak():
@@ -50,35 +66,19 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_from_profiles(name, key="traffic_bytes_per_launch"):
-    """A per-launch DRAM byte count recorded in a committed ncu summary under profiles/, if any."""
-    p = os.path.join(ROOT, "profiles", name)
+def traffic_record(name):
+    """A machine-readable ncu figure (profiles/traffic.json) for a kernel / workload, or None."""
     try:
-        for line in open(p):
-            if line.startswith(key + ":"):
-                return int(line.split(":")[1].strip())
+        return json.load(open(TRAFFIC_PATH)).get(name)
     except (OSError, ValueError):
-        pass
-    return None
-
-
-def traffic_ratio_from_profiles(name):
-    """DRAM bytes / algorithmic bytes of one step-kernel launch, from a committed ncu summary of a
-    smaller cut of the same config (the traffic scales with the bytes streamed)."""
-    try:
-        for line in open(os.path.join(ROOT, "profiles", name)):
-            if line.startswith("traffic_ratio:"):
-                return float(line.split(":")[1].strip())
-    except (OSError, ValueError):
-        pass
-    return None
+        return None
 
 
 def step_algorithmic_bytes(cfg, positions):
     """Bytes one decode token must move (the roofline numerator): every weight streamed once
     (layer linears + the tied LM head, weight_bytes), the token's embedding row, and the K and V
     rows of the context read by attention (fp16), averaged over the timed positions."""
-    kv_dim = cfg.n_kv_heads * cfg.head_dim
+    kv_dim = cfg.n_kv_heads * cfg.head_dim // max(1, cfg.tp_size)
     embed_row = cfg.embed_dim // 32 * 34
     kv = sum(2 * cfg.n_layers * (p + 1) * kv_dim * 2 for p in positions) / max(1, len(positions))
     return int(cfg.weight_bytes + embed_row + kv)
@@ -94,6 +94,7 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
@@ -111,8 +112,6 @@ class ClockSampler:
             self.proc.terminate()
             out, _ = self.proc.communicate(timeout=10)
             self.lines = [l for l in out.splitlines() if l.strip()]
-        else:
-            self.lines = []
 
     def summary(self):
         sm, mx, reasons = [], [], set()
@@ -134,6 +133,16 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def cpu_model_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
 def synth_model(fb, config, tmp, layers=0):
     path = os.path.join(tmp, f"{config}.gguf")
     if layers > 0:
@@ -141,6 +150,84 @@ def synth_model(fb, config, tmp, layers=0):
     else:
         fb.synth_write(path, config, seed=2024)
     return path
+
+
+def shm_dir(need_bytes):
+    try:
+        st = os.statvfs("/dev/shm")
+        return "/dev/shm" if st.f_bavail * st.f_frsize > need_bytes else None
+    except OSError:
+        return None
+
+
+# ------------------------------------------------------------------ GPU decode measurement
+def measure_decode(fb, torch, model, prompt_len, steps, warmup, repeats, dist=None, tp=False, seed=7,
+                   e2e_steps=None, clocks_index=None):
+    """Prefill (untimed, token by token as the reference), W warm-up steps, then R timed regions of
+    K device-resident decode steps at the same positions; e2e through fence_forward +
+    fence_sample_greedy from the host. Returns a dict (times max over ranks)."""
+    cfg = model.config
+    rng = np.random.default_rng(seed)
+    prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, prompt_len)]
+    d = None
+    for pos, t in enumerate(prompt):
+        d = model.forward(t, pos)
+    first = model.sample_greedy(d)
+    pos = prompt_len
+    warm_ids = model.decode_greedy(first, pos, warmup)
+    pos += warmup
+    tok = warm_ids[-1]
+    torch.cuda.synchronize()
+    # repeats: enough timed regions to span MIN_TIMED_S (the same count on every rank)
+    if repeats <= 0:
+        probe = model.time_decode(tok, pos, steps)
+        repeats = int(min(60, max(3, math.ceil(MIN_TIMED_S * 1e3 / max(probe, 1e-3)))))
+    if dist:
+        t = torch.tensor([repeats], device="cuda", dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        repeats = int(t.item())
+    times = []
+    clk = ClockSampler(clocks_index) if clocks_index is not None else None
+    if clk:
+        clk.__enter__()
+    try:
+        for _ in range(repeats):
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            ms = model.time_decode(tok, pos, steps)  # CUDA events; raises on a device wait error
+            torch.cuda.synchronize()
+            times.append(ms)
+    finally:
+        if clk:
+            clk.__exit__()
+    if dist:
+        t = torch.tensor(times, device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times = [float(x) for x in t.tolist()]
+        dist.barrier()
+    ms = statistics.median(times)
+    positions = range(pos, pos + steps)
+    pos += steps
+    # e2e through the reference-facing API: forward(token, pos) from the host (16-byte state H2D from
+    # pinned memory, 16-byte state D2H) + sample_greedy every step
+    e2e_steps = e2e_steps or min(steps, 64)
+    nxt = tok
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        dl = model.forward(nxt, pos + i)
+        nxt = model.sample_greedy(dl)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    return {"ms": ms, "times": times, "repeats": repeats, "positions": positions, "e2e_tok_s": e2e_steps / e2e_s,
+            "e2e_steps": e2e_steps, "step_bytes": step_algorithmic_bytes(cfg, positions),
+            "clocks": clk.summary() if clk else None}
 
 
 def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
@@ -185,16 +272,72 @@ def measure_gemv_roofline(fb, torch, copies=32, launches=256, pdl=True):
     return ms
 
 
-def cpu_decode_sample(path, budget_s, max_tokens, threads):
-    """Oracle port of the token loop on the host cores: decode tokens at positions 0.. until the time
-    budget is spent (at least one). Returns (tokens, seconds)."""
+# ------------------------------------------------------------------ CPU legs (checker libraries)
+def cpu_reference_gemv():
+    """The reference's own scalar Q6_K dequant-dot GEMV (cpu_gemv_q6k, tests/test_gemv_q6k.cu:117-128,
+    compiled unmodified into oracle/_ref/libref_cpu.so) on config 0 (4096 x 4096, seeded blocks,
+    x N(0,1) rounded to fp16): 1 thread as shipped, and all host threads as a row split of the
+    unchanged per-row loop (one call per row range, threads released from the GIL by ctypes).
+    Median of 5 runs each, in GB/s of CONFIG0_BYTES. None when the library was not built."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as orc  # CPU-baseline leg only
-    m = orc.OracleModel(path, max_ctx=4096, kv_bf16=True, threads=threads)
+    ref = orc.ref_cpu()
+    if ref is None:
+        return None
+    M = K = 4096
     rng = np.random.default_rng(0)
+    # seeded Q6_K blocks with the config-0 distribution, generated here (no product library): ql/qh
+    # uniform bytes, int8 scales uniform in [-127, 127], d = fp16(1.5e-5)
+    blk = np.empty((M * K // 256, 210), np.uint8)
+    blk[:, :192] = rng.integers(0, 256, (blk.shape[0], 192), dtype=np.uint8)
+    blk[:, 192:208] = rng.integers(-127, 128, (blk.shape[0], 16)).astype(np.int8).view(np.uint8)
+    blk[:, 208:210] = np.frombuffer(np.float16(1.5e-5).tobytes(), np.uint8)
+    W = np.ascontiguousarray(blk)
+    x = rng.standard_normal(K).astype(np.float32).astype(np.float16).view(np.uint16).copy()
+    y = np.empty(M, np.float64)
+    row_bytes = K // 256 * 210
+
+    def run(threads):
+        if threads == 1:
+            t0 = time.perf_counter()
+            ref.ref_cpu_gemv_q6k(W.ctypes.data, x.ctypes.data, y.ctypes.data, M, K)
+            return time.perf_counter() - t0
+        bounds = [M * i // threads for i in range(threads + 1)]
+
+        def part(i):
+            r0, r1 = bounds[i], bounds[i + 1]
+            ref.ref_cpu_gemv_q6k(W.ctypes.data + r0 * row_bytes, x.ctypes.data, y.ctypes.data + 8 * r0, r1 - r0, K)
+        ths = [threading.Thread(target=part, args=(i,)) for i in range(threads)]
+        t0 = time.perf_counter()
+        for t in ths:
+            t.start()
+        for t in ths:
+            t.join()
+        return time.perf_counter() - t0
+
+    threads = os.cpu_count() or 1
+    run(1)  # warm-up
+    t1 = statistics.median(run(1) for _ in range(5))
+    run(threads)
+    tn = statistics.median(run(threads) for _ in range(5))
+    return {"gbs_1_thread": CONFIG0_BYTES / t1 / 1e9, "gbs_all_threads": CONFIG0_BYTES / tn / 1e9,
+            "s_1_thread": t1, "s_all_threads": tn, "threads": threads, "cpu": cpu_model_name()}
+
+
+def cpu_port_decode(path, start_pos, budget_s, max_tokens, threads, seed=7):
+    """The CPU restatement of the token loop (oracle/fence_oracle.c, fp64 accumulation) decoding
+    at positions start_pos.. of a cache pre-filled with seeded K/V rows (the prefill's stand-in),
+    one warm-up token, then tokens until the budget is spent (at least one). Returns (n, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc  # CPU legs only
+    m = orc.OracleModel(path, max_ctx=max(4096, start_pos + max_tokens + 2), kv_bf16=False, threads=threads)
+    m.fill_kv(start_pos, seed)
+    rng = np.random.default_rng(seed)
+    V = m.vocab_size
+    m.forward(int(rng.integers(0, V)), start_pos)  # warm-up (page cache)
     n, t0 = 0, time.perf_counter()
     while n < max_tokens:
-        m.forward(int(rng.integers(0, m.vocab_size)), n)
+        m.forward(int(rng.integers(0, V)), start_pos + 1 + n)
         n += 1
         if time.perf_counter() - t0 > budget_s:
             break
@@ -204,63 +347,122 @@ def cpu_decode_sample(path, budget_s, max_tokens, threads):
 
 
 def run_reference_arm(args, rank, world):
+    """--impl reference: the reference's algorithm for the path on the host cores (rank 0 only)."""
     if rank != 0:
         return
-    fb = _load_pkg()
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import importlib.util
+    import oracle as orc  # reference arm only
+    # the binding module for its config table and struct layout only: the product library is not loaded
+    spec = importlib.util.spec_from_file_location(
+        "fence_b200_cfg", os.path.join(ROOT, "-damn-low-level-fence-inference-version-1_b200", "__init__.py"))
+    cfgmod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(cfgmod)
     threads = os.cpu_count() or 1
+    start = args.prompt + args.warmup
     with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
-        path = synth_model(fb, args.config, tmp)
-        # warm-up: touch the weights once (page cache) with one token
-        cpu_decode_sample(path, 0.0, 1, threads)
-        budget = min(150.0, 2.0 * max(args.steps, 1))
-        n, dt = cpu_decode_sample(path, budget, args.steps, threads)
+        path = os.path.join(tmp, f"{args.config}.gguf")
+        fields = dict(cfgmod.CONFIGS[args.config])
+        fields["seed"] = 2024
+        orc.synth_write(path, cfgmod.SynthSpec, fields, threads)
+        budget = min(120.0, 3.0 * max(args.steps, 1))
+        n, dt = cpu_port_decode(path, start, budget, args.steps, threads)
     value = n / dt
+    sample = (f"{n} of {args.steps} decode tokens of {args.config} at positions {start + 1}..{start + n} "
+              f"(K/V of positions 0..{start} pre-filled with seeded rows in place of the {args.prompt}-token prefill), "
+              f"oracle/fence_oracle.c on {threads} threads, bounded to {budget:.0f} s")
     line = {
         "impl": "reference", "metric": "decode_tokens_per_s", "value": round(value, 4), "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": round(1e3 * dt / n, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic", "config": {"workload": f"{args.config} batch-1 greedy decode (CPU, reference algorithm)",
-                                        "model": args.config},
+        "higher_is_better": True, "scaling": "strong" if args.tp else "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded random-init GGUF, config shapes)",
+        "config": {"workload": f"{args.config} batch-1 greedy decode (CPU restatement of the reference's token loop)",
+                   "model": args.config, "prefill_positions": start},
         "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{n} decode tokens at positions 0..{n - 1} of {args.config}, "
-                                   f"oracle/fence_oracle.c on {threads} threads (steps bounded to {n} of {args.steps} "
-                                   f"requested by a {150:.0f} s budget)"},
+                         "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ extras (N = 1, rank 0)
+def extra_config1(fb, torch, args, kv):
+    """Config 1 (Qwen3-4B shape, Q6_K): this engine's decode and, beside it, the reference's own
+    CUDA forward (src/model/qwen3.cu rebuilt unmodified for sm_100a, oracle/_ref/ref_model) on the
+    same model file, prompt length and B200."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc  # reference-on-B200 comparator only
+    out = {}
+    with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
+        path = synth_model(fb, "qwen3-4b", tmp)
+        m = fb.Model(path, max_ctx=4096, kv_dtype=kv)
+        r = measure_decode(fb, torch, m, 128, 128, 4, 0)
+        cfg = m.config
+        m.close()
+        peak, _ = hbm_peak()
+        gbs = r["step_bytes"] / (r["ms"] / 128 * 1e-3) / 1e9
+        out = {"workload": "qwen3-4b batch-1 greedy decode, 128 prompt tokens, 128 timed steps",
+               "tok_s": round(128 / (r["ms"] / 1e3), 2), "e2e_tok_s": round(r["e2e_tok_s"], 2),
+               "roofline_frac": round(gbs / peak, 4), "achieved_gbs": round(gbs, 1)}
+        if os.path.exists(orc.REF_MODEL):
+            prompt = ",".join(str(int(t)) for t in np.random.default_rng(7).integers(0, cfg.vocab_size, 128))
+            try:
+                p = subprocess.run([orc.REF_MODEL, path, os.path.join(tmp, "ref.bin"), "--tokens", prompt,
+                                    "--steps", "65", "--no-logits"], capture_output=True, text=True, timeout=600)
+                rec = json.loads(p.stdout.strip().splitlines()[-1])
+                out["reference_b200_tok_s"] = round(rec["ref_decode_tok_s"], 2)
+                out["reference_b200_prefill_tok_s"] = round(rec["ref_prefill_tok_s"], 2)
+                out["reference_b200"] = ("the reference's unmodified CUDA forward (src/model/qwen3.cu, -O3 "
+                                         "--use_fast_math, sm_100a) via oracle/_ref/ref_model: 128-token prefill, "
+                                         "64 greedy steps, host-timed forward + sample_greedy")
+            except Exception as e:  # the comparator is optional
+                out["reference_b200_error"] = str(e)[:200]
+    return out
+
+
+def extra_config3_tp1(fb, torch, args, kv):
+    """Config 3 (Qwen3-14B shape) on one GPU: the single-GPU base of the tensor-parallel runs."""
+    with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
+        path = synth_model(fb, "qwen3-14b", tmp)
+        m = fb.Model(path, max_ctx=4096, kv_dtype=kv)
+        r = measure_decode(fb, torch, m, 512, 64, 4, 0)
+        m.close()
+    peak, _ = hbm_peak()
+    gbs = r["step_bytes"] / (r["ms"] / 64 * 1e-3) / 1e9
+    return {"workload": "qwen3-14b batch-1 greedy decode on 1 GPU, 512 prompt tokens, 64 timed steps",
+            "tok_s": round(64 / (r["ms"] / 1e3), 2), "roofline_frac": round(gbs / peak, 4)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=248)
-    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-4b")
+    ap.add_argument("--config", default=None, help="default: llama3-8b-q8 at one rank, qwen3-14b (TP) at N > 1")
     ap.add_argument("--prompt", type=int, default=None, help="prefill tokens (default: the config's own)")
     ap.add_argument("--layers", type=int, default=0, help="cut the model to this many layers (ncu captures)")
-    ap.add_argument("--tp", action="store_true",
-                    help="with N > 1: one model split over the N ranks (tensor parallel, strong scaling) instead "
-                         "of N independent replicas (the default for configs 1 and 2)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N > 1: N independent replicas (weak scaling) instead of one tensor-parallel model")
+    ap.add_argument("--repeats", type=int, default=0, help="timed regions (0: enough for >= 1.5 s)")
     ap.add_argument("--kv", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--tmp", default=None, help="directory for the synthetic GGUF (default: /dev/shm if roomy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the extra keys (config 0 / 1 / 3-TP1)")
     ap.add_argument("--mode", default="decode", choices=["decode", "gemv"],
                     help="gemv: only the config-0 Q6_K GEMV roofline measurement (small; used for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.prompt is None:
-        args.prompt = PROMPT_LEN.get(args.config, 128)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    args.tp = world > 1 and not args.replicas
+    if args.config is None:
+        args.config = "qwen3-14b" if args.tp else "llama3-8b-q8"
+    if args.prompt is None:
+        args.prompt = PROMPT_LEN.get(args.config, 128)
     if args.tmp is None:
-        try:
-            st = os.statvfs("/dev/shm")
-            need = 12e9 * world + 12e9  # one model file per rank (+ the CPU-baseline copy)
-            args.tmp = "/dev/shm" if st.f_bavail * st.f_frsize > need else None
-        except OSError:
-            args.tmp = None
+        args.tmp = shm_dir(20e9 * (1 if args.tp else world) + 20e9)
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
@@ -283,7 +485,9 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     fb = _load_pkg()
-    tp = args.tp and world > 1
+    kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
+    tp = args.tp
+    max_ctx = max(4096, args.prompt + args.warmup + args.steps + 64 + 8)
     with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
         if tp:
             # one model file for all ranks: rank 0 writes it, the others read it (same host)
@@ -294,110 +498,98 @@ def main():
             if rank == 0:
                 synth_model(fb, args.config, box[0], args.layers)
             dist.barrier(group=gloo)
-        else:
-            # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
-            path = synth_model(fb, args.config, tmp, args.layers)
-        kv = fb.FENCE_KV_F16 if args.kv == "f16" else fb.FENCE_KV_BF16
-        e2e_steps = min(args.steps, max(16, args.steps // 2))
-        total_pos = args.prompt + args.warmup + args.steps + e2e_steps + 8
-        max_ctx = max(4096, total_pos)
-        if tp:
             model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world)
             import fence_b200.tp as fbtp
             fbtp.connect(model, gloo)
             dist.barrier(group=gloo)  # every rank has read the file before rank 0 removes it
         else:
+            # every rank writes its own copy (same seed -> identical bytes); ranks stay independent
+            path = synth_model(fb, args.config, tmp, args.layers)
             model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local)
         cfg = model.config
-        rng = np.random.default_rng(7 if tp else 7 + rank)  # tensor parallel: every rank feeds the same tokens
-        prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, args.prompt)]
-        # prefill (token by token, as the reference) — untimed
-        d = None
-        for pos, t in enumerate(prompt):
-            d = model.forward(t, pos)
-        first = model.sample_greedy(d)
-        pos = args.prompt
-        # warm-up decode steps (device-resident chain)
-        warm_ids = model.decode_greedy(first, pos, args.warmup)
-        pos += args.warmup
-        tok = warm_ids[-1]
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        with ClockSampler(local) as clk:
-            torch.cuda.synchronize()
-            ms = model.time_decode(tok, pos, args.steps)
-            torch.cuda.synchronize()
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-            dist.barrier()
-        pos += args.steps
+        r = measure_decode(fb, torch, model, args.prompt, args.steps, args.warmup, args.repeats, dist=dist, tp=tp,
+                           seed=7 if tp else 7 + rank, clocks_index=local)
+        model.close()
+        derr = fb.lib().fence_device_error()
+        if derr != 0:
+            print(json.dumps({"error": f"device error word {derr} after the timed regions"}), flush=True)
+            sys.exit(1)
+        ms = r["ms"]
         tok_s = args.steps / (ms / 1e3)
         value = tok_s if tp else tok_s * world  # one sequence over all ranks / one per replica
-
-        # e2e through the reference-facing API: forward(token, pos) from the host (16-byte state
-        # H2D from pinned memory) + sample_greedy (4-byte id D2H + sync) every step
-        e2e_pos = pos
-        nxt = tok
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for i in range(e2e_steps):
-            dl = model.forward(nxt, e2e_pos + i)
-            nxt = model.sample_greedy(dl)
-        e2e_s = time.perf_counter() - t0
-        e2e_val = e2e_steps / e2e_s * (1 if tp else world)
-        step_bytes = step_algorithmic_bytes(cfg, range(pos - args.steps, pos))
-        model.close()
+        e2e_val = r["e2e_tok_s"] * (1 if tp else world)
+        # CPU legs on the same model file, rank 0 of a single-rank run only
+        cpu_port = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.layers:
+            threads = os.cpu_count() or 1
+            start = args.prompt + args.warmup
+            n, dt = cpu_port_decode(path, start, 15.0, 32, threads)
+            cpu_port = {"value": round(n / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
+                        "sample": f"{n} decode tokens of {args.config} at positions {start + 1}..{start + n} "
+                                  f"(K/V of positions 0..{start} pre-filled with seeded rows), "
+                                  f"oracle/fence_oracle.c (fp64) on {threads} threads, ~15 s"}
 
     peak, peak_kind = hbm_peak()
-    gemv_ms = measure_gemv_roofline(fb, torch, pdl=True)
-    gemv_ms_serial = measure_gemv_roofline(fb, torch, pdl=False)
-    achieved = CONFIG0_BYTES / (gemv_ms * 1e-3) / 1e9
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = os.cpu_count() or 1
-        with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
-            p = synth_model(fb, args.config, tmp)
-            cpu_decode_sample(p, 0.0, 1, threads)
-            n, dt = cpu_decode_sample(p, 20.0, 64, threads)
-        cpu = {"value": round(n / dt, 4), "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"{n} decode tokens of {args.config} at positions 0..{n - 1} through the oracle port "
-                         f"(oracle/fence_oracle.c, fp64) on {threads} host threads, ~20 s"}
-    launches_per_step = 1  # the persistent step kernel: one launch per token
+    step_bytes = r["step_bytes"]
     step_us = ms / args.steps * 1e3
     step_gbs = step_bytes / (step_us * 1e-6) / 1e9
-    ratio = traffic_ratio_from_profiles(f"step_kernel_{args.config.replace('-', '_')}.md")
-    step_traffic = int(ratio * step_bytes) if ratio else None
+    trec = traffic_record(f"step_kernel_{args.config.replace('-', '_')}")
+    step_traffic = int(trec["ratio"] * step_bytes) if trec and "ratio" in trec else None
     line = {
         "metric": "decode_tokens_per_s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
         "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8xint16",
         "data": "synthetic (seeded random-init GGUF, config shapes)",
         "config": {"workload": f"{args.config} batch-1 greedy decode, {args.prompt} prompt tokens, positions "
-                               f"{args.prompt + args.warmup}..{args.prompt + args.warmup + args.steps - 1}"
+                               f"{r['positions'][0]}..{r['positions'][-1]}"
                                + (f" ({args.layers}-layer cut for profiling, not the config)" if args.layers else ""),
-                   "model": args.config, "kv_cache": args.kv, "global_batch": world, "seq_len": total_pos,
+                   "model": args.config, "kv_cache": args.kv, "global_batch": 1 if tp else world,
+                   "seq_len": r["positions"][-1] + 1,
                    "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
+                   "repeats": r["repeats"], "timing": "median of the repeats of K steps, max over ranks",
                    "l2": "weights larger than L2 (no flush needed)"},
         "roofline": {"bound": "hbm", "kernel": "step_kernel (one launch = one whole token step)",
                      "achieved": round(step_gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(step_gbs / peak, 4), "peak_kind": peak_kind,
                      "traffic": step_traffic, "us_per_launch": round(step_us, 2),
-                     "algorithmic_bytes_per_launch": step_bytes},
-        "gemv_config0": {"kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches in a CUDA graph",
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4),
-                         "traffic": traffic_from_profiles("gemv_q6k_config0.md"),
-                         "us_per_launch": round(gemv_ms * 1e3, 3),
-                         "us_per_launch_serialized": round(gemv_ms_serial * 1e3, 3),
-                         "algorithmic_bytes_per_launch": CONFIG0_BYTES},
-        "e2e": {"value": round(e2e_val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 4},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
-        "cpu_baseline": cpu,
+                     "algorithmic_bytes_per_launch": step_bytes,
+                     "traffic_source": (trec or {}).get("summary")},
+        "e2e": {"value": round(e2e_val, 3), "unit": "tokens/s", "h2d_bytes_per_step": 16, "d2h_bytes_per_step": 16,
+                "steps": r["e2e_steps"]},
+        "gpu_launches": args.steps,
+        "gpu_launches_note": "one step-kernel launch per decode step; the K-step region is repeated `repeats` times",
+        "clocks": r["clocks"],
+        "cpu_baseline": None,
+        "cpu_port_decode": cpu_port,
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        g = cpu_reference_gemv()
+        if g:
+            line["cpu_baseline"] = {
+                "value": round(g["gbs_all_threads"] * 1e9 / step_bytes, 5), "unit": "tokens/s", "cores": g["threads"],
+                "kind": "reference",
+                "sample": (f"the reference's scalar Q6_K dequant-dot GEMV cpu_gemv_q6k (tests/test_gemv_q6k.cu:117-128, "
+                           f"oracle/_ref/libref_cpu.so) on config 0, median of 5: {g['gbs_all_threads']:.3f} GB/s on "
+                           f"{g['threads']} threads (row split), {g['gbs_1_thread']:.3f} GB/s on 1 thread; value = that "
+                           f"weight-streaming rate over this config's {step_bytes / 1e9:.3f} GB per token"),
+                "gbs_all_threads": round(g["gbs_all_threads"], 4), "gbs_1_thread": round(g["gbs_1_thread"], 4),
+                "cpu": g["cpu"]}
+    if rank == 0 and world == 1 and not args.no_extras and not args.layers:
+        gemv_ms = measure_gemv_roofline(fb, torch, pdl=True)
+        gemv_ms_serial = measure_gemv_roofline(fb, torch, pdl=False)
+        achieved = CONFIG0_BYTES / (gemv_ms * 1e-3) / 1e9
+        grec = traffic_record("gemv_q6k_config0") or {}
+        line["gemv_config0"] = {
+            "kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches in a CUDA graph",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "traffic": grec.get("bytes_per_launch"), "us_per_launch": round(gemv_ms * 1e3, 3),
+            "us_per_launch_serialized": round(gemv_ms_serial * 1e3, 3), "algorithmic_bytes_per_launch": CONFIG0_BYTES}
+        line["config1"] = extra_config1(fb, torch, args, kv)
+        line["config3_tp1"] = extra_config3_tp1(fb, torch, args, kv)
+        derr = fb.lib().fence_device_error()
+        if derr != 0:
+            print(json.dumps({"error": f"device error word {derr} after the extra measurements"}), flush=True)
+            sys.exit(1)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:

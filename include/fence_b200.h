@@ -172,9 +172,12 @@ int fence_sample_nucleus_dev(const float* logits, int vocab, const int* history,
  * split-context partials live in a per-device static array of FENCE_ATTN_STATIC_FLOATS floats
  * (2 MiB). Same split and same results as fence_gqa_attention; a call that needs more than the
  * array (n_q_heads * chunks * (head_dim + 2) floats, chunks as in fence_gqa_attention) returns
- * FENCE_E_SCRATCH without launching. The first call on each device resolves the array's address
- * (cudaGetSymbolAddress) and must come before any stream capture. Calls that overlap in time on
- * one device race on the shared array: order them on one stream. */
+ * FENCE_E_SCRATCH without launching. At head_dim 128 and 64 chunks that admits up to 63 query
+ * heads, at head_dim 256 up to 31. The first call on each device resolves the array's address
+ * (cudaGetSymbolAddress) and caches it per device ordinal; make that first call before any stream
+ * capture. The cache does not survive cudaDeviceReset: after a reset of a device the address may
+ * change, so do not call this entry point on that device again in the same process. Calls that
+ * overlap in time on one device race on the shared array: order them on one stream. */
 #define FENCE_ATTN_STATIC_FLOATS 524288
 int fence_gqa_attention_static(float* attn_out, const float* q, const uint16_t* k_cache,
                                const uint16_t* v_cache, int head_dim, int n_q_heads, int n_kv_heads,
@@ -213,16 +216,22 @@ typedef struct fence_load_opts {
     int device;         /* CUDA device ordinal                                            */
     int use_graph;      /* capture the token step in a CUDA graph (default 1)             */
     int verbose;        /* print the reference's load banner                              */
-    /* tensor parallel: rank `tp_rank` of `tp_size` (see fence_tp_connect); nccl_comm is unused
-     * (the ranks exchange inside the step kernel over NVLink peer memory) and must be NULL */
+    /* tensor parallel: rank `tp_rank` of `tp_size` (see fence_tp_connect); the ranks exchange
+     * inside the step kernel over NVLink peer memory, so no communicator is passed */
     int tp_rank, tp_size;
-    void* nccl_comm;
     /* 1 (default): the whole token step is one persistent kernel (weights of all phases stream
      * continuously, phases separated by a grid-wide counter); 0: one kernel per phase            */
     int step_kernel;
+    /* Test only, no counterpart in the reference: index of a step-kernel phase whose grid-counter
+     * wait is given a target that no CTA ever reaches, so that this bounded wait runs out (about a
+     * second), the step ends early with invalid results and the error surfaces as
+     * FENCE_E_DEVICE_WAIT (fence_device_error, and the status of the engine calls that sync).
+     * -1 (the default) = off. */
+    int wait_test_phase;
 } fence_load_opts;
 
-/* Fills *opts with defaults (max_ctx 4096, fp16 KV, device 0, graphs on, single rank, step kernel). */
+/* Fills *opts with defaults (max_ctx 4096, fp16 KV, device 0, graphs on, single rank, step kernel,
+ * wait_test_phase -1). */
 void fence_load_opts_default(fence_load_opts* opts);
 
 /* Qwen3Model::load (src/model/qwen3.cu:116-228): mmap the GGUF, read the config from its metadata

@@ -560,6 +560,33 @@ void oracle_model_close(oracle_model* m) {
     free(m);
 }
 
+/* Benchmark support (not in the reference): fills the K and V cache rows of positions [0, n_pos)
+ * of every layer with seeded values (SplitMix64 words mapped to about N(0, 0.5) through a sum of
+ * four uniforms), rounded to the cache type, as a stand-in for a prefill of n_pos tokens: the
+ * decode steps after it do exactly the work they would do after a real prefill. */
+static uint64_t o_splitmix(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+int oracle_model_fill_kv(oracle_model* m, int n_pos, uint64_t seed) {
+    if (!m || n_pos < 0 || n_pos > m->max_ctx) return -1;
+    const size_t kvd = (size_t)m->nkv * m->hd;
+    for (int l = 0; l < m->L; ++l)
+        for (int c = 0; c < 2; ++c) {
+            uint16_t* base = (c ? m->vc : m->kc) + (size_t)l * m->max_ctx * kvd;
+            for (size_t i = 0; i < (size_t)n_pos * kvd; ++i) {
+                const uint64_t r = o_splitmix(seed ^ ((uint64_t)(2 * l + c) << 40) ^ i);
+                float u = 0.f;
+                for (int j = 0; j < 4; ++j) u += (float)((r >> (16 * j)) & 0xffff) / 65536.0f;
+                const float v = (u - 2.0f) * 0.866f;
+                base[i] = m->kv_bf16 ? oracle_f2bf(v) : oracle_f2h(v);
+            }
+        }
+    return 0;
+}
+
 void oracle_model_dims(const oracle_model* m, int* d) {
     d[0] = m->L;
     d[1] = m->H;

@@ -74,6 +74,7 @@ oracle_model* oracle_model_open(const char* path, int max_ctx, int kv_bf16, int 
 void oracle_model_close(oracle_model* m);
 /* dims[0..9] = layers, embed, ff, heads, kv_heads, head_dim, vocab, max_ctx, linear_type, qk_norm */
 void oracle_model_dims(const oracle_model* m, int* dims);
+int oracle_model_fill_kv(oracle_model* m, int n_pos, uint64_t seed);
 /* Qwen3Model::forward (qwen3.cu:241-265): logits[vocab] for `token` at `pos`. 0 = ok. */
 int oracle_forward(oracle_model* m, int token, int pos, float* logits);
 /* Hidden state after the final norm of the last forward (embed_dim floats). */

@@ -4,6 +4,8 @@
 * _ref/libref_cpu.so : the reference's own fp64 host oracle and golden blocks, compiled from the
                        reference tree (tests/test_gemv_q6k.cu, tests/test_q6k_dot.cu)
 * _ref/ref_model     : the reference's CUDA forward rebuilt for sm_100a (GPU only)
+* _ref/ref_model_tsw : the same forward, restated with a per-linear type switch to the reference's
+                       own gemv_q8_0 for Q8_0 linears (all-Q8_0 config 2; GPU only)
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this module.
 """
@@ -18,6 +20,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_CPU_SO = os.path.join(HERE, "_ref", "libref_cpu.so")
 REF_MODEL = os.path.join(HERE, "_ref", "ref_model")
+# oracle extension: the reference's forward restated with a per-linear type switch to its own
+# gemv_q8_0 (all-Q8_0 models, which the reference's loader cannot run); GPU only
+REF_MODEL_TSW = os.path.join(HERE, "_ref", "ref_model_tsw")
 
 _vp = ctypes.c_void_p
 _o = None
@@ -54,6 +59,7 @@ def oracle() -> ctypes.CDLL:
             "oracle_model_dims": (None, [_vp, _vp]),
             "oracle_forward": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
             "oracle_last_hidden": (None, [_vp, _vp]),
+            "oracle_model_fill_kv": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_uint64]),
         }
         for n, (res, args) in sig.items():
             f = getattr(L, n)
@@ -81,6 +87,32 @@ def ref_cpu() -> ctypes.CDLL | None:
         L.ref_dot_case_name.restype = ctypes.c_char_p
         _r = L
     return _r
+
+
+SYNTH_SO = os.path.join(HERE, "libsynth.so")
+_s = None
+
+
+def synth_write(path: str, spec_cls, fields: dict, threads: int = 0) -> None:
+    """Writes a seeded synthetic GGUF through oracle/libsynth.so (the package's writer built on its
+    own), byte-identical to the product library's fence_synth_write_gguf. spec_cls is the
+    fence_synth_spec ctypes structure; fields override its defaults."""
+    global _s
+    if _s is None:
+        L = ctypes.CDLL(SYNTH_SO)
+        L.fence_synth_spec_default.argtypes = [ctypes.c_void_p]
+        L.fence_synth_spec_default.restype = None
+        L.fence_synth_write_gguf.argtypes = [ctypes.c_char_p, ctypes.c_void_p, ctypes.c_int]
+        L.fence_synth_write_gguf.restype = ctypes.c_int
+        L.oracle_synth_last_error.restype = ctypes.c_char_p
+        _s = L
+    spec = spec_cls()
+    _s.fence_synth_spec_default(ctypes.byref(spec))
+    for k, v in fields.items():
+        setattr(spec, k, v)
+    rc = _s.fence_synth_write_gguf(path.encode(), ctypes.byref(spec), threads)
+    if rc != 0:
+        raise RuntimeError(f"synth_write failed ({rc}): {_s.oracle_synth_last_error().decode()}")
 
 
 def _p(a: np.ndarray):
@@ -125,6 +157,11 @@ class OracleModel:
         oracle().oracle_model_dims(self._h, _p(d))
         (self.n_layers, self.embed_dim, self.ff_dim, self.n_heads, self.n_kv_heads, self.head_dim,
          self.vocab_size, self.max_ctx, self.linear_type, self.qk_norm) = (int(v) for v in d)
+
+    def fill_kv(self, n_pos: int, seed: int = 1) -> None:
+        """Seeded K/V rows for positions [0, n_pos): stands in for a prefill (benchmark use)."""
+        if oracle().oracle_model_fill_kv(self._h, n_pos, seed) != 0:
+            raise ValueError("fill_kv: bad position count")
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         out = np.empty(self.vocab_size, dtype=np.float32)

@@ -41,3 +41,23 @@ def orc():
 @pytest.fixture(scope="session")
 def tmpdir_session(tmp_path_factory):
     return tmp_path_factory.mktemp("fence")
+
+
+@pytest.fixture(autouse=True)
+def _device_error_word(request):
+    """After every GPU test: no kernel of the library gave up on a bounded wait (the device error
+    word, read and cleared by fence_device_error, is 0). Tests that make a wait run out on purpose
+    read and clear the word themselves."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    mod = sys.modules.get("fence_b200")
+    if mod is None or mod._lib is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    for d in range(torch.cuda.device_count()):
+        with torch.cuda.device(d):
+            word = mod.lib().fence_device_error()
+            assert word == 0, f"device {d}: device error word {word} after {request.node.nodeid}"

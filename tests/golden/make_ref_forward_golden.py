@@ -31,8 +31,8 @@ def fixture_tokens():
     return prompt, teacher
 
 
-def run_reference(model_path, prompt, teacher, steps, max_ctx, out_path, logits=True):
-    cmd = [orc.REF_MODEL, model_path, out_path, "--tokens", ",".join(map(str, prompt)), "--steps", str(steps),
+def run_reference(model_path, prompt, teacher, steps, max_ctx, out_path, logits=True, binary=None):
+    cmd = [binary or orc.REF_MODEL, model_path, out_path, "--tokens", ",".join(map(str, prompt)), "--steps", str(steps),
            "--max-ctx", str(max_ctx)]
     if teacher:
         cmd += ["--teacher", ",".join(map(str, teacher))]

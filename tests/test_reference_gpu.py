@@ -2,6 +2,11 @@
 for sm_100a as oracle/_ref/ref_model), the bar BASELINE.json's north star sets: logits within
 max-abs 2e-2 per logit and identical greedy ids for the first 64 generated tokens.
 
+All-Q8_0 models (config 2) cannot run on the reference's forward (its loader casts every linear to
+Q6_K); they are compared with oracle/_ref/ref_model_tsw, the same forward restated with a
+per-linear type switch to the reference's own gemv_q8_0 on fp32 x. That harness is first pinned to
+the unmodified forward on a Q6_K model, where the two must agree exactly.
+
 The reference keeps its KV cache in fp16, and so does the engine by default: the strict comparison
 runs that configuration. The optional bf16 cache rounds each cached K/V element with a 2^-8
 relative step instead of fp16's 2^-11, so its logits sit further from the reference's; it is
@@ -24,9 +29,13 @@ LOGIT_ATOL = 2e-2
 BF16_LOGIT_ATOL = 8e-2
 
 
-def need_ref(orc):
-    if not os.path.exists(orc.REF_MODEL):
-        pytest.skip("oracle/_ref/ref_model was not built (reference tree absent at build time)")
+def need_ref(orc, binary=None):
+    if not os.path.exists(binary or orc.REF_MODEL):
+        pytest.skip("oracle/_ref reference binaries were not built (reference tree absent at build time)")
+
+
+def shm_dir(tmp_path):
+    return "/dev/shm" if os.path.isdir("/dev/shm") else str(tmp_path)
 
 
 def engine_teacher(fb, path, kv, prompt, teacher, steps, max_ctx):
@@ -63,18 +72,55 @@ def test_tiny_model_vs_reference(fb, orc, tmp_path):
             assert np.array_equal(ids, rids)
 
 
-@pytest.mark.parametrize("config,prompt_len", [("qwen3-4b", 128)])
-def test_config1_greedy_64_vs_reference(fb, orc, tmp_path, config, prompt_len):
-    """Config 1 (Qwen3-4B shape): free-running greedy decode, 64 tokens, fp16 KV."""
+def test_type_switch_harness_pinned_to_reference_forward(fb, orc, tmp_path):
+    """On a Q6_K model the type-switch harness runs exactly the reference's kernels in the
+    reference's order: its logits and ids equal the unmodified forward's bit for bit."""
     need_ref(orc)
-    d = "/dev/shm" if os.path.isdir("/dev/shm") else str(tmp_path)
+    need_ref(orc, orc.REF_MODEL_TSW)
+    p = str(tmp_path / "tiny.gguf")
+    fb.synth_write(p, "tiny-q6k", seed=23)
+    rng = np.random.default_rng(31)
+    prompt = rng.integers(0, 2048, 20).tolist()
+    (V, _, rids, rlog), _ = run_reference(p, prompt, [], 16, 256, str(tmp_path / "a.bin"))
+    (V2, _, tids, tlog), _ = run_reference(p, prompt, [], 16, 256, str(tmp_path / "b.bin"), binary=orc.REF_MODEL_TSW)
+    assert V == V2
+    assert np.array_equal(rids, tids)
+    assert np.array_equal(rlog, tlog)
+
+
+def test_tiny_q8_vs_reference_type_switch(fb, orc, tmp_path):
+    """All-Q8_0 tiny model against the type-switch harness (reference gemv_q8_0 on fp32 x)."""
+    need_ref(orc, orc.REF_MODEL_TSW)
+    p = str(tmp_path / "tq8.gguf")
+    fb.synth_write(p, "tiny-q8", seed=25)
+    rng = np.random.default_rng(35)
+    prompt = rng.integers(0, 2048, 24).tolist()
+    teacher = rng.integers(0, 2048, 31).tolist()
+    (V, _, rids, rlog), _ = run_reference(p, prompt, teacher, 32, 256, str(tmp_path / "d.bin"),
+                                          binary=orc.REF_MODEL_TSW)
+    ids, log = engine_teacher(fb, p, fb.FENCE_KV_F16, prompt, teacher, 32, 256)
+    err = np.abs(log.astype(np.float64) - rlog)
+    assert err.max() < LOGIT_ATOL, err.max()
+    assert np.array_equal(ids, rids)
+
+
+# (config, prompt tokens, reference binary): config 1 and config 3 (at one GPU) run the unmodified
+# forward; config 2 (all Q8_0, 4000-position prefill, max_ctx 4096) the type-switch harness
+FULL_CONFIGS = [("qwen3-4b", 128, "ref"), ("llama3-8b-q8", 4000, "tsw"), ("qwen3-14b", 512, "ref")]
+
+
+@pytest.mark.parametrize("config,prompt_len,binary", FULL_CONFIGS)
+def test_config_greedy_64_vs_reference(fb, orc, tmp_path, config, prompt_len, binary):
+    """Free-running greedy decode, 64 tokens, fp16 KV, at the config's full shape and prefill."""
+    exe = orc.REF_MODEL if binary == "ref" else orc.REF_MODEL_TSW
+    need_ref(orc, exe)
     import tempfile
-    with tempfile.TemporaryDirectory(dir=d) as tmp:
-        p = os.path.join(tmp, "c1.gguf")
+    with tempfile.TemporaryDirectory(dir=shm_dir(tmp_path)) as tmp:
+        p = os.path.join(tmp, "m.gguf")
         fb.synth_write(p, config, seed=2024)
-        prompt = np.random.default_rng(77).integers(0, 151936, prompt_len).tolist()
+        prompt = np.random.default_rng(77).integers(0, fb.CONFIGS[config]["vocab_size"], prompt_len).tolist()
         steps = 64
-        (V, _, rids, rlog), out = run_reference(p, prompt, [], steps, 4096, os.path.join(tmp, "d.bin"))
+        (V, _, rids, rlog), out = run_reference(p, prompt, [], steps, 4096, os.path.join(tmp, "d.bin"), binary=exe)
         ids, log = engine_teacher(fb, p, fb.FENCE_KV_F16, prompt, list(rids), steps, 4096)
         err = np.abs(log.astype(np.float64) - rlog).max(axis=1)
         srt = np.sort(rlog, axis=1)
@@ -91,6 +137,8 @@ def test_config1_greedy_64_vs_reference(fb, orc, tmp_path, config, prompt_len):
         for s, m, e in ties:
             assert m <= 2 * e, report
         assert len(ties) <= 2, report
+        if config != "qwen3-4b":
+            return
         # optional bf16 KV cache under teacher forcing on the reference ids
         ids_b, log_b = engine_teacher(fb, p, fb.FENCE_KV_BF16, prompt, list(rids), steps, 4096)
         err_b = np.abs(log_b.astype(np.float64) - rlog).max()
