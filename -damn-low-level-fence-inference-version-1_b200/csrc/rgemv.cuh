@@ -60,6 +60,7 @@ struct RGemvArgs {
     int wt;
     int I;            // items (64 weights) per row
     int np;           // parts per row (rows longer than the consumer lanes are split in np equal parts)
+    int ipl;          // step kernel: items per consumer lane (1 or 2; lane p of a row owns items p, p + LP)
     int R;            // rows per stage (dual: even; rows 2p, 2p+1 are gate/up of pair p)
     int dual;
     int Mv;           // virtual rows (dual: gate/up pairs)
@@ -145,21 +146,24 @@ __host__ __device__ inline int rg_row_pieces(int rs, int np, int ip) {
 // x: one 40-word record per item in shared memory, built by a group of lanes.
 //   Q6_K: xh[16] | xl[16] | corr[4] | xs | 0 0 0 ; word 4c+k = elements 4k..4k+3 of column c
 //   Q8_0: xh[16] | xl[16] | 0 0 0 0 | xs0 | xs1 | 0 0 ; word w = elements 4w..4w+3 of the item
-// Q6_K records are built by 4 lanes (lane q: column q), Q8_0 records by 2 lanes (lane q: block q).
+// Every record is built by 4 lanes of one warp, 16 values each: Q6_K lane q holds column q, Q8_0
+// lane q elements 16q..16q+15 (block q / 2, whose scale is a max over the lane pair).
 // The arithmetic is make_slice's (gemv.cuh) element for element; the group's amax is an exact max.
+constexpr int RG_LPI = 4;   // lanes per x record
+constexpr int RG_NV = 16;   // x values per lane
 template <int WT>
 __device__ __forceinline__ int rg_task_base(int item, int q) {
     if (WT == WT_Q6K) {
         const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
         return b * 256 + h * 128 + q * 32 + l16 * 16;
     }
-    return item * 64 + q * 32;
+    return item * 64 + q * 16;
 }
 
-// Raw x values of one record-building task (Q6_K: 16 values of column q; Q8_0: 32 of block q).
+// Raw x values of one record-building task (Q6_K: 16 values of column q; Q8_0: elements 16q..).
 template <int WT, int XM>
-__device__ __forceinline__ void rg_load_task(const void* xsrc, int base, float (&v)[(WT == WT_Q6K) ? 16 : 32]) {
-    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+__device__ __forceinline__ void rg_load_task(const void* xsrc, int base, float (&v)[RG_NV]) {
+    constexpr int NV = RG_NV;
     if (XM == X_F16) {
         const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xsrc) + base);
 #pragma unroll
@@ -189,9 +193,9 @@ __device__ __forceinline__ void rg_load_task(const void* xsrc, int base, float (
 // item's scale (a max over the lane group: exact) and store the task's words of the record.
 // All lanes of the warp call this (shuffles); lanes with active == false store nothing.
 template <int WT, int XM>
-__device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 32], const float (&w)[(WT == WT_Q6K) ? 16 : 32],
-                                               int q, float rms, uint32_t rec, bool active) {
-    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+__device__ __forceinline__ void rg_quant_store(float (&v)[RG_NV], const float (&w)[RG_NV], int q, float rms,
+                                               uint32_t rec, bool active) {
+    constexpr int NV = RG_NV;
     if (XM == X_NORM || XM == X_NORM_R16) {  // w[i] * x[i] * rms, the reference's order (ops.cuh:43)
 #pragma unroll
         for (int e = 0; e < NV; ++e) v[e] = (v[e] * w[e]) * rms;
@@ -203,10 +207,8 @@ __device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 
     float amax = 0.f;
 #pragma unroll
     for (int e = 0; e < NV; ++e) amax = fmaxf(amax, fabsf(v[e]));
-    if (WT == WT_Q6K) {  // one scale per item: max over its 4 columns
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));      // Q8_0: the block's lane pair
+    if (WT == WT_Q6K) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));  // Q6_K: the item
     float inv;
     const float xs = quant_scale(amax, inv);
     if (!active) return;
@@ -223,7 +225,7 @@ __device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 
             hw |= hb << (8 * j);
             lw |= lb << (8 * j);
         }
-        const uint32_t wi = (WT == WT_Q6K) ? (uint32_t)(4 * q + k) : (uint32_t)(8 * q + k);
+        const uint32_t wi = (uint32_t)(4 * q + k);
         asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 4u * wi), "r"(hw) : "memory");
         asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 64u + 4u * wi), "r"(lw) : "memory");
     }
@@ -233,11 +235,12 @@ __device__ __forceinline__ void rg_quant_store(float (&v)[(WT == WT_Q6K) ? 16 : 
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rec + 144u), "r"(__float_as_uint(xs)),
                          "r"(0u), "r"(0u), "r"(0u) : "memory");
     } else {
-        asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 144u + 4u * q), "r"(__float_as_uint(xs)) : "memory");
+        if ((q & 1) == 0)
+            asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 144u + 2u * q), "r"(__float_as_uint(xs)) : "memory");
         if (q == 0)
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rec + 128u), "r"(0u), "r"(0u), "r"(0u),
                          "r"(0u) : "memory");
-        else
+        else if (q == 1)
             asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(rec + 152u), "r"(0u), "r"(0u) : "memory");
     }
 }
@@ -283,16 +286,17 @@ __device__ __forceinline__ void rg_load_x(uint32_t rec, int item, RX& x) {
 
 // The words of one item a lane needs from a stage: Q6_K ql0 | ql1 | qh (12 words), its scale word
 // and the super-block d; Q8_0 the 4 quant chunks (16 words) and the item's two d.
-struct RW {
-    uint32_t w[16];
+template <int WT>
+struct RWT {
+    uint32_t w[WT == WT_Q6K ? 12 : 16];
     uint32_t sc, d;
 };
 
 // Loads an item's words: q, s, d are 32-bit shared addresses of the item's record, its scale word
 // (Q6_K) and its d (Q6_K: the super-block's fp16; Q8_0: the item's two fp16).
 template <int WT>
-__device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d, uint32_t sw, RW& r) {
-    if (WT == WT_Q6K) {
+__device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d, uint32_t sw, RWT<WT>& r) {
+    if constexpr (WT == WT_Q6K) {
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             const uint4 u = lds128(q + 16u * k);
@@ -313,8 +317,8 @@ __device__ __forceinline__ void rg_item_load(uint32_t q, uint32_t s, uint32_t d,
 
 // 64-weight item dot of loaded words with the lane's x.
 template <int WT>
-__device__ __forceinline__ float rg_item_compute(const RW& r, const RX& x) {
-    if (WT == WT_Q6K) {
+__device__ __forceinline__ float rg_item_compute(const RWT<WT>& r, const RX& x) {
+    if constexpr (WT == WT_Q6K) {
         int hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
         int lo0 = x.corr[0], lo1 = x.corr[1], lo2 = x.corr[2], lo3 = x.corr[3];
 #pragma unroll
@@ -362,7 +366,7 @@ __device__ __forceinline__ float rg_item_compute(const RW& r, const RX& x) {
 // 64-weight item dot of repacked weights straight from shared memory.
 template <int WT>
 __device__ __forceinline__ float rg_item_dot(uint32_t q, uint32_t s, uint32_t d, const RX& x) {
-    RW r;
+    RWT<WT> r;
     rg_item_load<WT>(q, s, d, x.sw, r);
     return rg_item_compute<WT>(r, x);
 }
@@ -463,12 +467,12 @@ __global__ void __launch_bounds__(RG_NT, 2) rgemv_kernel(const __grid_constant__
 
     // ================= consumers
     constexpr int NT = RG_NL;
-    constexpr int LPI = (WT == WT_Q6K) ? 4 : 2;  // lanes per x record
-    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    constexpr int LPI = RG_LPI;  // lanes per x record
+    constexpr int NV = RG_NV;
     constexpr bool NORM = (XM == X_NORM || XM == X_NORM_R16);
     const int ntask = I * LPI;
     // norm weights do not depend on the previous kernel: fetch them before the wait
-    constexpr int PASSES = (WT == WT_Q6K) ? 2 : 1;  // task passes kept in registers (more re-read x)
+    constexpr int PASSES = 2;  // task passes kept in registers (more re-read x)
     float wv[PASSES][NV];
     if (NORM) {
 #pragma unroll

@@ -21,16 +21,22 @@ static bool plan_step_gemv(RGemvArgs& g, int grid, std::string& err) {
         err = "step kernel: empty GEMV phase";
         return false;
     }
-    int np = (I + SK_NL - 1) / SK_NL;
-    while (np <= I && I % np) ++np;
-    const int IP = I / np;
-    int R = std::min((SK_NL / IP) / np, SK_MAX_R);
+    if (I > SK_NL) {
+        err = "step kernel: a linear input width above " + std::to_string(SK_NL * 64) + " values";
+        return false;
+    }
+    // each consumer lane owns one item of one row for the whole phase; a stage holds as many whole
+    // rows as the consumer lanes allow
+    const int J = 1;
+    const int LP = I;
+    int R = std::min(SK_NL / LP, SK_MAX_R);
     const int vcta = (g.Mv + grid - 1) / grid;
     const int rows_cta = vcta * (g.dual ? 2 : 1);
     R = std::max(1, std::min(R, rows_cta));
     int mp = 1;
-    for (int r = 0; r < R; ++r) mp = std::max(mp, rg_row_pieces(r, np, IP));
-    g.np = np;
+    for (int r = 0; r < R; ++r) mp = std::max(mp, rg_part_pieces(r, 0, 1, LP));
+    g.np = 1;
+    g.ipl = J;
     g.R = R;
     g.mp = mp;
     g.rows_cta = rows_cta;

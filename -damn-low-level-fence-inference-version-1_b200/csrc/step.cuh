@@ -8,12 +8,15 @@
 // the consumer warps run the phases in order, separated by a grid-wide phase counter.
 //
 //  * grid: one CTA per SM (cooperative launch: all CTAs co-resident, which the counter needs);
-//    block: SK_NW consumer warps + 1 producer warp (16 warps: 128 registers each).
+//    block: SK_NW = 11 consumer warps + 1 producer warp (384 threads: 168 registers each, so the
+//    stage loop, the x prologue and the attention unit run without register spills; measured
+//    faster than 15 consumer warps at 128 registers and than 8 at 168).
 //  * producer warp (lane 0): walks every GEMV phase's rows of this CTA in order and streams them
 //    (rgemv.cuh repacked layout: q, s, d slices of R rows per stage, 1-D bulk copies, no
 //    multicast) into the ring; it only ever waits for free slots.
-//  * consumers, per GEMV phase (the rgemv.cuh design with 480 lanes): norm weights fetched before
-//    the phase wait; wait for the counter; x quantised once per CTA into shared memory; every stage
+//  * consumers, per GEMV phase (the rgemv.cuh design with 352 lanes): norm weights pulled into L2
+//    by the producer a ring ahead; wait for the counter; x quantised once per CTA into shared
+//    memory (4 lanes per 64-value record); every stage
 //    worked on by all lanes (lane <-> (row, item), x in registers, segmented shuffle reduction,
 //    one shared-memory piece per (row, warp)); after the last stage one thread per row adds the
 //    pieces in a fixed order and runs the fused epilogue; then the CTA counts itself done.
@@ -38,9 +41,9 @@
 
 namespace fence {
 
-constexpr int SK_NW = 15;                 // consumer warps
+constexpr int SK_NW = 11;                 // consumer warps
 constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
-constexpr int SK_NL = SK_NW * 32;         // consumer lanes (480)
+constexpr int SK_NL = SK_NW * 32;         // consumer lanes (352)
 constexpr int SK_MAX_R = 64;              // rows per stage
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
 // Exchange buffer of one rank (tensor parallel): an argmax counter, one argmax (value bits |
@@ -126,17 +129,6 @@ __host__ __device__ inline SKSmem sk_smem_layout(int ring, int slot_bytes, int s
     return L;
 }
 
-// Copies phase descriptor k from global to a shared-memory buffer (consumer warp w, lanes 0..).
-__device__ __forceinline__ void sk_fetch_desc(const SPhase* src, uint8_t* dst, int lane) {
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-    for (int i = lane; i < (int)(sizeof(SPhase) / 16); i += 32) d4[i] = s4[i];
-    if (lane == 0 && sizeof(SPhase) % 16) {
-        const uint8_t* sb = reinterpret_cast<const uint8_t*>(src);
-        for (uint32_t b = sizeof(SPhase) / 16 * 16; b < sizeof(SPhase); ++b) dst[b] = sb[b];
-    }
-}
-
 __device__ __forceinline__ unsigned long long sk_ld_acquire(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -193,8 +185,8 @@ template <int WT, int XM>
 __device__ __forceinline__ void sk_quantise(const void* xsrc, const float* norm_w, float eps, int I, uint32_t xq_sa,
                                             float* misc) {
     constexpr int NT = SK_NL;
-    constexpr int LPI = (WT == WT_Q6K) ? 4 : 2;
-    constexpr int NV = (WT == WT_Q6K) ? 16 : 32;
+    constexpr int LPI = RG_LPI;
+    constexpr int NV = RG_NV;
     constexpr bool NORM = (XM == X_NORM || XM == X_NORM_R16);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ntask = I * LPI;
@@ -272,60 +264,62 @@ __device__ __noinline__ void sk_quantise_xm(int xm, const void* xsrc, const floa
     }
 }
 
-// ---- the stage loop of a GEMV phase (consumers), one loop for both weight types: only the item
-// dot branches on the (phase-uniform) type. Returns the ring stages consumed.
+// Bounded wait for a filled ring slot (the consumer side). Fast path: one try (the abort flag, a
+// shared-memory load queued behind the other warps' weight loads, is read only when the slot is not
+// full yet). Returns false when the CTA gave up (abort flag set, device error recorded).
+__device__ __forceinline__ bool sk_wait_full(uint64_t* bar, uint32_t par, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, par)) return true;
+    if (*abort_flag) return false;
+    for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
+        if (mbar_try_wait(bar, par)) return true;
+    if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+    *abort_flag = 1;
+    return false;
+}
+
+// ---- the stage loop of a GEMV phase (consumers), one loop for both weight types: every stage worked
+// on by all consumer lanes (lane <-> (row of the stage, item), x in registers), a segmented shuffle
+// reduction per row inside each warp, one shared-memory piece per (row, warp); only the item dot
+// branches on the (phase-uniform) type. Returns the ring stages consumed.
 __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& rr, uint32_t use, int ring,
                                               int slot_bytes, uint32_t smem_sa, uint32_t xq_sa, float* acc,
-                                              uint64_t* full, uint64_t* empty, volatile int* abort_flag,
-                                              unsigned long long& wait_cycles, bool timing) {
+                                              uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool q6 = g.wt == WT_Q6K;
-    const int I = g.I, NP = g.np, IP = I / NP, R = g.R, MP = g.mp;
+    const int I = g.I, LP = I, R = g.R, MP = g.mp;
     const int qb = rg_qbytes(g.wt), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
     const RSlot SS = rg_slot(g.wt, I, R, g.w.iph);
-    const int sl = tid / IP, itp = tid - sl * IP;
-    const int rs = sl / NP, pt = sl - rs * NP, it = pt * IP + itp;
+    const int rs = tid / LP, it = tid - rs * LP;
     const bool lane_on = rs < R;
     RX x;
     if (lane_on) {
         if (q6) rg_load_x<WT_Q6K>(xq_sa + it * XQ_WORDS * 4, it, x);
         else rg_load_x<WT_Q80>(xq_sa + it * XQ_WORDS * 4, it, x);
     }
-    const int slot_lo = sl * IP;
-    const int seg_hi = min(slot_lo + IP - 1 - warp * 32, 31);
+    const int slot_lo = rs * LP;
+    const int seg_hi = min(slot_lo + LP - 1 - warp * 32, 31);
     const bool head = lane == max(slot_lo - warp * 32, 0);
-    int pidx = warp - (slot_lo >> 5);
-    for (int p2 = 0; p2 < pt; ++p2) pidx += rg_part_pieces(rs, p2, NP, IP);
+    const int pidx = warp - (slot_lo >> 5);  // this segment's piece index in its row's reduction
+    // shared-memory offsets of the lane's words inside a slot, and of its reduction piece
     const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
     const uint32_t s_off = SS.s_off + (uint32_t)(rs * rg_sbytes_row(g.wt, I) + it * 4);
     const uint32_t d_off =
         SS.d_off + (q6 ? (uint32_t)(rs * (dbr / 2) + ((it + g.w.iph) >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
-    const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
+    const uint32_t acc_sa = smem_u32(acc) + (uint32_t)(rs * MP + pidx) * 4u;
+    const int rows = (int)(rr.r_end - rr.r_begin);
     const uint32_t ring_u = (uint32_t)ring;
+    // the d copy of a stage starts at the 16-byte boundary below its first row's d
+    uint32_t dd = (uint32_t)(((uint64_t)rr.r_begin * dbr) & 15u);
+    const uint32_t dstep = (uint32_t)(R * dbr);
     uint32_t slot = use % ring_u, par = (use / ring_u) & 1u;  // advanced incrementally below
-    for (int s = 0; s < nstages; ++s, ++use) {
-        const long long row0 = rr.r_begin + (long long)s * R;
-        const int nrows = (int)min((long long)R, rr.r_end - row0);
-        // fast path: the slot is usually full already (one try; the abort flag, a shared-memory
-        // load queued behind the other warps' weight loads, is read only when it is not)
-        bool ok = mbar_try_wait(&full[slot], par);
-        if (!ok && !*abort_flag) {
-            const long long w0 = timing ? clock64() : 0;
-            for (uint32_t w = 0; w < FENCE_WAIT_ROUNDS && !*abort_flag; ++w)
-                if (mbar_try_wait(&full[slot], par)) { ok = true; break; }
-            if (timing) wait_cycles += (unsigned long long)(clock64() - w0);
-            if (!ok) {
-                if (!*abort_flag) set_device_error(SK_WAIT_ERR);
-                *abort_flag = 1;
-            }
-        }
-        const bool on = ok && lane_on && rs < nrows;
+    for (int r0 = 0; r0 < rows; r0 += R, ++use) {
+        const bool ok = sk_wait_full(&full[slot], par, abort_flag);
+        const bool on = ok && lane_on && rs < rows - r0;
         float v = 0.f;
         if (on) {
             const uint32_t base = smem_sa + slot * (uint32_t)slot_bytes;
-            const uint32_t ddelta = (uint32_t)(((uint64_t)row0 * dbr) & 15u);
-            if (q6) v = rg_item_dot<WT_Q6K>(base + q_off, base + s_off, base + d_off + ddelta, x);
-            else v = rg_item_dot<WT_Q80>(base + q_off, base + s_off, base + d_off + ddelta, x);
+            if (q6) v = rg_item_dot<WT_Q6K>(base + q_off, base + s_off, base + d_off + dd, x);
+            else v = rg_item_dot<WT_Q80>(base + q_off, base + s_off, base + d_off + dd, x);
         }
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -333,8 +327,10 @@ __device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& 
             if (lane + o <= seg_hi) v += t;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (on && head) acc[(size_t)(row0 - rr.r_begin + rs) * MP + pidx] = v;
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the slot's bytes are no longer read
+        if (on && head)
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(acc_sa + (uint32_t)(r0 * MP) * 4u), "f"(v) : "memory");
+        dd = (dd + dstep) & 15u;
         if (++slot == ring_u) {
             slot = 0;
             par ^= 1u;
@@ -785,9 +781,9 @@ template <bool TP>
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
                                              const float* rpre, float& best_v, int& best_i, const StepArgs& A,
                                              const SPhase& ph, unsigned tag) {
-    const int NP = g.np, IP = g.I / g.np, R = g.R, MP = g.mp;
+    const int LP = g.I, R = g.R, MP = g.mp;
     auto row_sum = [&](int rl) {
-        const int n = rg_row_pieces(rl % R, NP, IP);
+        const int n = rg_part_pieces(rl % R, 0, 1, LP);
         float t = 0.f;
         for (int k = 0; k < n; ++k) t += acc[(size_t)rl * MP + k];
         return t;
@@ -841,12 +837,15 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 32);
     float* warp_best_v = misc + 40;
     int* warp_best_i = reinterpret_cast<int*>(misc + 72);
+    uint64_t* dbar = reinterpret_cast<uint64_t*>(misc + 96);  // [2] descriptor copies (phase k: k & 1)
 
     if (tid == 0) {
         for (int s = 0; s < ring; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], SK_NW);
         }
+        mbar_init(&dbar[0], 1);
+        mbar_init(&dbar[1], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -877,6 +876,9 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 }
                 if (ph.kind != SP_GEMV) continue;
                 const RGemvArgs& g = ph.g;
+                // the phase's norm weights are read by every CTA in its x prologue: into L2 now,
+                // a ring's depth ahead (they are otherwise evicted by the weight stream)
+                if (g.norm_w && c < 8) bulk_prefetch_l2(g.norm_w, (uint32_t)g.I * 256u);
                 const SKRows rr = sk_rows(g, c, G);
                 const int I = g.I, R = g.R;
                 const int qb = rg_qbytes(g.wt), sbr = rg_sbytes_row(g.wt, I), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
@@ -931,13 +933,22 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     int best_i = -1;
     const int pos = A.state->pos;  // fixed for the whole step (advanced only at its very end)
     const unsigned long long launch0 = TP ? *reinterpret_cast<volatile unsigned long long*>(A.launch) : 0ull;
-    if (warp == 0) sk_fetch_desc(&A.ph[0], desc, lane);
-    named_bar_sync(1, NT);
+    // descriptor k arrives on dbar[k & 1], completing that barrier's phase k >> 1
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&dbar[0], SK_DESC);
+        bulk_g2s(desc, &A.ph[0], SK_DESC, &dbar[0]);
+    }
     bool attn_pre = false;  // this thread issued tile 0 of its CTA's first attention unit
     for (int k = 0; k < NPH; ++k) {
+        // the next phase's descriptor: one bulk copy into the buffer phase k - 1 used (every consumer
+        // thread is past that phase's end barrier), landing while this phase runs
+        if (tid == 0 && k + 1 < NPH) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(&dbar[(k + 1) & 1], SK_DESC);
+            bulk_g2s(desc + ((k + 1) & 1) * SK_DESC, &A.ph[k + 1], SK_DESC, &dbar[(k + 1) & 1]);
+        }
+        if (!mbar_wait(&dbar[k & 1], (uint32_t)(k >> 1) & 1u)) *abort_flag = 1;
         const SPhase& ph = *reinterpret_cast<const SPhase*>(desc + (k & 1) * SK_DESC);
-        // the next phase's descriptor, read while this phase runs (ordered by the phase-end barrier)
-        if (warp == SK_NW - 1 && k + 1 < NPH) sk_fetch_desc(&A.ph[k + 1], desc + ((k + 1) & 1) * SK_DESC, lane);
         if (k > 0) {  // wait until every CTA has finished phase k-1
             if (tid == 0) {
                 // acquire: the other CTAs' phase k-1 writes (released by their counts) become
@@ -1006,8 +1017,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
-            use = sk_stages(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag, wcyc,
-                            A.trace != nullptr);
+            use = sk_stages(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
             named_bar_sync(1, NT);  // every piece of every row is in shared memory
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 2] = sk_ns();
             if (ph.epi == EPI_RESID) {
@@ -1019,7 +1029,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                                  TP && ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
             // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
             // records are dead; the next descriptor was fetched at this phase's start)
-            if (k + 1 < NPH && tid < ATTN_THREADS) {
+            if (k + 1 < NPH && tid < ATTN_THREADS && mbar_wait(&dbar[(k + 1) & 1], (uint32_t)((k + 1) >> 1) & 1u)) {
                 const SPhase& nx = *reinterpret_cast<const SPhase*>(desc + ((k + 1) & 1) * SK_DESC);
                 if (nx.kind == SP_ATTN) {
                     const int seq = pos + 1;
