@@ -103,7 +103,8 @@ struct fence_model {
     StepArgs sargs{};
     StepPlan splan{};
     float* qkv_bias = nullptr;      // fused q|k|v bias when the model has any
-    int attn_nchunk = 0;
+    int attn_nchunk = 0;            // per-phase attention kernel: chunks per KV head
+    int step_nchunk = 0;            // step kernel: chunks per KV head its partials hold
     // tensor parallel (tp_n > 1): this rank's shard; the exchange buffer is shared with the peers
     int tp_n = 1, tp_rank = 0, vocab0 = 0, vocab_n = 0;
     float* hidden_b = nullptr;      // residual stream after the odd reductions
@@ -317,6 +318,7 @@ int build_step_phases(fence_model* m) {
         SPhase at{};
         at.kind = SP_ATTN;
         at.at = L.attn;
+        at.at.nchunk = m->step_nchunk;
         ph.push_back(at);
         SPhase o = gemv(L.o), gu = gemv(L.gu), dn = gemv(L.down);
         tp_red(o, 2 * l);
@@ -670,11 +672,14 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     // chunks per KV head: 64-position chunks up to 120 (the merge keeps G x chunks scale factors in
     // the CTA's score buffer); longer contexts get longer chunks
     m->attn_nchunk = std::min(120, std::max(32, (c.max_ctx + ATTN_CHUNK - 1) / ATTN_CHUNK));
+    // the step kernel's attention units span at most SK_ATT_MAXLEN positions: enough chunks to cover max_ctx
+    m->step_nchunk = std::max(m->attn_nchunk, (c.max_ctx + SK_ATT_MAXLEN - 1) / SK_ATT_MAXLEN);
+    const int part_chunks = std::max(m->attn_nchunk, m->step_nchunk);
     bool ok = cudaMalloc(&m->kcache, kv_elems * 2) == cudaSuccess && cudaMalloc(&m->vcache, kv_elems * 2) == cudaSuccess &&
               cudaMemset(m->kcache, 0, kv_elems * 2) == cudaSuccess && cudaMemset(m->vcache, 0, kv_elems * 2) == cudaSuccess &&
               cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qdl + 2 * kvdl) * 4) == cudaSuccess &&
               cudaMalloc(&m->attn_out, qdl * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)vn * 4) == cudaSuccess &&
-              cudaMalloc(&m->attn_part, (size_t)Hkv_l * m->attn_nchunk * G * SK_PART_STRIDE * 4) == cudaSuccess &&
+              cudaMalloc(&m->attn_part, (size_t)Hkv_l * part_chunks * G * SK_PART_STRIDE * 4) == cudaSuccess &&
               cudaMalloc(&m->act, Fl * 4) == cudaSuccess &&
               cudaMalloc(&m->counters, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&
               cudaMemset(m->counters, 0, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&

@@ -372,46 +372,98 @@ struct SKMma<__nv_bfloat16> {
     }
 };
 
+// Tiles of 64 positions one attention unit of the step kernel holds in shared memory at once: all
+// of its K tiles are in flight together, and each V tile later reuses its K tile's buffer.
+constexpr int SK_ATT_TILES = 4;
+constexpr int SK_ATT_MAXLEN = SK_ATT_TILES * ATTN_CMAX;  // 256 positions per unit at most
+
 // Positions per attention unit of the step kernel: up to `solo` positions one unit per KV head
 // walks the whole context (no merge); beyond, the context of each KV head is spread over the CTAs
-// available to it (ctas / n_kv_heads), in whole 64-position tiles, never more chunks than the
-// partials hold (nchunk).
+// available to it (ctas / n_kv_heads), in whole 64-position tiles, at most SK_ATT_MAXLEN per unit,
+// never more chunks than the partials hold (nchunk; the engine sizes them so that nchunk units of
+// SK_ATT_MAXLEN cover max_ctx).
 __host__ __device__ __forceinline__ int sk_attn_clen(int seq, int nchunk, int ctas, int n_kv_heads, int solo) {
     if (seq <= solo) return (seq + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
     const int per_head = ctas / n_kv_heads > 1 ? ctas / n_kv_heads : 1;
     int clen = (seq + per_head - 1) / per_head;
     const int cmin = (seq + nchunk - 1) / nchunk;
     if (clen < cmin) clen = cmin;
-    return (clen + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
+    clen = (clen + ATTN_CMAX - 1) / ATTN_CMAX * ATTN_CMAX;
+    return clen < SK_ATT_MAXLEN ? clen : SK_ATT_MAXLEN;
 }
 
 // Floats per (KV head, chunk, query head) record of the step kernel's attention partials: 128
 // unnormalised outputs, the max and the exp-sum, padded so that every record is 16-byte aligned.
 constexpr int SK_PART_STRIDE = 132;
-// Partial records the merging unit stages at a time: the K/V tiles, q, scores and the four
-// 128-float rows after them (40,960 bytes of the unit's scratch).
-constexpr int SK_MERGE_RECS = (2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 +
-                               4 * 128 * 4) / (SK_PART_STRIDE * 4);
 
-// Shared memory of one attention unit (sk_attn_unit's carve-up): K and V tiles, fp32 q, scores,
-// new k / v, norm weights, RoPE row, softmax state, padding, q as (high, remainder) pairs.
+// Shared memory of one attention unit (sk_attn_unit's carve-up): SK_ATT_TILES K/V tile buffers,
+// the scores / softmax weights [G][SK_ATT_MAXLEN] (the fp32 q [G][128] before them), q as (high,
+// remainder) pairs, new k / v, norm weights, RoPE row, softmax state and a flag.
+constexpr int SK_ATT_TILE_BYTES = ATTN_CMAX * 128 * 2;
 constexpr int sk_attn_scratch_bytes() {
-    return 2 * ATTN_CMAX * 128 * 2 + ATTN_MAX_G * 128 * 4 + ATTN_MAX_G * ATTN_CMAX * 4 + 4 * 128 * 4 + 64 * 8 +
-           3 * ATTN_MAX_G * 4 + 16 + 2 * ATTN_MAX_G * 64 * 4;
+    return SK_ATT_TILES * SK_ATT_TILE_BYTES + ATTN_MAX_G * SK_ATT_MAXLEN * 4 + 2 * ATTN_MAX_G * 64 * 4 +
+           4 * 128 * 4 + 64 * 8 + 3 * ATTN_MAX_G * 4 + 16;
+}
+// Partial records the merging unit stages at a time (in the tile buffers and scores)
+constexpr int SK_MERGE_RECS = (SK_ATT_TILES * SK_ATT_TILE_BYTES + ATTN_MAX_G * SK_ATT_MAXLEN * 4) / (SK_PART_STRIDE * 4);
+static_assert(SK_MERGE_RECS >= ATTN_MAX_G, "merge staging holds at least one chunk");
+
+// cp.async.wait_group with a run-time count (n clamped to 0..7)
+__device__ __forceinline__ void cp_async_wait_upto(int n) {
+    switch (n <= 0 ? 0 : (n >= 7 ? 7 : n)) {
+        case 0: cp_async_wait_group<0>(); break;
+        case 1: cp_async_wait_group<1>(); break;
+        case 2: cp_async_wait_group<2>(); break;
+        case 3: cp_async_wait_group<3>(); break;
+        case 4: cp_async_wait_group<4>(); break;
+        case 5: cp_async_wait_group<5>(); break;
+        case 6: cp_async_wait_group<6>(); break;
+        default: cp_async_wait_group<7>(); break;
+    }
 }
 
-// One attention unit of the step kernel (KV head h, context chunk c of clen positions), run by
-// threads 0..ATTN_THREADS-1 (named barrier 2). The semantics are attention.cuh's fused chunk
-// (q/k RMSNorm, NeoX RoPE, KV store of the new row, softmax(q.K^T / sqrt(hd)) V in fp32, reference
-// src/kernels/ops.cuh:66-177,320-443); the schedule is cut for latency:
-//  * the context is walked in 64-position tiles; the first tile's K/V rows and every small input
-//    (q, new k/v, norm weights, RoPE row) go out as one batch of 16-byte async copies, and the
-//    next tile's K rows load while this tile's softmax and P.V run, its V rows while the next
-//    scores run (the producer warp already pulled the unit's K/V rows into L2);
-//  * q.K^T and P.V run on the tensor cores (mma.sync m16n8k16, fp32 accumulators): the query
-//    heads are the rows of A, and the fp32 operand (q, or the softmax weights P) is split into
-//    a KVT high part and a KVT remainder, two products summed, so it keeps ~22 (f16) or ~16
-//    (bf16) bits while K and V enter exactly as cached;
+// Rows [ts, te) of a K or V head (except pos, which the unit produces) into a tile buffer: 16-byte
+// chunk ch of row r at chunk ch ^ (r & 7) (conflict-free mma operand loads). Threads 0..ATTN_THREADS-1.
+template <typename KVT>
+__device__ __forceinline__ void sk_attn_stage(KVT* dst, const KVT* src, long long stride_t, int ts, int te, int pos) {
+    constexpr int HD = 128, CH = 16;
+    for (int idx = threadIdx.x; idx < (te - ts) * CH; idx += ATTN_THREADS) {
+        const int r = idx >> 4, ch = idx & 15;
+        const int t = ts + r;
+        if (t == pos) continue;
+        cp_async16(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16),
+                   reinterpret_cast<const uint8_t*>(src + (long long)t * stride_t) + ch * 16);
+    }
+}
+
+// Issues the K tiles of attention unit (h, c) as one cp.async group per tile (threads
+// 0..ATTN_THREADS-1, the unit's own threads, which later wait for them): run at the end of the
+// phase before attention, so they load across the phase change. The cache rows before pos are not
+// written by that phase; the row at pos is skipped, as the unit produces it.
+template <typename KVT>
+__device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int c, int clen, int pos, uint8_t* sm) {
+    constexpr int HD = 128, TILE = ATTN_CMAX;
+    KVT* kt = reinterpret_cast<KVT*>(sm);
+    const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
+    const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
+    for (int ts = t0, i = 0; ts < t1; ts += TILE, ++i) {
+        sk_attn_stage<KVT>(kt + i * TILE * HD, kb, a.stride_t, ts, min(ts + TILE, t1), pos);
+        cp_async_commit();
+    }
+}
+
+// One attention unit of the step kernel (KV head h, context chunk c of clen <= SK_ATT_MAXLEN
+// positions), run by threads 0..ATTN_THREADS-1 (named barrier 2). The semantics are attention.cuh's
+// fused chunk (q/k RMSNorm, NeoX RoPE, KV store of the new row, softmax(q.K^T / sqrt(hd)) V in fp32,
+// reference src/kernels/ops.cuh:66-177,320-443); the schedule is cut for latency:
+//  * every K tile of the chunk is in flight at once (issued across the phase change when `pre`),
+//    together with the small inputs (q, new k/v, norm weights, RoPE row);
+//  * pass 1, per tile as it lands: q.K^T on the tensor cores (mma.sync m16n8k16, fp32 accumulators;
+//    query heads = rows of A; the fp32 q is split into a KVT high part and a KVT remainder, two
+//    products summed, so it keeps ~22 (f16) / ~16 (bf16) bits while K enters exactly as cached);
+//    the tile's buffer then takes its V rows, which load while the later scores run;
+//  * the chunk's exact softmax (max, exp, sum over all its positions, a warp per head);
+//  * pass 2, per tile: P.V on the tensor cores, P split the same way as q;
 //  * the unit writes its chunk's unnormalised output, max and exp-sum to the partials; the last
 //    unit of the KV head to arrive (arrival counter) merges the head's chunks, so attention is a
 //    single phase; for a single chunk the unit writes the normalised output itself.
@@ -420,58 +472,49 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
                                           uint8_t* sm, bool pre) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
-    constexpr int HD = 128, CH = HD * (int)sizeof(KVT) / 16, EPC = 16 / (int)sizeof(KVT);
-    constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX;
-    static_assert(CH == 16 && TILE == 64 && NT == 256 && NW == 8 && ATTN_MAX_G <= 8, "unit geometry");
-    KVT* sk = reinterpret_cast<KVT*>(sm);
-    KVT* sv = sk + TILE * HD;
-    float* sq = reinterpret_cast<float*>(sv + TILE * HD);  // [G][HD] fp32 q, later the merge weights
-    float* ss = sq + ATTN_MAX_G * HD;                       // [G][TILE] scores, then P
-    float* skn = ss + ATTN_MAX_G * TILE;                    // [HD] new k (rotated, cache-rounded)
-    float* svn = skn + HD;                                  // [HD] new v
+    constexpr int HD = 128, EPC = 16 / (int)sizeof(KVT);
+    constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX, ML = SK_ATT_MAXLEN;
+    static_assert(TILE == 64 && NT == 256 && NW == 8 && ATTN_MAX_G <= 8, "unit geometry");
+    KVT* kv = reinterpret_cast<KVT*>(sm);                                      // [SK_ATT_TILES][TILE][HD]
+    float* ss = reinterpret_cast<float*>(sm + SK_ATT_TILES * SK_ATT_TILE_BYTES);  // [G][ML] scores, then P
+    float* sq = ss;                                                             // [G][HD] fp32 q (before the scores)
+    uint32_t* sqa = reinterpret_cast<uint32_t*>(ss + ATTN_MAX_G * ML);          // [2][G][HD/2] q high / remainder
+    float* skn = reinterpret_cast<float*>(sqa + 2 * ATTN_MAX_G * (HD / 2));     // [HD] new k (rotated, cache-rounded)
+    float* svn = skn + HD;                                                      // [HD] new v
     float* sqw = svn + HD;
     float* skw = sqw + HD;
-    float2* srope = reinterpret_cast<float2*>(skw + HD);    // [HD/2]
+    float2* srope = reinterpret_cast<float2*>(skw + HD);                        // [HD/2]
     float* smax = reinterpret_cast<float*>(srope + HD / 2);
     float* ssum = smax + ATTN_MAX_G;
-    float* sresc = ssum + ATTN_MAX_G;
-    uint32_t* sqa = reinterpret_cast<uint32_t*>(sresc + ATTN_MAX_G + 4);  // [2][G][HD/2] q high / remainder pairs
+    float* sinv = ssum + ATTN_MAX_G;
+    int* flag = reinterpret_cast<int*>(sinv + ATTN_MAX_G);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = a.n_q_heads / a.n_kv_heads;
     const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
+    const int n = t1 - t0, T = (n + TILE - 1) / TILE;
     const bool owns_new = pos >= t0 && pos < t1;
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
     const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
-    // rows [ts, te) except pos -> tile rows, 16-byte chunk ch of row r at chunk ch ^ (r & 7)
-    auto stage = [&](KVT* dst, const KVT* src, int ts, int te) {
-        for (int idx = tid; idx < (te - ts) * CH; idx += NT) {
-            const int r = idx >> 4, ch = idx & 15;
-            const int t = ts + r;
-            if (t == pos) continue;  // produced by this unit
-            cp_async16(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16),
-                       reinterpret_cast<const uint8_t*>(src + (long long)t * a.stride_t) + ch * 16);
-        }
-    };
-    // the new row (cache-rounded floats) into its tile slot, when pos lies in [ts, ts + TILE)
-    auto put_new = [&](KVT* dst, const float* row, int ts) {
-        const int r = pos - ts;
+    auto tile = [&](int i) { return kv + i * TILE * HD; };
+    // the new row (cache-rounded floats) into its tile slot, when pos lies in tile i
+    auto put_new = [&](int i, const float* row) {
+        const int r = pos - (t0 + i * TILE);
         if (r < 0 || r >= TILE || tid >= HD) return;
         const int d = tid;
-        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(dst + r * HD) + (((d / EPC) ^ (r & 7)) * 16))[d % EPC] =
+        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + (((d / EPC) ^ (r & 7)) * 16))[d % EPC] =
             C::from(row[d]);
     };
-    // rows [n, round16(n)) of a partial tile: zero, so that P.V's last k-step reads finite values
-    auto zero_tail = [&](KVT* dst, int n) {
-        const int n16 = (n + 15) & ~15;
-        for (int idx = tid; idx < (n16 - n) * CH; idx += NT) {
-            const int r = n + (idx >> 4), ch = idx & 15;
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16)) =
+    // rows [m, round16(m)) of a partial V tile: zero, so that P.V's last k-step reads finite values
+    auto zero_tail = [&](int i, int m) {
+        const int m16 = (m + 15) & ~15;
+        for (int idx = tid; idx < (m16 - m) * 16; idx += NT) {
+            const int r = m + (idx >> 4), ch = idx & 15;
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + ((ch ^ (r & 7)) * 16)) =
                 make_uint4(0u, 0u, 0u, 0u);
         }
     };
 
-    // ---- first batch: small inputs + K rows of tile 0 (group 1), V rows of tile 0 (group 2); with
-    //      pre, tile 0's K and V rows went out as one earlier group (sk_attn_prefetch_tile0)
+    // ---- small inputs (one group); without `pre` the K tiles follow, one group each
     const int qh0 = h * G;
     for (int i = tid; i < G * (HD / 4); i += NT) cp_async16(sq + 4 * i, a.q + (long long)qh0 * HD + 4 * i);
     if (tid < HD / 4) {
@@ -486,15 +529,16 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         cp_async16(reinterpret_cast<float*>(srope) + 4 * i,
                    reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
     }
-    if (!pre) stage(sk, kb, t0, min(t0 + TILE, t1));  // pre: tile 0 is in flight already
     cp_async_commit();
-    if (!pre) stage(sv, vb, t0, min(t0 + TILE, t1));
-    cp_async_commit();
-    if (tid < ATTN_MAX_G) {
-        smax[tid] = -INFINITY;
-        ssum[tid] = 0.f;
+    if (!pre) {
+        for (int i = 0; i < T; ++i) {
+            sk_attn_stage<KVT>(tile(i), kb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), pos);
+            cp_async_commit();
+        }
+        cp_async_wait_upto(T);  // the small inputs (the K tiles may still be in flight)
+    } else {
+        cp_async_wait_group<0>();  // the small inputs; the K tiles went out a phase earlier
     }
-    cp_async_wait_group<1>();
     named_bar_sync(2, NT);
     // ---- q/k RMSNorm (w * x * rms) and NeoX rotation, a warp per head; the new K/V row
     for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
@@ -548,25 +592,23 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             }
         }
     }
-    named_bar_sync(2, NT);
-    put_new(sk, skn, t0);
+    named_bar_sync(2, NT);  // sq is dead: ss takes the scores from here on
 
     const float scale = 1.0f / sqrtf((float)HD);
     const int gr = lane >> 2, q4 = lane & 3;  // fragment row (query head) and column pair
-    float oh[2][4] = {}, ol[2][4] = {};        // P.V accumulators: dims 16 warp + 8 j + 2 q4 + {0, 1}
-    for (int ts = t0; ts < t1; ts += TILE) {
-        const int nt = min(ts + TILE, t1) - ts;
-        const bool more = ts + TILE < t1;
-        if (ts != t0) {
-            cp_async_wait_group<1>();  // K rows of this tile (its V rows may still be in flight)
-            put_new(sk, skn, ts);
-        }
+    // ---- pass 1: scores of every tile; a tile's buffer then takes its V rows
+    for (int i = 0; i < T; ++i) {
+        const int ts = t0 + i * TILE, nt = min(TILE, t1 - ts);
+        // K tile i: the groups after it are the later K tiles and the V tiles issued so far (T - 1)
+        if (!pre) cp_async_wait_upto(T - 1);
+        else cp_async_wait_upto(i);  // groups after K tile i: the V tiles issued so far (i)
+        put_new(i, skn);
         named_bar_sync(2, NT);
-        // ---- scores: warp w -> positions 8w .. 8w + 7 of the tile, 8 k-steps of 16 dims
+        // warp w -> positions 8w .. 8w + 7 of the tile, 8 k-steps of 16 dims
         if (8 * warp < nt) {
             float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
             const int r = 8 * warp + gr;  // B column = tile row
-            const uint32_t* krow = reinterpret_cast<const uint32_t*>(sk + r * HD);
+            const uint32_t* krow = reinterpret_cast<const uint32_t*>(tile(i) + r * HD);
             const uint32_t* qa = sqa + gr * (HD / 2);
             const bool live = gr < G;
 #pragma unroll
@@ -581,75 +623,60 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             }
             if (live) {  // d[0], d[1]: head gr, tile rows 8 warp + 2 q4 + {0, 1}
                 const int col = 8 * warp + 2 * q4;
-                if (col < nt) ss[gr * TILE + col] = (dh[0] + dl[0]) * scale;
-                if (col + 1 < nt) ss[gr * TILE + col + 1] = (dh[1] + dl[1]) * scale;
+                if (col < nt) ss[gr * ML + i * TILE + col] = (dh[0] + dl[0]) * scale;
+                if (col + 1 < nt) ss[gr * ML + i * TILE + col + 1] = (dh[1] + dl[1]) * scale;
             }
         }
+        named_bar_sync(2, NT);  // the K tile is dead
+        sk_attn_stage<KVT>(tile(i), vb, a.stride_t, ts, ts + nt, pos);
+        cp_async_commit();
+    }
+    // ---- the chunk's softmax, a warp per head: max, exp, sum; P (zero beyond n) back into ss
+    for (int g = warp; g < G; g += NW) {
+        float* sr = ss + g * ML;
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, sr[j]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int j = lane; j < T * TILE; j += 32) {
+            const float e = j < n ? expf(sr[j] - m) : 0.f;
+            sr[j] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            smax[g] = m;
+            ssum[g] = l;
+        }
+    }
+    // ---- pass 2: P.V per tile as its V rows land; warp w -> dims 16w .. 16w + 15 (two n-tiles)
+    float oh[2][4] = {}, ol[2][4] = {};  // dims 16 warp + 8 j + 2 q4 + {0, 1}
+    const bool live = gr < G;
+    // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
+    const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lch = 2 * warp + (lane >> 4);
+    for (int i = 0; i < T; ++i) {
+        const int nt = min(TILE, t1 - (t0 + i * TILE));
+        cp_async_wait_upto(T - 1 - i);  // V tile i (the later V tiles may still be in flight)
+        put_new(i, svn);
+        if (nt < TILE) zero_tail(i, nt);
         named_bar_sync(2, NT);
-        if (more) {  // the K tile is free: next tile's K rows
-            stage(sk, kb, ts + TILE, min(ts + 2 * TILE, t1));
-            cp_async_commit();
-        }
-        // ---- online softmax statistics, a warp per head; P (zero beyond nt) back into ss
-        for (int g = warp; g < G; g += NW) {
-            const float s0 = lane < nt ? ss[g * TILE + lane] : -INFINITY;
-            const float s1 = lane + 32 < nt ? ss[g * TILE + lane + 32] : -INFINITY;
-            const float m = warp_max(fmaxf(s0, s1));
-            const float m_old = smax[g];
-            const float m_new = fmaxf(m_old, m);
-            const float e0 = lane < nt ? expf(s0 - m_new) : 0.f;
-            const float e1 = lane + 32 < nt ? expf(s1 - m_new) : 0.f;
-            ss[g * TILE + lane] = e0;
-            ss[g * TILE + lane + 32] = e1;
-            const float l = warp_sum(e0 + e1);
-            if (lane == 0) {
-                const float f = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-                sresc[g] = f;
-                ssum[g] = ssum[g] * f + l;
-                smax[g] = m_new;
-            }
-        }
-        if (more) cp_async_wait_group<1>();  // V rows of this tile (next K rows may be in flight)
-        else cp_async_wait_group<0>();
-        put_new(sv, svn, ts);
-        if (nt < TILE) zero_tail(sv, nt);
-        named_bar_sync(2, NT);
-        // ---- P.V: warp w -> dims 16w .. 16w + 15 (two n-tiles), k-steps of 16 positions
-        {
-            const float f = gr < G ? sresc[gr] : 0.f;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    oh[j][e] *= f;
-                    ol[j][e] *= f;
-                }
-            const float* prow = ss + gr * TILE;
-            const bool live = gr < G;
-            // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
-            const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lch = 2 * warp + (lane >> 4);
-            for (int ks = 0; ks < (nt + 15) / 16; ++ks) {
-                const int r = 16 * ks + lr;
-                const uint32_t addr = smem_u32(reinterpret_cast<uint8_t*>(sv + r * HD) + ((lch ^ (r & 7)) * 16));
-                uint32_t b[4];
-                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                             : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
-                             : "r"(addr));
-                const float2 p0 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 2 * q4) : make_float2(0.f, 0.f);
-                const float2 p2 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 8 + 2 * q4) : make_float2(0.f, 0.f);
-                const float h0x = M::round(p0.x), h0y = M::round(p0.y), h2x = M::round(p2.x), h2y = M::round(p2.y);
-                const uint32_t ah0 = M::pack(h0x, h0y), ah2 = M::pack(h2x, h2y);
-                const uint32_t al0 = M::pack(p0.x - h0x, p0.y - h0y), al2 = M::pack(p2.x - h2x, p2.y - h2y);
-                M::mma(oh[0], ah0, ah2, b[0], b[1]);
-                M::mma(ol[0], al0, al2, b[0], b[1]);
-                M::mma(oh[1], ah0, ah2, b[2], b[3]);
-                M::mma(ol[1], al0, al2, b[2], b[3]);
-            }
-        }
-        named_bar_sync(2, NT);  // V tile and ss are free
-        if (more) {
-            stage(sv, vb, ts + TILE, min(ts + 2 * TILE, t1));
-            cp_async_commit();
+        const float* prow = ss + gr * ML + i * TILE;
+        for (int ks = 0; ks < (nt + 15) / 16; ++ks) {
+            const int r = 16 * ks + lr;
+            const uint32_t addr = smem_u32(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + ((lch ^ (r & 7)) * 16));
+            uint32_t b[4];
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                         : "r"(addr));
+            const float2 p0 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 2 * q4) : make_float2(0.f, 0.f);
+            const float2 p2 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 8 + 2 * q4) : make_float2(0.f, 0.f);
+            const float h0x = M::round(p0.x), h0y = M::round(p0.y), h2x = M::round(p2.x), h2y = M::round(p2.y);
+            const uint32_t ah0 = M::pack(h0x, h0y), ah2 = M::pack(h2x, h2y);
+            const uint32_t al0 = M::pack(p0.x - h0x, p0.y - h0y), al2 = M::pack(p2.x - h2x, p2.y - h2y);
+            M::mma(oh[0], ah0, ah2, b[0], b[1]);
+            M::mma(ol[0], al0, al2, b[0], b[1]);
+            M::mma(oh[1], ah0, ah2, b[2], b[3]);
+            M::mma(ol[1], al0, al2, b[2], b[3]);
         }
     }
     // ---- output (single chunk) or this chunk's partials: head gr, dims 16 warp + 8 j + 2 q4 + {0, 1}
@@ -664,7 +691,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             else *reinterpret_cast<float2*>(pbase + gr * SK_PART_STRIDE + d) = o;
         }
     }
-    if (n_active == 1) return;
+    if (n_active == 1) return;  // (the caller's barrier orders the next unit's reuse of the buffers)
     if (tid < G) *reinterpret_cast<float2*>(pbase + tid * SK_PART_STRIDE + HD) = make_float2(smax[tid], ssum[tid]);
     // ---- the last unit of KV head h to arrive merges the head's chunks: output (query head
     //      qh0 + g, dim d) = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M), one pass in chunk order
@@ -673,7 +700,6 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     //      last unit stages the head's partial records in shared memory with one batch of async
     //      copies per SK_MERGE_RECS records.
     named_bar_sync(2, NT);
-    int* flag = reinterpret_cast<int*>(sresc + ATTN_MAX_G);  // outside the staging area
     if (tid == 0) {
         unsigned old;
         asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counter + h) : "memory");
@@ -723,29 +749,6 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         if (g < G) a.out[(long long)qh0 * HD + i] = Ox[j] / Lx[j];
     }
     if (tid == 0) a.counter[h] = 0u;  // every unit of head h has arrived: zero for the next layer
-}
-
-// Issues the K and V rows of tile 0 of attention unit (h, c) as one cp.async group (threads
-// 0..ATTN_THREADS-1, the unit's own threads, which later wait for it): run at the end of the
-// phase before attention, so the rows load across the phase change. The cache rows before pos
-// are not written by that phase; the row at pos is skipped, as the unit produces it.
-template <typename KVT>
-__device__ __forceinline__ void sk_attn_prefetch_tile0(const AttnArgs& a, int h, int c, int clen, int pos,
-                                                       uint8_t* sm) {
-    constexpr int HD = 128, CH = 16, TILE = ATTN_CMAX;
-    KVT* sk = reinterpret_cast<KVT*>(sm);
-    KVT* sv = sk + TILE * HD;
-    const int t0 = c * clen, te = min(min(t0 + clen, pos + 1), t0 + TILE);
-    const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
-    const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
-    for (int idx = threadIdx.x; idx < (te - t0) * CH; idx += ATTN_THREADS) {
-        const int r = idx >> 4, ch = idx & 15, t = t0 + r;
-        if (t == pos) continue;
-        const uint32_t so = (uint32_t)r * HD * sizeof(KVT) + ((ch ^ (r & 7)) * 16);
-        cp_async16(reinterpret_cast<uint8_t*>(sk) + so, reinterpret_cast<const uint8_t*>(kb + (long long)t * a.stride_t) + ch * 16);
-        cp_async16(reinterpret_cast<uint8_t*>(sv) + so, reinterpret_cast<const uint8_t*>(vb + (long long)t * a.stride_t) + ch * 16);
-    }
-    cp_async_commit();
 }
 
 // x of a phase after a tensor-parallel reduction: hbuf[i] = hin[i] + sum over ranks (rank order)
@@ -1035,8 +1038,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                     const int seq = pos + 1;
                     const int clen = sk_attn_clen(seq, nx.at.nchunk, G, nx.at.n_kv_heads, A.attn_solo);
                     const int nch = (seq + clen - 1) / clen;
-                    if (c < nx.at.n_kv_heads * nch) {
-                        sk_attn_prefetch_tile0<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch);
+                    if (nch <= nx.at.nchunk && c < nx.at.n_kv_heads * nch) {
+                        sk_attn_prefetch_k<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch);
                         attn_pre = true;
                     }
                 }
@@ -1046,7 +1049,12 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             const int seq = pos + 1;
             const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads, A.attn_solo);
             const int nch = (seq + clen - 1) / clen;
-            const int units = at.n_kv_heads * nch;
+            // the partials hold at.nchunk chunks per KV head (the engine sizes them for max_ctx)
+            const int units = nch <= at.nchunk ? at.n_kv_heads * nch : 0;
+            if (nch > at.nchunk && tid == 0) {
+                set_device_error(SK_WAIT_ERR);
+                *abort_flag = 1;
+            }
             for (int u = c; u < units; u += G) {
                 // the first unit's tile 0 may have been issued at the end of the previous phase
                 if (tid < ATTN_THREADS) sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre);
