@@ -668,7 +668,10 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     }
 
     const int HD = c.head_dim, G = c.n_heads / c.n_kv_heads;
-    const size_t kv_elems = (size_t)c.n_layers * Hkv_l * c.max_ctx * HD;
+    // KV cache [layer][kv_head][max_ctx][SK_ATT_RSTR]: rows padded from 128 to 136 elements, so that
+    // one bulk copy moves a whole 64-position tile into the bank-conflict-free layout the step
+    // kernel's attention reads (the 8 padding elements of a row are never read as data)
+    const size_t kv_elems = (size_t)c.n_layers * Hkv_l * c.max_ctx * SK_ATT_RSTR;
     // chunks per KV head: 64-position chunks up to 120 (the merge keeps G x chunks scale factors in
     // the CTA's score buffer); longer contexts get longer chunks
     m->attn_nchunk = std::min(120, std::max(32, (c.max_ctx + ATTN_CHUNK - 1) / ATTN_CHUNK));
@@ -782,7 +785,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     };
 
     m->launches.resize(c.n_layers);
-    const size_t kv_layer = (size_t)Hkv_l * c.max_ctx * HD;
+    const size_t kv_layer = (size_t)Hkv_l * c.max_ctx * SK_ATT_RSTR;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
@@ -835,8 +838,8 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         at.vc = static_cast<uint8_t*>(m->vcache) + l * kv_layer * 2;
         at.kc_w = const_cast<void*>(at.kc);
         at.vc_w = const_cast<void*>(at.vc);
-        at.stride_t = HD;
-        at.stride_h = (long long)c.max_ctx * HD;
+        at.stride_t = SK_ATT_RSTR;
+        at.stride_h = (long long)c.max_ctx * SK_ATT_RSTR;
         at.n_q_heads = Hq_l;
         at.n_kv_heads = Hkv_l;
         at.nchunk = m->attn_nchunk;

@@ -399,7 +399,10 @@ constexpr int SK_PART_STRIDE = 132;
 // Shared memory of one attention unit (sk_attn_unit's carve-up): SK_ATT_TILES K/V tile buffers,
 // the scores / softmax weights [G][SK_ATT_MAXLEN] (the fp32 q [G][128] before them), q as (high,
 // remainder) pairs, new k / v, norm weights, RoPE row, softmax state and a flag.
-constexpr int SK_ATT_TILE_BYTES = ATTN_CMAX * 128 * 2;
+// Tile rows are padded to 136 elements (272 bytes): the eight rows an mma fragment or an ldmatrix
+// reads sit 4 banks apart, so the row-contiguous layout the bulk copies write is conflict-free.
+constexpr int SK_ATT_RSTR = 136;
+constexpr int SK_ATT_TILE_BYTES = ATTN_CMAX * SK_ATT_RSTR * 2;
 constexpr int sk_attn_scratch_bytes() {
     return SK_ATT_TILES * SK_ATT_TILE_BYTES + ATTN_MAX_G * SK_ATT_MAXLEN * 4 + 2 * ATTN_MAX_G * 64 * 4 +
            4 * 128 * 4 + 64 * 8 + 3 * ATTN_MAX_G * 4 + 16;
@@ -408,48 +411,31 @@ constexpr int sk_attn_scratch_bytes() {
 constexpr int SK_MERGE_RECS = (SK_ATT_TILES * SK_ATT_TILE_BYTES + ATTN_MAX_G * SK_ATT_MAXLEN * 4) / (SK_PART_STRIDE * 4);
 static_assert(SK_MERGE_RECS >= ATTN_MAX_G, "merge staging holds at least one chunk");
 
-// cp.async.wait_group with a run-time count (n clamped to 0..7)
-__device__ __forceinline__ void cp_async_wait_upto(int n) {
-    switch (n <= 0 ? 0 : (n >= 7 ? 7 : n)) {
-        case 0: cp_async_wait_group<0>(); break;
-        case 1: cp_async_wait_group<1>(); break;
-        case 2: cp_async_wait_group<2>(); break;
-        case 3: cp_async_wait_group<3>(); break;
-        case 4: cp_async_wait_group<4>(); break;
-        case 5: cp_async_wait_group<5>(); break;
-        case 6: cp_async_wait_group<6>(); break;
-        default: cp_async_wait_group<7>(); break;
-    }
+// Rows [ts, te) of a K or V head into a tile buffer: ONE 1-D bulk copy (TMA, no multicast) of the
+// rows as they lie in the cache (rows of SK_ATT_RSTR elements, the engine's padded layout),
+// completing on the tile's mbarrier; issued by one thread. The row at pos may arrive stale or new:
+// the unit writes it into the tile itself after the copy has landed.
+template <typename KVT>
+__device__ __forceinline__ void sk_attn_rows(KVT* dst, const KVT* src, long long stride_t, int ts, int te, uint64_t* bar) {
+    const uint32_t bytes = (uint32_t)(te - ts) * (uint32_t)(SK_ATT_RSTR * sizeof(KVT));
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_g2s(dst, src + (long long)ts * stride_t, bytes, bar);
 }
 
-// Rows [ts, te) of a K or V head (except pos, which the unit produces) into a tile buffer: 16-byte
-// chunk ch of row r at chunk ch ^ (r & 7) (conflict-free mma operand loads). Threads 0..ATTN_THREADS-1.
+// Issues the K tiles of attention unit (h, c) (thread 0): run at the end of the phase before
+// attention, so they load across the phase change. The cache rows before pos are not written by
+// that phase; the row at pos is replaced by the unit.
 template <typename KVT>
-__device__ __forceinline__ void sk_attn_stage(KVT* dst, const KVT* src, long long stride_t, int ts, int te, int pos) {
-    constexpr int HD = 128, CH = 16;
-    for (int idx = threadIdx.x; idx < (te - ts) * CH; idx += ATTN_THREADS) {
-        const int r = idx >> 4, ch = idx & 15;
-        const int t = ts + r;
-        if (t == pos) continue;
-        cp_async16(reinterpret_cast<uint8_t*>(dst + r * HD) + ((ch ^ (r & 7)) * 16),
-                   reinterpret_cast<const uint8_t*>(src + (long long)t * stride_t) + ch * 16);
-    }
-}
-
-// Issues the K tiles of attention unit (h, c) as one cp.async group per tile (threads
-// 0..ATTN_THREADS-1, the unit's own threads, which later wait for them): run at the end of the
-// phase before attention, so they load across the phase change. The cache rows before pos are not
-// written by that phase; the row at pos is skipped, as the unit produces it.
-template <typename KVT>
-__device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int c, int clen, int pos, uint8_t* sm) {
-    constexpr int HD = 128, TILE = ATTN_CMAX;
+__device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int c, int clen, int pos, uint8_t* sm,
+                                                   uint64_t* abar) {
+    constexpr int TILE = ATTN_CMAX;
     KVT* kt = reinterpret_cast<KVT*>(sm);
     const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
-    for (int ts = t0, i = 0; ts < t1; ts += TILE, ++i) {
-        sk_attn_stage<KVT>(kt + i * TILE * HD, kb, a.stride_t, ts, min(ts + TILE, t1), pos);
-        cp_async_commit();
-    }
+    if (threadIdx.x != 0) return;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the generic use of the scratch
+    for (int ts = t0, i = 0; ts < t1; ts += TILE, ++i)
+        sk_attn_rows<KVT>(kt + i * TILE * SK_ATT_RSTR, kb, a.stride_t, ts, min(ts + TILE, t1), &abar[i]);
 }
 
 // One attention unit of the step kernel (KV head h, context chunk c of clen <= SK_ATT_MAXLEN
@@ -458,24 +444,26 @@ __device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int
 // reference src/kernels/ops.cuh:66-177,320-443); the schedule is cut for latency:
 //  * every K tile of the chunk is in flight at once (issued across the phase change when `pre`),
 //    together with the small inputs (q, new k/v, norm weights, RoPE row);
-//  * pass 1, per tile as it lands: q.K^T on the tensor cores (mma.sync m16n8k16, fp32 accumulators;
-//    query heads = rows of A; the fp32 q is split into a KVT high part and a KVT remainder, two
-//    products summed, so it keeps ~22 (f16) / ~16 (bf16) bits while K enters exactly as cached);
-//    the tile's buffer then takes its V rows, which load while the later scores run;
+//  * pass 1, every position of the chunk at once: q.K^T on the tensor cores (mma.sync m16n8k16,
+//    fp32 accumulators, up to four independent chains per warp; query heads = rows of A; the fp32
+//    q is split into a KVT high part and a KVT remainder, two products summed, so it keeps ~22
+//    (f16) / ~16 (bf16) bits while K enters exactly as cached); the tile buffers then take the V
+//    rows, which load during the softmax;
 //  * the chunk's exact softmax (max, exp, sum over all its positions, a warp per head);
-//  * pass 2, per tile: P.V on the tensor cores, P split the same way as q;
+//  * pass 2: P.V on the tensor cores over the whole chunk, P split the same way as q;
 //  * the unit writes its chunk's unnormalised output, max and exp-sum to the partials; the last
 //    unit of the KV head to arrive (arrival counter) merges the head's chunks, so attention is a
 //    single phase; for a single chunk the unit writes the normalised output itself.
 template <typename KVT>
 __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
-                                          uint8_t* sm, bool pre) {
+                                          uint8_t* sm, bool pre, uint64_t* abar, volatile int* abort_flag) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
     constexpr int HD = 128, EPC = 16 / (int)sizeof(KVT);
     constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX, ML = SK_ATT_MAXLEN;
     static_assert(TILE == 64 && NT == 256 && NW == 8 && ATTN_MAX_G <= 8, "unit geometry");
-    KVT* kv = reinterpret_cast<KVT*>(sm);                                      // [SK_ATT_TILES][TILE][HD]
+    constexpr int RSTR = SK_ATT_RSTR;
+    KVT* kv = reinterpret_cast<KVT*>(sm);                                      // [SK_ATT_TILES][TILE][RSTR]
     float* ss = reinterpret_cast<float*>(sm + SK_ATT_TILES * SK_ATT_TILE_BYTES);  // [G][ML] scores, then P
     float* sq = ss;                                                             // [G][HD] fp32 q (before the scores)
     uint32_t* sqa = reinterpret_cast<uint32_t*>(ss + ATTN_MAX_G * ML);          // [2][G][HD/2] q high / remainder
@@ -495,22 +483,25 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     const bool owns_new = pos >= t0 && pos < t1;
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
     const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
-    auto tile = [&](int i) { return kv + i * TILE * HD; };
+    auto tile = [&](int i) { return kv + i * TILE * RSTR; };
+    // tile buffer i: its mbarrier completes once per fill (K, then V), so a unit waits on parity 0
+    // for its K rows and on parity 1 for its V rows
+    auto wait_tile = [&](int i, uint32_t par) {
+        if (!mbar_wait(&abar[i], par)) *abort_flag = 1;
+    };
     // the new row (cache-rounded floats) into its tile slot, when pos lies in tile i
     auto put_new = [&](int i, const float* row) {
         const int r = pos - (t0 + i * TILE);
         if (r < 0 || r >= TILE || tid >= HD) return;
         const int d = tid;
-        reinterpret_cast<KVT*>(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + (((d / EPC) ^ (r & 7)) * 16))[d % EPC] =
-            C::from(row[d]);
+        tile(i)[r * RSTR + d] = C::from(row[d]);
     };
     // rows [m, round16(m)) of a partial V tile: zero, so that P.V's last k-step reads finite values
     auto zero_tail = [&](int i, int m) {
         const int m16 = (m + 15) & ~15;
         for (int idx = tid; idx < (m16 - m) * 16; idx += NT) {
             const int r = m + (idx >> 4), ch = idx & 15;
-            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + ((ch ^ (r & 7)) * 16)) =
-                make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(tile(i) + r * RSTR + ch * 8) = make_uint4(0u, 0u, 0u, 0u);
         }
     };
 
@@ -530,15 +521,12 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
                    reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
     }
     cp_async_commit();
-    if (!pre) {
-        for (int i = 0; i < T; ++i) {
-            sk_attn_stage<KVT>(tile(i), kb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), pos);
-            cp_async_commit();
-        }
-        cp_async_wait_upto(T);  // the small inputs (the K tiles may still be in flight)
-    } else {
-        cp_async_wait_group<0>();  // the small inputs; the K tiles went out a phase earlier
+    if (!pre && tid == 0) {  // the K tiles (with `pre` they went out at the end of the previous phase)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the previous unit's reads
+        for (int i = 0; i < T; ++i)
+            sk_attn_rows<KVT>(tile(i), kb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), &abar[i]);
     }
+    cp_async_wait_group<0>();  // the small inputs
     named_bar_sync(2, NT);
     // ---- q/k RMSNorm (w * x * rms) and NeoX rotation, a warp per head; the new K/V row
     for (int g = warp; g < G + (owns_new ? 1 : 0); g += NW) {
@@ -596,40 +584,51 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
 
     const float scale = 1.0f / sqrtf((float)HD);
     const int gr = lane >> 2, q4 = lane & 3;  // fragment row (query head) and column pair
-    // ---- pass 1: scores of every tile; a tile's buffer then takes its V rows
-    for (int i = 0; i < T; ++i) {
-        const int ts = t0 + i * TILE, nt = min(TILE, t1 - ts);
-        // K tile i: the groups after it are the later K tiles and the V tiles issued so far (T - 1)
-        if (!pre) cp_async_wait_upto(T - 1);
-        else cp_async_wait_upto(i);  // groups after K tile i: the V tiles issued so far (i)
-        put_new(i, skn);
-        named_bar_sync(2, NT);
-        // warp w -> positions 8w .. 8w + 7 of the tile, 8 k-steps of 16 dims
-        if (8 * warp < nt) {
-            float dh[4] = {0.f, 0.f, 0.f, 0.f}, dl[4] = {0.f, 0.f, 0.f, 0.f};
-            const int r = 8 * warp + gr;  // B column = tile row
-            const uint32_t* krow = reinterpret_cast<const uint32_t*>(tile(i) + r * HD);
-            const uint32_t* qa = sqa + gr * (HD / 2);
-            const bool live = gr < G;
+    const bool live = gr < G;
+    // ---- pass 1: scores of every position of the chunk at once: warp w takes the 8-position groups
+    //      w, w + 8, w + 16, w + 24 (group p: tile p / 8, rows 8 (p % 8) ..), independent mma chains
+    for (int i = 0; i < T; ++i) wait_tile(i, 0u);  // every K tile
+    for (int i = 0; i < T; ++i) put_new(i, skn);
+    named_bar_sync(2, NT);
+    {
+        constexpr int GPW = SK_ATT_TILES;  // position groups per warp
+        float dh[GPW][4], dl[GPW][4];
 #pragma unroll
-            for (int ks = 0; ks < HD / 16; ++ks) {
-                const uint32_t b0 = krow[(((2 * ks) ^ (r & 7)) << 2) + q4];
-                const uint32_t b1 = krow[(((2 * ks + 1) ^ (r & 7)) << 2) + q4];
-                const uint32_t ah0 = live ? qa[8 * ks + q4] : 0u, ah2 = live ? qa[8 * ks + 4 + q4] : 0u;
-                const uint32_t al0 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + q4] : 0u;
-                const uint32_t al2 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + 4 + q4] : 0u;
-                M::mma(dh, ah0, ah2, b0, b1);
-                M::mma(dl, al0, al2, b0, b1);
-            }
-            if (live) {  // d[0], d[1]: head gr, tile rows 8 warp + 2 q4 + {0, 1}
-                const int col = 8 * warp + 2 * q4;
-                if (col < nt) ss[gr * ML + i * TILE + col] = (dh[0] + dl[0]) * scale;
-                if (col + 1 < nt) ss[gr * ML + i * TILE + col + 1] = (dh[1] + dl[1]) * scale;
+        for (int j = 0; j < GPW; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dh[j][e] = dl[j][e] = 0.f;
+        const uint32_t* qa = sqa + gr * (HD / 2);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            const uint32_t ah0 = live ? qa[8 * ks + q4] : 0u, ah2 = live ? qa[8 * ks + 4 + q4] : 0u;
+            const uint32_t al0 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + q4] : 0u;
+            const uint32_t al2 = live ? qa[ATTN_MAX_G * (HD / 2) + 8 * ks + 4 + q4] : 0u;
+#pragma unroll
+            for (int j = 0; j < GPW; ++j) {
+                const int p = warp + NW * j;  // position group
+                if (8 * p >= n) continue;     // warp-uniform
+                const int r = 8 * (p & 7) + gr;
+                const uint32_t* krow = reinterpret_cast<const uint32_t*>(tile(p >> 3) + r * RSTR);
+                const uint32_t b0 = krow[8 * ks + q4];
+                const uint32_t b1 = krow[8 * ks + 4 + q4];
+                M::mma(dh[j], ah0, ah2, b0, b1);
+                M::mma(dl[j], al0, al2, b0, b1);
             }
         }
-        named_bar_sync(2, NT);  // the K tile is dead
-        sk_attn_stage<KVT>(tile(i), vb, a.stride_t, ts, ts + nt, pos);
-        cp_async_commit();
+        if (live) {  // d[0], d[1]: head gr, chunk positions 8 p + 2 q4 + {0, 1}
+#pragma unroll
+            for (int j = 0; j < GPW; ++j) {
+                const int col = 8 * (warp + NW * j) + 2 * q4;
+                if (col < n) ss[gr * ML + col] = (dh[j][0] + dl[j][0]) * scale;
+                if (col + 1 < n) ss[gr * ML + col + 1] = (dh[j][1] + dl[j][1]) * scale;
+            }
+        }
+    }
+    named_bar_sync(2, NT);  // the K tiles are dead: their buffers take the V rows
+    if (tid == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the generic reads of the K rows
+        for (int i = 0; i < T; ++i)
+            sk_attn_rows<KVT>(tile(i), vb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), &abar[i]);
     }
     // ---- the chunk's softmax, a warp per head: max, exp, sum; P (zero beyond n) back into ss
     for (int g = warp; g < G; g += NW) {
@@ -649,35 +648,32 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             ssum[g] = l;
         }
     }
-    // ---- pass 2: P.V per tile as its V rows land; warp w -> dims 16w .. 16w + 15 (two n-tiles)
-    float oh[2][4] = {}, ol[2][4] = {};  // dims 16 warp + 8 j + 2 q4 + {0, 1}
-    const bool live = gr < G;
+    // ---- pass 2: P.V over the chunk; warp w -> dims 16w .. 16w + 15 (two n-tiles), k-steps of 16 positions
+    for (int i = 0; i < T; ++i) wait_tile(i, 1u);  // every V tile
+    for (int i = 0; i < T; ++i) put_new(i, svn);
+    if (n < T * TILE) zero_tail(T - 1, n - (T - 1) * TILE);
+    named_bar_sync(2, NT);
+    float oh[2][2][4] = {}, ol[2][2][4] = {};  // [k-step parity][n-tile j]: dims 16 warp + 8 j + 2 q4 + {0, 1}
     // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
     const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lch = 2 * warp + (lane >> 4);
-    for (int i = 0; i < T; ++i) {
-        const int nt = min(TILE, t1 - (t0 + i * TILE));
-        cp_async_wait_upto(T - 1 - i);  // V tile i (the later V tiles may still be in flight)
-        put_new(i, svn);
-        if (nt < TILE) zero_tail(i, nt);
-        named_bar_sync(2, NT);
-        const float* prow = ss + gr * ML + i * TILE;
-        for (int ks = 0; ks < (nt + 15) / 16; ++ks) {
-            const int r = 16 * ks + lr;
-            const uint32_t addr = smem_u32(reinterpret_cast<uint8_t*>(tile(i) + r * HD) + ((lch ^ (r & 7)) * 16));
-            uint32_t b[4];
-            asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                         : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
-                         : "r"(addr));
-            const float2 p0 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 2 * q4) : make_float2(0.f, 0.f);
-            const float2 p2 = live ? *reinterpret_cast<const float2*>(prow + 16 * ks + 8 + 2 * q4) : make_float2(0.f, 0.f);
-            const float h0x = M::round(p0.x), h0y = M::round(p0.y), h2x = M::round(p2.x), h2y = M::round(p2.y);
-            const uint32_t ah0 = M::pack(h0x, h0y), ah2 = M::pack(h2x, h2y);
-            const uint32_t al0 = M::pack(p0.x - h0x, p0.y - h0y), al2 = M::pack(p2.x - h2x, p2.y - h2y);
-            M::mma(oh[0], ah0, ah2, b[0], b[1]);
-            M::mma(ol[0], al0, al2, b[0], b[1]);
-            M::mma(oh[1], ah0, ah2, b[2], b[3]);
-            M::mma(ol[1], al0, al2, b[2], b[3]);
-        }
+    const float* prow = ss + gr * ML;
+    for (int kp = 0; kp < (n + 15) / 16; ++kp) {  // k-step kp: chunk positions 16 kp ..
+        const int r = 16 * (kp & 3) + lr;
+        const uint32_t addr = smem_u32(tile(kp >> 2) + r * RSTR + lch * 8);
+        uint32_t b[4];
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                     : "r"(addr));
+        const float2 p0 = live ? *reinterpret_cast<const float2*>(prow + 16 * kp + 2 * q4) : make_float2(0.f, 0.f);
+        const float2 p2 = live ? *reinterpret_cast<const float2*>(prow + 16 * kp + 8 + 2 * q4) : make_float2(0.f, 0.f);
+        const float h0x = M::round(p0.x), h0y = M::round(p0.y), h2x = M::round(p2.x), h2y = M::round(p2.y);
+        const uint32_t ah0 = M::pack(h0x, h0y), ah2 = M::pack(h2x, h2y);
+        const uint32_t al0 = M::pack(p0.x - h0x, p0.y - h0y), al2 = M::pack(p2.x - h2x, p2.y - h2y);
+        const int e = kp & 1;  // two accumulator sets: half the dependent chain length
+        M::mma(oh[e][0], ah0, ah2, b[0], b[1]);
+        M::mma(ol[e][0], al0, al2, b[0], b[1]);
+        M::mma(oh[e][1], ah0, ah2, b[2], b[3]);
+        M::mma(ol[e][1], al0, al2, b[2], b[3]);
     }
     // ---- output (single chunk) or this chunk's partials: head gr, dims 16 warp + 8 j + 2 q4 + {0, 1}
     float* pbase = a.part + (((long long)h * a.nchunk + c) * G) * SK_PART_STRIDE;
@@ -686,7 +682,8 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int d = 16 * warp + 8 * j + 2 * q4;
-            const float2 o = make_float2((oh[j][0] + ol[j][0]) * inv, (oh[j][1] + ol[j][1]) * inv);
+            const float2 o = make_float2(((oh[0][j][0] + ol[0][j][0]) + (oh[1][j][0] + ol[1][j][0])) * inv,
+                                         ((oh[0][j][1] + ol[0][j][1]) + (oh[1][j][1] + ol[1][j][1])) * inv);
             if (n_active == 1) *reinterpret_cast<float2*>(a.out + (long long)(qh0 + gr) * HD + d) = o;
             else *reinterpret_cast<float2*>(pbase + gr * SK_PART_STRIDE + d) = o;
         }
@@ -694,8 +691,9 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     if (n_active == 1) return;  // (the caller's barrier orders the next unit's reuse of the buffers)
     if (tid < G) *reinterpret_cast<float2*>(pbase + tid * SK_PART_STRIDE + HD) = make_float2(smax[tid], ssum[tid]);
     // ---- the last unit of KV head h to arrive merges the head's chunks: output (query head
-    //      qh0 + g, dim d) = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M), one pass in chunk order
-    //      with a running rescale (deterministic whichever unit merges). The arrival is one
+    //      qh0 + g, dim d) = sum_c o_c e^(m_c - M) / sum_c l_c e^(m_c - M), the weights e^(m_c - M)
+    //      computed once per (head, chunk), chunks in order (deterministic whichever unit merges;
+    //      more chunks than one staging batch holds rescale per batch). The arrival is one
     //      acq_rel atomic after the CTA barrier (cumulative release of the unit's partials); the
     //      last unit stages the head's partial records in shared memory with one batch of async
     //      copies per SK_MERGE_RECS records.
@@ -709,14 +707,15 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     if (!*flag) return;
     constexpr int RS = SK_PART_STRIDE, NO = ATTN_MAX_G * HD / NT;  // outputs per thread (<= 4)
     float* sp = reinterpret_cast<float*>(sm);                     // [batch][G][RS] staged records
+    float* sw = reinterpret_cast<float*>(sqa);                    // [G][per_batch] chunk weights
     const float* hb = a.part + (long long)h * a.nchunk * G * RS;
     const int per_batch = SK_MERGE_RECS / G;
-    float Mx[NO], Lx[NO], Ox[NO];
+    float Ox[NO];
 #pragma unroll
-    for (int j = 0; j < NO; ++j) {
-        Mx[j] = -INFINITY;
-        Lx[j] = 0.f;
-        Ox[j] = 0.f;
+    for (int j = 0; j < NO; ++j) Ox[j] = 0.f;
+    if (tid < G) {
+        smax[tid] = -INFINITY;  // running max and exp-sum of head tid (this unit's own were stored)
+        ssum[tid] = 0.f;
     }
     for (int cb = 0; cb < n_active; cb += per_batch) {
         const int nb = min(per_batch, n_active - cb);
@@ -726,27 +725,37 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         cp_async_commit();
         cp_async_wait_group<0>();
         named_bar_sync(2, NT);
+        if (tid < G) {  // head g = tid: the batch's chunk weights e^(m_c - M) and the new running max / sum
+            const int g = tid;
+            float mb = smax[g];
+            for (int cc = 0; cc < nb; ++cc) mb = fmaxf(mb, sp[(cc * G + g) * RS + HD]);
+            const float f = smax[g] == -INFINITY ? 0.f : expf(smax[g] - mb);
+            float l = ssum[g] * f;
+            for (int cc = 0; cc < nb; ++cc) {
+                const float w = expf(sp[(cc * G + g) * RS + HD] - mb);
+                sw[g * per_batch + cc] = w;
+                l += sp[(cc * G + g) * RS + HD + 1] * w;
+            }
+            smax[g] = mb;
+            ssum[g] = l;
+            sinv[g] = f;  // rescale of the outputs accumulated over earlier batches
+        }
+        named_bar_sync(2, NT);
 #pragma unroll
         for (int j = 0; j < NO; ++j) {
             const int i = tid + j * NT, g = i / HD, d = i - g * HD;
             if (g < G) {
-                for (int cc = 0; cc < nb; ++cc) {
-                    const float* pr = sp + (cc * G + g) * RS;
-                    const float mc = pr[HD], lc = pr[HD + 1], oc = pr[d];
-                    const float Mn = fmaxf(Mx[j], mc);
-                    const float f1 = (Mx[j] == -INFINITY) ? 0.f : expf(Mx[j] - Mn), f2 = expf(mc - Mn);
-                    Lx[j] = Lx[j] * f1 + lc * f2;
-                    Ox[j] = Ox[j] * f1 + oc * f2;
-                    Mx[j] = Mn;
-                }
+                float o = Ox[j] * sinv[g];
+                for (int cc = 0; cc < nb; ++cc) o += sp[(cc * G + g) * RS + d] * sw[g * per_batch + cc];
+                Ox[j] = o;
             }
         }
-        named_bar_sync(2, NT);  // the next batch overwrites the staging area
+        named_bar_sync(2, NT);  // the next batch overwrites the staging area and the weights
     }
 #pragma unroll
     for (int j = 0; j < NO; ++j) {
         const int i = tid + j * NT, g = i / HD;
-        if (g < G) a.out[(long long)qh0 * HD + i] = Ox[j] / Lx[j];
+        if (g < G) a.out[(long long)qh0 * HD + i] = Ox[j] / ssum[g];
     }
     if (tid == 0) a.counter[h] = 0u;  // every unit of head h has arrived: zero for the next layer
 }
@@ -841,6 +850,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     float* warp_best_v = misc + 40;
     int* warp_best_i = reinterpret_cast<int*>(misc + 72);
     uint64_t* dbar = reinterpret_cast<uint64_t*>(misc + 96);  // [2] descriptor copies (phase k: k & 1)
+    uint64_t* abar = reinterpret_cast<uint64_t*>(misc + 104); // [SK_ATT_TILES] attention tile buffers
 
     if (tid == 0) {
         for (int s = 0; s < ring; ++s) {
@@ -849,6 +859,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         }
         mbar_init(&dbar[0], 1);
         mbar_init(&dbar[1], 1);
+        for (int i = 0; i < SK_ATT_TILES; ++i) mbar_init(&abar[i], 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -941,7 +952,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         mbar_arrive_expect_tx(&dbar[0], SK_DESC);
         bulk_g2s(desc, &A.ph[0], SK_DESC, &dbar[0]);
     }
-    bool attn_pre = false;  // this thread issued tile 0 of its CTA's first attention unit
+    int attn_pre = 0;  // K tiles of this CTA's first attention unit issued at the end of the phase before
     for (int k = 0; k < NPH; ++k) {
         // the next phase's descriptor: one bulk copy into the buffer phase k - 1 used (every consumer
         // thread is past that phase's end barrier), landing while this phase runs
@@ -1030,17 +1041,20 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             if (!*abort_flag)
                 sk_epilogues<TP>(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph,
                                  TP && ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
-            // attention next: this CTA's first unit's tile 0 loads across the phase change (the x
-            // records are dead; the next descriptor was fetched at this phase's start)
-            if (k + 1 < NPH && tid < ATTN_THREADS && mbar_wait(&dbar[(k + 1) & 1], (uint32_t)((k + 1) >> 1) & 1u)) {
+            // attention next: this CTA's first unit's K tiles load across the phase change (the x
+            // records are dead; the next descriptor was fetched at this phase's start); not after a
+            // prefetch that no unit consumed, nor in a step that gave up
+            if (k + 1 < NPH && tid < ATTN_THREADS && attn_pre == 0 && !*abort_flag &&
+                mbar_wait(&dbar[(k + 1) & 1], (uint32_t)((k + 1) >> 1) & 1u)) {
                 const SPhase& nx = *reinterpret_cast<const SPhase*>(desc + ((k + 1) & 1) * SK_DESC);
                 if (nx.kind == SP_ATTN) {
                     const int seq = pos + 1;
                     const int clen = sk_attn_clen(seq, nx.at.nchunk, G, nx.at.n_kv_heads, A.attn_solo);
                     const int nch = (seq + clen - 1) / clen;
-                    if (nch <= nx.at.nchunk && c < nx.at.n_kv_heads * nch) {
-                        sk_attn_prefetch_k<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch);
-                        attn_pre = true;
+                    if (nch <= nx.at.nchunk && nx.at.stride_t == SK_ATT_RSTR && c < nx.at.n_kv_heads * nch) {
+                        sk_attn_prefetch_k<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch, abar);
+                        const int t0 = (c % nch) * clen;
+                        attn_pre = (min(t0 + clen, seq) - t0 + ATTN_CMAX - 1) / ATTN_CMAX;
                     }
                 }
             }
@@ -1050,15 +1064,17 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads, A.attn_solo);
             const int nch = (seq + clen - 1) / clen;
             // the partials hold at.nchunk chunks per KV head (the engine sizes them for max_ctx)
-            const int units = nch <= at.nchunk ? at.n_kv_heads * nch : 0;
-            if (nch > at.nchunk && tid == 0) {
+            const bool fits = nch <= at.nchunk && at.stride_t == SK_ATT_RSTR;  // the engine's KV layout
+            const int units = fits ? at.n_kv_heads * nch : 0;
+            if (!fits && tid == 0) {
                 set_device_error(SK_WAIT_ERR);
                 *abort_flag = 1;
             }
             for (int u = c; u < units; u += G) {
                 // the first unit's tile 0 may have been issued at the end of the previous phase
-                if (tid < ATTN_THREADS) sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre);
-                attn_pre = false;
+                if (tid < ATTN_THREADS)
+                    sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre > 0, abar, abort_flag);
+                attn_pre = 0;
                 named_bar_sync(1, NT);  // the next unit reuses the scratch
                 if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
             }
@@ -1076,7 +1092,11 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         }
     }
 
-    cp_async_wait_all();  // an attention tile prefetch of a step that gave up is not left in flight
+    cp_async_wait_all();
+    if (attn_pre > 0 && tid == 0)  // K tiles prefetched for a unit that did not run (a step that gave up):
+        for (int i = 0; i < attn_pre; ++i)  // let the copies land (bounded) before the CTA exits
+            for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS; ++it)
+                if (mbar_try_wait(&abar[i], 0u)) break;
     // ---- argmax of the LM head: thread -> warp -> CTA -> (last CTA of the step) global
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
