@@ -36,6 +36,9 @@ RMat rmat_carve(int wt, long long rows, int K, uint8_t* base, int iph = 0);
 cudaError_t rmat_fill(int wt, const uint8_t* src, long long rows, int K, const RMat& m, long long dst_row0,
                       int dst_stride, cudaStream_t st, int src_K = 0, int item0 = 0);
 RGemvPlan plan_rgemv(RGemvArgs& a, int sms, int smem_budget);
+unsigned long long sk_tile_plan(int wt, int I, int Mv, int dual, int G, int RB, int CI, unsigned long long* tcta);
+cudaError_t sk_retile(int wt, const RMat& m, int I, int Mv, int dual, int G, int RB, int CI,
+                      const unsigned long long* d_tcta, uint8_t* dst, cudaStream_t st);
 cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
                         float top_p, int top_k, float rep_penalty, float min_p, bool dynamic_temp,
@@ -94,7 +97,9 @@ struct fence_model {
     int fwd_valid = 0;               // h_out holds the state of the step that produced m->logits
     std::vector<LayerLaunch> launches;
     RPhase lm{};
-    uint8_t* rarena = nullptr;      // repacked linears (rgemv.cuh layouts)
+    uint8_t* rarena = nullptr;      // repacked linears (rgemv.cuh layouts; freed once the step kernel's tiles exist)
+    uint8_t* tarena = nullptr;      // the step kernel's tiled linears
+    unsigned long long* d_tcta = nullptr;  // per GEMV phase, per CTA: first tile offset
     // persistent token-step kernel (step.cuh)
     int use_step = 0;
     std::vector<SPhase> h_phases;
@@ -335,6 +340,41 @@ int build_step_phases(fence_model* m) {
     m->splan = plan_step(ph, m->dev, err);
     if (!m->splan.ok) return set_error(FENCE_E_UNSUPPORTED, "%s", err.c_str());
     if (m->splan.grid > 4096) return set_error(FENCE_E_UNSUPPORTED, "step kernel: more than 4096 SMs");
+    // re-tile every GEMV phase's matrix for the step kernel (per-CTA row blocks x K-slices, one bulk
+    // copy per tile), then drop the row-major copy
+    {
+        const int G = m->splan.grid;
+        size_t ngemv = 0;
+        for (const SPhase& p : ph) ngemv += p.kind == SP_GEMV;
+        std::vector<unsigned long long> tc(ngemv * G);
+        std::vector<unsigned long long> base(ngemv);
+        unsigned long long total = 0;
+        size_t gi = 0;
+        for (const SPhase& p : ph) {
+            if (p.kind != SP_GEMV) continue;
+            const RGemvArgs& g = p.g;
+            base[gi] = total;
+            total += (sk_tile_plan(g.wt, g.I, g.Mv, g.dual, G, g.RB, g.CI, &tc[gi * G]) + 255) / 256 * 256;
+            ++gi;
+        }
+        FENCE_CUDA_TRY(cudaMalloc(&m->tarena, total + 256));
+        FENCE_CUDA_TRY(cudaMemset(m->tarena, 0, total + 256));
+        FENCE_CUDA_TRY(cudaMalloc(&m->d_tcta, tc.size() * sizeof(unsigned long long)));
+        FENCE_CUDA_TRY(cudaMemcpy(m->d_tcta, tc.data(), tc.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+        gi = 0;
+        for (SPhase& p : ph) {
+            if (p.kind != SP_GEMV) continue;
+            RGemvArgs& g = p.g;
+            g.tb = m->tarena + base[gi];
+            g.tcta = m->d_tcta + gi * G;
+            FENCE_CUDA_TRY(sk_retile(g.wt, g.w, g.I, g.Mv, g.dual, G, g.RB, g.CI, g.tcta, const_cast<uint8_t*>(g.tb),
+                                     m->stream));
+            ++gi;
+        }
+        FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
+        cudaFree(m->rarena);  // the per-phase path (step_kernel = 0) is the only reader of the row-major copy
+        m->rarena = nullptr;
+    }
     FENCE_CUDA_TRY(cudaMalloc(&m->d_phases, ph.size() * sizeof(SPhase)));
     FENCE_CUDA_TRY(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(SPhase), cudaMemcpyHostToDevice));
     FENCE_CUDA_TRY(cudaMalloc(&m->d_bar, sizeof(unsigned long long)));
@@ -397,6 +437,8 @@ void free_model(fence_model* m) {
     cudaFree(m->token_log);
     cudaFree(m->rope);
     cudaFree(m->rarena);
+    cudaFree(m->tarena);
+    cudaFree(m->d_tcta);
     cudaFree(m->qkv_bias);
     cudaFree(m->d_phases);
     cudaFree(m->d_bar);

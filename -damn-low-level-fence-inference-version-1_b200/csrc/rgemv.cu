@@ -66,6 +66,87 @@ __global__ void repack_q80_kernel(const uint8_t* __restrict__ src, long long row
     dd[3] = b1[1];
 }
 
+// Row-major repacked matrix -> the step kernel's tiles (sk_tile_bytes): CTA c of G holds the
+// virtual rows [Mv c / G, Mv (c + 1) / G) (dual: both rows of each gate/up pair), cut into row blocks
+// of RB rows and K-slices of CI items, tiles in (block, slice) order from byte tcta[c]. One thread
+// per (row, item) record; Q8_0 chunk positions re-swizzled by the item's slot in its slice; the
+// thread of slot 0 also writes the row's Q6_K d entries of the slice. dst must be zeroed.
+__device__ __forceinline__ int rt_vbegin(long long Mv, int c, int G) { return (int)((Mv * c) / G); }
+__global__ void retile_kernel(int wt, RMat m, int I, int Mv, int dual, int G, int RB, int CI,
+                              const unsigned long long* __restrict__ tcta, uint8_t* __restrict__ dst) {
+    const long long rows = (long long)Mv * (dual ? 2 : 1);
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= rows * I) return;
+    const long long r = idx / I;
+    const int it = (int)(idx - r * I);
+    const int v = (int)(dual ? r / 2 : r);
+    int c = (int)min((long long)G - 1, ((long long)v * G) / Mv);
+    while (c > 0 && rt_vbegin(Mv, c, G) > v) --c;
+    while (c + 1 < G && rt_vbegin(Mv, c + 1, G) <= v) ++c;
+    const int f = dual ? 2 : 1;
+    const long long r_begin = (long long)f * rt_vbegin(Mv, c, G);
+    const int rows_c = f * (rt_vbegin(Mv, c + 1, G) - rt_vbegin(Mv, c, G));
+    const int rl = (int)(r - r_begin), b = rl / RB, rb = rl - b * RB;
+    const int rows_b = min(RB, rows_c - b * RB);
+    const int ns = (I + CI - 1) / CI, j = it / CI, is = it - j * CI;
+    const int items = min(CI, I - j * CI);
+    const unsigned long long block_bytes =
+        (unsigned long long)(ns - 1) * sk_tile_bytes(wt, RB, CI, CI) + sk_tile_bytes(wt, RB, I - (ns - 1) * CI, CI);
+    uint32_t s_off, d_off;
+    sk_tile_bytes(wt, rows_b, items, CI, &s_off, &d_off);
+    uint8_t* t = dst + tcta[c] + (unsigned long long)b * block_bytes +
+                 (unsigned long long)j * sk_tile_bytes(wt, rows_b, CI, CI);
+    const uint32_t rec = (uint32_t)(rb * items + is);
+    if (wt == WT_Q80) {
+        const uint8_t* sq = m.q + ((size_t)r * I + it) * 64;
+        const int fs = (it >> 1) & 3, fd = (is >> 1) & 3;
+        uint8_t* dq = t + (size_t)rec * 64;
+        for (int p = 0; p < 4; ++p) {
+            const int k = p ^ fs;  // the chunk at source position p
+            for (int e = 0; e < 16; ++e) dq[16 * (k ^ fd) + e] = sq[16 * p + e];
+        }
+        const uint8_t* sd = m.d + ((size_t)r * I + it) * 4;
+        for (int e = 0; e < 4; ++e) t[d_off + rec * 4 + e] = sd[e];
+    } else {
+        const uint8_t* sq = m.q + ((size_t)r * I + it) * 48;
+        for (int e = 0; e < 48; ++e) t[(size_t)rec * 48 + e] = sq[e];
+        const uint8_t* ss = m.s + (size_t)r * rg_sbytes_row(WT_Q6K, I) + (size_t)it * 4;
+        for (int e = 0; e < 4; ++e) t[s_off + rec * 4 + e] = ss[e];
+        if (is == 0) {
+            const int ndq = sk_ndq(CI), dbr = rg_dbytes_row(WT_Q6K, I, m.iph), nsb = dbr / 2;
+            const int sb0 = (j * CI + m.iph) >> 2;
+            for (int e = 0; e < ndq && sb0 + e < nsb; ++e) {
+                t[d_off + (rb * ndq + e) * 2] = m.d[(size_t)r * dbr + (sb0 + e) * 2];
+                t[d_off + (rb * ndq + e) * 2 + 1] = m.d[(size_t)r * dbr + (sb0 + e) * 2 + 1];
+            }
+        }
+    }
+}
+
+// Tile offsets of every CTA (host): tcta[c] for c < G and the matrix's tiled bytes (return).
+unsigned long long sk_tile_plan(int wt, int I, int Mv, int dual, int G, int RB, int CI, unsigned long long* tcta) {
+    const int ns = (I + CI - 1) / CI, f = dual ? 2 : 1;
+    unsigned long long off = 0;
+    for (int c = 0; c < G; ++c) {
+        tcta[c] = off;
+        const int rows_c = f * (int)(((long long)Mv * (c + 1)) / G - ((long long)Mv * c) / G);
+        for (int r0 = 0; r0 < rows_c; r0 += RB) {
+            const int rows_b = std::min(RB, rows_c - r0);
+            for (int j = 0; j < ns; ++j) off += sk_tile_bytes(wt, rows_b, std::min(CI, I - j * CI), CI);
+        }
+    }
+    return off;
+}
+
+cudaError_t sk_retile(int wt, const RMat& m, int I, int Mv, int dual, int G, int RB, int CI,
+                      const unsigned long long* d_tcta, uint8_t* dst, cudaStream_t st) {
+    const long long n = (long long)Mv * (dual ? 2 : 1) * I;
+    const int threads = 256;
+    retile_kernel<<<(unsigned)((n + threads - 1) / threads), threads, 0, st>>>(wt, m, I, Mv, dual, G, RB, CI, d_tcta,
+                                                                              dst);
+    return cudaGetLastError();
+}
+
 size_t rmat_bytes(int wt, long long rows, int K, int iph) {
     const int I = K / 64;
     auto pad = [](size_t x) { return (x + 64 + 255) / 256 * 256; };

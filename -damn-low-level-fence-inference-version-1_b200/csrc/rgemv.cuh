@@ -60,7 +60,7 @@ struct RGemvArgs {
     int wt;
     int I;            // items (64 weights) per row
     int np;           // parts per row (rows longer than the consumer lanes are split in np equal parts)
-    int ipl;          // step kernel: items per consumer lane (1 or 2; lane p of a row owns items p, p + LP)
+    int ipl;          // (unused by the tiled step kernel; kept 1)
     int R;            // rows per stage (dual: even; rows 2p, 2p+1 are gate/up of pair p)
     int dual;
     int Mv;           // virtual rows (dual: gate/up pairs)
@@ -85,7 +85,31 @@ struct RGemvArgs {
     DecodeState* state;
     int* token_log;
     int token_log_cap;
+    // step kernel: the matrix re-tiled per CTA into row blocks of RB rows x K-slices of CI items,
+    // each tile contiguous (sk_tile_bytes) and streamed by one bulk copy; tcta[c] = byte offset of
+    // CTA c's first tile in tb
+    const uint8_t* tb;
+    const unsigned long long* tcta;
+    int RB, CI;
+    int pad_[2];
 };
+
+// ---- tiles of the step kernel's weights (one (row block, K-slice) of one CTA's rows)
+// Q8_0: q [n][64] (chunk k of record (row, slot s) at 16-byte position k ^ ((s >> 1) & 3)) | d [n][4]
+// Q6_K: q [n][48] | s [n][4] | d [rows][ndq] (fp16 d of the super-blocks the slice overlaps)
+// with n = rows x items records in (row, slot) order, every part 16-byte aligned.
+__host__ __device__ inline int sk_ndq(int CI) { return (CI + 3) / 4 + 1; }
+__host__ __device__ inline uint32_t sk_tile_bytes(int wt, int rows, int items, int CI, uint32_t* s_off = nullptr,
+                                                  uint32_t* d_off = nullptr) {
+    const uint32_t n = (uint32_t)rows * (uint32_t)items;
+    const uint32_t q = n * (uint32_t)(wt == WT_Q6K ? 48 : 64);
+    const uint32_t so = q;
+    const uint32_t doff = (wt == WT_Q6K) ? ((so + 4u * n + 15u) & ~15u) : q;
+    const uint32_t db = (wt == WT_Q6K) ? (uint32_t)rows * (uint32_t)sk_ndq(CI) * 2u : 4u * n;
+    if (s_off) *s_off = so;
+    if (d_off) *d_off = doff;
+    return (doff + db + 15u) & ~15u;
+}
 
 // Launch plan (host).
 struct RGemvPlan {

@@ -21,27 +21,23 @@ static bool plan_step_gemv(RGemvArgs& g, int grid, std::string& err) {
         err = "step kernel: empty GEMV phase";
         return false;
     }
-    if (I > SK_NL) {
-        err = "step kernel: a linear input width above " + std::to_string(SK_NL * 64) + " values";
-        return false;
-    }
-    // each consumer lane owns one item of one row for the whole phase; a stage holds as many whole
-    // rows as the consumer lanes allow
-    const int J = 1;
-    const int LP = I;
-    int R = std::min(SK_NL / LP, SK_MAX_R);
     const int vcta = (g.Mv + grid - 1) / grid;
     const int rows_cta = vcta * (g.dual ? 2 : 1);
-    R = std::max(1, std::min(R, rows_cta));
+    // tiles of RB rows x CI items, one item per consumer lane: slices of 8 to 32 items (a row's lanes
+    // inside one warp), as many rows of the CTA per block as the lanes allow
+    const int CI = std::max(1, std::min(std::min(I, 32), std::max(8, SK_NL / std::max(1, rows_cta))));
+    const int RB = std::max(1, std::min(rows_cta, SK_NL / CI));
     int mp = 1;
-    for (int r = 0; r < R; ++r) mp = std::max(mp, rg_part_pieces(r, 0, 1, LP));
+    for (int r = 0; r < RB; ++r) mp = std::max(mp, rg_part_pieces(r, 0, 1, CI));
     g.np = 1;
-    g.ipl = J;
-    g.R = R;
+    g.ipl = 1;
+    g.R = RB;
+    g.RB = RB;
+    g.CI = CI;
     g.mp = mp;
     g.rows_cta = rows_cta;
     g.ring = 0;
-    g.slot_bytes = (int)((rg_slot(g.wt, I, R, g.w.iph).bytes + 127u) & ~127u);
+    g.slot_bytes = (int)((sk_tile_bytes(g.wt, RB, std::min(CI, I), CI) + 127u) & ~127u);
     return true;
 }
 
@@ -58,7 +54,7 @@ static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err
         if (!plan_step_gemv(ph.g, grid, err)) return P;
         slot = std::max(slot, ph.g.slot_bytes);
         accf = std::max(accf, ph.g.rows_cta * ph.g.mp);
-        int need = ph.g.I * XQ_WORDS * 4;
+        int need = ph.g.I * (int)SK_XQB;
         if (ph.embed || ph.tp_sum) need += ph.g.I * 64 * 4;  // fp32 x row (embedding / reduced) after the records
         scratch = std::max(scratch, need);
     }

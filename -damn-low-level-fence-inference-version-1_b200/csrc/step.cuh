@@ -45,6 +45,9 @@ constexpr int SK_NW = 11;                 // consumer warps
 constexpr int SK_NT = SK_NW * 32 + 32;    // + producer warp
 constexpr int SK_NL = SK_NW * 32;         // consumer lanes (352)
 constexpr int SK_MAX_R = 64;              // rows per stage
+// x records of the step kernel: 176 bytes apart (an odd number of 16-byte chunks), so the lanes of a
+// quarter-warp reading eight consecutive items' records hit eight different bank groups
+constexpr uint32_t SK_XQB = 176;
 constexpr uint32_t SK_BAR_SPINS = 1u << 20;
 // Exchange buffer of one rank (tensor parallel): an argmax counter, one argmax (value bits |
 // index << 32) per rank, then partials [2][tp_n][tp_h] (a rank's rows adjacent, so the writing
@@ -226,7 +229,7 @@ __device__ __forceinline__ void sk_quantise(const void* xsrc, const float* norm_
     }
     if (warp * 32 < ntask) {  // warp-uniform (shuffles inside)
         const int item = mine ? tid / LPI : 0;
-        rg_quant_store<WT, XM>(xv, wv, tid % LPI, rms, xq_sa + item * XQ_WORDS * 4, mine);
+        rg_quant_store<WT, XM>(xv, wv, tid % LPI, rms, xq_sa + item * SK_XQB, mine);
     }
     for (int b0 = NT + warp * 32; b0 < ntask; b0 += NT) {
         const int idx = b0 + lane;
@@ -246,7 +249,7 @@ __device__ __forceinline__ void sk_quantise(const void* xsrc, const float* norm_
                 tw[4 * cc + 3] = f.w;
             }
         }
-        rg_quant_store<WT, XM>(t, tw, q, rms, xq_sa + item * XQ_WORDS * 4, active);
+        rg_quant_store<WT, XM>(t, tw, q, rms, xq_sa + item * SK_XQB, active);
     }
     named_bar_sync(1, NT);  // records complete; misc free again
 }
@@ -277,64 +280,69 @@ __device__ __forceinline__ bool sk_wait_full(uint64_t* bar, uint32_t par, volati
     return false;
 }
 
-// ---- the stage loop of a GEMV phase (consumers), one loop for both weight types: every stage worked
-// on by all consumer lanes (lane <-> (row of the stage, item), x in registers), a segmented shuffle
-// reduction per row inside each warp, one shared-memory piece per (row, warp); only the item dot
-// branches on the (phase-uniform) type. Returns the ring stages consumed.
-__device__ __forceinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& rr, uint32_t use, int ring,
-                                              int slot_bytes, uint32_t smem_sa, uint32_t xq_sa, float* acc,
-                                              uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
+// ---- the stage loop of a GEMV phase (consumers) over the CTA's tiles (row block b x K-slice j, in
+// that order). Lane <-> (row rl of the block, item slot is of the slice): per tile it loads its
+// item's x record (shared by the lanes of the other rows: a broadcast) and its weight record, does
+// the exact integer item dot and adds it to a register accumulator; after a block's last slice a
+// segmented shuffle reduction over the row's CI lanes leaves one shared-memory piece per (row,
+// warp). No reduction sits between the tiles of a block. Returns the ring stages consumed. Out of
+// line: the loop gets the whole register budget.
+template <int WT>
+__device__ __noinline__ uint32_t sk_stages(const RGemvArgs& g, const SKRows& rr, uint32_t use, int ring,
+                                           int slot_bytes, uint32_t smem_sa, uint32_t xq_sa, float* acc,
+                                           uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool q6 = g.wt == WT_Q6K;
-    const int I = g.I, LP = I, R = g.R, MP = g.mp;
-    const int qb = rg_qbytes(g.wt), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
-    const RSlot SS = rg_slot(g.wt, I, R, g.w.iph);
-    const int rs = tid / LP, it = tid - rs * LP;
-    const bool lane_on = rs < R;
-    RX x;
-    if (lane_on) {
-        if (q6) rg_load_x<WT_Q6K>(xq_sa + it * XQ_WORDS * 4, it, x);
-        else rg_load_x<WT_Q80>(xq_sa + it * XQ_WORDS * 4, it, x);
-    }
-    const int slot_lo = rs * LP;
-    const int seg_hi = min(slot_lo + LP - 1 - warp * 32, 31);
+    const int I = g.I, RB = g.RB, CI = g.CI, MP = g.mp;
+    const int rows = (int)(rr.r_end - rr.r_begin);
+    const int ns = (I + CI - 1) / CI, ndq = sk_ndq(CI);
+    const int rl = tid / CI, is = tid - rl * CI;
+    const bool lane_on = rl < RB;
+    const int slot_lo = rl * CI;
+    const int seg_hi = min(slot_lo + CI - 1 - warp * 32, 31);
     const bool head = lane == max(slot_lo - warp * 32, 0);
     const int pidx = warp - (slot_lo >> 5);  // this segment's piece index in its row's reduction
-    // shared-memory offsets of the lane's words inside a slot, and of its reduction piece
-    const uint32_t q_off = (uint32_t)(rs * I + it) * qb;
-    const uint32_t s_off = SS.s_off + (uint32_t)(rs * rg_sbytes_row(g.wt, I) + it * 4);
-    const uint32_t d_off =
-        SS.d_off + (q6 ? (uint32_t)(rs * (dbr / 2) + ((it + g.w.iph) >> 2)) * 2u : (uint32_t)(rs * I + it) * 4u);
-    const uint32_t acc_sa = smem_u32(acc) + (uint32_t)(rs * MP + pidx) * 4u;
-    const int rows = (int)(rr.r_end - rr.r_begin);
+    const uint32_t sw = ((uint32_t)(is >> 1) & 3u) << 4;  // Q8_0 chunk position swizzle of this slot
+    const uint32_t acc_sa = smem_u32(acc) + (uint32_t)(rl * MP + pidx) * 4u;
     const uint32_t ring_u = (uint32_t)ring;
-    // the d copy of a stage starts at the 16-byte boundary below its first row's d
-    uint32_t dd = (uint32_t)(((uint64_t)rr.r_begin * dbr) & 15u);
-    const uint32_t dstep = (uint32_t)(R * dbr);
     uint32_t slot = use % ring_u, par = (use / ring_u) & 1u;  // advanced incrementally below
-    for (int r0 = 0; r0 < rows; r0 += R, ++use) {
-        const bool ok = sk_wait_full(&full[slot], par, abort_flag);
-        const bool on = ok && lane_on && rs < rows - r0;
-        float v = 0.f;
-        if (on) {
-            const uint32_t base = smem_sa + slot * (uint32_t)slot_bytes;
-            if (q6) v = rg_item_dot<WT_Q6K>(base + q_off, base + s_off, base + d_off + dd, x);
-            else v = rg_item_dot<WT_Q80>(base + q_off, base + s_off, base + d_off + dd, x);
+    for (int r0 = 0; r0 < rows; r0 += RB) {
+        const int rows_b = min(RB, rows - r0);
+        const bool row_on = lane_on && rl < rows_b;
+        float a = 0.f;
+        for (int j = 0; j < ns; ++j, ++use) {
+            const int items = min(CI, I - j * CI);
+            uint32_t s_off, d_off;
+            sk_tile_bytes(WT, rows_b, items, CI, &s_off, &d_off);
+            const bool ok = sk_wait_full(&full[slot], par, abort_flag);
+            if (ok && row_on && is < items) {
+                const int it = j * CI + is;
+                const uint32_t base = smem_sa + slot * (uint32_t)slot_bytes;
+                const uint32_t rec = (uint32_t)(rl * items + is);
+                RX x;
+                rg_load_x<WT>(xq_sa + (uint32_t)it * SK_XQB, it, x);
+                x.sw = sw;
+                RWT<WT> w;
+                const uint32_t dad = WT == WT_Q6K
+                    ? base + d_off + (uint32_t)(rl * ndq + ((it + g.w.iph) >> 2) - ((j * CI + g.w.iph) >> 2)) * 2u
+                    : base + d_off + rec * 4u;
+                rg_item_load<WT>(base + rec * (uint32_t)rg_qbytes(WT), base + s_off + rec * 4u, dad, x.sw, w);
+                a += rg_item_compute<WT>(w, x);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);  // the slot's bytes are no longer read
+            if (++slot == ring_u) {
+                slot = 0;
+                par ^= 1u;
+            }
         }
+        // the row's CI lanes, inside this warp: fixed tree (deterministic)
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const float t = __shfl_down_sync(0xffffffffu, v, o);
-            if (lane + o <= seg_hi) v += t;
+            const float t = __shfl_down_sync(0xffffffffu, a, o);
+            if (lane + o <= seg_hi) a += t;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);  // the slot's bytes are no longer read
-        if (on && head)
-            asm volatile("st.shared.f32 [%0], %1;" ::"r"(acc_sa + (uint32_t)(r0 * MP) * 4u), "f"(v) : "memory");
-        dd = (dd + dstep) & 15u;
-        if (++slot == ring_u) {
-            slot = 0;
-            par ^= 1u;
-        }
+        if (row_on && head)
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(acc_sa + (uint32_t)(r0 * MP) * 4u), "f"(a) : "memory");
     }
     return use;
 }
@@ -422,20 +430,35 @@ __device__ __forceinline__ void sk_attn_rows(KVT* dst, const KVT* src, long long
     bulk_g2s(dst, src + (long long)ts * stride_t, bytes, bar);
 }
 
-// Issues the K tiles of attention unit (h, c) (thread 0): run at the end of the phase before
-// attention, so they load across the phase change. The cache rows before pos are not written by
-// that phase; the row at pos is replaced by the unit.
+// Tile buffers of a chunk of T tiles: K tile i in buffer i; V tile i in buffer i + SK_ATT_TILES / 2
+// when the chunk has at most SK_ATT_TILES / 2 tiles (its K and V then load together), else in
+// buffer i once the scores of K tile i are done.
+__device__ __forceinline__ int sk_attn_vbuf(int T, int i) { return T <= SK_ATT_TILES / 2 ? i + SK_ATT_TILES / 2 : i; }
+
+// Issues the tiles of attention unit (h, c) that can load before its scores: the K tiles, and the V
+// tiles when they have buffers of their own (thread 0). Run at the end of the phase before attention,
+// so they load across the phase change; the cache rows before pos are not written by that phase and
+// the row at pos is replaced by the unit. Returns the tile count T.
 template <typename KVT>
-__device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int c, int clen, int pos, uint8_t* sm,
+__device__ __forceinline__ int sk_attn_issue_early(const AttnArgs& a, int h, int c, int clen, int pos, uint8_t* sm,
                                                    uint64_t* abar) {
     constexpr int TILE = ATTN_CMAX;
     KVT* kt = reinterpret_cast<KVT*>(sm);
     const int t0 = c * clen, t1 = min(t0 + clen, pos + 1);
+    const int T = (t1 - t0 + TILE - 1) / TILE;
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
-    if (threadIdx.x != 0) return;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the generic use of the scratch
-    for (int ts = t0, i = 0; ts < t1; ts += TILE, ++i)
-        sk_attn_rows<KVT>(kt + i * TILE * SK_ATT_RSTR, kb, a.stride_t, ts, min(ts + TILE, t1), &abar[i]);
+    const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
+    if (threadIdx.x == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the generic use of the scratch
+        for (int ts = t0, i = 0; ts < t1; ts += TILE, ++i) {
+            sk_attn_rows<KVT>(kt + i * TILE * SK_ATT_RSTR, kb, a.stride_t, ts, min(ts + TILE, t1), &abar[i]);
+            if (T <= SK_ATT_TILES / 2) {
+                const int vbi = sk_attn_vbuf(T, i);
+                sk_attn_rows<KVT>(kt + vbi * TILE * SK_ATT_RSTR, vb, a.stride_t, ts, min(ts + TILE, t1), &abar[vbi]);
+            }
+        }
+    }
+    return T;
 }
 
 // One attention unit of the step kernel (KV head h, context chunk c of clen <= SK_ATT_MAXLEN
@@ -456,7 +479,8 @@ __device__ __forceinline__ void sk_attn_prefetch_k(const AttnArgs& a, int h, int
 //    single phase; for a single chunk the unit writes the normalised output itself.
 template <typename KVT>
 __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
-                                          uint8_t* sm, bool pre, uint64_t* abar, volatile int* abort_flag) {
+                                          uint8_t* sm, bool pre, uint64_t* abar, uint32_t& apar,
+                                          volatile int* abort_flag) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
     constexpr int HD = 128, EPC = 16 / (int)sizeof(KVT);
@@ -484,17 +508,19 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     const KVT* kb = reinterpret_cast<const KVT*>(a.kc) + (long long)h * a.stride_h;
     const KVT* vb = reinterpret_cast<const KVT*>(a.vc) + (long long)h * a.stride_h;
     auto tile = [&](int i) { return kv + i * TILE * RSTR; };
-    // tile buffer i: its mbarrier completes once per fill (K, then V), so a unit waits on parity 0
-    // for its K rows and on parity 1 for its V rows
-    auto wait_tile = [&](int i, uint32_t par) {
-        if (!mbar_wait(&abar[i], par)) *abort_flag = 1;
+    auto vtile = [&](int i) { return tile(sk_attn_vbuf(T, i)); };
+    // a buffer's mbarrier completes once per fill; apar (the same in every unit thread) holds the
+    // parity of each buffer's next completion
+    auto wait_buf = [&](int b) {
+        if (!mbar_wait(&abar[b], (apar >> b) & 1u)) *abort_flag = 1;
+        apar ^= 1u << b;
     };
     // the new row (cache-rounded floats) into its tile slot, when pos lies in tile i
-    auto put_new = [&](int i, const float* row) {
+    auto put_new = [&](int i, int buf, const float* row) {  // tile i held in buffer buf
         const int r = pos - (t0 + i * TILE);
         if (r < 0 || r >= TILE || tid >= HD) return;
         const int d = tid;
-        tile(i)[r * RSTR + d] = C::from(row[d]);
+        tile(buf)[r * RSTR + d] = C::from(row[d]);
     };
     // rows [m, round16(m)) of a partial V tile: zero, so that P.V's last k-step reads finite values
     auto zero_tail = [&](int i, int m) {
@@ -521,11 +547,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
                    reinterpret_cast<const float*>(a.rope + (long long)pos * (HD / 2)) + 4 * i);
     }
     cp_async_commit();
-    if (!pre && tid == 0) {  // the K tiles (with `pre` they went out at the end of the previous phase)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the previous unit's reads
-        for (int i = 0; i < T; ++i)
-            sk_attn_rows<KVT>(tile(i), kb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), &abar[i]);
-    }
+    if (!pre) sk_attn_issue_early<KVT>(a, h, c, clen, pos, sm, abar);  // else issued at the previous phase's end
     cp_async_wait_group<0>();  // the small inputs
     named_bar_sync(2, NT);
     // ---- q/k RMSNorm (w * x * rms) and NeoX rotation, a warp per head; the new K/V row
@@ -587,8 +609,8 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     const bool live = gr < G;
     // ---- pass 1: scores of every position of the chunk at once: warp w takes the 8-position groups
     //      w, w + 8, w + 16, w + 24 (group p: tile p / 8, rows 8 (p % 8) ..), independent mma chains
-    for (int i = 0; i < T; ++i) wait_tile(i, 0u);  // every K tile
-    for (int i = 0; i < T; ++i) put_new(i, skn);
+    for (int i = 0; i < T; ++i) wait_buf(i);  // every K tile
+    for (int i = 0; i < T; ++i) put_new(i, i, skn);
     named_bar_sync(2, NT);
     {
         constexpr int GPW = SK_ATT_TILES;  // position groups per warp
@@ -624,8 +646,8 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             }
         }
     }
-    named_bar_sync(2, NT);  // the K tiles are dead: their buffers take the V rows
-    if (tid == 0) {
+    named_bar_sync(2, NT);  // the K tiles are dead: long chunks load their V rows into those buffers
+    if (tid == 0 && T > SK_ATT_TILES / 2) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after the generic reads of the K rows
         for (int i = 0; i < T; ++i)
             sk_attn_rows<KVT>(tile(i), vb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), &abar[i]);
@@ -649,9 +671,9 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         }
     }
     // ---- pass 2: P.V over the chunk; warp w -> dims 16w .. 16w + 15 (two n-tiles), k-steps of 16 positions
-    for (int i = 0; i < T; ++i) wait_tile(i, 1u);  // every V tile
-    for (int i = 0; i < T; ++i) put_new(i, svn);
-    if (n < T * TILE) zero_tail(T - 1, n - (T - 1) * TILE);
+    for (int i = 0; i < T; ++i) wait_buf(sk_attn_vbuf(T, i));  // every V tile
+    for (int i = 0; i < T; ++i) put_new(i, sk_attn_vbuf(T, i), svn);
+    if (n < T * TILE) zero_tail(sk_attn_vbuf(T, T - 1), n - (T - 1) * TILE);
     named_bar_sync(2, NT);
     float oh[2][2][4] = {}, ol[2][2][4] = {};  // [k-step parity][n-tile j]: dims 16 warp + 8 j + 2 q4 + {0, 1}
     // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
@@ -659,7 +681,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     const float* prow = ss + gr * ML;
     for (int kp = 0; kp < (n + 15) / 16; ++kp) {  // k-step kp: chunk positions 16 kp ..
         const int r = 16 * (kp & 3) + lr;
-        const uint32_t addr = smem_u32(tile(kp >> 2) + r * RSTR + lch * 8);
+        const uint32_t addr = smem_u32(vtile(kp >> 2) + r * RSTR + lch * 8);
         uint32_t b[4];
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                      : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
@@ -793,7 +815,7 @@ template <bool TP>
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
                                              const float* rpre, float& best_v, int& best_i, const StepArgs& A,
                                              const SPhase& ph, unsigned tag) {
-    const int LP = g.I, R = g.R, MP = g.mp;
+    const int LP = g.CI, R = g.RB, MP = g.mp;
     auto row_sum = [&](int rl) {
         const int n = rg_part_pieces(rl % R, 0, 1, LP);
         float t = 0.f;
@@ -894,39 +916,32 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 // a ring's depth ahead (they are otherwise evicted by the weight stream)
                 if (g.norm_w && c < 8) bulk_prefetch_l2(g.norm_w, (uint32_t)g.I * 256u);
                 const SKRows rr = sk_rows(g, c, G);
-                const int I = g.I, R = g.R;
-                const int qb = rg_qbytes(g.wt), sbr = rg_sbytes_row(g.wt, I), dbr = rg_dbytes_row(g.wt, I, g.w.iph);
-                const RSlot SS = rg_slot(g.wt, I, R, g.w.iph);
-                const int nstages = (int)((rr.r_end - rr.r_begin + R - 1) / R);
+                const int rows = (int)(rr.r_end - rr.r_begin), I = g.I, RB = g.RB, CI = g.CI;
+                const uint8_t* src = g.tb + g.tcta[c];  // this CTA's tiles, in (row block, K-slice) order
                 unsigned long long pwait = 0;
                 bool stop = false;
-                for (int s = 0; s < nstages; ++s, ++use) {
-                    const int slot = use % ring;
-                    if (use >= (uint32_t)ring) {
-                        const long long w0 = A.trace ? clock64() : 0;
-                        bool ok = mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1);
-                        for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
-                            if (mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1)) { ok = true; break; }
-                        if (A.trace) pwait += (unsigned long long)(clock64() - w0);
-                        if (!ok) {
-                            if (!*abort_flag) set_device_error(SK_WAIT_ERR);
-                            *abort_flag = 1;
-                            stop = true;
-                            break;
+                for (int r0 = 0; r0 < rows && !stop; r0 += RB) {
+                    const int rows_b = min(RB, rows - r0);
+                    for (int j = 0; j * CI < I; ++j, ++use) {
+                        const int slot = use % ring;
+                        if (use >= (uint32_t)ring) {
+                            const long long w0 = A.trace ? clock64() : 0;
+                            bool ok = mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1);
+                            for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                                if (mbar_try_wait(&empty[slot], ((use / ring) - 1) & 1)) { ok = true; break; }
+                            if (A.trace) pwait += (unsigned long long)(clock64() - w0);
+                            if (!ok) {
+                                if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                                *abort_flag = 1;
+                                stop = true;
+                                break;
+                            }
                         }
+                        const uint32_t bytes = sk_tile_bytes(g.wt, rows_b, min(CI, I - j * CI), CI);
+                        mbar_arrive_expect_tx(&full[slot], bytes);
+                        bulk_g2s(smem + (size_t)slot * A.slot_bytes, src, bytes, &full[slot]);
+                        src += bytes;
                     }
-                    const long long row0 = rr.r_begin + (long long)s * R;
-                    const uint32_t nrows = (uint32_t)min((long long)R, rr.r_end - row0);
-                    uint8_t* dst = smem + (size_t)slot * A.slot_bytes;
-                    const uint32_t qbytes = nrows * (uint32_t)I * qb;
-                    const uint32_t sbytes = nrows * (uint32_t)sbr;
-                    const uint64_t d0 = (uint64_t)row0 * dbr;
-                    const uint64_t d0a = d0 & ~uint64_t(15);
-                    const uint32_t dbytes = ((uint32_t)(d0 - d0a) + nrows * (uint32_t)dbr + 15u) & ~15u;
-                    mbar_arrive_expect_tx(&full[slot], qbytes + sbytes + dbytes);
-                    bulk_g2s(dst, g.w.q + (uint64_t)row0 * I * qb, qbytes, &full[slot]);
-                    if (sbytes) bulk_g2s(dst + SS.s_off, g.w.s + (uint64_t)row0 * sbr, sbytes, &full[slot]);
-                    bulk_g2s(dst + SS.d_off, g.w.d + d0a, dbytes, &full[slot]);
                 }
                 if (A.trace) A.trace[((size_t)c * NPH + k) * SK_TRACE + 5] = pwait;
                 if (stop) break;
@@ -952,7 +967,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         mbar_arrive_expect_tx(&dbar[0], SK_DESC);
         bulk_g2s(desc, &A.ph[0], SK_DESC, &dbar[0]);
     }
-    int attn_pre = 0;  // K tiles of this CTA's first attention unit issued at the end of the phase before
+    int attn_pre = 0;  // tiles of this CTA's first attention unit issued at the end of the phase before
+    uint32_t apar = 0;  // attention tile buffers: parity of each one's next mbarrier completion
     for (int k = 0; k < NPH; ++k) {
         // the next phase's descriptor: one bulk copy into the buffer phase k - 1 used (every consumer
         // thread is past that phase's end barrier), landing while this phase runs
@@ -1031,7 +1047,10 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
-            use = sk_stages(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
+            if (g.wt == WT_Q6K)
+                use = sk_stages<WT_Q6K>(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
+            else
+                use = sk_stages<WT_Q80>(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
             named_bar_sync(1, NT);  // every piece of every row is in shared memory
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 2] = sk_ns();
             if (ph.epi == EPI_RESID) {
@@ -1052,9 +1071,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                     const int clen = sk_attn_clen(seq, nx.at.nchunk, G, nx.at.n_kv_heads, A.attn_solo);
                     const int nch = (seq + clen - 1) / clen;
                     if (nch <= nx.at.nchunk && nx.at.stride_t == SK_ATT_RSTR && c < nx.at.n_kv_heads * nch) {
-                        sk_attn_prefetch_k<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch, abar);
-                        const int t0 = (c % nch) * clen;
-                        attn_pre = (min(t0 + clen, seq) - t0 + ATTN_CMAX - 1) / ATTN_CMAX;
+                        attn_pre = sk_attn_issue_early<KVT>(nx.at, c / nch, c % nch, clen, pos, scratch, abar);
                     }
                 }
             }
@@ -1073,7 +1090,8 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             for (int u = c; u < units; u += G) {
                 // the first unit's tile 0 may have been issued at the end of the previous phase
                 if (tid < ATTN_THREADS)
-                    sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre > 0, abar, abort_flag);
+                    sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre > 0, abar, apar,
+                                      abort_flag);
                 attn_pre = 0;
                 named_bar_sync(1, NT);  // the next unit reuses the scratch
                 if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
@@ -1093,10 +1111,14 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
     }
 
     cp_async_wait_all();
-    if (attn_pre > 0 && tid == 0)  // K tiles prefetched for a unit that did not run (a step that gave up):
-        for (int i = 0; i < attn_pre; ++i)  // let the copies land (bounded) before the CTA exits
-            for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS; ++it)
-                if (mbar_try_wait(&abar[i], 0u)) break;
+    if (attn_pre > 0 && tid == 0) {  // tiles issued for a unit that did not run (a step that gave up):
+        uint32_t bufs = (1u << attn_pre) - 1u;  // let the copies land (bounded) before the CTA exits
+        if (attn_pre <= SK_ATT_TILES / 2) bufs |= bufs << (SK_ATT_TILES / 2);
+        for (int b = 0; b < SK_ATT_TILES; ++b)
+            if ((bufs >> b) & 1u)
+                for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS; ++it)
+                    if (mbar_try_wait(&abar[b], (apar >> b) & 1u)) break;
+    }
     // ---- argmax of the LM head: thread -> warp -> CTA -> (last CTA of the step) global
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
