@@ -1,8 +1,9 @@
-"""Tensor parallel on 2 GPUs (skipped with fewer): two ranks, one process each, decode the same
-tokens with the model split over them (heads / FFN rows / vocabulary rows per rank, o_proj and
-down partial rows exchanged over NVLink inside every step kernel), against the same model on one
-GPU. The two splits sum the row-parallel partials in a different order, so logits agree to the
-engine's tolerance, not bit for bit; the greedy id is the same on both ranks."""
+"""Tensor parallel on 2, 4 and 8 GPUs (each skipped with fewer): one process per rank decodes the
+same tokens with the model split over the ranks (heads / FFN rows / vocabulary rows per rank, o_proj
+and down partial rows exchanged over NVLink inside every step kernel). The gathered logits are
+compared with the same model on one GPU and with the CPU oracle's restatement of the reference
+forward (oracle/fence_oracle.c). The splits sum the row-parallel partials in a different order, so
+logits agree to the engine's tolerance, not bit for bit; the greedy id is the same on every rank."""
 import os
 import socket
 
@@ -23,7 +24,16 @@ SHAPES = {
     # super-block: its d is repeated in both ranks' rows
     "tp-q6k-cut": dict(config="tiny-q6k", n_layers=2, embed_dim=512, ff_dim=1280, n_heads=6, n_kv_heads=2,
                        vocab_size=2051),
+    # 8 ranks: 128 o_proj columns and 320 down columns per rank, so most ranks' slices start inside
+    # a Q6_K super-block; one KV head and one query head per rank
+    "tp8-q6k-cut": dict(config="tiny-q6k", n_layers=2, embed_dim=512, ff_dim=2560, n_heads=8, n_kv_heads=8,
+                        vocab_size=2051),
+    "tp8-q8": dict(config="tiny-q8", n_layers=2, embed_dim=1024, ff_dim=2048, n_heads=16, n_kv_heads=8,
+                   vocab_size=2051),
 }
+# (world size, shape): every shape whose heads and FFN rows split over the ranks
+CASES = [(2, s) for s in ("tp-q6k", "tp-q8", "tp-q6k-cut")] + [(4, "tp-q6k"), (4, "tp-q8"), (4, "tp8-q6k-cut"),
+                                                               (8, "tp8-q6k-cut"), (8, "tp8-q8")]
 STEPS = 40
 
 
@@ -64,20 +74,30 @@ def _rank(rank, world, port, path, out_dir, use_graph):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("shape", sorted(SHAPES))
+@pytest.mark.parametrize("world,shape", CASES)
 @pytest.mark.parametrize("use_graph", [True, False])
-def test_tp2_matches_single_gpu(fb, tmp_path, shape, use_graph):
+def test_tp_matches_single_gpu_and_oracle(fb, orc, tmp_path, world, shape, use_graph):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if world > 2 and not use_graph:
+        pytest.skip("eager launches are covered at 2 ranks")
     import torch.multiprocessing as mp
     kw = dict(SHAPES[shape])
     cfg = kw.pop("config")
     path = str(tmp_path / f"{shape}.gguf")
     fb.synth_write(path, cfg, seed=31, **kw)
-    mp.spawn(_rank, args=(2, _free_port(), path, str(tmp_path), use_graph), nprocs=2, join=True)
-    r = [np.load(tmp_path / f"r{k}.npz") for k in range(2)]
-    assert int(r[0]["v0"]) == 0 and int(r[1]["v0"]) == int(r[0]["vn"])
-    tp_logits = np.concatenate([r[0]["logits"], r[1]["logits"]], axis=1)
-    assert (r[0]["ids"] == r[1]["ids"]).all() and (r[0]["dec"] == r[1]["dec"]).all()
+    mp.spawn(_rank, args=(world, _free_port(), path, str(tmp_path), use_graph), nprocs=world, join=True)
+    r = [np.load(tmp_path / f"r{k}.npz") for k in range(world)]
+    assert int(r[0]["v0"]) == 0
+    for k in range(1, world):
+        assert int(r[k]["v0"]) == int(r[k - 1]["v0"]) + int(r[k - 1]["vn"])
+        assert (r[k]["ids"] == r[0]["ids"]).all() and (r[k]["dec"] == r[0]["dec"]).all()
+    tp_logits = np.concatenate([r[k]["logits"] for k in range(world)], axis=1)
+    # the CPU oracle (fp16 KV, the engine's default), teacher-forced on the same tokens
+    ora = orc.OracleModel(path, max_ctx=256, kv_bf16=False, threads=8)
+    ora_logits = np.stack([ora.forward(t, pos) for pos, t in enumerate(_tokens())])
+    ora.close()
+    np.testing.assert_allclose(tp_logits, ora_logits, rtol=0, atol=LOGIT_ATOL)
     m = fb.Model(path, max_ctx=256, device=0)
     ref, ref_ids = [], []
     for pos, t in enumerate(_tokens()):
