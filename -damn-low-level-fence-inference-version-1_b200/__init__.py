@@ -52,6 +52,7 @@ class LoadOpts(ctypes.Structure):
         ("max_ctx", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("device", ctypes.c_int),
         ("use_graph", ctypes.c_int), ("verbose", ctypes.c_int), ("tp_rank", ctypes.c_int),
         ("tp_size", ctypes.c_int), ("step_kernel", ctypes.c_int), ("wait_test_phase", ctypes.c_int),
+        ("moe_ep", ctypes.c_int),
     ]
 
 
@@ -182,6 +183,18 @@ CONFIGS = {
     "wide-q8": dict(arch=b"llama", n_layers=2, embed_dim=4096, ff_dim=1024, n_heads=32, n_kv_heads=8,
                     head_dim=128, vocab_size=2048, rope_freq_base=5e5, rms_eps=1e-5,
                     linear_type=GGML_Q8_0, qk_norm=0),
+    # config 4: Mixtral-8x7B shape, sparse MoE (8 experts, top-2), Q6_K linears, fp32 router
+    "mixtral-8x7b": dict(arch=b"llama", n_layers=32, embed_dim=4096, ff_dim=14336, n_heads=32, n_kv_heads=8,
+                         head_dim=128, vocab_size=32000, rope_freq_base=1e6, rms_eps=1e-5,
+                         linear_type=GGML_Q6_K, qk_norm=0, n_experts=8, n_experts_used=2),
+    # small sparse-MoE shapes for parity runs (FFN rows split 2/4/8 ways in whole 64-input items;
+    # tiny-moe-q8's 8 experts split 2/4/8 ways for expert parallelism)
+    "tiny-moe": dict(arch=b"llama", n_layers=2, embed_dim=512, ff_dim=1024, n_heads=8, n_kv_heads=8,
+                     head_dim=128, vocab_size=2048, rope_freq_base=1e6, rms_eps=1e-5,
+                     linear_type=GGML_Q6_K, qk_norm=0, n_experts=4, n_experts_used=2),
+    "tiny-moe-q8": dict(arch=b"llama", n_layers=2, embed_dim=512, ff_dim=512, n_heads=8, n_kv_heads=8,
+                        head_dim=128, vocab_size=2048, rope_freq_base=1e6, rms_eps=1e-5,
+                        linear_type=GGML_Q8_0, qk_norm=0, n_experts=8, n_experts_used=2),
 }
 
 
@@ -216,7 +229,7 @@ class Model:
 
     def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
                  use_graph: bool = True, verbose: bool = False, step_kernel: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1, wait_test_phase: int = -1):
+                 tp_rank: int = 0, tp_size: int = 1, wait_test_phase: int = -1, moe_ep: bool = False):
         L = lib()
         o = LoadOpts()
         L.fence_load_opts_default(ctypes.byref(o))
@@ -224,6 +237,7 @@ class Model:
         o.step_kernel = int(step_kernel)
         o.tp_rank, o.tp_size = tp_rank, tp_size
         o.wait_test_phase = wait_test_phase  # test only: a step-kernel phase whose counter wait runs out
+        o.moe_ep = int(moe_ep)  # sparse MoE over tp_size ranks: whole experts per rank instead of slices
         h = L.fence_model_load(path.encode(), ctypes.byref(o))
         if not h:
             raise FenceError(f"model load failed: {last_error()}")

@@ -50,6 +50,8 @@ struct LayerW {
     int t_qkv = 14, t_o = 14, t_gu = 14, t_down = 14;  // GGML type ids
     const float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
     const float *q_bias = nullptr, *k_bias = nullptr, *v_bias = nullptr;
+    const float* router = nullptr;  // sparse MoE: ffn_gate_inp [n_exp][H] fp32; gate/up/down are then the
+                                    // [K, M, n_exp] expert tensors (expert e's rows contiguous)
 };
 
 // One GEMV phase of the token step over repacked weights.
@@ -117,6 +119,11 @@ struct fence_model {
     uint8_t* xpeer[SK_TP_MAX] = {};  // every rank's exchange buffer as mapped here (own = xbuf)
     unsigned long long* tp_launch = nullptr;
     int tp_connected = 0;
+    // sparse MoE FFN: local experts [e_lo, e_lo + e_n) (all of them unless expert parallel), each
+    // with its repacked gate/up and down matrices ([layer][local expert])
+    int moe = 0, moe_ep = 0, e_lo = 0, e_n = 0;
+    std::vector<RMat> moe_gu, moe_dn;
+    float* moe_acc = nullptr;       // tensor parallel: the expert slots' partial rows before the last slot
     // device nucleus sampler (allocated on its first use)
     void* samp_scratch = nullptr;
     size_t samp_bytes = 0;
@@ -273,6 +280,20 @@ bool check_linear(const GGUFTensorInfo* t, uint64_t K, uint64_t M, std::string& 
     }
     return true;
 }
+// A sparse-MoE expert tensor: n_exp matrices [K, M] stacked as dims [K, M, n_exp].
+bool check_experts(const GGUFTensorInfo* t, uint64_t K, uint64_t M, uint64_t E, std::string& err) {
+    if (!t) return false;
+    if (t->type != GGMLType::Q6_K && t->type != GGMLType::Q8_0) {
+        err = "tensor " + t->name + " has type " + ggml_type_name(t->type) + " (engine streams Q6_K and Q8_0)";
+        return false;
+    }
+    if (t->n_dims != 3 || t->dims[0] != K || t->dims[1] != M || t->dims[2] != E) {
+        err = "tensor " + t->name + " must have dims [" + std::to_string(K) + ", " + std::to_string(M) + ", " +
+              std::to_string(E) + "]";
+        return false;
+    }
+    return true;
+}
 bool check_vec(const GGUFTensorInfo* t, uint64_t n, std::string& err) {
     if (!t) return true;  // optional vectors are checked by the caller
     if (t->type != GGMLType::F32 || t->n_elements() != n) {
@@ -328,10 +349,48 @@ int build_step_phases(fence_model* m) {
         SPhase o = gemv(L.o), gu = gemv(L.gu), dn = gemv(L.down);
         tp_red(o, 2 * l);
         tp_sum(gu, 2 * l);
-        tp_red(dn, 2 * l + 1);
         ph.push_back(o);
-        ph.push_back(gu);
-        ph.push_back(dn);
+        if (!m->moe) {
+            tp_red(dn, 2 * l + 1);
+            ph.push_back(gu);
+            ph.push_back(dn);
+            continue;
+        }
+        // sparse MoE: gate/up of every routed slot (slot 0 routes; later slots reuse its x records and
+        // need no grid wait), then down of every slot (slot 0 waits for every CTA's gate/up; later
+        // slots write the same rows of the same CTA and need none)
+        const int K = c.n_experts_used;
+        const size_t act_el = L.gu.a.act_f16 ? 2 : 4;
+        auto moe = [&](SPhase& p, int kind, int slot) {
+            p.moe = kind;
+            p.moe_slot = slot;
+            p.moe_seq = l + 1;
+            p.n_exp = c.n_experts;
+            p.n_used = K;
+            p.e_lo = m->e_lo;
+            p.e_n = m->e_n;
+            p.route_w = m->layers[l].router;
+            p.moe_acc = m->moe_acc;
+            p.moe_chain = slot > 0;
+        };
+        for (int s = 0; s < K; ++s) {
+            SPhase p = gu;
+            moe(p, SK_MOE_GU, s);
+            if (s > 0) {
+                p.moe_reuse_x = 1;
+                p.tp_sum = 0;
+            }
+            p.g.act = static_cast<uint8_t*>(m->act) + (size_t)s * L.gu.a.Mv * act_el;
+            ph.push_back(p);
+        }
+        for (int s = 0; s < K; ++s) {
+            SPhase p = dn;
+            moe(p, SK_MOE_DN, s);
+            p.g.x = static_cast<uint8_t*>(m->act) + (size_t)s * L.gu.a.Mv * act_el;
+            p.moe_last = s == K - 1;
+            if (p.moe_last) tp_red(p, 2 * l + 1);
+            ph.push_back(p);
+        }
     }
     SPhase lm = gemv(m->lm);
     tp_sum(lm, 2 * c.n_layers - 1);
@@ -350,11 +409,17 @@ int build_step_phases(fence_model* m) {
         std::vector<unsigned long long> base(ngemv);
         unsigned long long total = 0;
         size_t gi = 0;
-        for (const SPhase& p : ph) {
+        for (SPhase& p : ph) {
             if (p.kind != SP_GEMV) continue;
             const RGemvArgs& g = p.g;
             base[gi] = total;
-            total += (sk_tile_plan(g.wt, g.I, g.Mv, g.dual, G, g.RB, g.CI, &tc[gi * G]) + 255) / 256 * 256;
+            const unsigned long long tb = (sk_tile_plan(g.wt, g.I, g.Mv, g.dual, G, g.RB, g.CI, &tc[gi * G]) + 255) / 256 * 256;
+            if (!p.moe) {
+                total += tb;
+            } else if (p.moe_slot == 0) {  // one tile set per local expert; later slots share them
+                p.estride = (long long)tb;
+                total += tb * (unsigned long long)m->e_n;
+            }
             ++gi;
         }
         FENCE_CUDA_TRY(cudaMalloc(&m->tarena, total + 256));
@@ -362,13 +427,28 @@ int build_step_phases(fence_model* m) {
         FENCE_CUDA_TRY(cudaMalloc(&m->d_tcta, tc.size() * sizeof(unsigned long long)));
         FENCE_CUDA_TRY(cudaMemcpy(m->d_tcta, tc.data(), tc.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
         gi = 0;
-        for (SPhase& p : ph) {
+        for (size_t i = 0; i < ph.size(); ++i) {
+            SPhase& p = ph[i];
             if (p.kind != SP_GEMV) continue;
             RGemvArgs& g = p.g;
             g.tb = m->tarena + base[gi];
             g.tcta = m->d_tcta + gi * G;
-            FENCE_CUDA_TRY(sk_retile(g.wt, g.w, g.I, g.Mv, g.dual, G, g.RB, g.CI, g.tcta, const_cast<uint8_t*>(g.tb),
-                                     m->stream));
+            if (!p.moe) {
+                FENCE_CUDA_TRY(sk_retile(g.wt, g.w, g.I, g.Mv, g.dual, G, g.RB, g.CI, g.tcta, const_cast<uint8_t*>(g.tb),
+                                         m->stream));
+            } else if (p.moe_slot == 0) {
+                const std::vector<RMat>& mats = p.moe == SK_MOE_GU ? m->moe_gu : m->moe_dn;
+                for (int e = 0; e < m->e_n; ++e)
+                    FENCE_CUDA_TRY(sk_retile(g.wt, mats[(size_t)(p.moe_seq - 1) * m->e_n + e], g.I, g.Mv, g.dual, G,
+                                             g.RB, g.CI, g.tcta, const_cast<uint8_t*>(g.tb) + (size_t)e * p.estride,
+                                             m->stream));
+            } else {  // the tiles of this layer's slot-0 phase of the same kind (same shape, same CTA split)
+                for (size_t j = 0; j < i; ++j)
+                    if (ph[j].moe == p.moe && ph[j].moe_seq == p.moe_seq && ph[j].moe_slot == 0) {
+                        g.tb = ph[j].g.tb;
+                        p.estride = ph[j].estride;
+                    }
+            }
             ++gi;
         }
         FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
@@ -447,6 +527,7 @@ void free_model(fence_model* m) {
     cudaFree(m->xbuf);
     cudaFree(m->hidden_b);
     cudaFree(m->tp_launch);
+    cudaFree(m->moe_acc);
     cudaFree(m->samp_scratch);
     cudaFree(m->samp_hist);
     cudaFree(m->samp_out);
@@ -472,6 +553,7 @@ extern "C" void fence_load_opts_default(fence_load_opts* o) {
     o->tp_size = 1;
     o->step_kernel = 1;
     o->wait_test_phase = -1;
+    o->moe_ep = 0;
 }
 
 extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts* opts_in) {
@@ -563,8 +645,16 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         return bail(FENCE_E_UNSUPPORTED, "model_load: head_dim " + std::to_string(c.head_dim) + " (engine kernels are built for 128)");
     if (c.n_heads / c.n_kv_heads > ATTN_MAX_G)
         return bail(FENCE_E_UNSUPPORTED, "model_load: more than 8 query heads per KV head");
-    if (c.n_experts > 0)
-        return bail(FENCE_E_UNSUPPORTED, "model_load: mixture-of-experts FFN is not built in this library");
+    const bool moe = c.n_experts > 0;
+    if (moe) {
+        if (c.n_experts > SK_MOE_EMAX || c.n_experts_used < 1 || c.n_experts_used > 2 || c.n_experts_used > c.n_experts)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: sparse MoE needs at most " + std::to_string(SK_MOE_EMAX) +
+                                                 " experts and 1 or 2 routed per token");
+        if (!opts.step_kernel)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: sparse MoE runs in the step kernel (step_kernel = 1)");
+        if (opts.moe_ep && opts.tp_size > 1 && c.n_experts % opts.tp_size)
+            return bail(FENCE_E_UNSUPPORTED, "model_load: expert parallel needs the experts to split evenly over the ranks");
+    }
     if (embd->type != GGMLType::Q8_0 || embd->dims[0] != (uint64_t)c.embed_dim)
         return bail(FENCE_E_UNSUPPORTED, "model_load: token_embd.weight must be Q8_0 [embed_dim, vocab]");
     if (c.embed_dim % 64)
@@ -576,9 +666,17 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     // FFN rows (column-parallel, no exchange), o_proj and down by input columns (row-parallel: each
     // rank's partial rows are summed over the ranks), the tied LM head by vocabulary rows
     const int TPN = c.tp_size, TPR = c.tp_rank;
-    if (TPN > 1 && (c.n_heads % TPN || c.n_kv_heads % TPN || c.ff_dim % TPN))
+    // expert parallel (MoE, tp_size > 1, opts.moe_ep): each rank holds n_experts / tp_size whole
+    // experts; otherwise every rank holds a 1/tp_size slice of every expert (as a dense FFN)
+    const bool ep = moe && opts.moe_ep && TPN > 1;
+    if (TPN > 1 && (c.n_heads % TPN || c.n_kv_heads % TPN || (!ep && c.ff_dim % TPN)))
         return bail(FENCE_E_UNSUPPORTED, "model_load: heads / FFN rows do not split evenly over tp_size ranks");
-    const uint64_t qdl = qd / TPN, kvdl = kvd / TPN, Fl = F / TPN;
+    const uint64_t qdl = qd / TPN, kvdl = kvd / TPN, Fl = ep ? F : F / TPN;
+    const int FTPR = ep ? 0 : TPR;  // this rank's FFN row slice (expert parallel: whole experts)
+    m->moe = moe ? 1 : 0;
+    m->moe_ep = ep ? 1 : 0;
+    m->e_lo = ep ? TPR * (c.n_experts / TPN) : 0;
+    m->e_n = moe ? (ep ? c.n_experts / TPN : c.n_experts) : 0;
     const int Hq_l = c.n_heads / TPN, Hkv_l = c.n_kv_heads / TPN;
     const int Vl = (c.vocab_size + TPN - 1) / TPN, v0 = TPR * Vl, vn = std::min(c.vocab_size, v0 + Vl) - v0;
     m->tp_n = TPN;
@@ -606,7 +704,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     const size_t off_embd = place(embd);
     const size_t off_onorm = place(onorm);
     struct LOff {
-        size_t q, k, v, o, g, u, d, an, fn, qn, kn, qb, kb, vb;
+        size_t q, k, v, o, g, u, d, an, fn, qn, kn, qb, kb, vb, rt;
         bool has_qn, has_kn, has_qb, has_kb, has_vb;
     };
     std::vector<LOff> lo(c.n_layers);
@@ -618,16 +716,26 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         const GGUFTensorInfo *an = need(m, p + "attn_norm.weight", err), *q = need(m, p + "attn_q.weight", err),
                              *k = need(m, p + "attn_k.weight", err), *v = need(m, p + "attn_v.weight", err),
                              *o = need(m, p + "attn_output.weight", err), *fn = need(m, p + "ffn_norm.weight", err),
-                             *g = need(m, p + "ffn_gate.weight", err), *u = need(m, p + "ffn_up.weight", err),
-                             *d = need(m, p + "ffn_down.weight", err);
+                             *g = need(m, p + (moe ? "ffn_gate_exps.weight" : "ffn_gate.weight"), err),
+                             *u = need(m, p + (moe ? "ffn_up_exps.weight" : "ffn_up.weight"), err),
+                             *d = need(m, p + (moe ? "ffn_down_exps.weight" : "ffn_down.weight"), err),
+                             *rt = moe ? need(m, p + "ffn_gate_inp.weight", err) : nullptr;
         if (!err.empty()) return bail(FENCE_E_FORMAT, "model_load: " + err);
         const GGUFTensorInfo *qn = m->gguf.find_tensor(p + "attn_q_norm.weight"),
                              *kn = m->gguf.find_tensor(p + "attn_k_norm.weight"),
                              *qb = m->gguf.find_tensor(p + "attn_q.bias"), *kb = m->gguf.find_tensor(p + "attn_k.bias"),
                              *vb = m->gguf.find_tensor(p + "attn_v.bias");
+        const uint64_t E = (uint64_t)c.n_experts;
+        auto lin = [&](const GGUFTensorInfo* t, uint64_t K, uint64_t M) {
+            return moe ? check_experts(t, K, M, E, err) : check_linear(t, K, M, err);
+        };
+        if (moe && (rt->type != GGMLType::F32 || rt->n_dims != 2 || rt->dims[0] != H || rt->dims[1] != E)) {
+            err = "tensor " + rt->name + " must be F32 [" + std::to_string(H) + ", " + std::to_string(E) + "]";
+            return bail(FENCE_E_FORMAT, "model_load: " + err);
+        }
         if (!check_linear(q, H, qd, err) || !check_linear(k, H, kvd, err) || !check_linear(v, H, kvd, err) ||
-            !check_linear(o, qd, H, err) || !check_linear(g, H, F, err) || !check_linear(u, H, F, err) ||
-            !check_linear(d, F, H, err) || !check_vec(an, H, err) || !check_vec(fn, H, err) ||
+            !check_linear(o, qd, H, err) || !lin(g, H, F) || !lin(u, H, F) ||
+            !lin(d, F, H) || !check_vec(an, H, err) || !check_vec(fn, H, err) ||
             !check_vec(qn, c.head_dim, err) || !check_vec(kn, c.head_dim, err) || !check_vec(qb, qd, err) ||
             !check_vec(kb, kvd, err) || !check_vec(vb, kvd, err))
             return bail(FENCE_E_FORMAT, "model_load: " + err);
@@ -661,8 +769,11 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         if (qb) L.qb = place(qb);
         if (kb) L.kb = place(kb);
         if (vb) L.vb = place(vb);
+        if (rt) L.rt = place(rt);
+        // MoE: the routed experts' share of the expert tensors and the router are streamed per token
+        const uint64_t ffn = g->data_size_bytes + u->data_size_bytes + d->data_size_bytes;
         bytes_per_token += q->data_size_bytes + k->data_size_bytes + v->data_size_bytes + o->data_size_bytes +
-                           g->data_size_bytes + u->data_size_bytes + d->data_size_bytes;
+                           (moe ? ffn / E * (uint64_t)c.n_experts_used + rt->data_size_bytes : ffn);
     }
     c.has_qk_norm = lo[0].has_qn ? 1 : 0;
     c.weight_bytes = bytes_per_token;
@@ -707,6 +818,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         if (L.has_qb) w.q_bias = PF(L.qb);
         if (L.has_kb) w.k_bias = PF(L.kb);
         if (L.has_vb) w.v_bias = PF(L.vb);
+        if (moe) w.router = PF(L.rt);
     }
 
     const int HD = c.head_dim, G = c.n_heads / c.n_kv_heads;
@@ -725,7 +837,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
               cudaMalloc(&m->hidden, H * 4) == cudaSuccess && cudaMalloc(&m->qkv, (qdl + 2 * kvdl) * 4) == cudaSuccess &&
               cudaMalloc(&m->attn_out, qdl * 4) == cudaSuccess && cudaMalloc(&m->logits, (size_t)vn * 4) == cudaSuccess &&
               cudaMalloc(&m->attn_part, (size_t)Hkv_l * part_chunks * G * SK_PART_STRIDE * 4) == cudaSuccess &&
-              cudaMalloc(&m->act, Fl * 4) == cudaSuccess &&
+              cudaMalloc(&m->act, Fl * 4 * (moe ? 2 : 1)) == cudaSuccess &&
               cudaMalloc(&m->counters, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&
               cudaMemset(m->counters, 0, (Hkv_l + 1) * sizeof(unsigned)) == cudaSuccess &&
               cudaMalloc(&m->lm_val, 4096 * 4) == cudaSuccess && cudaMalloc(&m->lm_idx, 4096 * 4) == cudaSuccess &&
@@ -736,6 +848,8 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
               cudaMallocHost(&m->h_token, 64 * sizeof(int)) == cudaSuccess &&
               cudaMallocHost(&m->h_out, sizeof(DecodeState)) == cudaSuccess;
     if (!ok) return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
+    if (moe && TPN > 1 && cudaMalloc(&m->moe_acc, H * 4) != cudaSuccess)
+        return bail(FENCE_E_NOMEM, "model_load: device allocation failed");
     if (TPN > 1) {
         const size_t xb = sk_xb_bytes(TPN, (int)H);
         if (cudaMalloc(&m->hidden_b, H * 4) != cudaSuccess || cudaMalloc(&m->xbuf, xb) != cudaSuccess ||
@@ -767,15 +881,22 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     size_t rbytes = rmat_bytes(WT_Q80, vn, (int)H);
     size_t shard_bytes = (size_t)vn * (H / 32) * 34;  // LM-head shard (+ the layers' shards below)
     auto raw_row = [](int t, uint64_t K) { return t == 14 ? (K * 210 + 255) / 256 : K / 32 * 34; };
+    // FFN matrices per layer: one (dense), one per local expert (MoE); streamed per token: one, or the
+    // routed experts' (tensor parallel: every rank streams its slice of each; expert parallel: on
+    // average n_used / tp_size whole experts per rank)
+    const int n_ffn = moe ? m->e_n : 1;
+    const double ffn_streamed = moe ? (ep ? (double)c.n_experts_used / TPN : (double)c.n_experts_used) : 1.0;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         rbytes += rmat_bytes(wt_of(w.t_qkv), QKVR, (int)H) +
                   rmat_bytes(wt_of(w.t_o), (long long)H, (int)qdl, (int)((TPR * qdl / 64) & 3)) +
-                  rmat_bytes(wt_of(w.t_gu), 2 * (long long)Fl, (int)H) +
-                  rmat_bytes(wt_of(w.t_down), (long long)H, (int)Fl, (int)((TPR * Fl / 64) & 3));
-        shard_bytes += QKVR * raw_row(w.t_qkv, H) + H * raw_row(w.t_o, qdl) + 2 * Fl * raw_row(w.t_gu, H) +
-                       H * raw_row(w.t_down, Fl);
+                  (size_t)n_ffn * (rmat_bytes(wt_of(w.t_gu), 2 * (long long)Fl, (int)H) +
+                                   rmat_bytes(wt_of(w.t_down), (long long)H, (int)Fl, (int)((FTPR * Fl / 64) & 3)));
+        shard_bytes += QKVR * raw_row(w.t_qkv, H) + H * raw_row(w.t_o, qdl) +
+                       (size_t)(ffn_streamed * (double)(2 * Fl * raw_row(w.t_gu, H) + H * raw_row(w.t_down, Fl))) +
+                       (moe ? (size_t)c.n_experts * H * 4 : 0);
     }
+    if (moe) m->moe_gu.resize((size_t)c.n_layers * m->e_n), m->moe_dn.resize((size_t)c.n_layers * m->e_n);
     // Q8_0 rows only need 64-element items; Q6_K super-blocks need 256 (a rank's column slice too)
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
@@ -832,20 +953,29 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
         const int wq = wt_of(w.t_qkv), wo = wt_of(w.t_o), wg = wt_of(w.t_gu), wd = wt_of(w.t_down);
-        const int o_item0 = (int)(TPR * qdl / 64), d_item0 = (int)(TPR * Fl / 64);
-        const RMat rq = carve(wq, QKVR, (int)H, 0), ro = carve(wo, (long long)H, (int)qdl, o_item0 & 3),
-                   rg = carve(wg, 2 * (long long)Fl, (int)H, 0), rd = carve(wd, (long long)H, (int)Fl, d_item0 & 3);
+        const int o_item0 = (int)(TPR * qdl / 64), d_item0 = (int)(FTPR * Fl / 64);
+        const RMat rq = carve(wq, QKVR, (int)H, 0), ro = carve(wo, (long long)H, (int)qdl, o_item0 & 3);
         // this rank's rows (q/k/v heads, FFN rows) and input columns (o_proj, down)
-        const uint64_t rq_b = raw_row(w.t_qkv, H), rg_b = raw_row(w.t_gu, H);
+        const uint64_t rq_b = raw_row(w.t_qkv, H), rg_b = raw_row(w.t_gu, H), rd_b = raw_row(w.t_down, F);
 
         if (!fill(wq, w.q + TPR * qdl * rq_b, (long long)qdl, (int)H, rq, 0, 1) ||
             !fill(wq, w.k + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)qdl, 1) ||
             !fill(wq, w.v + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)(qdl + kvdl), 1) ||
-            rmat_fill(wo, w.o, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd, o_item0) != cudaSuccess ||
-            !fill(wg, w.gate + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 0, 2) ||
-            !fill(wg, w.up + TPR * Fl * rg_b, (long long)Fl, (int)H, rg, 1, 2) ||
-            rmat_fill(wd, w.down, (long long)H, (int)Fl, rd, 0, 1, st, (int)F, d_item0) != cudaSuccess)
+            rmat_fill(wo, w.o, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd, o_item0) != cudaSuccess)
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
+        // FFN: the dense matrices, or every local expert's (expert e's rows start at e * F (gate/up)
+        // and e * H (down) in the stacked tensors)
+        RMat rg{}, rd{};
+        for (int e = 0; e < n_ffn; ++e) {
+            const uint64_t ge = moe ? (uint64_t)(m->e_lo + e) : 0;
+            const RMat eg = carve(wg, 2 * (long long)Fl, (int)H, 0), ed = carve(wd, (long long)H, (int)Fl, d_item0 & 3);
+            if (!fill(wg, w.gate + (ge * F + FTPR * Fl) * rg_b, (long long)Fl, (int)H, eg, 0, 2) ||
+                !fill(wg, w.up + (ge * F + FTPR * Fl) * rg_b, (long long)Fl, (int)H, eg, 1, 2) ||
+                rmat_fill(wd, w.down + ge * H * rd_b, (long long)H, (int)Fl, ed, 0, 1, st, (int)F, d_item0) != cudaSuccess)
+                return bail(FENCE_E_NOMEM, "model_load: repacking failed");
+            if (e == 0) rg = eg, rd = ed;
+            if (moe) m->moe_gu[(size_t)l * m->e_n + e] = eg, m->moe_dn[(size_t)l * m->e_n + e] = ed;
+        }
         float* bias = nullptr;
         if (any_bias) {
             bias = m->qkv_bias + (size_t)l * QKVR;

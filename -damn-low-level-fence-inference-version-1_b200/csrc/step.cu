@@ -57,6 +57,7 @@ static StepPlan plan_step(std::vector<SPhase>& phases, int dev, std::string& err
         int need = ph.g.I * (int)SK_XQB;
         if (ph.embed || ph.tp_sum) need += ph.g.I * 64 * 4;  // fp32 x row (embedding / reduced) after the records
         scratch = std::max(scratch, need);
+        if (ph.moe) accf = std::max(accf, SK_NW * SK_MOE_EMAX);  // the router's reduction (sk_route)
     }
     P.scratch_bytes = (scratch + 15) / 16 * 16;
     P.acc_floats = accf;

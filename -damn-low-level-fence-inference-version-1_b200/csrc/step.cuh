@@ -81,7 +81,26 @@ struct __align__(16) SPhase {
     int red_idx;      // the step's reduction this phase produces (tp_red) or consumes (tp_sum)
     const float* hin;
     float* hout;
+    // sparse MoE FFN (no counterpart in the reference): a layer's FFN is one gate/up phase and one
+    // down phase per routed expert slot (slot 0 = the router's first choice). The gate/up phase of
+    // slot 0 computes the routing in its x prologue (every CTA, identically) from the normed x;
+    // the producer streams the tiles of the chosen expert (tb + local expert * estride).
+    int moe;          // 0 dense; SK_MOE_GU gate/up of an expert slot; SK_MOE_DN down of an expert slot
+    int moe_slot;
+    int moe_seq;      // the step's routing number this phase uses (1-based: layer + 1)
+    int moe_chain;    // no grid-counter wait: the phase reads nothing another CTA wrote since the last wait
+    int moe_reuse_x;  // the x records of the previous phase are this phase's (gate/up of a later slot)
+    int moe_last;     // down: the last slot (adds the residual / sends the partial row)
+    int n_exp, n_used;
+    int e_lo, e_n;    // local experts: global ids [e_lo, e_lo + e_n) (expert parallel: a rank's share)
+    long long estride;       // bytes between consecutive local experts' tile sets
+    const float* route_w;    // router [n_exp][H] fp32 (slot-0 gate/up phase)
+    float* moe_acc;          // tensor parallel: the slots' partial rows summed before the last slot sends
+    int pad_moe_[2];
 };
+enum : int { SK_MOE_GU = 1, SK_MOE_DN = 2 };
+constexpr int SK_MOE_EMAX = 16;   // experts a router may have
+constexpr int SK_MISC_ROUTE = 112; // misc floats: chosen experts [2] (int), weights [2], routing number
 
 struct StepArgs {
     const SPhase* ph;
@@ -265,6 +284,75 @@ __device__ __noinline__ void sk_quantise_xm(int xm, const void* xsrc, const floa
         case X_NORM: sk_quantise<WT, X_NORM>(xsrc, norm_w, eps, I, xq_sa, misc); break;
         default: sk_quantise<WT, X_NORM_R16>(xsrc, norm_w, eps, I, xq_sa, misc); break;
     }
+}
+
+// Routing of a sparse-MoE layer (consumers, every CTA the same way): r_e = W_r[e] . RMSNorm(x)
+// (fp32 router weights, per-thread partial sums in a fixed order, fixed reduction tree: the same
+// bits in every CTA), the n_used largest r_e (ties to the smaller expert id), weights = softmax
+// over the chosen logits (= the full softmax renormalised over them). Chosen ids and weights go to
+// misc[SK_MISC_ROUTE..+3], then the routing number `seq` to misc[SK_MISC_ROUTE + 4] for the
+// producer warp. red: SK_NW * SK_MOE_EMAX floats of free shared memory.
+__device__ __noinline__ void sk_route(const float* x, const float* nw, float eps, const float* Wr, int E, int K,
+                                      int H, float* red, float* misc, int seq) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float ss = 0.f;
+    for (int k = tid; k < H; k += SK_NL) {
+        const float v = x[k];
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    named_bar_sync(1, SK_NL);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < SK_NW; ++w) tot += red[w];
+    const float rms = rsqrtf(tot / (float)H + eps);
+    named_bar_sync(1, SK_NL);  // red is reused below
+    float p[SK_MOE_EMAX];
+#pragma unroll
+    for (int e = 0; e < SK_MOE_EMAX; ++e) p[e] = 0.f;
+    for (int k = tid; k < H; k += SK_NL) {
+        const float xn = x[k] * rms * nw[k];
+#pragma unroll
+        for (int e = 0; e < SK_MOE_EMAX; ++e)
+            if (e < E) p[e] += __ldg(Wr + (size_t)e * H + k) * xn;
+    }
+#pragma unroll
+    for (int e = 0; e < SK_MOE_EMAX; ++e) {
+        if (e < E) {
+            const float v = warp_sum(p[e]);
+            if (lane == 0) red[warp * SK_MOE_EMAX + e] = v;
+        }
+    }
+    named_bar_sync(1, SK_NL);
+    if (tid == 0) {
+        float r[SK_MOE_EMAX];
+        for (int e = 0; e < E; ++e) {
+            float t = 0.f;
+            for (int w = 0; w < SK_NW; ++w) t += red[w * SK_MOE_EMAX + e];
+            r[e] = t;
+        }
+        int s0 = 0, s1 = -1;
+        for (int e = 1; e < E; ++e)
+            if (r[e] > r[s0]) s0 = e;
+        if (K > 1)
+            for (int e = 0; e < E; ++e)
+                if (e != s0 && (s1 < 0 || r[e] > r[s1])) s1 = e;
+        float w0 = 1.f, w1 = 0.f;
+        if (K > 1) {
+            const float a = expf(r[s1] - r[s0]);
+            w0 = 1.f / (1.f + a);
+            w1 = a / (1.f + a);
+        }
+        int* rs = reinterpret_cast<int*>(misc + SK_MISC_ROUTE);
+        rs[0] = s0;
+        rs[1] = s1;
+        misc[SK_MISC_ROUTE + 2] = w0;
+        misc[SK_MISC_ROUTE + 3] = w1;
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(misc + SK_MISC_ROUTE + 4) = seq;
+    }
+    named_bar_sync(1, SK_NL);
 }
 
 // Bounded wait for a filled ring slot (the consumer side). Fast path: one try (the abort flag, a
@@ -814,7 +902,7 @@ __device__ __forceinline__ bool sk_tp_gather(const float* hin, float* hout, cons
 template <bool TP>
 __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const SKRows& rr, const float* acc,
                                              const float* rpre, float& best_v, int& best_i, const StepArgs& A,
-                                             const SPhase& ph, unsigned tag) {
+                                             const SPhase& ph, unsigned tag, bool moe_owned, float moe_w) {
     const int LP = g.CI, R = g.RB, MP = g.mp;
     auto row_sum = [&](int rl) {
         const int n = rg_part_pieces(rl % R, 0, 1, LP);
@@ -823,6 +911,29 @@ __device__ __forceinline__ void sk_epilogues(const RGemvArgs& g, int epi, const 
         return t;
     };
     const int nvr = rr.v_end - rr.v_begin;
+    if (ph.moe == SK_MOE_DN) {
+        // routed expert slot: its rows scaled by the slot's routing weight (0 when this rank holds
+        // none of the expert: expert parallel); one GPU: added to the residual stream slot by slot;
+        // tensor parallel: summed over the slots here, the last slot sends the partial rows
+        const float scale = moe_owned ? moe_w : 0.f;
+        for (int vr = threadIdx.x; vr < nvr; vr += SK_NL) {
+            const int row = rr.v_begin + vr;
+            const float v = moe_owned ? row_sum(vr) * scale : 0.f;
+            if (!TP) {
+                g.resid[row] = v + (vr < SK_RPRE ? rpre[vr] : g.resid[row]);
+            } else {
+                const float t = ph.moe_slot > 0 ? v + ph.moe_acc[row] : v;
+                if (!ph.moe_last) {
+                    ph.moe_acc[row] = t;
+                } else {
+                    const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(t);
+                    for (int p = 0; p < A.tp_n; ++p)
+                        sk_st_sys64(sk_xpart(A, p, ph.red_idx & 1) + (size_t)A.tp_rank * A.tp_h + row, w);
+                }
+            }
+        }
+        return;
+    }
     for (int vr = threadIdx.x; vr < nvr; vr += SK_NL) {
         const int row = rr.v_begin + vr;
         if (epi == EPI_SWIGLU) {
@@ -883,6 +994,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         mbar_init(&dbar[1], 1);
         for (int i = 0; i < SK_ATT_TILES; ++i) mbar_init(&abar[i], 1);
         *abort_flag = 0;
+        *reinterpret_cast<volatile int*>(misc + SK_MISC_ROUTE + 4) = 0;  // no routing yet in this step
         fence_barrier_init();
     }
     __syncthreads();
@@ -918,6 +1030,24 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 const SKRows rr = sk_rows(g, c, G);
                 const int rows = (int)(rr.r_end - rr.r_begin), I = g.I, RB = g.RB, CI = g.CI;
                 const uint8_t* src = g.tb + g.tcta[c];  // this CTA's tiles, in (row block, K-slice) order
+                if (ph.moe) {
+                    // the routed expert of this slot: wait (bounded) for this CTA's routing of the layer
+                    volatile int* rseq = reinterpret_cast<volatile int*>(misc + SK_MISC_ROUTE + 4);
+                    bool ok = *rseq >= ph.moe_seq;
+                    for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it) {
+                        __nanosleep(32);
+                        ok = *rseq >= ph.moe_seq;
+                    }
+                    if (!ok) {
+                        if (!*abort_flag) set_device_error(SK_WAIT_ERR);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    __threadfence_block();
+                    const int e = reinterpret_cast<volatile int*>(misc + SK_MISC_ROUTE)[ph.moe_slot] - ph.e_lo;
+                    if (e < 0 || e >= ph.e_n) continue;  // expert parallel: another rank's expert
+                    src += (size_t)e * (size_t)ph.estride;
+                }
                 unsigned long long pwait = 0;
                 bool stop = false;
                 for (int r0 = 0; r0 < rows && !stop; r0 += RB) {
@@ -979,7 +1109,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         }
         if (!mbar_wait(&dbar[k & 1], (uint32_t)(k >> 1) & 1u)) *abort_flag = 1;
         const SPhase& ph = *reinterpret_cast<const SPhase*>(desc + (k & 1) * SK_DESC);
-        if (k > 0) {  // wait until every CTA has finished phase k-1
+        if (k > 0 && !ph.moe_chain) {  // wait until every CTA has finished phase k-1
             if (tid == 0) {
                 // acquire: the other CTAs' phase k-1 writes (released by their counts) become
                 // visible to this thread and, through the CTA barrier below, to the whole CTA
@@ -1044,10 +1174,24 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 named_bar_sync(1, NT);
                 xsrc = hbuf;
             }
-            if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
-            else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
+            if (!ph.moe_reuse_x) {
+                if (g.wt == WT_Q6K) sk_quantise_xm<WT_Q6K>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
+                else sk_quantise_xm<WT_Q80>(ph.xm, xsrc, g.norm_w, g.eps, g.I, xq_sa, misc);
+            }
+            if (ph.moe == SK_MOE_GU && ph.moe_slot == 0)
+                sk_route(static_cast<const float*>(xsrc), g.norm_w, g.eps, ph.route_w, ph.n_exp, ph.n_used, g.I * 64,
+                         acc, misc, ph.moe_seq);
+            bool moe_owned = true;
+            float moe_w = 1.f;
+            if (ph.moe) {
+                const int e = reinterpret_cast<const int*>(misc + SK_MISC_ROUTE)[ph.moe_slot] - ph.e_lo;
+                moe_owned = e >= 0 && e < ph.e_n;
+                moe_w = misc[SK_MISC_ROUTE + 2 + ph.moe_slot];
+            }
             if (A.trace && tid == 0) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
-            if (g.wt == WT_Q6K)
+            if (!moe_owned) {
+                // expert parallel: another rank's expert, nothing streamed for this slot
+            } else if (g.wt == WT_Q6K)
                 use = sk_stages<WT_Q6K>(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
             else
                 use = sk_stages<WT_Q80>(g, rr, use, ring, A.slot_bytes, smem_sa, xq_sa, acc, full, empty, abort_flag);
@@ -1057,9 +1201,9 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 cp_async_wait_all();
                 named_bar_sync(1, NT);
             }
-            if (!*abort_flag)
+            if (!*abort_flag && (moe_owned || ph.moe == SK_MOE_DN))
                 sk_epilogues<TP>(g, ph.epi, rr, acc, rpre, best_v, best_i, A, ph,
-                                 TP && ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u);
+                                 TP && ph.tp_red ? sk_red_tag(A, launch0, ph.red_idx) : 0u, moe_owned, moe_w);
             // attention next: this CTA's first unit's K tiles load across the phase change (the x
             // records are dead; the next descriptor was fetched at this phase's start); not after a
             // prefetch that no unit consumed, nor in a step that gave up

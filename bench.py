@@ -50,7 +50,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 from __graft_entry__ import _load_pkg  # noqa: E402
 
-PROMPT_LEN = {"qwen3-4b": 128, "llama3-8b-q8": 4000, "qwen3-14b": 512}
+PROMPT_LEN = {"qwen3-4b": 128, "llama3-8b-q8": 4000, "qwen3-14b": 512, "mixtral-8x7b": 256}
+MODEL_GB = {"qwen3-4b": 3.5, "llama3-8b-q8": 8.6, "qwen3-14b": 12.5, "mixtral-8x7b": 39.0}  # file sizes
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
 FALLBACK_HBM_GBS = 6650.0
@@ -442,6 +443,8 @@ def main():
     ap.add_argument("--config", default=None, help="default: llama3-8b-q8 at one rank, qwen3-14b (TP) at N > 1")
     ap.add_argument("--prompt", type=int, default=None, help="prefill tokens (default: the config's own)")
     ap.add_argument("--layers", type=int, default=0, help="cut the model to this many layers (ncu captures)")
+    ap.add_argument("--ep", action="store_true",
+                    help="sparse MoE (mixtral-8x7b) with N > 1: whole experts per rank instead of a slice of each")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1: N independent replicas (weak scaling) instead of one tensor-parallel model")
     ap.add_argument("--repeats", type=int, default=0, help="timed regions (0: enough for >= 1.5 s)")
@@ -462,7 +465,8 @@ def main():
     if args.prompt is None:
         args.prompt = PROMPT_LEN.get(args.config, 128)
     if args.tmp is None:
-        args.tmp = shm_dir(20e9 * (1 if args.tp else world) + 20e9)
+        gb = MODEL_GB.get(args.config, 20.0) * 1e9
+        args.tmp = shm_dir(gb * (1 if args.tp else world) + 20e9)
 
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
@@ -498,7 +502,8 @@ def main():
             if rank == 0:
                 synth_model(fb, args.config, box[0], args.layers)
             dist.barrier(group=gloo)
-            model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world)
+            model = fb.Model(path, max_ctx=max_ctx, kv_dtype=kv, device=local, tp_rank=rank, tp_size=world,
+                             moe_ep=args.ep)
             import fence_b200.tp as fbtp
             fbtp.connect(model, gloo)
             dist.barrier(group=gloo)  # every rank has read the file before rank 0 removes it
@@ -545,7 +550,8 @@ def main():
                                + (f" ({args.layers}-layer cut for profiling, not the config)" if args.layers else ""),
                    "model": args.config, "kv_cache": args.kv, "global_batch": 1 if tp else world,
                    "seq_len": r["positions"][-1] + 1,
-                   "parallelism": f"tp{world}" if tp else (f"replicas{world}" if world > 1 else "single"),
+                   "parallelism": (f"ep{world}" if args.ep else f"tp{world}") if tp
+                   else (f"replicas{world}" if world > 1 else "single"),
                    "repeats": r["repeats"], "timing": "median of the repeats of K steps, max over ranks",
                    "l2": "weights larger than L2 (no flush needed)"},
         "roofline": {"bound": "hbm", "kernel": "step_kernel (one launch = one whole token step)",

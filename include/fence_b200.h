@@ -228,10 +228,16 @@ typedef struct fence_load_opts {
      * FENCE_E_DEVICE_WAIT (fence_device_error, and the status of the engine calls that sync).
      * -1 (the default) = off. */
     int wait_test_phase;
+    /* Sparse MoE models under tensor parallelism (no counterpart in the reference, which has no
+     * expert tensors): 0 (default) = every rank holds a 1/tp_size slice of every expert's FFN rows
+     * (all ranks stream both routed experts); 1 = expert parallel, rank r holds the experts
+     * [r * E / tp_size, (r + 1) * E / tp_size) whole (only the ranks holding a routed expert
+     * stream). Ignored for dense models and one rank. */
+    int moe_ep;
 } fence_load_opts;
 
 /* Fills *opts with defaults (max_ctx 4096, fp16 KV, device 0, graphs on, single rank, step kernel,
- * wait_test_phase -1). */
+ * wait_test_phase -1, moe_ep 0). */
 void fence_load_opts_default(fence_load_opts* opts);
 
 /* Qwen3Model::load (src/model/qwen3.cu:116-228): mmap the GGUF, read the config from its metadata

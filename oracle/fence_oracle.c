@@ -307,10 +307,16 @@ struct oracle_model {
     double* ybuf;
     const uint8_t *embd;
     const float* onorm;
+    /* sparse MoE FFN (no counterpart in the reference: Mixtral routing, see oracle_forward) */
+    int n_exp, n_used;
+    float *moe_out, *moe_tmp;
+    int* last_sel;       /* [L][n_used] experts chosen at the last forward */
+    float route_margin;  /* smallest gap between the last chosen and the best unchosen router logit */
     struct {
         const uint8_t *q, *k, *v, *o, *g, *u, *d;
         int tq, to, tg, td;
         const float *an, *fn, *qn, *kn, *qb, *kb, *vb;
+        const float* rt; /* router [n_exp][H] fp32 (MoE) */
     } * layer;
 };
 
@@ -475,6 +481,12 @@ oracle_model* oracle_model_open(const char* path, int max_ctx, int kv_bf16, int 
     m->nthreads = nthreads > 0 ? nthreads : 1;
     const o_tensor* on = find_t(m, "output_norm.weight");
     m->onorm = on ? (const float*)on->data : NULL;
+    m->n_exp = (int)kv_u32(m, arch, "expert_count", 0, NULL);
+    m->n_used = m->n_exp > 0 ? (int)kv_u32(m, arch, "expert_used_count", 2, NULL) : 0;
+    if (m->n_exp < 0 || m->n_exp > 64 || m->n_used < 0 || m->n_used > m->n_exp) {
+        oracle_model_close(m);
+        return NULL;
+    }
     m->layer = calloc((size_t)m->L, sizeof(*m->layer));
     char name[128];
 #define T(s) (snprintf(name, sizeof name, "blk.%d." s, l), find_t(m, name))
@@ -483,7 +495,18 @@ oracle_model* oracle_model_open(const char* path, int max_ctx, int kv_bf16, int 
                        *o = T("attn_output.weight"), *g = T("ffn_gate.weight"), *u = T("ffn_up.weight"),
                        *d = T("ffn_down.weight"), *an = T("attn_norm.weight"), *fn = T("ffn_norm.weight"),
                        *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight"), *qb = T("attn_q.bias"),
-                       *kb = T("attn_k.bias"), *vb = T("attn_v.bias");
+                       *kb = T("attn_k.bias"), *vb = T("attn_v.bias"), *rt = T("ffn_gate_inp.weight");
+        if (m->n_exp > 0) { /* experts: [K, M, n_exp] tensors, expert e's rows contiguous */
+            g = T("ffn_gate_exps.weight");
+            u = T("ffn_up_exps.weight");
+            d = T("ffn_down_exps.weight");
+            if (!rt || rt->type != 0 || rt->dims[0] != (uint64_t)m->H || rt->dims[1] != (uint64_t)m->n_exp) rt = NULL;
+            if (!rt) {
+                oracle_model_close(m);
+                return NULL;
+            }
+            m->layer[l].rt = (const float*)rt->data;
+        }
         if (!q || !k || !v || !o || !g || !u || !d || !an || !fn || !m->onorm) {
             oracle_model_close(m);
             return NULL;
@@ -529,6 +552,9 @@ oracle_model* oracle_model_open(const char* path, int max_ctx, int kv_bf16, int 
     m->act = (float*)calloc(m->F, 4);
     m->xh = (uint16_t*)calloc(mx, 2);
     m->ybuf = (double*)calloc(mx, 8);
+    m->moe_out = (float*)calloc(m->H, 4);
+    m->moe_tmp = (float*)calloc(m->H, 4);
+    m->last_sel = (int*)calloc((size_t)m->L * (m->n_used > 0 ? m->n_used : 1), sizeof(int));
     if (!m->kc || !m->vc) {
         oracle_model_close(m);
         return NULL;
@@ -557,6 +583,9 @@ void oracle_model_close(oracle_model* m) {
     free(m->act);
     free(m->xh);
     free(m->ybuf);
+    free(m->moe_out);
+    free(m->moe_tmp);
+    free(m->last_sel);
     free(m);
 }
 
@@ -600,6 +629,16 @@ void oracle_model_dims(const oracle_model* m, int* d) {
     d[9] = m->qk_norm;
 }
 
+void oracle_model_moe(const oracle_model* m, int* n_exp, int* n_used) {
+    *n_exp = m->n_exp;
+    *n_used = m->n_used;
+}
+
+float oracle_last_route(const oracle_model* m, int* sel) {
+    if (sel && m->n_used > 0) memcpy(sel, m->last_sel, (size_t)m->L * m->n_used * sizeof(int));
+    return m->route_margin;
+}
+
 void oracle_last_hidden(const oracle_model* m, float* out) { memcpy(out, m->final_hidden, (size_t)m->H * 4); }
 
 /* y = W x for one linear of either type; Q6_K inputs are rounded to fp16 first, as the reference
@@ -612,6 +651,52 @@ static void linear(oracle_model* m, int type, const uint8_t* W, const float* x, 
         oracle_gemv_q8_0(W, x, m->ybuf, M, K, m->nthreads);
     }
     for (int i = 0; i < M; ++i) y[i] = (float)m->ybuf[i];
+}
+
+static size_t o_row_bytes(int type, int K) { return type == 14 ? (size_t)K / 256 * 210 : (size_t)K / 32 * 34; }
+
+/* Sparse MoE FFN of layer l on m->normed (no counterpart in the reference, which has no expert
+ * tensors; Mixtral's published routing over the reference's per-op math): router logits
+ * r_e = sum_k W_r[e][k] * normed[k] (fp32 weights, accumulated in double), the n_used largest
+ * (ties to the smaller expert index), weights softmax over the chosen logits (the same as the
+ * full softmax renormalised over them), and out = sum_s w_s * down_e(SwiGLU(gate_e x, up_e x)),
+ * each expert's linears exactly the dense FFN's (qwen3.cu:317-341: fp16-rounded inputs for Q6_K).
+ * Parity unpinned: no reference fixture exists for it. */
+static void moe_ffn(oracle_model* m, int l) {
+    const __typeof__(m->layer[0])* w = &m->layer[l];
+    const int H = m->H, F = m->F, E = m->n_exp, K = m->n_used;
+    double r[64];
+    for (int e = 0; e < E; ++e) {
+        double a = 0.0;
+        for (int k = 0; k < H; ++k) a += (double)w->rt[(size_t)e * H + k] * (double)m->normed[k];
+        r[e] = a;
+    }
+    int sel[64];
+    int used[64] = {0};
+    for (int s = 0; s < K; ++s) {
+        int b = -1;
+        for (int e = 0; e < E; ++e)
+            if (!used[e] && (b < 0 || r[e] > r[b])) b = e;
+        sel[s] = b;
+        used[b] = 1;
+    }
+    double margin = 1e30;
+    for (int e = 0; e < E; ++e)
+        if (!used[e] && r[sel[K - 1]] - r[e] < margin) margin = r[sel[K - 1]] - r[e];
+    if (l == 0 || margin < m->route_margin) m->route_margin = (float)margin;
+    double z = 0.0, p[64];
+    for (int s = 0; s < K; ++s) z += (p[s] = exp(r[sel[s]] - r[sel[0]]));
+    for (int i = 0; i < H; ++i) m->moe_out[i] = 0.f;
+    for (int s = 0; s < K; ++s) {
+        const int e = sel[s];
+        m->last_sel[(size_t)l * K + s] = e;
+        const float ws = (float)(p[s] / z);
+        linear(m, w->tg, w->g + (size_t)e * F * o_row_bytes(w->tg, H), m->normed, m->gate, F, H);
+        linear(m, w->tg, w->u + (size_t)e * F * o_row_bytes(w->tg, H), m->normed, m->up, F, H);
+        oracle_silu_mul(m->act, m->gate, m->up, F);
+        linear(m, w->td, w->d + (size_t)e * H * o_row_bytes(w->td, F), m->act, m->moe_tmp, H, F);
+        for (int i = 0; i < H; ++i) m->moe_out[i] += ws * m->moe_tmp[i];
+    }
 }
 
 int oracle_forward(oracle_model* m, int token, int pos, float* logits) {
@@ -647,6 +732,11 @@ int oracle_forward(oracle_model* m, int token, int pos, float* logits) {
         /* MLP block, qwen3.cu:317-341 */
         memcpy(m->res, m->hidden, (size_t)H * 4);
         oracle_rms_norm(m->normed, m->hidden, w->fn, H, m->eps);
+        if (m->n_exp > 0) {
+            moe_ffn(m, l);
+            for (int i = 0; i < H; ++i) m->hidden[i] = m->res[i] + m->moe_out[i];
+            continue;
+        }
         linear(m, w->tg, w->g, m->normed, m->gate, F, H);
         linear(m, w->tg, w->u, m->normed, m->up, F, H);
         oracle_silu_mul(m->act, m->gate, m->up, F);

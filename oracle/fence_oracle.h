@@ -77,6 +77,14 @@ void oracle_model_dims(const oracle_model* m, int* dims);
 int oracle_model_fill_kv(oracle_model* m, int n_pos, uint64_t seed);
 /* Qwen3Model::forward (qwen3.cu:241-265): logits[vocab] for `token` at `pos`. 0 = ok. */
 int oracle_forward(oracle_model* m, int token, int pos, float* logits);
+/* Sparse MoE models (ffn_gate_inp + ffn_*_exps tensors, {arch}.expert_count / expert_used_count):
+ * the forward replaces the dense FFN by the routed experts (see moe_ffn in the source; no reference
+ * counterpart, parity unpinned). oracle_model_moe gives (n_exp, n_used), 0 for dense models;
+ * oracle_last_route copies the experts chosen per layer at the last forward ([L][n_used]) and
+ * returns the smallest router-logit gap between the last chosen expert and the best unchosen one
+ * (a tie there lets rounding pick either expert). */
+void oracle_model_moe(const oracle_model* m, int* n_exp, int* n_used);
+float oracle_last_route(const oracle_model* m, int* sel);
 /* Hidden state after the final norm of the last forward (embed_dim floats). */
 void oracle_last_hidden(const oracle_model* m, float* out);
 

@@ -60,6 +60,8 @@ def oracle() -> ctypes.CDLL:
             "oracle_forward": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, _vp]),
             "oracle_last_hidden": (None, [_vp, _vp]),
             "oracle_model_fill_kv": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_uint64]),
+            "oracle_model_moe": (None, [_vp, _vp, _vp]),
+            "oracle_last_route": (ctypes.c_float, [_vp, _vp]),
         }
         for n, (res, args) in sig.items():
             f = getattr(L, n)
@@ -157,6 +159,16 @@ class OracleModel:
         oracle().oracle_model_dims(self._h, _p(d))
         (self.n_layers, self.embed_dim, self.ff_dim, self.n_heads, self.n_kv_heads, self.head_dim,
          self.vocab_size, self.max_ctx, self.linear_type, self.qk_norm) = (int(v) for v in d)
+        ne, nu = ctypes.c_int(0), ctypes.c_int(0)
+        oracle().oracle_model_moe(self._h, ctypes.byref(ne), ctypes.byref(nu))
+        self.n_experts, self.n_experts_used = ne.value, nu.value
+
+    def last_route(self):
+        """(experts chosen per layer at the last forward [L, n_used], smallest router-logit gap between
+        the last chosen expert and the best unchosen one): MoE models only."""
+        sel = np.zeros((self.n_layers, max(1, self.n_experts_used)), dtype=np.int32)
+        margin = oracle().oracle_last_route(self._h, _p(sel))
+        return sel, float(margin)
 
     def fill_kv(self, n_pos: int, seed: int = 1) -> None:
         """Seeded K/V rows for positions [0, n_pos): stands in for a prefill (benchmark use)."""
