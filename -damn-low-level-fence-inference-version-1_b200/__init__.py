@@ -121,6 +121,14 @@ SIGNATURES = [
     ("fence_synth_write_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), ctypes.c_int]),
     ("fence_synth_fill_blocks", ctypes.c_int,
      [_vp, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
+    ("fence_tokenizer_load", _vp, [ctypes.c_char_p]),
+    ("fence_tokenizer_free", None, [_vp]),
+    ("fence_tokenizer_info", ctypes.c_int, [_vp, _c_int_p, _c_int_p, _c_int_p, _c_int_p]),
+    ("fence_tokenize", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_size_t, _c_int_p, ctypes.c_int, _c_int_p]),
+    ("fence_detokenize", ctypes.c_int, [_vp, _c_int_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t,
+                                        ctypes.POINTER(ctypes.c_size_t)]),
+    ("fence_format_chat", ctypes.c_int, [_vp, ctypes.c_char_p, ctypes.c_char_p, _c_int_p, ctypes.c_int, _c_int_p]),
+    ("fence_chat_append", ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_char_p, _c_int_p, ctypes.c_int, _c_int_p]),
 ]
 
 _lib = None
@@ -342,3 +350,78 @@ class Model:
         check(lib().fence_step_trace(self._h, token, pos, buf.ctypes.data, cap, ctypes.byref(nph), ctypes.byref(nct)),
               "step_trace")
         return buf[: nct.value * nph.value * 8].reshape(nct.value, nph.value, 8)
+
+
+# ------------------------------------------------------------------ tokenizer and chat prompts
+CHAT_FORMATS = ("ChatML", "LLaMA-3", "LLaMA-2", "Mistral", "Raw")  # FENCE_CHAT_* order
+TURN_BEGIN, TURN_SYSTEM, TURN_USER, TURN_ASSISTANT, TURN_END = range(5)
+
+
+def _b(text) -> bytes:
+    return text if isinstance(text, bytes) else text.encode("utf-8")
+
+
+class Tokenizer:
+    """The reference's Tokenizer API (src/tokenizer/tokenizer.h) over fence_tokenizer_*."""
+
+    def __init__(self, gguf_path: str):
+        h = lib().fence_tokenizer_load(gguf_path.encode())
+        if not h:
+            raise FenceError(f"tokenizer load failed: {last_error()}")
+        self._h = h
+        f, b, e, v = (ctypes.c_int() for _ in range(4))
+        check(lib().fence_tokenizer_info(h, ctypes.byref(f), ctypes.byref(b), ctypes.byref(e), ctypes.byref(v)))
+        self.chat_format, self.bos_id, self.eos_id, self.vocab_size = f.value, b.value, e.value, v.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().fence_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _ids_call(fn, *args, cap=256):
+        n = ctypes.c_int(0)
+        while True:
+            buf = (ctypes.c_int * max(cap, 1))()
+            rc = fn(*args, buf, cap, ctypes.byref(n))
+            if rc == 0:
+                return list(buf[:n.value])
+            if n.value <= cap:
+                check(rc)
+            cap = n.value
+
+    def encode(self, text) -> list:
+        t = _b(text)
+        return self._ids_call(lib().fence_tokenize, self._h, t, len(t), cap=len(t) + 8)
+
+    def decode(self, ids) -> bytes:
+        ids = list(ids)
+        arr = (ctypes.c_int * max(len(ids), 1))(*ids)
+        need = ctypes.c_size_t(0)
+        cap = 64 + 8 * len(ids)
+        while True:
+            buf = ctypes.create_string_buffer(cap)
+            rc = lib().fence_detokenize(self._h, arr, len(ids), buf, cap, ctypes.byref(need))
+            if rc == 0:
+                return buf.raw[:need.value]
+            if need.value + 1 <= cap:
+                check(rc)
+            cap = need.value + 1
+
+    def format_chat(self, system_prompt, user_message) -> list:
+        return self._ids_call(lib().fence_format_chat, self._h, _b(system_prompt), _b(user_message), cap=1024)
+
+    def append(self, tokens: list, turn: int, content=None) -> list:
+        """One multi-turn helper (TURN_*) appended to tokens; returns the new list."""
+        c = None if content is None else _b(content)
+        cap = len(tokens) + 64 + (4 * len(c) if c else 0)
+        buf = (ctypes.c_int * cap)(*tokens)
+        n = ctypes.c_int(len(tokens))
+        check(lib().fence_chat_append(self._h, turn, c, buf, cap, ctypes.byref(n)), "chat_append")
+        return list(buf[:n.value])

@@ -1,11 +1,11 @@
-// fence_main.cpp — the `fence` command line with the reference's flags and defaults
+// fence_main.cpp — the `fence` command line with the reference's flags, defaults and flow
 // (src/main.cu:17-162): --model --prompt --system --max-tokens --max-ctx --temp --top-p --top-k
-// --rep-penalty --debug --help. Sampling flags are applied to the model after load, as there.
-//
-// Text handling is minimal: the prompt is encoded by greedy longest match over the GGUF's
-// tokenizer.ggml.tokens after GPT-2 byte-to-unicode mapping, and generated ids are decoded the same
-// way; the reference's BPE merges and chat templates are not rebuilt. Harness flags on top:
-//   --tokens 1,2,3   prompt given as token ids (skips text encoding)
+// --rep-penalty --debug --help. The tokenizer and chat format come from the GGUF
+// (fence_tokenizer_*, the reference's Tokenizer); --prompt formats one turn with the system
+// prompt (format_chat) and streams the reply, no --prompt runs the interactive chat loop (history
+// kept across turns, cleared when fewer than 256 positions of max_ctx remain). Sampling flags are
+// applied to the model after load, as there. Harness flags on top:
+//   --tokens 1,2,3   prompt given as token ids (skips text encoding and the chat format)
 //   --seed N         sampler seed (the reference seeds from random_device)
 //   --kv f16|bf16    KV-cache element type (default f16, the reference cache type)
 //   --no-graph       launch kernels one by one instead of replaying the captured step
@@ -13,12 +13,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <iostream>
 #include <string>
-#include <unordered_map>
 #include <vector>
 
 #include "../../include/fence_b200.h"
-#include "gguf.h"
 
 namespace {
 
@@ -43,94 +42,47 @@ void print_usage(const char* prog) {
     printf("  --no-graph         Do not replay a captured CUDA graph\n");
 }
 
-// GPT-2 byte <-> unicode code point table (printable bytes map to themselves, the rest to 256+n).
-std::vector<int> byte_to_cp() {
-    std::vector<int> t(256, -1);
-    int n = 0;
-    for (int b = 0; b < 256; ++b) {
-        const bool keep = (b >= 33 && b <= 126) || (b >= 161 && b <= 172) || (b >= 174 && b <= 255);
-        t[b] = keep ? b : 256 + n++;
-    }
-    return t;
-}
-void put_utf8(std::string& s, int cp) {
-    if (cp < 0x80) s += (char)cp;
-    else if (cp < 0x800) {
-        s += (char)(0xC0 | (cp >> 6));
-        s += (char)(0x80 | (cp & 0x3F));
-    } else {
-        s += (char)(0xE0 | (cp >> 12));
-        s += (char)(0x80 | ((cp >> 6) & 0x3F));
-        s += (char)(0x80 | (cp & 0x3F));
-    }
+std::string detok(const fence_tokenizer* t, int id) {
+    char buf[1024];
+    size_t n = 0;
+    if (fence_detokenize(t, &id, 1, buf, sizeof buf, &n) == 0) return std::string(buf, n);
+    std::string big(n + 1, '\0');
+    fence_detokenize(t, &id, 1, &big[0], big.size(), &n);
+    big.resize(n);
+    return big;
 }
 
-struct Vocab {
-    std::vector<std::string> tokens;
-    std::unordered_map<std::string, int> index;
-    std::unordered_map<int, int> cp_to_byte;
-    int eos = 151645;  // reference default (tokenizer.h, Qwen <|im_end|>)
-    bool ok = false;
-
-    void load(const fence::GGUFFile& g) {
-        const auto* t = g.get_string_array("tokenizer.ggml.tokens");
-        if (!t) return;
-        tokens = *t;
-        for (int i = 0; i < (int)tokens.size(); ++i) index.emplace(tokens[i], i);
-        const auto b2c = byte_to_cp();
-        for (int b = 0; b < 256; ++b) cp_to_byte[b2c[b]] = b;
-        if (const auto* kv = g.find_metadata("tokenizer.ggml.eos_token_id")) {
-            if (kv->type == fence::GGUFValueType::UINT32) eos = (int)std::get<uint32_t>(kv->value);
-            if (kv->type == fence::GGUFValueType::INT32) eos = std::get<int32_t>(kv->value);
-        }
-        ok = true;
+// Qwen3Model::generate (qwen3.cu:463-519): token-by-token prefill of the whole history, then sample
+// (nucleus, the CLI's parameters), stop at eos or max_ctx, stream each new token's text. Returns
+// the history plus the reply (without eos), or an empty vector on an engine error.
+std::vector<int> generate(fence_model* m, const fence_tokenizer* tok, const std::vector<int>& prompt, int max_new,
+                          int eos, int max_ctx, bool debug) {
+    std::vector<int> out(prompt);
+    const auto t0 = std::chrono::steady_clock::now();
+    const float* logits = nullptr;
+    for (int i = 0; i < (int)prompt.size(); ++i)
+        if (!(logits = fence_forward(m, prompt[i], i))) return {};
+    const auto t1 = std::chrono::steady_clock::now();
+    const double pre_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+    printf("[prefill %zu tokens in %.0f ms (%.1f tok/s)]\n", prompt.size(), pre_ms, prompt.size() / (pre_ms / 1e3));
+    int pos = (int)prompt.size(), gen = 0;
+    for (int i = 0; i < max_new && pos < max_ctx; ++i) {
+        const int next = fence_sample_nucleus(m, logits, out.data(), (int)out.size());
+        if (next < 0) return {};
+        if (next == eos) break;
+        out.push_back(next);
+        ++gen;
+        if (tok) printf("%s", detok(tok, next).c_str());
+        else printf("%d ", next);
+        fflush(stdout);
+        if (debug) fprintf(stderr, "[step %d: id %d]\n", pos, next);
+        if (!(logits = fence_forward(m, next, pos))) return {};
+        ++pos;
     }
-    std::vector<int> encode(const std::string& text) const {
-        const auto b2c = byte_to_cp();
-        std::string u;
-        for (unsigned char ch : text) put_utf8(u, b2c[ch]);
-        std::vector<int> ids;
-        size_t pos = 0;
-        while (pos < u.size()) {
-            int best = -1;
-            size_t blen = 0;
-            for (size_t len = std::min<size_t>(128, u.size() - pos); len > 0; --len) {
-                auto it = index.find(u.substr(pos, len));
-                if (it != index.end()) {
-                    best = it->second;
-                    blen = len;
-                    break;
-                }
-            }
-            if (best < 0) {
-                ++pos;  // unknown byte: skip
-                continue;
-            }
-            ids.push_back(best);
-            pos += blen;
-        }
-        return ids;
-    }
-    std::string decode(int id) const {
-        if (id < 0 || id >= (int)tokens.size()) return "";
-        const std::string& s = tokens[id];
-        std::string out;
-        for (size_t i = 0; i < s.size();) {
-            const unsigned char c = s[i];
-            int cp, n;
-            if (c < 0x80) { cp = c; n = 1; }
-            else if ((c >> 5) == 6) { cp = c & 0x1F; n = 2; }
-            else if ((c >> 4) == 14) { cp = c & 0x0F; n = 3; }
-            else { cp = c & 0x07; n = 4; }
-            for (int k = 1; k < n && i + k < s.size(); ++k) cp = (cp << 6) | (s[i + k] & 0x3F);
-            auto it = cp_to_byte.find(cp);
-            if (it != cp_to_byte.end()) out += (char)it->second;
-            else out += s.substr(i, n);
-            i += n;
-        }
-        return out;
-    }
-};
+    const double dec_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t1).count();
+    if (gen > 0) printf("\n[generated %d tokens in %.0f ms (%.1f tok/s)]\n", gen, dec_ms, gen / (dec_ms / 1e3));
+    return out;
+}
 
 }  // namespace
 
@@ -173,31 +125,18 @@ int main(int argc, char** argv) {
         return 1;
     }
 
-    fence::GGUFFile g;
-    if (!g.open(model_path)) return 1;
-    Vocab vocab;
-    vocab.load(g);
-    g.close();
-
-    std::vector<int> ids;
-    if (!tokens_arg.empty()) {
-        for (const char* p = tokens_arg.c_str(); *p;) {
-            ids.push_back((int)strtol(p, const_cast<char**>(&p), 10));
-            while (*p == ',' || *p == ' ') ++p;
-        }
-    } else if (!prompt.empty()) {
-        if (!vocab.ok) {
-            fprintf(stderr, "Error: the model has no tokenizer.ggml.tokens; pass --tokens\n");
+    fence_tokenizer* tok = nullptr;
+    if (tokens_arg.empty()) {
+        tok = fence_tokenizer_load(model_path.c_str());
+        if (!tok) {
+            fprintf(stderr, "Error: %s (pass --tokens to skip text)\n", fence_last_error());
             return 1;
         }
-        ids = vocab.encode(prompt);
-    } else {
-        fprintf(stderr, "Error: interactive chat is not built; pass --prompt TEXT or --tokens LIST\n");
-        return 1;
-    }
-    if (ids.empty()) {
-        fprintf(stderr, "Error: empty prompt\n");
-        return 1;
+        int fmt = 0, bos = 0, eos = 0, nv = 0;
+        fence_tokenizer_info(tok, &fmt, &bos, &eos, &nv);
+        static const char* names[] = {"ChatML", "LLaMA-3", "LLaMA-2", "Mistral", "Raw"};
+        printf("Tokenizer: %d tokens, format=%s  bos=%d  eos=%d\n", nv, names[fmt], bos, eos);
+        printf("Chat format : %s\n\n", names[fmt]);
     }
 
     fence_load_opts o;
@@ -209,37 +148,103 @@ int main(int argc, char** argv) {
     fence_model* m = fence_model_load(model_path.c_str(), &o);
     if (!m) {
         fprintf(stderr, "Error: %s\n", fence_last_error());
+        fence_tokenizer_free(tok);
         return 1;
     }
     fence_set_sampling(m, temp, top_p, top_k, rep);
     if (have_seed) fence_set_seed(m, seed);
-
-    printf("Prompt tokens: %zu\n", ids.size());
-    std::vector<int> out(ids.size() + (size_t)max_tokens + 1);
-    int n_out = 0;
-    const auto t0 = std::chrono::steady_clock::now();
-    const int rc = fence_generate(m, ids.data(), (int)ids.size(), max_tokens, vocab.ok ? vocab.eos : -1, out.data(),
-                                  (int)out.size(), &n_out);
-    const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    if (rc) {
-        fprintf(stderr, "Error: %s\n", fence_last_error());
+    int eos = -1;
+    if (tok) fence_tokenizer_info(tok, nullptr, nullptr, &eos, nullptr);
+    auto fail = [&]() {
+        fprintf(stderr, "\nError: %s\n", fence_last_error());
         fence_model_free(m);
+        fence_tokenizer_free(tok);
         return 1;
-    }
-    printf("Assistant: ");
-    for (int i = (int)ids.size(); i < n_out; ++i) {
-        if (vocab.ok) printf("%s", vocab.decode(out[i]).c_str());
-        else printf("%d ", out[i]);
-    }
-    printf("\n");
-    const int gen = n_out - (int)ids.size();
-    printf("\n[%zu prompt + %d generated tokens in %.0f ms]\n", ids.size(), gen, sec * 1e3);
-    if (debug) {
-        printf("ids:");
-        for (int i = 0; i < n_out; ++i) printf(" %d", out[i]);
+    };
+    auto ids_of = [&](auto fn) {  // a tokenizer call into a growing buffer
+        std::vector<int> v(256);
+        int n = 0;
+        while (fn(v, n) != 0) {
+            if (n <= (int)v.size()) return std::vector<int>();
+            v.resize(n);
+        }
+        v.resize(n);
+        return v;
+    };
+
+    if (!tokens_arg.empty() || !prompt.empty()) {  // ---- single-prompt mode
+        std::vector<int> ids;
+        if (!tokens_arg.empty()) {
+            for (const char* p = tokens_arg.c_str(); *p;) {
+                ids.push_back((int)strtol(p, const_cast<char**>(&p), 10));
+                while (*p == ',' || *p == ' ') ++p;
+            }
+        } else {
+            ids = ids_of([&](std::vector<int>& v, int& n) {
+                return fence_format_chat(tok, system_prompt.c_str(), prompt.c_str(), v.data(), (int)v.size(), &n);
+            });
+        }
+        if (ids.empty()) {
+            fprintf(stderr, "Error: empty prompt\n");
+            fence_model_free(m);
+            fence_tokenizer_free(tok);
+            return 1;
+        }
+        printf("Prompt tokens: %zu\n", ids.size());
+        printf("Assistant: ");
+        fflush(stdout);
+        const std::vector<int> out = generate(m, tok, ids, max_tokens, eos, max_ctx, debug);
+        if (out.empty()) return fail();
         printf("\n");
+        if (debug) {
+            printf("ids:");
+            for (int id : out) printf(" %d", id);
+            printf("\n");
+        }
+        fence_model_free(m);
+        fence_tokenizer_free(tok);
+        return 0;
     }
-    (void)system_prompt;
+
+    // ---- interactive chat loop (main.cu:116-157)
+    printf("System: %s\n", system_prompt.c_str());
+    printf("Type your message (empty line to quit).\n\n");
+    std::vector<int> history;
+    auto append = [&](int turn, const char* content) {
+        int n = (int)history.size();
+        history.resize(history.size() + 4096 + (content ? 4 * strlen(content) : 0));
+        const int rc = fence_chat_append(tok, turn, content, history.data(), (int)history.size(), &n);
+        history.resize(rc == 0 ? n : 0);
+        return rc == 0;
+    };
+    auto start = [&]() {
+        history.clear();
+        append(FENCE_TURN_BEGIN, nullptr);
+        if (!system_prompt.empty()) append(FENCE_TURN_SYSTEM, system_prompt.c_str());
+    };
+    start();
+    while (true) {
+        printf("You: ");
+        fflush(stdout);
+        std::string line;
+        if (!std::getline(std::cin, line) || line.empty()) break;
+        if ((int)history.size() > max_ctx - 256) {
+            fprintf(stderr, "\n[Context limit approaching — clearing history]\n");
+            start();
+        }
+        append(FENCE_TURN_USER, line.c_str());
+        append(FENCE_TURN_ASSISTANT, nullptr);
+        printf("  [%zu tokens in context]\n", history.size());
+        printf("Assistant: ");
+        fflush(stdout);
+        std::vector<int> out = generate(m, tok, history, max_tokens, eos, max_ctx, debug);
+        if (out.empty()) return fail();
+        printf("\n\n");
+        history = std::move(out);
+        append(FENCE_TURN_END, nullptr);
+    }
     fence_model_free(m);
+    fence_tokenizer_free(tok);
+    printf("Goodbye!\n");
     return 0;
 }

@@ -338,6 +338,53 @@ int fence_synth_write_gguf(const char* path, const fence_synth_spec* spec, int n
 int fence_synth_fill_blocks(void* dst, int ggml_type, size_t n_blocks, uint64_t seed,
                             uint64_t stream_id, float d);
 
+/* =====================================================================================
+ * 4. Tokenizer and chat prompts — the reference's Tokenizer (src/tokenizer/tokenizer.h:15-129,
+ *    tokenizer.cpp:165-627) and detect_chat_format (src/model/chat_template.h:36-60), host only.
+ *    Byte-level BPE read from the GGUF (tokenizer.ggml.tokens / merges / bos / eos,
+ *    tokenizer.chat_template, general.architecture) with the reference's results: merges over the
+ *    whole text, lowest rank then leftmost pair; greedy longest match when the file has no merges;
+ *    characters missing from the vocabulary dropped; '?' for bytes that cannot be decoded.
+ *    Buffers too small for a result return FENCE_E_ARG with the size needed in *n_out / *len_out.
+ * ===================================================================================== */
+typedef struct fence_tokenizer fence_tokenizer;
+
+/* ChatFormat (chat_template.h:25-31), same order */
+#define FENCE_CHAT_CHATML  0
+#define FENCE_CHAT_LLAMA3  1
+#define FENCE_CHAT_LLAMA2  2
+#define FENCE_CHAT_MISTRAL 3
+#define FENCE_CHAT_RAW     4
+
+/* Tokenizer::load_from_gguf (tokenizer.cpp:165-248). NULL on failure (fence_last_error). */
+fence_tokenizer* fence_tokenizer_load(const char* gguf_path);
+void fence_tokenizer_free(fence_tokenizer* t);
+/* chat_format(), bos_id(), eos_id(), vocab_size() (tokenizer.h:64-76); any pointer may be NULL. */
+int fence_tokenizer_info(const fence_tokenizer* t, int* chat_format, int* bos_id, int* eos_id,
+                         int* vocab_size);
+/* Tokenizer::encode (tokenizer.cpp:265-325): len bytes of UTF-8 text -> *n_out ids in out[cap]. */
+int fence_tokenize(const fence_tokenizer* t, const char* text, size_t len, int* out, int cap,
+                   int* n_out);
+/* Tokenizer::decode of n ids, concatenated (tokenizer.cpp:403-414): *len_out bytes plus a NUL. */
+int fence_detokenize(const fence_tokenizer* t, const int* ids, int n, char* out, size_t cap,
+                     size_t* len_out);
+/* Tokenizer::format_chat (tokenizer.cpp:416-428): sequence start, system turn (skipped when
+ * system_prompt is NULL or empty), user turn, assistant header. */
+int fence_format_chat(fence_tokenizer* t, const char* system_prompt, const char* user_message,
+                      int* out, int cap, int* n_out);
+/* The multi-turn helpers begin_sequence / append_system_turn / append_user_turn /
+ * append_assistant_header / append_turn_end (tokenizer.cpp:478-627): appends the turn's ids to
+ * tokens[0 .. *n_inout) (capacity cap) and updates *n_inout. content is used by SYSTEM and USER.
+ * As in the reference, a LLaMA-2 / Mistral system prompt is held in the tokenizer until the first
+ * user turn, so a tokenizer carries one conversation at a time (not thread safe). */
+#define FENCE_TURN_BEGIN     0
+#define FENCE_TURN_SYSTEM    1
+#define FENCE_TURN_USER      2
+#define FENCE_TURN_ASSISTANT 3
+#define FENCE_TURN_END       4
+int fence_chat_append(fence_tokenizer* t, int turn, const char* content, int* tokens, int cap,
+                      int* n_inout);
+
 #ifdef __cplusplus
 } /* extern "C" */
 

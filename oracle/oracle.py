@@ -95,6 +95,78 @@ SYNTH_SO = os.path.join(HERE, "libsynth.so")
 _s = None
 
 
+REF_TOK = os.path.join(HERE, "_ref", "libref_tok.so")
+_rt = None
+
+
+def ref_tok() -> ctypes.CDLL | None:
+    """The reference's own Tokenizer (src/tokenizer/tokenizer.cpp) behind ref_tok_harness.cpp, or
+    None when it was not built (no reference tree when `make` ran)."""
+    global _rt
+    if _rt is None and os.path.exists(REF_TOK):
+        L = ctypes.CDLL(REF_TOK)
+        L.ref_tok_load.restype, L.ref_tok_load.argtypes = _vp, [ctypes.c_char_p]
+        L.ref_tok_free.argtypes = [_vp]
+        L.ref_tok_info.argtypes = [_vp] + [ctypes.POINTER(ctypes.c_int)] * 4
+        L.ref_tok_encode.restype = ctypes.c_int
+        L.ref_tok_encode.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, _vp, ctypes.c_int]
+        L.ref_tok_decode.restype = ctypes.c_size_t
+        L.ref_tok_decode.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t]
+        L.ref_tok_format_chat.restype = ctypes.c_int
+        L.ref_tok_format_chat.argtypes = [_vp, ctypes.c_char_p, ctypes.c_char_p, _vp, ctypes.c_int]
+        L.ref_tok_append.restype = ctypes.c_int
+        L.ref_tok_append.argtypes = [_vp, ctypes.c_int, ctypes.c_char_p, _vp, ctypes.c_int, ctypes.c_int]
+        _rt = L
+    return _rt
+
+
+class RefTokenizer:
+    """Python face of the reference tokenizer harness (same methods as fence_b200.Tokenizer)."""
+
+    def __init__(self, path: str):
+        L = ref_tok()
+        self._L = L
+        self._h = L.ref_tok_load(path.encode())
+        if not self._h:
+            raise RuntimeError(f"reference tokenizer could not load {path}")
+        v = [ctypes.c_int() for _ in range(4)]
+        L.ref_tok_info(self._h, *[ctypes.byref(x) for x in v])
+        self.chat_format, self.bos_id, self.eos_id, self.vocab_size = (x.value for x in v)
+
+    def close(self):
+        if self._h:
+            self._L.ref_tok_free(self._h)
+            self._h = None
+
+    def encode(self, text) -> list:
+        t = text if isinstance(text, bytes) else text.encode("utf-8")
+        cap = len(t) + 8
+        buf = np.zeros(cap, np.int32)
+        n = self._L.ref_tok_encode(self._h, t, len(t), buf.ctypes.data, cap)
+        return [int(x) for x in buf[:n]]
+
+    def decode(self, ids) -> bytes:
+        a = np.asarray(list(ids) or [0], np.int32)
+        cap = 64 + 8 * len(a)
+        out = ctypes.create_string_buffer(cap)
+        n = self._L.ref_tok_decode(self._h, a.ctypes.data, len(list(ids)), out, cap)
+        return out.raw[:n]
+
+    def format_chat(self, system_prompt, user_message) -> list:
+        buf = np.zeros(4096, np.int32)
+        b = [x if isinstance(x, bytes) else x.encode("utf-8") for x in (system_prompt, user_message)]
+        n = self._L.ref_tok_format_chat(self._h, b[0], b[1], buf.ctypes.data, 4096)
+        return [int(x) for x in buf[:n]]
+
+    def append(self, tokens: list, turn: int, content=None) -> list:
+        c = b"" if content is None else (content if isinstance(content, bytes) else content.encode("utf-8"))
+        cap = len(tokens) + 64 + 4 * len(c)
+        buf = np.zeros(cap, np.int32)
+        buf[:len(tokens)] = tokens
+        n = self._L.ref_tok_append(self._h, turn, c, buf.ctypes.data, len(tokens), cap)
+        return [int(x) for x in buf[:n]]
+
+
 def synth_write(path: str, spec_cls, fields: dict, threads: int = 0) -> None:
     """Writes a seeded synthetic GGUF through oracle/libsynth.so (the package's writer built on its
     own), byte-identical to the product library's fence_synth_write_gguf. spec_cls is the

@@ -1,6 +1,8 @@
 """The decode engine (fused kernels, CUDA graph) against the CPU oracle's restatement of the
 reference forward (src/model/qwen3.cu:241-341) on seeded synthetic GGUF models. Both token-step
 implementations are covered: the persistent step kernel (default) and one kernel per phase."""
+import os
+
 import numpy as np
 import pytest
 
@@ -176,3 +178,22 @@ def test_step_kernel_matches_phase_kernels(fb, models, cfg):
         outs.append(np.stack(logs))
         m.close()
     np.testing.assert_allclose(outs[0], outs[1], rtol=0, atol=LOGIT_ATOL)
+
+
+def test_cli_prompt_and_interactive_chat(fb, tmp_path):
+    """The `fence` CLI end to end: the GGUF's tokenizer and chat format (LLaMA-3 by architecture; the
+    synthetic vocabulary holds only "<id>" strings, so the format's words drop out and the prompt is
+    its three ids), streamed nucleus sampling, and the interactive loop on stdin."""
+    import subprocess
+    p = str(tmp_path / "cli.gguf")
+    fb.synth_write(p, "tiny-q8", write_tokenizer=1)
+    exe = os.path.join(fb.HERE, "fence")
+    r = subprocess.run([exe, "--model", p, "--prompt", "<5><7><11>", "--max-tokens", "8", "--seed", "3",
+                        "--max-ctx", "128"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "Chat format : LLaMA-3" in r.stdout and "Prompt tokens: 3" in r.stdout
+    assert "[generated 8 tokens" in r.stdout
+    r = subprocess.run([exe, "--model", p, "--max-tokens", "4", "--seed", "3", "--max-ctx", "128"],
+                       input="<1><2>\n<3>\n\n", capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.count("Assistant:") == 2 and "Goodbye!" in r.stdout
