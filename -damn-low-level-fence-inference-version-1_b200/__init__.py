@@ -52,7 +52,7 @@ class LoadOpts(ctypes.Structure):
         ("max_ctx", ctypes.c_int), ("kv_dtype", ctypes.c_int), ("device", ctypes.c_int),
         ("use_graph", ctypes.c_int), ("verbose", ctypes.c_int), ("tp_rank", ctypes.c_int),
         ("tp_size", ctypes.c_int), ("step_kernel", ctypes.c_int), ("wait_test_phase", ctypes.c_int),
-        ("moe_ep", ctypes.c_int),
+        ("moe_ep", ctypes.c_int), ("prefill", ctypes.c_int),
     ]
 
 
@@ -121,6 +121,8 @@ SIGNATURES = [
     ("fence_synth_write_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(SynthSpec), ctypes.c_int]),
     ("fence_synth_fill_blocks", ctypes.c_int,
      [_vp, ctypes.c_int, ctypes.c_size_t, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_float]),
+    ("fence_prefill", _vp, [_vp, _c_int_p, ctypes.c_int, ctypes.c_int]),
+    ("fence_gemm_f16", ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     ("fence_tokenizer_load", _vp, [ctypes.c_char_p]),
     ("fence_tokenizer_free", None, [_vp]),
     ("fence_tokenizer_info", ctypes.c_int, [_vp, _c_int_p, _c_int_p, _c_int_p, _c_int_p]),
@@ -237,7 +239,8 @@ class Model:
 
     def __init__(self, path: str, max_ctx: int = 4096, kv_dtype: int = FENCE_KV_F16, device: int = 0,
                  use_graph: bool = True, verbose: bool = False, step_kernel: bool = True,
-                 tp_rank: int = 0, tp_size: int = 1, wait_test_phase: int = -1, moe_ep: bool = False):
+                 tp_rank: int = 0, tp_size: int = 1, wait_test_phase: int = -1, moe_ep: bool = False,
+                 prefill: bool = True):
         L = lib()
         o = LoadOpts()
         L.fence_load_opts_default(ctypes.byref(o))
@@ -246,6 +249,7 @@ class Model:
         o.tp_rank, o.tp_size = tp_rank, tp_size
         o.wait_test_phase = wait_test_phase  # test only: a step-kernel phase whose counter wait runs out
         o.moe_ep = int(moe_ep)  # sparse MoE over tp_size ranks: whole experts per rank instead of slices
+        o.prefill = int(prefill)  # keep the repacked weights for the batched (tensor-core) prefill
         h = L.fence_model_load(path.encode(), ctypes.byref(o))
         if not h:
             raise FenceError(f"model load failed: {last_error()}")
@@ -269,6 +273,16 @@ class Model:
         p = lib().fence_forward(self._h, token, pos)
         if not p:
             raise FenceError(f"forward failed: {last_error()}")
+        return p
+
+    def prefill(self, tokens, pos0: int = 0) -> int:
+        """fence_prefill: tokens at positions pos0.. (batched where the model allows it); returns the
+        device address of the last token's logits."""
+        ids = list(tokens)
+        arr = (ctypes.c_int * len(ids))(*ids)
+        p = lib().fence_prefill(self._h, arr, len(ids), pos0)
+        if not p:
+            raise FenceError(f"prefill failed: {last_error()}")
         return p
 
     def vocab_shard(self):

@@ -20,6 +20,7 @@
 #include <cstring>
 #include <random>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "attention.cuh"
@@ -40,11 +41,16 @@ unsigned long long sk_tile_plan(int wt, int I, int Mv, int dual, int G, int RB, 
 cudaError_t sk_retile(int wt, const RMat& m, int I, int Mv, int dual, int G, int RB, int CI,
                       const unsigned long long* d_tcta, uint8_t* dst, cudaStream_t st);
 cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
+struct TGArgs;
+template <int EPI>
+cudaError_t launch_tc_gemm(const TGArgs& a, cudaStream_t st);
+cudaError_t launch_dequant(int wt, const RMat& m, int rows, int I, __half* W, float* bscale, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
                         float top_p, int top_k, float rep_penalty, float min_p, bool dynamic_temp,
                         std::mt19937& rng);
 
 struct LayerW {
+    // linears: the GGUF rows in the host file mapping (streamed to the device per layer at load)
     const uint8_t *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     const uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
     int t_qkv = 14, t_o = 14, t_gu = 14, t_down = 14;  // GGML type ids
@@ -124,6 +130,13 @@ struct fence_model {
     int moe = 0, moe_ep = 0, e_lo = 0, e_n = 0;
     std::vector<RMat> moe_gu, moe_dn;
     float* moe_acc = nullptr;       // tensor parallel: the expert slots' partial rows before the last slot
+    // batched prefill (prefill.cu): the repacked row-major weights are kept for it (one rank, dense
+    // FFN, opts.prefill); its scratch is allocated on the first call for pf_cap tokens per chunk
+    int prefill_ok = 0;
+    int pf_cap = 0;
+    int* pf_tok = nullptr;
+    float *pf_hidden = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_attn = nullptr, *pf_bscale = nullptr;
+    __half *pf_x16 = nullptr, *pf_act = nullptr, *pf_w = nullptr;
     // device nucleus sampler (allocated on its first use)
     void* samp_scratch = nullptr;
     size_t samp_bytes = 0;
@@ -137,6 +150,106 @@ struct fence_model {
 };
 
 namespace {
+
+// Streaming host -> device upload of GGUF data (the reference copies tensor by tensor with
+// synchronous pageable cudaMemcpy, qwen3.cu:104-111). A ring of pinned staging buffers: worker
+// threads copy the next chunk out of the file mapping (taking the page faults of a cold file in
+// parallel) while the DMA engine moves the previous chunks; each buffer is reused once its copy has
+// completed (an event per buffer). A piece is `rows` rows of `width` bytes, `pitch` bytes apart in
+// the file, packed row after row at the destination: a whole tensor, a rank's rows of it, or a
+// rank's column slice of every row. Copies are ordered on the stream, so kernels enqueued after them
+// on that stream read the data.
+struct Uploader {
+    static constexpr int NB = 4;
+    static constexpr size_t CHUNK = 32u << 20;
+    cudaStream_t st = nullptr;
+    uint8_t* pin[NB] = {};
+    cudaEvent_t ev[NB] = {};
+    bool busy[NB] = {};
+    int cur = 0;
+    int threads = 1;
+    size_t bytes = 0;
+
+    int init(cudaStream_t s) {
+        st = s;
+        threads = (int)std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+        for (int i = 0; i < NB; ++i) {
+            if (cudaMallocHost(&pin[i], CHUNK) != cudaSuccess || cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
+                return set_error(FENCE_E_NOMEM, "upload: pinned staging allocation failed");
+        }
+        return FENCE_OK;
+    }
+    ~Uploader() {
+        for (int i = 0; i < NB; ++i) {
+            if (ev[i]) {
+                cudaEventSynchronize(ev[i]);
+                cudaEventDestroy(ev[i]);
+            }
+            if (pin[i]) cudaFreeHost(pin[i]);
+        }
+    }
+    // host side of one chunk: rows [r0, r1) of the piece, or bytes [b0, b1) of a single-row piece
+    void pack(uint8_t* dst, const uint8_t* src, size_t pitch, size_t width, size_t r0, size_t r1) const {
+        const size_t n = r1 - r0;
+        auto work = [&](size_t a, size_t b) {
+            if (width == pitch) {
+                std::memcpy(dst + a * width, src + (r0 + a) * pitch, (b - a) * width);
+            } else {
+                for (size_t r = a; r < b; ++r) std::memcpy(dst + r * width, src + (r0 + r) * pitch, width);
+            }
+        };
+        const int nt = (int)std::min<size_t>((size_t)threads, (n * width) >> 22 ? n : 1);  // threads for >= 4 MB
+        if (nt <= 1) {
+            work(0, n);
+            return;
+        }
+        std::vector<std::thread> th;
+        for (int t = 0; t < nt; ++t) th.emplace_back(work, n * t / nt, n * (t + 1) / nt);
+        for (auto& x : th) x.join();
+    }
+    int put(uint8_t* dst, const uint8_t* src, size_t pitch, size_t width, size_t rows) {
+        if (rows == 1) {  // one contiguous range: chunk it as rows of 64 KB (and a remainder)
+            const size_t unit = 65536, full = width / unit, tail = width - full * unit;
+            if (full) {
+                const int rc = put_rows(dst, src, unit, unit, full);
+                if (rc) return rc;
+            }
+            return tail ? put_rows(dst + full * unit, src + full * unit, tail, tail, 1) : FENCE_OK;
+        }
+        return put_rows(dst, src, pitch, width, rows);
+    }
+    int put_rows(uint8_t* dst, const uint8_t* src, size_t pitch, size_t width, size_t rows) {
+        if (width > CHUNK) return set_error(FENCE_E_UNSUPPORTED, "upload: a row of %zu bytes exceeds the staging chunk", width);
+        const size_t per = CHUNK / width;
+        for (size_t r0 = 0; r0 < rows; r0 += per) {
+            const size_t r1 = std::min(rows, r0 + per);
+            if (busy[cur] && cudaEventSynchronize(ev[cur]) != cudaSuccess)
+                return set_error(FENCE_E_NOMEM, "upload: staging copy failed");
+            pack(pin[cur], src, pitch, width, r0, r1);
+            if (cudaMemcpyAsync(dst + r0 * width, pin[cur], (r1 - r0) * width, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaEventRecord(ev[cur], st) != cudaSuccess)
+                return set_error(FENCE_E_NOMEM, "upload: host to device copy failed");
+            busy[cur] = true;
+            cur = (cur + 1) % NB;
+            bytes += (r1 - r0) * width;
+        }
+        return FENCE_OK;
+    }
+};
+
+// Bytes of the blocks covering input columns [c0, c1) of a row of a Q6_K (super-blocks of 256) or
+// Q8_0 (blocks of 32) matrix, and the first covering block.
+struct ColCover {
+    size_t b0, nb, bytes;
+};
+ColCover col_cover(int ggml_type, uint64_t c0, uint64_t c1) {
+    const uint64_t bs = ggml_type == 14 ? 256 : 32, ts = ggml_type == 14 ? 210 : 34;
+    ColCover cc;
+    cc.b0 = c0 / bs;
+    cc.nb = (c1 + bs - 1) / bs - cc.b0;
+    cc.bytes = cc.nb * ts;
+    return cc;
+}
 
 int step_attn_solo() {
 #ifdef FENCE_TUNE_ENV
@@ -452,8 +565,10 @@ int build_step_phases(fence_model* m) {
             ++gi;
         }
         FENCE_CUDA_TRY(cudaStreamSynchronize(m->stream));
-        cudaFree(m->rarena);  // the per-phase path (step_kernel = 0) is the only reader of the row-major copy
-        m->rarena = nullptr;
+        if (!m->prefill_ok) {  // the per-phase path and the batched prefill are the readers of the row-major copy
+            cudaFree(m->rarena);
+            m->rarena = nullptr;
+        }
     }
     FENCE_CUDA_TRY(cudaMalloc(&m->d_phases, ph.size() * sizeof(SPhase)));
     FENCE_CUDA_TRY(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(SPhase), cudaMemcpyHostToDevice));
@@ -528,6 +643,15 @@ void free_model(fence_model* m) {
     cudaFree(m->hidden_b);
     cudaFree(m->tp_launch);
     cudaFree(m->moe_acc);
+    cudaFree(m->pf_tok);
+    cudaFree(m->pf_hidden);
+    cudaFree(m->pf_qkv);
+    cudaFree(m->pf_q);
+    cudaFree(m->pf_attn);
+    cudaFree(m->pf_bscale);
+    cudaFree(m->pf_x16);
+    cudaFree(m->pf_act);
+    cudaFree(m->pf_w);
     cudaFree(m->samp_scratch);
     cudaFree(m->samp_hist);
     cudaFree(m->samp_out);
@@ -554,6 +678,7 @@ extern "C" void fence_load_opts_default(fence_load_opts* o) {
     o->step_kernel = 1;
     o->wait_test_phase = -1;
     o->moe_ep = 0;
+    o->prefill = 1;
 }
 
 extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts* opts_in) {
@@ -684,7 +809,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     m->vocab0 = v0;
     m->vocab_n = vn;
 
-    // ---- collect and validate tensors, lay out the device arena
+    // ---- collect and validate tensors; lay out the device arena of the tensors kept as they are in
+    // the file (embedding, norms, biases, router); the linears stay in the file mapping until the
+    // per-layer streaming upload below
     struct Up {
         const GGUFTensorInfo* t;
         size_t off;
@@ -749,14 +876,14 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         if (c.linear_type == 0) c.linear_type = (int)q->type;
         LOff& L = lo[l];
         L.an = place(an);
-        L.q = place(q);
-        L.k = place(k);
-        L.v = place(v);
-        L.o = place(o);
         L.fn = place(fn);
-        L.g = place(g);
-        L.u = place(u);
-        L.d = place(d);
+        w.q = static_cast<const uint8_t*>(q->data);
+        w.k = static_cast<const uint8_t*>(k->data);
+        w.v = static_cast<const uint8_t*>(v->data);
+        w.o = static_cast<const uint8_t*>(o->data);
+        w.gate = static_cast<const uint8_t*>(g->data);
+        w.up = static_cast<const uint8_t*>(u->data);
+        w.down = static_cast<const uint8_t*>(d->data);
         L.has_qn = qn && kn;  // the reference applies q/k-norm only when both exist (qwen3.cu:292)
         L.has_kn = L.has_qn;
         if (L.has_qn) {
@@ -781,7 +908,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     if (opts.verbose) {
         printf("Config: layers=%d embed=%d ff=%d heads=%d/%d head_dim=%d vocab=%d\n", c.n_layers, c.embed_dim,
                c.ff_dim, c.n_heads, c.n_kv_heads, c.head_dim, c.vocab_size);
-        printf("Copying weights to GPU (%.2f GB)...\n", total / 1e9);
+        printf("Copying embedding and norms to GPU (%.2f GB); linears stream per layer...\n", total / 1e9);
     }
 
     // ---- device allocations (everything above is host-side parsing and validation)
@@ -789,28 +916,20 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(FENCE_E_NOMEM, "model_load: stream creation failed");
     if (cudaMalloc(&m->arena, total) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: weight arena allocation failed");
-    auto t0 = std::chrono::steady_clock::now();
+    const auto t0 = std::chrono::steady_clock::now();
+    Uploader up;
+    if (up.init(m->stream) != FENCE_OK) return bail(FENCE_E_NOMEM, fence_last_error());
     for (const Up& u : ups)
-        if (cudaMemcpy(m->arena + u.off, u.t->data, u.t->data_size_bytes, cudaMemcpyHostToDevice) != cudaSuccess)
-            return bail(FENCE_E_NOMEM, "model_load: weight upload failed for " + u.t->name);
-    if (opts.verbose)
-        printf("Weights loaded in %.1f s\n", std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+        if (up.put(m->arena + u.off, static_cast<const uint8_t*>(u.t->data), u.t->data_size_bytes, u.t->data_size_bytes, 1))
+            return bail(FENCE_E_NOMEM, std::string("model_load: upload of ") + u.t->name + ": " + fence_last_error());
     m->tok_embd = m->arena + off_embd;
     m->out_norm = reinterpret_cast<const float*>(m->arena + off_onorm);
     for (int l = 0; l < c.n_layers; ++l) {
         LayerW& w = m->layers[l];
         const LOff& L = lo[l];
-        auto P = [&](size_t off) { return m->arena + off; };
         auto PF = [&](size_t off) { return reinterpret_cast<const float*>(m->arena + off); };
         w.attn_norm = PF(L.an);
-        w.q = P(L.q);
-        w.k = P(L.k);
-        w.v = P(L.v);
-        w.o = P(L.o);
         w.ffn_norm = PF(L.fn);
-        w.gate = P(L.g);
-        w.up = P(L.u);
-        w.down = P(L.d);
         if (L.has_qn) {
             w.q_norm = PF(L.qn);
             w.k_norm = PF(L.kn);
@@ -925,7 +1044,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
     for (const LayerW& w : m->layers) any_bias = any_bias || w.q_bias || w.k_bias || w.v_bias;
     if (any_bias) {
         if (cudaMalloc(&m->qkv_bias, (size_t)c.n_layers * QKVR * 4) != cudaSuccess ||
-            cudaMemset(m->qkv_bias, 0, (size_t)c.n_layers * QKVR * 4) != cudaSuccess)
+            cudaMemsetAsync(m->qkv_bias, 0, (size_t)c.n_layers * QKVR * 4, m->stream) != cudaSuccess)
             return bail(FENCE_E_NOMEM, "model_load: bias allocation failed");
     }
     cudaStream_t st = m->stream;
@@ -949,6 +1068,29 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
 
     m->launches.resize(c.n_layers);
     const size_t kv_layer = (size_t)Hkv_l * c.max_ctx * SK_ATT_RSTR;
+    // Streaming upload of the linears, one layer at a time: this rank's pieces only (its q/k/v and
+    // FFN rows, the blocks covering its o_proj / down input columns, its experts) go through the
+    // pinned staging ring into one device staging buffer and are repacked from there on the same
+    // stream, so the next layer's copies overwrite the buffer only after the repack has read it.
+    const uint64_t q_c0 = (uint64_t)TPR * qdl, f_c0 = (uint64_t)FTPR * Fl;
+    auto a256 = [](size_t x) { return align_up(x, 256); };
+    size_t stage_bytes = 0;
+    for (const LayerW& w : m->layers) {
+        // exactly the pieces `take` carves below, each rounded to 256 bytes
+        const size_t b = a256(qdl * raw_row(w.t_qkv, H)) + 2 * a256(kvdl * raw_row(w.t_qkv, H)) +
+                         a256(H * col_cover(w.t_o, q_c0, q_c0 + qdl).bytes) +
+                         (size_t)n_ffn * (2 * a256(Fl * raw_row(w.t_gu, H)) + a256(H * col_cover(w.t_down, f_c0, f_c0 + Fl).bytes));
+        stage_bytes = std::max(stage_bytes, b);
+    }
+    uint8_t* stage = nullptr;
+    if (cudaMalloc(&stage, stage_bytes) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: staging allocation failed");
+    struct StageFree {
+        uint8_t* p;
+        cudaStream_t s;
+        ~StageFree() {
+            if (p) cudaStreamSynchronize(s), cudaFree(p);
+        }
+    } stage_free{stage, st};
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerW& w = m->layers[l];
         LayerLaunch& L = m->launches[l];
@@ -957,11 +1099,29 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         const RMat rq = carve(wq, QKVR, (int)H, 0), ro = carve(wo, (long long)H, (int)qdl, o_item0 & 3);
         // this rank's rows (q/k/v heads, FFN rows) and input columns (o_proj, down)
         const uint64_t rq_b = raw_row(w.t_qkv, H), rg_b = raw_row(w.t_gu, H), rd_b = raw_row(w.t_down, F);
-
-        if (!fill(wq, w.q + TPR * qdl * rq_b, (long long)qdl, (int)H, rq, 0, 1) ||
-            !fill(wq, w.k + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)qdl, 1) ||
-            !fill(wq, w.v + TPR * kvdl * rq_b, (long long)kvdl, (int)H, rq, (long long)(qdl + kvdl), 1) ||
-            rmat_fill(wo, w.o, (long long)H, (int)qdl, ro, 0, 1, st, (int)qd, o_item0) != cudaSuccess)
+        const ColCover oc = col_cover(w.t_o, q_c0, q_c0 + qdl), dc = col_cover(w.t_down, f_c0, f_c0 + Fl);
+        const uint64_t obs = w.t_o == 14 ? 256 : 32, dbs = w.t_down == 14 ? 256 : 32;
+        uint8_t* sp = stage;
+        auto take = [&](size_t bytes) {
+            uint8_t* p = sp;
+            sp += a256(bytes);
+            return p;
+        };
+        bool over = false;  // set if a piece would pass the staging buffer's end (checked before any copy)
+        auto room = [&]() { over = over || sp > stage + stage_bytes; };
+        uint8_t *sq = take(qdl * rq_b), *sk = take(kvdl * rq_b), *sv = take(kvdl * rq_b), *so = take(H * oc.bytes);
+        room();
+        if (over) return bail(FENCE_E_NOMEM, "model_load: staging plan too small");
+        if (up.put(sq, w.q + TPR * qdl * rq_b, qdl * rq_b, qdl * rq_b, 1) ||
+            up.put(sk, w.k + TPR * kvdl * rq_b, kvdl * rq_b, kvdl * rq_b, 1) ||
+            up.put(sv, w.v + TPR * kvdl * rq_b, kvdl * rq_b, kvdl * rq_b, 1) ||
+            up.put(so, w.o + oc.b0 * (oc.bytes / oc.nb), raw_row(w.t_o, qd), oc.bytes, H))
+            return bail(FENCE_E_NOMEM, std::string("model_load: ") + fence_last_error());
+        if (!fill(wq, sq, (long long)qdl, (int)H, rq, 0, 1) ||
+            !fill(wq, sk, (long long)kvdl, (int)H, rq, (long long)qdl, 1) ||
+            !fill(wq, sv, (long long)kvdl, (int)H, rq, (long long)(qdl + kvdl), 1) ||
+            rmat_fill(wo, so, (long long)H, (int)qdl, ro, 0, 1, st, (int)(oc.nb * obs), (int)((q_c0 - oc.b0 * obs) / 64)) !=
+                cudaSuccess)
             return bail(FENCE_E_NOMEM, "model_load: repacking failed");
         // FFN: the dense matrices, or every local expert's (expert e's rows start at e * F (gate/up)
         // and e * H (down) in the stacked tensors)
@@ -969,9 +1129,16 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         for (int e = 0; e < n_ffn; ++e) {
             const uint64_t ge = moe ? (uint64_t)(m->e_lo + e) : 0;
             const RMat eg = carve(wg, 2 * (long long)Fl, (int)H, 0), ed = carve(wd, (long long)H, (int)Fl, d_item0 & 3);
-            if (!fill(wg, w.gate + (ge * F + FTPR * Fl) * rg_b, (long long)Fl, (int)H, eg, 0, 2) ||
-                !fill(wg, w.up + (ge * F + FTPR * Fl) * rg_b, (long long)Fl, (int)H, eg, 1, 2) ||
-                rmat_fill(wd, w.down + ge * H * rd_b, (long long)H, (int)Fl, ed, 0, 1, st, (int)F, d_item0) != cudaSuccess)
+            uint8_t *sg = take(Fl * rg_b), *su = take(Fl * rg_b), *sd = take(H * dc.bytes);
+            room();
+            if (over) return bail(FENCE_E_NOMEM, "model_load: staging plan too small");
+            if (up.put(sg, w.gate + (ge * F + f_c0) * rg_b, Fl * rg_b, Fl * rg_b, 1) ||
+                up.put(su, w.up + (ge * F + f_c0) * rg_b, Fl * rg_b, Fl * rg_b, 1) ||
+                up.put(sd, w.down + ge * H * rd_b + dc.b0 * (dc.bytes / dc.nb), rd_b, dc.bytes, H))
+                return bail(FENCE_E_NOMEM, std::string("model_load: ") + fence_last_error());
+            if (!fill(wg, sg, (long long)Fl, (int)H, eg, 0, 2) || !fill(wg, su, (long long)Fl, (int)H, eg, 1, 2) ||
+                rmat_fill(wd, sd, (long long)H, (int)Fl, ed, 0, 1, st, (int)(dc.nb * dbs),
+                          (int)((f_c0 - dc.b0 * dbs) / 64)) != cudaSuccess)
                 return bail(FENCE_E_NOMEM, "model_load: repacking failed");
             if (e == 0) rg = eg, rd = ed;
             if (moe) m->moe_gu[(size_t)l * m->e_n + e] = eg, m->moe_dn[(size_t)l * m->e_n + e] = ed;
@@ -979,9 +1146,9 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         float* bias = nullptr;
         if (any_bias) {
             bias = m->qkv_bias + (size_t)l * QKVR;
-            if ((w.q_bias && cudaMemcpy(bias, w.q_bias + TPR * qdl, qdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
-                (w.k_bias && cudaMemcpy(bias + qdl, w.k_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess) ||
-                (w.v_bias && cudaMemcpy(bias + qdl + kvdl, w.v_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice) != cudaSuccess))
+            if ((w.q_bias && cudaMemcpyAsync(bias, w.q_bias + TPR * qdl, qdl * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) ||
+                (w.k_bias && cudaMemcpyAsync(bias + qdl, w.k_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess) ||
+                (w.v_bias && cudaMemcpyAsync(bias + qdl + kvdl, w.v_bias + TPR * kvdl, kvdl * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess))
                 return bail(FENCE_E_NOMEM, "model_load: bias upload failed");
         }
         if (!phase(L.qkv, rq, wq, (int)H, (int)QKVR, 0, wq == WT_Q6K ? X_NORM_R16 : X_NORM, EPI_STORE) ||
@@ -1027,6 +1194,13 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         at.counter = m->counters;
         L.attn = at;
     }
+    // every layer's pieces are repacked: the staging buffer goes before the step kernel's tiles are built
+    if (cudaStreamSynchronize(st) != cudaSuccess) return bail(FENCE_E_NOMEM, "model_load: upload / repack failed");
+    cudaFree(stage);
+    stage_free.p = nullptr;
+    if (opts.verbose)
+        printf("Weights streamed: %.2f GB in %.1f s\n", up.bytes / 1e9,
+               std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
     // LM head: tied token_embd (the reference ignores output.weight, qwen3.cu:180-212,261)
     {
         const RMat rl = carve(WT_Q80, vn, (int)H, 0);
@@ -1046,6 +1220,7 @@ extern "C" fence_model* fence_model_load(const char* path, const fence_load_opts
         a.token_log = m->token_log;
         a.token_log_cap = m->token_log_cap;
     }
+    m->prefill_ok = (opts.prefill && TPN == 1 && !moe) ? 1 : 0;
     if (opts.step_kernel && TPN == 1) {  // tensor parallel: once the ranks are connected (fence_tp_connect)
         const int rc = build_step_phases(m);
         if (rc != FENCE_OK) return bail(rc, std::string("model_load: ") + fence_last_error());
@@ -1173,6 +1348,140 @@ extern "C" const float* fence_forward(fence_model* m, int token_id, int pos) {
     return m->logits;
 }
 
+namespace {
+
+// Scratch of the batched prefill for chunks of up to `cap` tokens (allocated once, on first use).
+int prefill_scratch(fence_model* m, int cap) {
+    if (m->pf_cap >= cap) return FENCE_OK;
+    const fence_config& c = m->cfg;
+    const size_t H = c.embed_dim, F = c.ff_dim, qd = (size_t)c.n_heads * c.head_dim,
+                 QKVR = qd + 2 * (size_t)c.n_kv_heads * c.head_dim;
+    size_t wmax = 0, rmax = 0;
+    auto see = [&](const RPhase& r) {
+        wmax = std::max(wmax, (size_t)r.a.Mv * (r.a.dual ? 2 : 1) * (size_t)r.a.I * 64);
+        rmax = std::max(rmax, (size_t)r.a.Mv * (r.a.dual ? 2 : 1));
+    };
+    for (const LayerLaunch& L : m->launches) {
+        see(L.qkv);
+        see(L.o);
+        see(L.gu);
+        see(L.down);
+    }
+    cudaFree(m->pf_tok), cudaFree(m->pf_hidden), cudaFree(m->pf_qkv), cudaFree(m->pf_q), cudaFree(m->pf_attn);
+    cudaFree(m->pf_bscale), cudaFree(m->pf_x16), cudaFree(m->pf_act), cudaFree(m->pf_w);
+    m->pf_cap = 0;
+    const size_t P = (size_t)cap;
+    if (cudaMalloc(&m->pf_tok, P * 4) != cudaSuccess || cudaMalloc(&m->pf_hidden, P * H * 4) != cudaSuccess ||
+        cudaMalloc(&m->pf_qkv, P * QKVR * 4) != cudaSuccess || cudaMalloc(&m->pf_q, P * qd * 4) != cudaSuccess ||
+        cudaMalloc(&m->pf_attn, P * qd * 4) != cudaSuccess || cudaMalloc(&m->pf_bscale, rmax * 4) != cudaSuccess ||
+        cudaMalloc(&m->pf_x16, P * std::max(H, qd) * 2) != cudaSuccess || cudaMalloc(&m->pf_act, P * F * 2) != cudaSuccess ||
+        cudaMalloc(&m->pf_w, wmax * 2) != cudaSuccess)
+        return set_error(FENCE_E_NOMEM, "prefill: scratch allocation failed");
+    m->pf_cap = cap;
+    return FENCE_OK;
+}
+
+// One linear of the chunk: its repacked weights dequantised to fp16 rows, then the tensor-core GEMM
+// with the given epilogue.
+template <int EPI>
+int prefill_linear(fence_model* m, const RPhase& r, const __half* A, int P, TGArgs a) {
+    const int rows = r.a.Mv * (r.a.dual ? 2 : 1);
+    FENCE_CUDA_TRY(launch_dequant(r.a.wt, r.a.w, rows, r.a.I, m->pf_w, m->pf_bscale, m->stream));
+    a.A = A;
+    a.B = m->pf_w;
+    a.bscale = m->pf_bscale;
+    a.P = P;
+    a.N = rows;
+    a.K = r.a.I * 64;
+    FENCE_CUDA_TRY(launch_tc_gemm<EPI>(a, m->stream));
+    return FENCE_OK;
+}
+
+// tokens[0 .. n) at positions pos0 .. pos0 + n - 1 through every layer in chunks: the K/V cache rows
+// of those positions are written (the residual stream of the chunk is not needed afterwards).
+int prefill_batched(fence_model* m, const int* tokens, int n, int pos0) {
+    const fence_config& c = m->cfg;
+    const int H = c.embed_dim, HD = c.head_dim, Hq = c.n_heads, Hkv = c.n_kv_heads, qd = Hq * HD,
+              QKVR = qd + 2 * Hkv * HD, F = c.ff_dim;
+    const int cap = std::min(n, 2048);
+    if (const int rc = prefill_scratch(m, std::max(cap, m->pf_cap))) return rc;
+    cudaStream_t st = m->stream;
+    const size_t kv_layer = (size_t)Hkv * c.max_ctx * SK_ATT_RSTR;
+    const long long stride_h = (long long)c.max_ctx * SK_ATT_RSTR;
+    for (int c0 = 0; c0 < n; c0 += cap) {
+        const int P = std::min(cap, n - c0), p0 = pos0 + c0;
+        FENCE_CUDA_TRY(cudaMemcpyAsync(m->pf_tok, tokens + c0, (size_t)P * 4, cudaMemcpyHostToDevice, st));
+        FENCE_CUDA_TRY(cudaStreamSynchronize(st));  // the host ids may be reused by the caller
+        embed_rows_kernel<<<P, 256, 0, st>>>(m->tok_embd, m->pf_tok, H, m->pf_hidden);
+        for (int l = 0; l < c.n_layers; ++l) {
+            const LayerLaunch& L = m->launches[l];
+            const LayerW& w = m->layers[l];
+            rmsnorm_rows_kernel<<<P, 256, 0, st>>>(m->pf_hidden, w.attn_norm, H, c.rms_eps, m->pf_x16);
+            TGArgs a{};
+            a.C = m->pf_qkv;
+            a.ldc = QKVR;
+            a.bias = L.qkv.a.bias;
+            if (const int rc = prefill_linear<TG_EPI_STORE>(m, L.qkv, m->pf_x16, P, a)) return rc;
+            uint8_t* kc = static_cast<uint8_t*>(m->kcache) + (size_t)l * kv_layer * 2;
+            uint8_t* vc = static_cast<uint8_t*>(m->vcache) + (size_t)l * kv_layer * 2;
+            if (c.kv_dtype == FENCE_KV_BF16) {
+                auto* k16 = reinterpret_cast<__nv_bfloat16*>(kc);
+                auto* v16 = reinterpret_cast<__nv_bfloat16*>(vc);
+                prefill_qk_kernel<__nv_bfloat16><<<P, 128, 0, st>>>(m->pf_qkv, QKVR, Hq, Hkv, w.q_norm, w.k_norm,
+                                                                    c.rms_eps, m->rope, p0, m->pf_q, k16, v16, stride_h,
+                                                                    SK_ATT_RSTR);
+                prefill_attn_kernel<__nv_bfloat16><<<dim3(P, Hkv), PA_THREADS, 0, st>>>(m->pf_q, Hq, Hkv, k16, v16,
+                                                                                       stride_h, SK_ATT_RSTR, p0, m->pf_attn);
+            } else {
+                auto* k16 = reinterpret_cast<__half*>(kc);
+                auto* v16 = reinterpret_cast<__half*>(vc);
+                prefill_qk_kernel<__half><<<P, 128, 0, st>>>(m->pf_qkv, QKVR, Hq, Hkv, w.q_norm, w.k_norm, c.rms_eps,
+                                                             m->rope, p0, m->pf_q, k16, v16, stride_h, SK_ATT_RSTR);
+                prefill_attn_kernel<__half><<<dim3(P, Hkv), PA_THREADS, 0, st>>>(m->pf_q, Hq, Hkv, k16, v16, stride_h,
+                                                                                SK_ATT_RSTR, p0, m->pf_attn);
+            }
+            f32_to_f16_rows_kernel<<<592, 256, 0, st>>>(m->pf_attn, (long long)P * qd, m->pf_x16);
+            a = TGArgs{};
+            a.C = m->pf_hidden;
+            a.ldc = H;
+            if (const int rc = prefill_linear<TG_EPI_ADD>(m, L.o, m->pf_x16, P, a)) return rc;
+            rmsnorm_rows_kernel<<<P, 256, 0, st>>>(m->pf_hidden, w.ffn_norm, H, c.rms_eps, m->pf_x16);
+            a = TGArgs{};
+            a.H = m->pf_act;
+            a.ldh = F;
+            if (const int rc = prefill_linear<TG_EPI_SWIGLU>(m, L.gu, m->pf_x16, P, a)) return rc;
+            a = TGArgs{};
+            a.C = m->pf_hidden;
+            a.ldc = H;
+            if (const int rc = prefill_linear<TG_EPI_ADD>(m, L.down, m->pf_act, P, a)) return rc;
+        }
+        FENCE_CUDA_TRY(cudaGetLastError());
+    }
+    return FENCE_OK;
+}
+
+}  // namespace
+
+extern "C" const float* fence_prefill(fence_model* m, const int* tokens, int n, int pos0) {
+    if (!m || !tokens || n <= 0 || pos0 < 0 || pos0 + n > (m ? m->cfg.max_ctx : 0)) {
+        set_error(FENCE_E_ARG, "prefill: bad arguments (n=%d pos0=%d)", n, pos0);
+        return nullptr;
+    }
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->cfg.vocab_size) {
+            set_error(FENCE_E_ARG, "prefill: token %d out of range", tokens[i]);
+            return nullptr;
+        }
+    cudaSetDevice(m->dev);
+    if (m->prefill_ok && n > 1) {
+        if (prefill_batched(m, tokens, n - 1, pos0) != FENCE_OK) return nullptr;
+    } else {
+        for (int i = 0; i + 1 < n; ++i)
+            if (!fence_forward(m, tokens[i], pos0 + i)) return nullptr;
+    }
+    return fence_forward(m, tokens[n - 1], pos0 + n - 1);  // the last token through the decode step: its logits
+}
+
 extern "C" int fence_sample_greedy(fence_model* m, const float* d_logits) {
     if (!m || !d_logits) return set_error(FENCE_E_ARG, "sample_greedy: null argument");
     cudaSetDevice(m->dev);
@@ -1208,9 +1517,17 @@ extern "C" int fence_generate(fence_model* m, const int* prompt, int n_prompt, i
     cudaSetDevice(m->dev);
     m->fwd_valid = 0;
     std::vector<int> output(prompt, prompt + n_prompt);
-    // prefill, token by token as in the reference (qwen3.cu:478-481); no host sync between tokens
-    for (int i = 0; i < n_prompt; ++i) {
+    for (int i = 0; i < n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= m->cfg.vocab_size) return set_error(FENCE_E_ARG, "generate: prompt id out of range");
+    // prefill: all but the last prompt token batched on the tensor cores where the model allows it,
+    // else token by token as in the reference (qwen3.cu:478-481); the last one through the decode
+    // step, which leaves its logits; no host sync between tokens
+    int first = 0;
+    if (m->prefill_ok && n_prompt > 1) {
+        if (const int rc = prefill_batched(m, prompt, n_prompt - 1, 0)) return rc;
+        first = n_prompt - 1;
+    }
+    for (int i = first; i < n_prompt; ++i) {
         int rc = set_state(m, prompt[i], i, 0);
         if (!rc) rc = run_step(m);
         if (rc) return rc;

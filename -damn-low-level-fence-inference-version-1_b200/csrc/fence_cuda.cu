@@ -6,4 +6,5 @@
 #include "ops.cu"
 #include "attention_static.cu"
 #include "sampler_dev.cu"
+#include "prefill.cu"
 #include "engine.cu"

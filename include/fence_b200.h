@@ -234,10 +234,15 @@ typedef struct fence_load_opts {
      * [r * E / tp_size, (r + 1) * E / tp_size) whole (only the ranks holding a routed expert
      * stream). Ignored for dense models and one rank. */
     int moe_ep;
+    /* 1 (default): keep the repacked row-major weights next to the step kernel's tiles so that
+     * fence_prefill / fence_generate run the prompt as batched tensor-core GEMMs (one rank, dense
+     * FFN; about the model's weight bytes again in device memory); 0: free them (prefill token by
+     * token, as the reference does). */
+    int prefill;
 } fence_load_opts;
 
 /* Fills *opts with defaults (max_ctx 4096, fp16 KV, device 0, graphs on, single rank, step kernel,
- * wait_test_phase -1, moe_ep 0). */
+ * wait_test_phase -1, moe_ep 0, prefill 1). */
 void fence_load_opts_default(fence_load_opts* opts);
 
 /* Qwen3Model::load (src/model/qwen3.cu:116-228): mmap the GGUF, read the config from its metadata
@@ -254,6 +259,12 @@ int  fence_set_sampling(fence_model* m, float temperature, float top_p, int top_
 /* Qwen3Model::forward (qwen3.cu:241-265): one token at position pos; returns the DEVICE pointer
  * of the fp32 logits [vocab] (valid until the next forward), NULL on error. */
 const float* fence_forward(fence_model* m, int token_id, int pos);
+/* The prefill loop of Qwen3Model::generate (qwen3.cu:478-481: forward(prompt[i], i) per token) for
+ * tokens[0 .. n) at positions pos0 .. pos0 + n - 1: the same K/V cache rows and, for the last token,
+ * the same logits (device pointer returned, as fence_forward). With opts.prefill on one rank and a
+ * dense FFN, all tokens but the last run as batched fp16 tensor-core GEMMs (weights dequantised per
+ * layer; logits within the decode path's tolerance, not bit-identical); otherwise token by token. */
+const float* fence_prefill(fence_model* m, const int* tokens, int n, int pos0);
 /* Qwen3Model::sample_greedy (qwen3.cu:344-349): argmax of device logits, reference tie order. */
 int fence_sample_greedy(fence_model* m, const float* d_logits);
 /* Qwen3Model::sample_nucleus (qwen3.cu:351-460): repetition penalty per occurrence in history,
@@ -297,6 +308,12 @@ int fence_copy_logits(fence_model* m, float* host_out);
 #define FENCE_TP_HANDLE_BYTES 64
 int fence_tp_handle(fence_model* m, void* out, int cap);
 int fence_tp_connect(fence_model* m, const void* handles, int n_ranks);
+
+/* No counterpart in the reference: the batched prefill's tensor-core GEMM on its own (tcgen05, fp32
+ * accumulators in tensor memory): C[P][N] = A[P][K] . B[N][K]^T for fp16 row-major A and B
+ * (16-byte aligned), fp32 row-major C, K % 64 == 0; asynchronous on the stream. */
+int fence_gemm_f16(const uint16_t* A, const uint16_t* B, float* C, int P, int N, int K,
+                   fence_stream_t stream);
 
 /* Times n_steps device-resident decode steps with CUDA events on the engine's stream; *ms = total. */
 int fence_time_decode(fence_model* m, int token, int pos, int n_steps, float* ms);
