@@ -217,12 +217,82 @@ extern "C" int fence_set_launch_flags(int flags) {
     return old;
 }
 
+// Plan of the register-resident Q6_K GEMV (gemv_q6k_reg_kernel): rows of 16-byte multiple length
+// (K % 2048 == 0), K <= 4096 (one 64-element item per lane), rows split over one CTA per SM, each
+// CTA's rows in up to 4 chunk slots that fit half an SM's shared memory (so the next GEMV's CTA sits
+// beside it and loads its weights early); ok = 0 otherwise.
+struct GQPlan {
+    int ok = 0, grid = 0, rows_cta = 0, RC = 0, slots = 0, slot_bytes = 0, smem = 0;
+};
+static GQPlan plan_q6k_reg(int M, int K) {
+    GQPlan p;
+    if (K <= 0 || K > 4096 || K % 2048 || M <= 0) return p;
+    const int I = K / 64, rowB = K / 256 * 210;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = device_sms(dev);
+    p.rows_cta = (M + sms - 1) / sms;
+    p.grid = (M + p.rows_cta - 1) / p.rows_cta;
+    const int budget = std::min(device_smem_optin(dev) - 1024, 112 * 1024);
+    const int fixed = I * XQ_WORDS * 4 + (2 * p.rows_cta + 2) * 4 + 8 + 2 * GQ_MAX_SLOTS * 8 + 16 + 64;
+    const int avail = budget - fixed;
+    if (avail < 4 * rowB) return p;
+    p.RC = std::max(1, std::min((p.rows_cta + 3) / 4, avail / 4 / rowB));
+    p.slots = std::min(4, (p.rows_cta + p.RC - 1) / p.RC);
+    p.slot_bytes = (p.RC * rowB + 127) / 128 * 128;
+    p.smem = p.slots * p.slot_bytes + fixed;
+    if (p.smem > budget) return p;
+    p.ok = 1;
+    return p;
+}
+
+static cudaError_t launch_q6k_reg(const GQArgs& a, const GQPlan& pl, cudaStream_t st, bool pdl) {
+    static int attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(gemv_q6k_reg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(GQ_NT);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_q6k_reg_kernel, a);
+}
+
 // ------------------------------------------------------------------ drop-in entries
 static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* bias, float* y,
                            int M, int K, cudaStream_t st) {
     if (!W || !x || !y || M <= 0 || K <= 0 || K % 256 != 0)
         return set_error(FENCE_E_ARG, "gemv_q6k: need non-null pointers, M > 0, K %% 256 == 0 (M=%d K=%d)", M, K);
     const bool aligned = (reinterpret_cast<uintptr_t>(W) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const GQPlan gq = plan_q6k_reg(M, K);
+    if (aligned && gq.ok) {
+        GQArgs a{};
+        a.W = reinterpret_cast<const uint8_t*>(W);
+        a.x = x;
+        a.bias = bias;
+        a.y = y;
+        a.M = M;
+        a.K = K;
+        a.I = K / 64;
+        a.rowB = K / 256 * 210;
+        a.rows_cta = gq.rows_cta;
+        a.RC = gq.RC;
+        a.slots = gq.slots;
+        a.slot_bytes = gq.slot_bytes;
+        return cuda_status(launch_q6k_reg(a, gq, st, (g_launch_flags & FENCE_LAUNCH_PDL) != 0), "gemv_q6k launch");
+    }
     GemvPlan pl = plan_gemv(WT_Q6K, K, M, 0, 0);
     cudaError_t e;
     if (aligned && pl.ok) {

@@ -800,6 +800,178 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
 }
 
 // --------------------------------------------------------------------------------------------
+// Register-resident Q6_K GEMV for the drop-in gemv_q6k (fp16 x, plain store, optional bias) when a
+// CTA's rows fit its shared memory in chunk slots and K <= 4096: lane <-> item. Each CTA owns
+// consecutive rows; its producer lane issues every chunk of rows (1-D bulk copies on mbarriers)
+// before griddepcontrol.wait, so under programmatic dependent launch the whole CTA's weights load
+// while the previous kernel runs. After the wait, the x prologue quantises each 64-element item
+// with 8 threads (one 16-byte load of fp16 x each; the item's max by shuffles) into shared-memory
+// records; every consumer lane then keeps ITS item's record in registers for all rows. A row is
+// worked on by LPR lanes (one item each: 64 lanes for K > 2048, else 32), so a row costs one item
+// dot per lane and one shuffle reduction per warp, with no x reloads; the two warps' pieces of a
+// row are summed in a fixed order at the end (deterministic). Consumer warps: GQ_NW.
+constexpr int GQ_NW = 12;
+constexpr int GQ_NT = GQ_NW * 32 + 32;
+constexpr int GQ_MAX_SLOTS = 8;
+
+struct GQArgs {
+    const uint8_t* W;  // 16-byte aligned, rows of rowB bytes (rowB % 16 == 0)
+    const uint16_t* x;
+    const float* bias;
+    float* y;
+    int M, K, I, rowB;
+    int rows_cta;      // rows of the first CTAs (the last may have fewer)
+    int RC, slots;     // rows per chunk, chunk slots
+    int slot_bytes;
+};
+
+__host__ __device__ inline uint32_t gq_xrec_off(int slots, int slot_bytes) { return (uint32_t)(slots * slot_bytes); }
+
+__global__ void __launch_bounds__(GQ_NT, 2) gemv_q6k_reg_kernel(const __grid_constant__ GQArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NTC = GQ_NW * 32;
+    const int I = a.I;
+    const int r0 = blockIdx.x * a.rows_cta;
+    const int rows = max(0, min(a.rows_cta, a.M - r0));
+    const int nch = (rows + a.RC - 1) / a.RC;
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t xq_sa = sbase + gq_xrec_off(a.slots, a.slot_bytes);
+    float* part = reinterpret_cast<float*>(smem + gq_xrec_off(a.slots, a.slot_bytes) + I * XQ_WORDS * 4);  // [rows][2]
+    uint64_t* full = reinterpret_cast<uint64_t*>(part + 2 * a.rows_cta + 2);
+    full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(full) + 7) & ~uintptr_t(7));
+    uint64_t* empty = full + GQ_MAX_SLOTS;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + GQ_MAX_SLOTS);
+    if (tid == 0) {
+        for (int s = 0; s < a.slots; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], GQ_NW);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (tid == 0) pdl_launch_dependents();
+
+    if (warp == GQ_NW) {
+        // ---- producer lane: every chunk of this CTA's rows (weights never depend on the previous kernel)
+        if (lane == 0) {
+            for (int i = 0; i < nch; ++i) {
+                const int slot = i % a.slots;
+                if (i >= a.slots) {
+                    bool ok = mbar_try_wait(&empty[slot], ((i / a.slots) - 1) & 1);
+                    for (uint32_t it = 0; !ok && it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                        ok = mbar_try_wait(&empty[slot], ((i / a.slots) - 1) & 1);
+                    if (!ok) {
+                        if (!*abort_flag) set_device_error(-5);
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+                const int n = min(a.RC, rows - i * a.RC);
+                const uint32_t bytes = (uint32_t)n * (uint32_t)a.rowB;
+                mbar_arrive_expect_tx(&full[slot], bytes);
+                bulk_g2s(smem + (size_t)slot * a.slot_bytes, a.W + (size_t)(r0 + i * a.RC) * a.rowB, bytes, &full[slot]);
+            }
+        }
+        return;
+    }
+
+    // ---- consumers
+    pdl_wait();  // x and y belong to the stream's previous work
+    // x prologue: task t = (item, run c, half): 8 consecutive fp16 of run c of the item
+    for (int t0 = 0; t0 < I * 8; t0 += NTC) {
+        const int t = t0 + tid;
+        const bool on = t < I * 8;
+        const int item = on ? t >> 3 : 0, c = (t >> 1) & 3, hh = t & 1;
+        const int b = item >> 2, h = (item >> 1) & 1, l16 = item & 1;
+        const int base = b * 256 + h * 128 + c * 32 + l16 * 16 + hh * 8;
+        float v[8];
+        if (on) {
+            const uint4 u = *reinterpret_cast<const uint4*>(a.x + base);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[2 * k] = half_bits_to_float(w[k]);
+                v[2 * k + 1] = half_bits_to_float(w[k] >> 16);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = 0.f;
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(v[k]));
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));  // the item's 8 tasks
+        float inv;
+        const float xs = quant_scale(amax, inv);
+        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+        int sum = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int q = __float2int_rn(v[k] * inv);
+            sum += q;
+            uint32_t hb, lb;
+            split16(q, hb, lb);
+            hw[k >> 2] |= hb << (8 * (k & 3));
+            lw[k >> 2] |= lb << (8 * (k & 3));
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);  // the run's two halves
+        if (on) {
+            const uint32_t rec = xq_sa + (uint32_t)item * XQ_WORDS * 4;
+            const int wi = c * 4 + hh * 2;  // XSlice word index of the first of this task's two words
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(rec + wi * 4), "r"(hw[0]), "r"(hw[1]) : "memory");
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(rec + (16 + wi) * 4), "r"(lw[0]), "r"(lw[1]) : "memory");
+            if (hh == 0) asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + (32 + c) * 4), "r"(-32 * sum) : "memory");
+            if (hh == 0 && c == 0) {
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 36 * 4), "r"(__float_as_uint(xs)) : "memory");
+                asm volatile("st.shared.b32 [%0], %1;" ::"r"(rec + 37 * 4), "r"(0u) : "memory");
+            }
+        }
+    }
+    named_bar_sync(1, NTC);
+
+    const int LPR = I > 32 ? 64 : 32, WPG = LPR / 32, NG = GQ_NW / WPG;
+    const int g = warp / WPG, item = (warp % WPG) * 32 + lane;
+    const bool has_item = item < I;
+    XSlice<WT_Q6K> xs;
+    load_slice<WT_Q6K>(xq_sa + (uint32_t)(has_item ? item : 0) * XQ_WORDS * 4, xs);
+    const uint32_t ioff = (uint32_t)(item >> 2) * 210u;
+    for (int i = 0; i < nch; ++i) {
+        const int slot = i % a.slots;
+        bool ok = mbar_try_wait(&full[slot], (i / a.slots) & 1);
+        if (!ok && !*abort_flag) {
+            for (uint32_t it = 0; it < FENCE_WAIT_ROUNDS && !*abort_flag; ++it)
+                if (mbar_try_wait(&full[slot], (i / a.slots) & 1)) { ok = true; break; }
+            if (!ok) {
+                if (!*abort_flag) set_device_error(-5);
+                *abort_flag = 1;
+            }
+        }
+        const int n = min(a.RC, rows - i * a.RC);
+        if (ok) {
+            const uint32_t cb = sbase + (uint32_t)slot * a.slot_bytes;
+            for (int rr = g; rr < n; rr += NG) {
+                float d = has_item ? item_dot<WT_Q6K>(cb + (uint32_t)rr * a.rowB + ioff, item, xs) : 0.f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                if (lane == 0) part[(i * a.RC + rr) * 2 + (warp % WPG)] = d;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    named_bar_sync(1, NTC);
+    if (*abort_flag) return;
+    for (int r = tid; r < rows; r += NTC) {
+        float v = part[r * 2] + (WPG > 1 ? part[r * 2 + 1] : 0.f);
+        if (a.bias) v += a.bias[r0 + r];
+        a.y[r0 + r] = v;
+    }
+}
+
+// --------------------------------------------------------------------------------------------
 // Simple kernels for shapes the streaming kernel does not take (K % 64 != 0 for Q8_0, huge K,
 // misaligned weights): one warp per row, fp32 accumulation in the reference's per-lane order.
 __global__ void gemv_q6k_simple_kernel(const uint8_t* __restrict__ W, const uint16_t* __restrict__ x,
