@@ -41,9 +41,7 @@ unsigned long long sk_tile_plan(int wt, int I, int Mv, int dual, int G, int RB, 
 cudaError_t sk_retile(int wt, const RMat& m, int I, int Mv, int dual, int G, int RB, int CI,
                       const unsigned long long* d_tcta, uint8_t* dst, cudaStream_t st);
 cudaError_t rgemv_dispatch(int xm, int epi, const RGemvArgs& a, const RGemvPlan& P, cudaStream_t st);
-struct TGArgs;
-template <int EPI>
-cudaError_t launch_tc_gemm(const TGArgs& a, cudaStream_t st);
+
 cudaError_t launch_dequant(int wt, const RMat& m, int rows, int I, __half* W, float* bscale, cudaStream_t st);
 int host_sample_nucleus(const float* logits, int vocab, const int* history, int n_history, float temperature,
                         float top_p, int top_k, float rep_penalty, float min_p, bool dynamic_temp,
@@ -1387,13 +1385,11 @@ template <int EPI>
 int prefill_linear(fence_model* m, const RPhase& r, const __half* A, int P, TGArgs a) {
     const int rows = r.a.Mv * (r.a.dual ? 2 : 1);
     FENCE_CUDA_TRY(launch_dequant(r.a.wt, r.a.w, rows, r.a.I, m->pf_w, m->pf_bscale, m->stream));
-    a.A = A;
-    a.B = m->pf_w;
     a.bscale = m->pf_bscale;
     a.P = P;
     a.N = rows;
     a.K = r.a.I * 64;
-    FENCE_CUDA_TRY(launch_tc_gemm<EPI>(a, m->stream));
+    FENCE_CUDA_TRY(launch_tc_gemm<EPI>(a, A, m->pf_w, m->stream));
     return FENCE_OK;
 }
 
@@ -1430,15 +1426,15 @@ int prefill_batched(fence_model* m, const int* tokens, int n, int pos0) {
                 prefill_qk_kernel<__nv_bfloat16><<<P, 128, 0, st>>>(m->pf_qkv, QKVR, Hq, Hkv, w.q_norm, w.k_norm,
                                                                     c.rms_eps, m->rope, p0, m->pf_q, k16, v16, stride_h,
                                                                     SK_ATT_RSTR);
-                prefill_attn_kernel<__nv_bfloat16><<<dim3(P, Hkv), PA_THREADS, 0, st>>>(m->pf_q, Hq, Hkv, k16, v16,
-                                                                                       stride_h, SK_ATT_RSTR, p0, m->pf_attn);
+                FENCE_CUDA_TRY(launch_prefill_attn<__nv_bfloat16>(m->pf_q, Hq, Hkv, k16, v16, stride_h, SK_ATT_RSTR, p0, P,
+                                                                  m->pf_attn, st));
             } else {
                 auto* k16 = reinterpret_cast<__half*>(kc);
                 auto* v16 = reinterpret_cast<__half*>(vc);
                 prefill_qk_kernel<__half><<<P, 128, 0, st>>>(m->pf_qkv, QKVR, Hq, Hkv, w.q_norm, w.k_norm, c.rms_eps,
                                                              m->rope, p0, m->pf_q, k16, v16, stride_h, SK_ATT_RSTR);
-                prefill_attn_kernel<__half><<<dim3(P, Hkv), PA_THREADS, 0, st>>>(m->pf_q, Hq, Hkv, k16, v16, stride_h,
-                                                                                SK_ATT_RSTR, p0, m->pf_attn);
+                FENCE_CUDA_TRY(launch_prefill_attn<__half>(m->pf_q, Hq, Hkv, k16, v16, stride_h, SK_ATT_RSTR, p0, P,
+                                                           m->pf_attn, st));
             }
             f32_to_f16_rows_kernel<<<592, 256, 0, st>>>(m->pf_attn, (long long)P * qd, m->pf_x16);
             a = TGArgs{};

@@ -14,11 +14,15 @@
 //
 // tc_gemm_kernel: C[P x N] = A[P x K] . B[N x K]^T, A and B fp16 row-major (K-major operands), fp32
 // accumulation in tensor memory. CTA tile 128 x 256, K steps of 64 through a 4-stage shared-memory
-// ring filled by cp.async (16-byte chunks into the no-swizzle canonical layout: 8-row x 16-byte core
-// matrices, 128 bytes apart along K and 1024 bytes apart along M/N); one thread issues four
-// tcgen05.mma (M128 N256 K16) per stage and commits them to the stage's mbarrier; the loaders wait on
-// it before refilling that stage, after the next stage's MMAs are already queued. Epilogue: each warp reads its 32 accumulator lanes (rows)
-// with tcgen05.ld, 32 columns at a time.
+// ring. Warp-specialised: one lane loads each stage's A and B tiles with two TMA tensor copies
+// (cp.async.bulk.tensor.2d, 128-byte swizzle, no multicast) completing on the stage's "full"
+// mbarrier; one lane issues the stage's four tcgen05.mma (M128 N256 K16, operands described by
+// 128-byte-swizzle K-major shared-memory descriptors) and commits them to the stage's "empty"
+// mbarrier, which the loading lane waits on before refilling the stage; the last commit signals the
+// epilogue. Epilogue: each warp reads its 32 accumulator lanes (rows) with tcgen05.ld, 32 columns at
+// a time.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include "attention.cuh"
@@ -33,14 +37,14 @@ constexpr int TG_BM = 128, TG_BN = 256, TG_BK = 64, TG_STAGES = 4, TG_THREADS = 
 constexpr int TG_A_BYTES = TG_BM * TG_BK * 2;
 constexpr int TG_B_BYTES = TG_BN * TG_BK * 2;
 constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
-constexpr int TG_SMEM = TG_STAGES * TG_STAGE_BYTES + 128;  // + mbarriers and the tensor-memory address
+constexpr int TG_SMEM = TG_STAGES * TG_STAGE_BYTES + 1024 + 256;  // + 1024-byte alignment slack, barriers
 constexpr uint32_t TG_TMEM_COLS = 256;
 
 enum : int { TG_EPI_STORE = 0, TG_EPI_ADD = 1, TG_EPI_SWIGLU = 2 };
 
 struct TGArgs {
-    const __half* A;      // [P][K]
-    const __half* B;      // [N][K]
+    CUtensorMap tmA;      // A [P][K] fp16, box 64 x 128, 128-byte swizzle
+    CUtensorMap tmB;      // B [N][K] fp16, box 64 x 256, 128-byte swizzle
     const float* bscale;  // [N] multiplies column n of the product (undoes the weight row scaling); null = 1
     int P, N, K;
     float* C;             // STORE / ADD: [P][ldc]
@@ -50,32 +54,23 @@ struct TGArgs {
     int ldh;
 };
 
-// 64-bit shared-memory matrix descriptor (no swizzle, K-major): start address, leading-dimension
-// byte offset (between core matrices along K), stride-dimension byte offset (between 8-row groups),
-// descriptor version 1.
-__device__ __forceinline__ uint64_t tg_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+// 64-bit shared-memory matrix descriptor, K-major with 128-byte swizzle: start address, leading-
+// dimension byte offset (unused for this layout: 16), stride-dimension byte offset 1024 (8 rows of
+// 128 bytes), descriptor version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t tg_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
 }
 // Instruction descriptor, kind::f16: fp32 accumulator, A and B fp16, both K-major, N, M.
 __host__ __device__ constexpr uint32_t tg_idesc(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// One stage's operand tiles: chunk (row, k8) of an R-row tile goes to core matrix (row / 8, k8) at
-// ((row / 8) * 8 + k8) * 128 + (row % 8) * 16. Rows past `rows` are zero-filled.
-__device__ __forceinline__ void tg_load_tile(uint32_t sbase, const __half* g, int ld, int row0, int rows, int k0,
-                                             int R) {
-    const int n = R * 8;
-    for (int c = threadIdx.x; c < n; c += TG_THREADS) {
-        const int rr = c & 7, kc = (c >> 3) & 7, grp = c >> 6;
-        const int row = grp * 8 + rr;
-        const uint32_t dst = sbase + (uint32_t)((grp * 8 + kc) * 128 + rr * 16);
-        const bool ok = row0 + row < rows;
-        const __half* src = ok ? g + (size_t)(row0 + row) * ld + k0 + kc * 8 : g;
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0)
-                     : "memory");
-    }
+__device__ __forceinline__ void tg_tma_load(uint32_t dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 __device__ __forceinline__ float tg_silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
@@ -85,14 +80,25 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_con
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int p0 = blockIdx.x * TG_BM, n0 = blockIdx.y * TG_BN;
-    const uint32_t sbase = smem_u32(smem);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TG_STAGES * TG_STAGE_BYTES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TG_STAGES);
+    // 1024-byte aligned tiles (the 128-byte swizzle pattern repeats every 8 rows of 128 bytes)
+    const uint32_t sraw = smem_u32(smem);
+    const uint32_t sbase = (sraw + 1023u) & ~1023u;
+    uint8_t* bar_area = smem + (sbase - sraw) + TG_STAGES * TG_STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+    uint64_t* empty = full + TG_STAGES;
+    uint64_t* done = empty + TG_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     if (tid == 0) {
-        for (int s = 0; s < TG_STAGES; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < TG_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
         fence_barrier_init();
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&a.tmB)) : "memory");
     }
-    if (warp == 0) {
+    if (warp == 2) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TG_TMEM_COLS)
                      : "memory");
@@ -102,30 +108,35 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_con
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
-
     const int nk = a.K / TG_BK;
-    constexpr uint32_t idesc = tg_idesc(TG_BM, TG_BN);
     bool ok = true;
-    for (int s = 0; s < TG_STAGES - 1; ++s) {
-        if (s < nk) {
-            const uint32_t st = sbase + (uint32_t)(s * TG_STAGE_BYTES);
-            tg_load_tile(st, a.A, a.K, p0, a.P, s * TG_BK, TG_BM);
-            tg_load_tile(st + TG_A_BYTES, a.B, a.K, n0, a.N, s * TG_BK, TG_BN);
-        }
-        cp_async_commit();
-    }
-    for (int kt = 0; kt < nk; ++kt) {
-        cp_async_wait_group<TG_STAGES - 2>();                      // k-tile kt has landed (this thread's part)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer: k-tile kt into stage kt % STAGES once that stage's previous MMAs are done
+        for (int kt = 0; kt < nk && ok; ++kt) {
             const int s = kt % TG_STAGES;
+            if (kt >= TG_STAGES && !mbar_wait(&empty[s], (uint32_t)((kt / TG_STAGES) - 1) & 1u)) ok = false;
+            if (!ok) break;
+            const uint32_t st = sbase + (uint32_t)(s * TG_STAGE_BYTES);
+            mbar_arrive_expect_tx(&full[s], (uint32_t)TG_STAGE_BYTES);
+            tg_tma_load(st, &a.tmA, kt * TG_BK, p0, &full[s]);
+            tg_tma_load(st + TG_A_BYTES, &a.tmB, kt * TG_BK, n0, &full[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = tg_idesc(TG_BM, TG_BN);
+        for (int kt = 0; kt < nk && ok; ++kt) {
+            const int s = kt % TG_STAGES;
+            if (!mbar_wait(&full[s], (uint32_t)(kt / TG_STAGES) & 1u)) {
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t sa = sbase + (uint32_t)(s * TG_STAGE_BYTES), sb = sa + TG_A_BYTES;
 #pragma unroll
-            for (int t = 0; t < TG_BK / 16; ++t) {
-                const uint64_t da = tg_desc(sa + (uint32_t)t * 256u, 128u, 1024u);
-                const uint64_t db = tg_desc(sb + (uint32_t)t * 256u, 128u, 1024u);
+            for (int t = 0; t < TG_BK / 16; ++t) {  // K = 16 per MMA: 32 bytes further along the swizzled rows
+                const uint64_t da = tg_desc(sa + (uint32_t)t * 32u);
+                const uint64_t db = tg_desc(sb + (uint32_t)t * 32u);
                 const uint32_t acc = (kt > 0 || t > 0) ? 1u : 0u;
                 asm volatile(
                     "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -134,24 +145,15 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_con
                     : "memory");
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             smem_u32(&bars[s]))
+                             smem_u32(&empty[s]))
                          : "memory");
         }
-        // refill the stage of k-tile kt - 1 with k-tile kt + STAGES - 1 once its MMAs are done (they
-        // ran while k-tile kt's were queued behind them)
-        const int kn = kt + TG_STAGES - 1;
-        if (kn < nk) {
-            const int sn = kn % TG_STAGES;
-            if (kt >= 1 && !mbar_wait(&bars[sn], (uint32_t)((kt - 1) / TG_STAGES) & 1u)) ok = false;
-            const uint32_t st = sbase + (uint32_t)(sn * TG_STAGE_BYTES);
-            tg_load_tile(st, a.A, a.K, p0, a.P, kn * TG_BK, TG_BM);
-            tg_load_tile(st + TG_A_BYTES, a.B, a.K, n0, a.N, kn * TG_BK, TG_BN);
-        }
-        cp_async_commit();
+        // every MMA issued so far completes before this arrival
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(done))
+                     : "memory");
     }
-    cp_async_wait_all();
-    // every MMA of the tile is complete once the last stage's commit has arrived
-    if (nk > 0 && !mbar_wait(&bars[(nk - 1) % TG_STAGES], (uint32_t)((nk - 1) / TG_STAGES) & 1u)) ok = false;
+    __syncwarp();
+    if (!mbar_wait(done, 0u)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     // ---- epilogue: warp w holds rows p0 + 32 w + lane, 32 columns per tensor-memory load
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_con
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0)
+    if (warp == 2)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TG_TMEM_COLS) : "memory");
 }
 
@@ -364,87 +366,244 @@ __global__ void prefill_qk_kernel(const float* __restrict__ qkv, int ldqkv, int 
     }
 }
 
-// Causal GQA attention of the chunk's tokens over the cache (gqa_attention, ops.cuh:320-403): CTA
-// (token p, KV head h) computes its G query heads over positions 0 .. pos0 + p in 64-position tiles
-// with an online softmax (fp32; K and V as cached).
-constexpr int PA_THREADS = 128, PA_TILE = 64;
+// Causal GQA attention of the chunk's tokens over the cache (gqa_attention, ops.cuh:320-403) as
+// flash-attention tiles on the tensor cores (mma.sync m16n8k16, fp32 accumulators): CTA (block of
+// 64 query positions, query head), 4 warps of 16 query rows; 64-key K / V tiles double-buffered in
+// shared memory (cp.async, rows padded to 136 elements as in the cache, so fragment loads are
+// conflict-free); online softmax per row in registers. Precision: q and the softmax weights P are
+// split into a cache-type high part and its remainder, two products summed (~22 bits for fp16,
+// ~16 for bf16) while K and V enter exactly as cached — the decode step's attention numerics.
+constexpr int FA_BQ = 64, FA_BK = 64, FA_THREADS = 128, FA_RS = 136;
+
 template <typename KVT>
-__global__ void __launch_bounds__(PA_THREADS) prefill_attn_kernel(const float* __restrict__ q, int Hq, int Hkv,
-                                                                   const KVT* __restrict__ kc, const KVT* __restrict__ vc,
-                                                                   long long stride_h, int stride_t, int pos0,
-                                                                   float* __restrict__ out) {
-    using C = KVConv<KVT>;
-    constexpr int HD = 128;
-    __shared__ float sq[8][HD];
-    __shared__ float skv[PA_TILE][HD + 1];
-    __shared__ float sp[8][PA_TILE];
-    __shared__ float sm[8], sl[8], sc[8];
-    const int p = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int G = Hq / Hkv, seq = pos0 + p + 1;
-    const float scale = rsqrtf((float)HD);
-    for (int i = tid; i < G * HD; i += PA_THREADS) sq[i / HD][i % HD] = q[((size_t)p * Hq + h * G) * HD + i];
-    if (tid < G) {
-        sm[tid] = -INFINITY;
-        sl[tid] = 0.f;
+struct FAMma;
+template <>
+struct FAMma<__half> {
+    static __device__ __forceinline__ uint32_t pack(float x, float y) {
+        const __half2 h = __floats2half2_rn(x, y);
+        return *reinterpret_cast<const uint32_t*>(&h);
     }
-    float acc[8];
-#pragma unroll
-    for (int g = 0; g < 8; ++g) acc[g] = 0.f;
+    static __device__ __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+    static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+template <>
+struct FAMma<__nv_bfloat16> {
+    static __device__ __forceinline__ uint32_t pack(float x, float y) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+    static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+template <typename KVT>
+__global__ void __launch_bounds__(FA_THREADS) prefill_flash_kernel(const float* __restrict__ q, int Hq, int Hkv,
+                                                                    const KVT* __restrict__ kc, const KVT* __restrict__ vc,
+                                                                    long long stride_h, int stride_t, int pos0, int P,
+                                                                    float* __restrict__ out) {
+    using MM = FAMma<KVT>;
+    constexpr int HD = 128;
+    extern __shared__ __align__(128) uint8_t smem[];
+    KVT(*sk)[FA_BK * FA_RS] = reinterpret_cast<KVT(*)[FA_BK * FA_RS]>(smem);  // [2] K tiles
+    KVT(*sv)[FA_BK * FA_RS] = sk + 2;                                          // [2] V tiles
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    const int hq = blockIdx.y, h = hq / (Hq / Hkv);
+    const int p_lo = blockIdx.x * FA_BQ, r0 = p_lo + warp * 16;
+    const int qpos_max = pos0 + min(p_lo + FA_BQ, P) - 1;
+    const int nkt = qpos_max / FA_BK + 1;
     const KVT* kb = kc + (size_t)h * stride_h;
     const KVT* vb = vc + (size_t)h * stride_h;
-    for (int t0 = 0; t0 < seq; t0 += PA_TILE) {
-        const int n = min(PA_TILE, seq - t0);
-        __syncthreads();  // q / softmax state ready; the previous tile's V reads are done
-        for (int i = tid; i < n * HD; i += PA_THREADS)
-            skv[i / HD][i % HD] = C::to(kb[(size_t)(t0 + i / HD) * stride_t + (i % HD)]);
-        __syncthreads();
-        for (int i = tid; i < G * PA_TILE; i += PA_THREADS) {
-            const int g = i / PA_TILE, j = i % PA_TILE;
-            float s = -INFINITY;
-            if (j < n) {
-                float d = 0.f;
-#pragma unroll 8
-                for (int k = 0; k < HD; ++k) d += sq[g][k] * skv[j][k];
-                s = d * scale;
-            }
-            sp[g][j] = s;
-        }
-        __syncthreads();
-        for (int g = warp; g < G; g += PA_THREADS / 32) {  // online softmax, a warp per head
-            const float a = sp[g][lane], b = sp[g][lane + 32];
-            const float mt = warp_max(fmaxf(a, b));
-            const float mo = sm[g], mn = fmaxf(mo, mt);
-            const float ea = expf(a - mn), eb = expf(b - mn);
-            sp[g][lane] = ea;
-            sp[g][lane + 32] = eb;
-            const float sum = warp_sum(ea + eb);
-            if (lane == 0) {
-                const float corr = mo == -INFINITY ? 0.f : expf(mo - mn);
-                sc[g] = corr;
-                sl[g] = sl[g] * corr + sum;
-                sm[g] = mn;
-            }
-        }
-        for (int i = tid; i < n * HD; i += PA_THREADS)  // V tile over the K tile (scores are done)
-            skv[i / HD][i % HD] = C::to(vb[(size_t)(t0 + i / HD) * stride_t + (i % HD)]);
-        __syncthreads();
+    const float scale = rsqrtf((float)HD);
+
+    // this warp's 16 query rows as A fragments, high part and remainder, 8 steps of 16 dims
+    uint32_t qa[8][4], qr[8][4];
+    {
+        const int ra = min(r0 + g, P - 1), rb = min(r0 + g + 8, P - 1);
+        const float* qa_row = q + ((size_t)ra * Hq + hq) * HD;
+        const float* qb_row = q + ((size_t)rb * Hq + hq) * HD;
 #pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            if (g < G) {
-                float o = acc[g] * sc[g];
-                for (int j = 0; j < n; ++j) o += sp[g][j] * skv[j][tid];
-                acc[g] = o;
+        for (int ks = 0; ks < 8; ++ks) {
+            const int c0 = ks * 16 + 2 * t;
+            const float2 x0 = *reinterpret_cast<const float2*>(qa_row + c0);
+            const float2 x1 = *reinterpret_cast<const float2*>(qb_row + c0);
+            const float2 x2 = *reinterpret_cast<const float2*>(qa_row + c0 + 8);
+            const float2 x3 = *reinterpret_cast<const float2*>(qb_row + c0 + 8);
+            const float2 xs[4] = {x0, x1, x2, x3};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                qa[ks][i] = MM::pack(xs[i].x, xs[i].y);
+                qr[ks][i] = MM::pack(xs[i].x - MM::round(xs[i].x), xs[i].y - MM::round(xs[i].y));
             }
         }
     }
+    float o[16][4];
 #pragma unroll
-    for (int g = 0; g < 8; ++g)
-        if (g < G) out[((size_t)p * Hq + h * G + g) * HD + tid] = acc[g] / sl[g];
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+    const int qpos[2] = {pos0 + r0 + g, pos0 + r0 + g + 8};
+
+    auto load_tile = [&](int kt, int buf) {  // keys past the block's last query are zero-filled
+        for (int c = tid; c < FA_BK * 16; c += FA_THREADS) {
+            const int row = c >> 4, ch = c & 15, key = kt * FA_BK + row;
+            const bool ok = key <= qpos_max;
+            const uint32_t dk = smem_u32(&sk[buf][row * FA_RS + ch * 8]);
+            const uint32_t dv = smem_u32(&sv[buf][row * FA_RS + ch * 8]);
+            const KVT* srck = ok ? kb + (size_t)key * stride_t + ch * 8 : kb;
+            const KVT* srcv = ok ? vb + (size_t)key * stride_t + ch * 8 : vb;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dk), "l"(srck), "r"(ok ? 16 : 0) : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dv), "l"(srcv), "r"(ok ? 16 : 0) : "memory");
+        }
+        cp_async_commit();
+    };
+    load_tile(0, 0);
+    for (int kt = 0; kt < nkt; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < nkt) load_tile(kt + 1, buf ^ 1);
+        else cp_async_commit();
+        cp_async_wait_group<1>();
+        __syncthreads();
+        const KVT* K = sk[buf];
+        const KVT* V = sv[buf];
+        // ---- scores of 64 keys: 8 n-tiles of 8 keys
+        float s[8][4];
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+            const KVT* krow = K + (nt * 8 + g) * FA_RS + 2 * t;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + ks * 16);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + ks * 16 + 8);
+                MM::mma(s[nt], qa[ks], b0, b1);
+                MM::mma(s[nt], qr[ks], b0, b1);
+            }
+        }
+        // ---- causal mask, scale, online softmax (rows g and g + 8 of the warp)
+        float mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int kp = kt * FA_BK + nt * 8 + 2 * t + (e & 1);
+                const float v = kp <= qpos[e >> 1] ? s[nt][e] * scale : -INFINITY;
+                s[nt][e] = v;
+                mt[e >> 1] = fmaxf(mt[e >> 1], v);
+            }
+        }
+        float corr[2], ls[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 1));
+            mt[r] = fmaxf(mt[r], __shfl_xor_sync(0xffffffffu, mt[r], 2));
+            const float mn = fmaxf(mrow[r], mt[r]);
+            corr[r] = mrow[r] == -INFINITY ? 0.f : expf(mrow[r] - mn);
+            mrow[r] = mn;
+            ls[r] = 0.f;
+        }
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float pv = s[nt][e] == -INFINITY ? 0.f : expf(s[nt][e] - mrow[e >> 1]);
+                s[nt][e] = pv;
+                ls[e >> 1] += pv;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+            lrow[r] = lrow[r] * corr[r] + ls[r];
+        }
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+            o[n][0] *= corr[0];
+            o[n][1] *= corr[0];
+            o[n][2] *= corr[1];
+            o[n][3] *= corr[1];
+        }
+        // ---- O += P . V: 4 steps of 16 keys, B fragments by ldmatrix.trans from the V tile
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t pa[4], pr[4];
+            const float e0[4] = {s[2 * j][0], s[2 * j][2], s[2 * j + 1][0], s[2 * j + 1][2]};
+            const float e1[4] = {s[2 * j][1], s[2 * j][3], s[2 * j + 1][1], s[2 * j + 1][3]};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                pa[i] = MM::pack(e0[i], e1[i]);
+                pr[i] = MM::pack(e0[i] - MM::round(e0[i]), e1[i] - MM::round(e1[i]));
+            }
+            const int mi = lane >> 3, ri = lane & 7;
+            const KVT* vrow = V + (j * 16 + (mi & 1) * 8 + ri) * FA_RS + (mi >> 1) * 8;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                uint32_t b[4];
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                             : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                             : "r"(smem_u32(vrow + u * 16)));
+                MM::mma(o[2 * u], pa, b[0], b[1]);
+                MM::mma(o[2 * u], pr, b[0], b[1]);
+                MM::mma(o[2 * u + 1], pa, b[2], b[3]);
+                MM::mma(o[2 * u + 1], pr, b[2], b[3]);
+            }
+        }
+        __syncthreads();  // this buffer is refilled two tiles later
+    }
+    // ---- normalised rows out
+    const int rows[2] = {r0 + g, r0 + g + 8};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (rows[r] >= P) continue;
+        const float inv = 1.f / lrow[r];
+        float* orow = out + ((size_t)rows[r] * Hq + hq) * HD + 2 * t;
+#pragma unroll
+        for (int n = 0; n < 16; ++n)
+            *reinterpret_cast<float2*>(orow + n * 8) = make_float2(o[n][2 * r] * inv, o[n][2 * r + 1] * inv);
+    }
 }
 
 // ------------------------------------------------------------------ launchers
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link-time libcuda dependency).
+static PFN_cuTensorMapEncodeTiled tg_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(p);
+    }
+    return fn;
+}
+
+// 2-D fp16 row-major [rows][K] (16-byte aligned base, K % 64 == 0), box 64 x box_rows, 128-byte
+// swizzle, out-of-range rows read as zero.
+static bool tg_tensor_map(CUtensorMap* tm, const __half* base, int rows, int K, int box_rows) {
+    PFN_cuTensorMapEncodeTiled enc = tg_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Fills a.tmA / a.tmB from the operand pointers and launches. A, B: 16-byte aligned, K % 64 == 0.
 template <int EPI>
-cudaError_t launch_tc_gemm(const TGArgs& a, cudaStream_t st) {
+cudaError_t launch_tc_gemm(TGArgs& a, const __half* A, const __half* B, cudaStream_t st) {
     static int attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -454,8 +613,30 @@ cudaError_t launch_tc_gemm(const TGArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr_set[dev] = 1;
     }
+    if (!tg_tensor_map(&a.tmA, A, a.P, a.K, TG_BM) || !tg_tensor_map(&a.tmB, B, a.N, a.K, TG_BN))
+        return cudaErrorInvalidValue;
     const dim3 grid((unsigned)((a.P + TG_BM - 1) / TG_BM), (unsigned)((a.N + TG_BN - 1) / TG_BN));
     tc_gemm_kernel<EPI><<<grid, TG_THREADS, TG_SMEM, st>>>(a);
+    return cudaGetLastError();
+}
+
+constexpr int FA_SMEM = 4 * FA_BK * FA_RS * 2;  // K and V tiles, double-buffered
+
+template <typename KVT>
+cudaError_t launch_prefill_attn(const float* q, int Hq, int Hkv, const KVT* kc, const KVT* vc, long long stride_h,
+                                int stride_t, int pos0, int P, float* out, cudaStream_t st) {
+    static int attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (!attr_set[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(prefill_flash_kernel<KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = 1;
+    }
+    prefill_flash_kernel<KVT><<<dim3((P + FA_BQ - 1) / FA_BQ, Hq), FA_THREADS, FA_SMEM, st>>>(q, Hq, Hkv, kc, vc, stride_h,
+                                                                                          stride_t, pos0, P, out);
     return cudaGetLastError();
 }
 
@@ -478,12 +659,12 @@ extern "C" int fence_gemm_f16(const uint16_t* A, const uint16_t* B, float* C, in
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15)
         return set_error(FENCE_E_ALIGN, "gemm_f16: A and B must be 16-byte aligned");
     TGArgs a{};
-    a.A = reinterpret_cast<const __half*>(A);
-    a.B = reinterpret_cast<const __half*>(B);
     a.P = P;
     a.N = N;
     a.K = K;
     a.C = C;
     a.ldc = N;
-    return cuda_status(launch_tc_gemm<TG_EPI_STORE>(a, (cudaStream_t)stream), "gemm_f16 launch");
+    return cuda_status(launch_tc_gemm<TG_EPI_STORE>(a, reinterpret_cast<const __half*>(A), reinterpret_cast<const __half*>(B),
+                                                    (cudaStream_t)stream),
+                       "gemm_f16 launch");
 }

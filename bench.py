@@ -459,8 +459,9 @@ def main():
     ap.add_argument("--tmp", default=None, help="directory for the synthetic GGUF (default: /dev/shm if roomy)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the extra keys (config 0 / 1 / 3-TP1)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "gemv"],
-                    help="gemv: only the config-0 Q6_K GEMV roofline measurement (small; used for ncu captures)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "gemv", "prefill"],
+                    help="gemv: only the config-0 Q6_K GEMV roofline measurement (small; used for ncu captures); "
+                         "prefill: only the batched prefill of --prompt tokens of --config")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -487,6 +488,31 @@ def main():
         ms = measure_gemv_roofline(fb, torch, copies=16, launches=max(args.steps, 1), pdl=True)
         print(json.dumps({"metric": "gemv_q6k_config0_GBps", "value": round(CONFIG0_BYTES / (ms * 1e-3) / 1e9, 1),
                           "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "peak": peak, "peak_kind": peak_kind}))
+        return
+    if args.mode == "prefill":
+        fb = _load_pkg()
+        with tempfile.TemporaryDirectory(dir=args.tmp) as tmp:
+            path = synth_model(fb, args.config, tmp, args.layers)
+            m = fb.Model(path, max_ctx=max(4096, args.prompt + 8))
+            c = m.config
+            rng = np.random.default_rng(7)
+            m.prefill([int(t) for t in rng.integers(0, c.vocab_size, 64)])  # scratch allocation, warm-up
+            toks = [int(t) for t in rng.integers(0, c.vocab_size, args.prompt)]
+            times = []
+            for _ in range(max(1, args.steps)):
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                m.prefill(toks)
+                torch.cuda.synchronize()
+                times.append(time.perf_counter() - t0)
+            m.close()
+        qd, kvd = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+        params = c.n_layers * (c.embed_dim * (qd + 2 * kvd) + qd * c.embed_dim + 3 * c.embed_dim * c.ff_dim)
+        s_med = statistics.median(times)
+        print(json.dumps({"metric": "prefill_tokens_per_s", "value": round(args.prompt / s_med, 1), "unit": "tokens/s",
+                          "config": args.config, "layers": c.n_layers, "tokens": args.prompt, "s": round(s_med, 4),
+                          "linear_tflop": round(2 * params * (args.prompt - 1) / 1e12, 2),
+                          "linear_tflops_if_all_time": round(2 * params * (args.prompt - 1) / s_med / 1e12, 1)}))
         return
     dist = None
     if world > 1:

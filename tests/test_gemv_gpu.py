@@ -91,6 +91,48 @@ def test_q6k_shapes(fb, orc, torch_cuda, M, K):
     assert_close(run_q6k(fb, torch_cuda, W, x, M, K), orc.gemv_q6k(W, x, M, K))
 
 
+@pytest.mark.parametrize("M,K", [(1, 2048), (300, 2048), (4096, 2048), (149, 4096), (10000, 4096), (6144, 4096)])
+def test_q6k_shapes_with_bias(fb, orc, torch_cuda, M, K):
+    W = fb.synth_blocks(fb.GGML_Q6_K, M * K // 256, seed=M * 3 + K)
+    x = (np.random.default_rng(M).standard_normal(K) * 2).astype(np.float32).astype(np.float16).view(np.uint16)
+    ref = orc.gemv_q6k(W, x, M, K)
+    assert_close(run_q6k(fb, torch_cuda, W, x, M, K), ref)
+    bias = np.random.default_rng(M + 1).standard_normal(M).astype(np.float32)
+    assert_close(run_q6k(fb, torch_cuda, W, x, M, K, bias=bias), ref + bias)
+
+
+def test_q6k_pdl_chain_reads_the_previous_kernels_output(fb, orc, torch_cuda):
+    """With FENCE_LAUNCH_PDL the GEMV streams its weights before the previous kernel ends, but its x
+    (here written by the kernel just before it) is read only after griddepcontrol.wait: x2 starts as
+    NaN bits each round and every round uses a new x, so an early read would show in y2."""
+    torch = torch_cuda
+    M = K = 4096
+    W1 = fb.synth_blocks(fb.GGML_Q6_K, M * K // 256, seed=31)
+    W2 = fb.synth_blocks(fb.GGML_Q6_K, M * K // 256, seed=32)
+    t1, p1 = dev_bytes(torch, W1, 0)
+    t2, p2 = dev_bytes(torch, W2, 0)
+    old = fb.lib().fence_set_launch_flags(fb.FENCE_LAUNCH_PDL)
+    try:
+        for r in range(3):
+            x = np.random.default_rng(40 + r).standard_normal(K).astype(np.float32).astype(np.float16).view(np.uint16)
+            tx = torch.from_numpy(x.view(np.int16).copy()).cuda()
+            y1 = torch.empty(M, dtype=torch.float32, device="cuda")
+            x2 = torch.full((M,), 0x7E00, dtype=torch.int16, device="cuda")  # fp16 NaN
+            y2 = torch.full((M,), float("nan"), dtype=torch.float32, device="cuda")
+            torch.cuda.synchronize()
+            fb.call("fence_gemv_q6k", p1, tx.data_ptr(), y1.data_ptr(), M, K, None)
+            fb.call("fence_f32_to_f16", x2.data_ptr(), y1.data_ptr(), M, None)
+            fb.call("fence_gemv_q6k", p2, x2.data_ptr(), y2.data_ptr(), M, K, None)
+            torch.cuda.synchronize()
+            got_y1 = y1.cpu().numpy()
+            got_x2 = x2.cpu().numpy().view(np.uint16)
+            assert_close(got_y1, orc.gemv_q6k(W1, x, M, K))
+            assert np.array_equal(got_x2, got_y1.astype(np.float16).view(np.uint16))
+            assert_close(y2.cpu().numpy(), orc.gemv_q6k(W2, got_x2, M, K))
+    finally:
+        fb.lib().fence_set_launch_flags(old)
+
+
 def test_q6k_misaligned_pointer_and_bias(fb, orc, torch_cuda):
     M, K = 129, 1024
     W = fb.synth_blocks(fb.GGML_Q6_K, M * K // 256, seed=5)
