@@ -13,8 +13,9 @@
 // weights stay normal fp16 numbers; the GEMM epilogue multiplies the scale back out).
 //
 // tc_gemm_kernel: C[P x N] = A[P x K] . B[N x K]^T, A and B fp16 row-major (K-major operands), fp32
-// accumulation in tensor memory. CTA tile 128 x 256, K steps of 64 through a 4-stage shared-memory
-// ring. Warp-specialised: one lane loads each stage's A and B tiles with two TMA tensor copies
+// accumulation in tensor memory. CTA tile 128 x 256, K steps of 64 through a 2-stage shared-memory
+// ring (97 KB), two CTAs per SM so one CTA's epilogue overlaps the other's MMAs (their two 256-column
+// accumulators fill the SM's tensor memory). Warp-specialised: one lane loads each stage's A and B tiles with two TMA tensor copies
 // (cp.async.bulk.tensor.2d, 128-byte swizzle, no multicast) completing on the stage's "full"
 // mbarrier; one lane issues the stage's four tcgen05.mma (M128 N256 K16, operands described by
 // 128-byte-swizzle K-major shared-memory descriptors) and commits them to the stage's "empty"
@@ -33,7 +34,7 @@
 
 namespace fence {
 
-constexpr int TG_BM = 128, TG_BN = 256, TG_BK = 64, TG_STAGES = 4, TG_THREADS = 128;
+constexpr int TG_BM = 128, TG_BN = 256, TG_BK = 64, TG_STAGES = 2, TG_THREADS = 128;
 constexpr int TG_A_BYTES = TG_BM * TG_BK * 2;
 constexpr int TG_B_BYTES = TG_BN * TG_BK * 2;
 constexpr int TG_STAGE_BYTES = TG_A_BYTES + TG_B_BYTES;
@@ -76,7 +77,7 @@ __device__ __forceinline__ void tg_tma_load(uint32_t dst, const CUtensorMap* tm,
 __device__ __forceinline__ float tg_silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
 
 template <int EPI>
-__global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_constant__ TGArgs a) {
+__global__ void __launch_bounds__(TG_THREADS, 2) tc_gemm_kernel(const __grid_constant__ TGArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int p0 = blockIdx.x * TG_BM, n0 = blockIdx.y * TG_BN;
@@ -208,68 +209,102 @@ __global__ void __launch_bounds__(TG_THREADS, 1) tc_gemm_kernel(const __grid_con
 
 // ------------------------------------------------------------------ weight dequantisation
 // Repacked row r of an RMat (rgemv.cuh layouts, one rank: item0 = 0) -> fp16 row r of W[M][K] in the
-// natural column order, times 2^e_r with e_r the largest exponent keeping the row's largest |w| at or
-// below 2^14; bscale[r] = 2^-e_r. One CTA per row.
+// natural column order, times 2^e_r with e_r the largest exponent keeping a bound on the row's
+// largest |w| below 2^14; bscale[r] = 2^-e_r.
 //   Q6_K item i of a row: super-block j = i / 4, half h = (i / 2) & 1, l16 = i & 1; its element
 //   (c, e) (column run c < 4, e < 16) is column 256 j + 128 h + 32 c + 16 l16 + e, value
 //   d_j * scale_c * (q6 - 32) with q6 = low nibble of byte (c & 1) * 16 + e (its high nibble for
 //   c >= 2) | crumb c of byte 32 + e << 4 of the item's 48-byte record.
 //   Q8_0 item i: chunk k of 16 int8 at record position k ^ ((i >> 1) & 3); block scales d0, d1.
+// One warp per row. The row's scale exponent comes from a bound on its largest |w| taken from the
+// block scales alone (Q8_0: max |d| * 127; Q6_K: max over sub-blocks |d * scale| * 32), then every
+// lane turns whole items into fp16 with 16-byte loads and stores.
 template <int WT>
-__device__ __forceinline__ float dq_value(const RMat& m, int I, long long r, int it, int c, int e, int* col) {
-    if (WT == WT_Q6K) {
-        const uint8_t* q = m.q + ((size_t)r * I + it) * 48;
-        const uint8_t lo = q[(c & 1) * 16 + e];
-        const int nib = c >= 2 ? lo >> 4 : lo & 15;
-        const int q6 = nib | (((q[32 + e] >> (2 * c)) & 3) << 4);
-        const int sc = (int8_t)m.s[(size_t)r * rg_sbytes_row(WT_Q6K, I) + (size_t)it * 4 + c];
-        const uint8_t* dp = m.d + (size_t)r * rg_dbytes_row(WT_Q6K, I, 0) + (size_t)(it >> 2) * 2;
-        const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
-        *col = (it >> 2) * 256 + ((it >> 1) & 1) * 128 + c * 32 + (it & 1) * 16 + e;
-        return d * (float)sc * (float)(q6 - 32);
-    } else {
-        const int k = c;  // chunk (16 elements)
-        const uint8_t* q = m.q + ((size_t)r * I + it) * 64;
-        const int qv = (int8_t)q[16 * (k ^ ((it >> 1) & 3)) + e];
-        const uint8_t* dp = m.d + ((size_t)r * I + it) * 4 + (k >> 1) * 2;
-        const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
-        *col = it * 64 + 16 * k + e;
-        return d * (float)qv;
-    }
-}
-
-template <int WT>
-__global__ void dequant_rows_kernel(RMat m, int I, __half* __restrict__ W, float* __restrict__ bscale) {
-    __shared__ float red[32];
-    const long long r = blockIdx.x;
+__global__ void dequant_rows_kernel(RMat m, int I, int rows, __half* __restrict__ W, float* __restrict__ bscale) {
+    const int lane = threadIdx.x & 31;
+    const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
     const int n = I * 64;
-    float amax = 0.f;
-    for (int x = threadIdx.x; x < n; x += blockDim.x) {
-        int col;
-        amax = fmaxf(amax, fabsf(dq_value<WT>(m, I, r, x >> 6, (x >> 4) & 3, x & 15, &col)));
+    float bound = 0.f;
+    if (WT == WT_Q6K) {
+        const uint8_t* dr = m.d + (size_t)r * rg_dbytes_row(WT_Q6K, I, 0);
+        const int8_t* sr = reinterpret_cast<const int8_t*>(m.s + (size_t)r * rg_sbytes_row(WT_Q6K, I));
+        for (int it = lane; it < I; it += 32) {
+            const float d = fabsf(half_bits_to_float((uint32_t)dr[(it >> 2) * 2] | ((uint32_t)dr[(it >> 2) * 2 + 1] << 8)));
+            int smax = 0;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) smax = max(smax, abs((int)sr[it * 4 + c]));
+            bound = fmaxf(bound, d * (float)smax * 32.f);
+        }
+    } else {
+        const uint16_t* dr = reinterpret_cast<const uint16_t*>(m.d + (size_t)r * I * 4);
+        for (int i = lane; i < 2 * I; i += 32) bound = fmaxf(bound, fabsf(half_bits_to_float(dr[i])) * 127.f);
     }
-    amax = warp_max(amax);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_max(v);
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    amax = red[0];
+    bound = warp_max(bound);
     int e = 0;
-    if (amax > 0.f && isfinite(amax)) {
+    if (bound > 0.f && isfinite(bound)) {
         int ex;
-        frexpf(amax, &ex);  // amax in [2^(ex-1), 2^ex)
-        e = 14 - ex;        // amax * 2^e < 2^14
+        frexpf(bound, &ex);  // bound in [2^(ex-1), 2^ex)
+        e = 14 - ex;         // every |w| * 2^e < 2^14
     }
-    const float s = ldexpf(1.f, e);
-    if (threadIdx.x == 0) bscale[r] = ldexpf(1.f, -e);
-    for (int x = threadIdx.x; x < n; x += blockDim.x) {
-        int col;
-        const float v = dq_value<WT>(m, I, r, x >> 6, (x >> 4) & 3, x & 15, &col);
-        W[(size_t)r * n + col] = __float2half_rn(v * s);
+    const float sc2 = ldexpf(1.f, e);
+    if (lane == 0) bscale[r] = ldexpf(1.f, -e);
+    __half* wrow = W + (size_t)r * n;
+    for (int it = lane; it < I; it += 32) {
+        if (WT == WT_Q6K) {
+            // item it: super-block j, half h, l16; run c covers columns 256 j + 128 h + 32 c + 16 l16 + [0, 16)
+            const uint4* q = reinterpret_cast<const uint4*>(m.q + ((size_t)r * I + it) * 48);
+            const uint4 u0 = q[0], u1 = q[1], u2 = q[2];
+            const uint8_t* lo0 = reinterpret_cast<const uint8_t*>(&u0);
+            const uint8_t* lo1 = reinterpret_cast<const uint8_t*>(&u1);
+            const uint8_t* hi = reinterpret_cast<const uint8_t*>(&u2);
+            const uint32_t sw = *reinterpret_cast<const uint32_t*>(m.s + (size_t)r * rg_sbytes_row(WT_Q6K, I) + (size_t)it * 4);
+            const uint8_t* dp = m.d + (size_t)r * rg_dbytes_row(WT_Q6K, I, 0) + (size_t)(it >> 2) * 2;
+            const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8)) * sc2;
+            const int col0 = (it >> 2) * 256 + ((it >> 1) & 1) * 128 + (it & 1) * 16;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float ds = d * (float)(int8_t)(sw >> (8 * c));
+                const uint8_t* lo = (c & 1) ? lo1 : lo0;
+                uint32_t words[8];
+#pragma unroll
+                for (int e2 = 0; e2 < 16; e2 += 2) {
+                    float v[2];
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int nib = c >= 2 ? lo[e2 + k] >> 4 : lo[e2 + k] & 15;
+                        const int q6 = nib | (((hi[e2 + k] >> (2 * c)) & 3) << 4);
+                        v[k] = ds * (float)(q6 - 32);
+                    }
+                    const __half2 h2 = __floats2half2_rn(v[0], v[1]);
+                    words[e2 / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(wrow + col0 + c * 32);
+                dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+                dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+            }
+        } else {
+            const uint4* q = reinterpret_cast<const uint4*>(m.q + ((size_t)r * I + it) * 64);
+            const uint32_t dw = *reinterpret_cast<const uint32_t*>(m.d + ((size_t)r * I + it) * 4);
+            const float d0 = half_bits_to_float(dw & 0xffffu) * sc2, d1 = half_bits_to_float(dw >> 16) * sc2;
+            const int f = (it >> 1) & 3;
+#pragma unroll
+            for (int p2 = 0; p2 < 4; ++p2) {
+                const int k = p2 ^ f;  // the chunk stored at record position p2: elements 16 k .. 16 k + 15
+                const uint4 u = q[p2];
+                const int8_t* b = reinterpret_cast<const int8_t*>(&u);
+                const float d = (k >> 1) ? d1 : d0;
+                uint32_t words[8];
+#pragma unroll
+                for (int e2 = 0; e2 < 16; e2 += 2) {
+                    const __half2 h2 = __floats2half2_rn(d * (float)b[e2], d * (float)b[e2 + 1]);
+                    words[e2 / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(wrow + it * 64 + 16 * k);
+                dst[0] = make_uint4(words[0], words[1], words[2], words[3]);
+                dst[1] = make_uint4(words[4], words[5], words[6], words[7]);
+            }
+        }
     }
 }
 
@@ -641,8 +676,9 @@ cudaError_t launch_prefill_attn(const float* q, int Hq, int Hkv, const KVT* kc, 
 }
 
 cudaError_t launch_dequant(int wt, const RMat& m, int rows, int I, __half* W, float* bscale, cudaStream_t st) {
-    if (wt == WT_Q6K) dequant_rows_kernel<WT_Q6K><<<rows, 256, 0, st>>>(m, I, W, bscale);
-    else dequant_rows_kernel<WT_Q80><<<rows, 256, 0, st>>>(m, I, W, bscale);
+    const unsigned blocks = (unsigned)((rows + 7) / 8);  // 8 warps (rows) per CTA
+    if (wt == WT_Q6K) dequant_rows_kernel<WT_Q6K><<<blocks, 256, 0, st>>>(m, I, rows, W, bscale);
+    else dequant_rows_kernel<WT_Q80><<<blocks, 256, 0, st>>>(m, I, rows, W, bscale);
     return cudaGetLastError();
 }
 
