@@ -568,7 +568,7 @@ __device__ __forceinline__ int sk_attn_issue_early(const AttnArgs& a, int h, int
 template <typename KVT>
 __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int clen, int n_active, int pos,
                                           uint8_t* sm, bool pre, uint64_t* abar, uint32_t& apar,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag, unsigned long long* tr) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
     constexpr int HD = 128, EPC = 16 / (int)sizeof(KVT);
@@ -700,6 +700,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     for (int i = 0; i < T; ++i) wait_buf(i);  // every K tile
     for (int i = 0; i < T; ++i) put_new(i, i, skn);
     named_bar_sync(2, NT);
+    if (tr && tid == 0) tr[4] = sk_ns();  // trace: inputs ready, K tiles landed
     {
         constexpr int GPW = SK_ATT_TILES;  // position groups per warp
         float dh[GPW][4], dl[GPW][4];
@@ -740,6 +741,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
         for (int i = 0; i < T; ++i)
             sk_attn_rows<KVT>(tile(i), vb, a.stride_t, t0 + i * TILE, min(t0 + (i + 1) * TILE, t1), &abar[i]);
     }
+    if (tr && tid == 0) tr[5] = sk_ns();  // trace: scores done
     // ---- the chunk's softmax, a warp per head: max, exp, sum; P (zero beyond n) back into ss
     for (int g = warp; g < G; g += NW) {
         float* sr = ss + g * ML;
@@ -763,6 +765,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
     for (int i = 0; i < T; ++i) put_new(i, sk_attn_vbuf(T, i), svn);
     if (n < T * TILE) zero_tail(sk_attn_vbuf(T, T - 1), n - (T - 1) * TILE);
     named_bar_sync(2, NT);
+    if (tr && tid == 0) tr[6] = sk_ns();  // trace: V tiles landed
     float oh[2][2][4] = {}, ol[2][2][4] = {};  // [k-step parity][n-tile j]: dims 16 warp + 8 j + 2 q4 + {0, 1}
     // ldmatrix.trans addresses: lane -> row (lane & 7) + 8 (bit 3) of tile rows 16 ks.., chunk 2w + (bit 4)
     const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lch = 2 * warp + (lane >> 4);
@@ -798,6 +801,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
             else *reinterpret_cast<float2*>(pbase + gr * SK_PART_STRIDE + d) = o;
         }
     }
+    if (tr && tid == 0) tr[7] = sk_ns();  // trace: P.V done, output / partial written
     if (n_active == 1) return;  // (the caller's barrier orders the next unit's reuse of the buffers)
     if (tid < G) *reinterpret_cast<float2*>(pbase + tid * SK_PART_STRIDE + HD) = make_float2(smax[tid], ssum[tid]);
     // ---- the last unit of KV head h to arrive merges the head's chunks: output (query head
@@ -1235,7 +1239,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                 // the first unit's tile 0 may have been issued at the end of the previous phase
                 if (tid < ATTN_THREADS)
                     sk_attn_unit<KVT>(at, u / nch, u % nch, clen, nch, pos, scratch, attn_pre > 0, abar, apar,
-                                      abort_flag);
+                                      abort_flag, (A.trace && u == c) ? A.trace + ((size_t)c * NPH + k) * SK_TRACE : nullptr);
                 attn_pre = 0;
                 named_bar_sync(1, NT);  // the next unit reuses the scratch
                 if (A.trace && tid == 0 && u == c) A.trace[((size_t)c * NPH + k) * SK_TRACE + 1] = sk_ns();
@@ -1246,7 +1250,7 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         if (tid == 0) {
             if (A.trace) {
                 A.trace[((size_t)c * NPH + k) * SK_TRACE + 3] = sk_ns();
-                A.trace[((size_t)c * NPH + k) * SK_TRACE + 4] = wcyc;
+                if (ph.kind == SP_GEMV) A.trace[((size_t)c * NPH + k) * SK_TRACE + 4] = wcyc;
             }
             // release (cumulative): every consumer write of this CTA, ordered before by the CTA
             // barrier, is visible before the count
