@@ -311,11 +311,20 @@ __device__ __noinline__ void sk_route(const float* x, const float* nw, float eps
     float p[SK_MOE_EMAX];
 #pragma unroll
     for (int e = 0; e < SK_MOE_EMAX; ++e) p[e] = 0.f;
-    for (int k = tid; k < H; k += SK_NL) {
-        const float xn = x[k] * rms * nw[k];
+    // 16-byte loads, every expert row's load of an iteration issued before any use (H % 64 == 0):
+    // a few L2 round trips per thread instead of one per element
+    const int H4 = H >> 2;
+    for (int k4 = tid; k4 < H4; k4 += SK_NL) {
+        const float4 xv = reinterpret_cast<const float4*>(x)[k4];
+        const float4 wv = reinterpret_cast<const float4*>(nw)[k4];
+        float4 wr[SK_MOE_EMAX];
 #pragma unroll
         for (int e = 0; e < SK_MOE_EMAX; ++e)
-            if (e < E) p[e] += __ldg(Wr + (size_t)e * H + k) * xn;
+            if (e < E) wr[e] = __ldg(reinterpret_cast<const float4*>(Wr + (size_t)e * H) + k4);
+        const float x0 = xv.x * rms * wv.x, x1 = xv.y * rms * wv.y, x2 = xv.z * rms * wv.z, x3 = xv.w * rms * wv.w;
+#pragma unroll
+        for (int e = 0; e < SK_MOE_EMAX; ++e)
+            if (e < E) p[e] += wr[e].x * x0 + wr[e].y * x1 + wr[e].z * x2 + wr[e].w * x3;
     }
 #pragma unroll
     for (int e = 0; e < SK_MOE_EMAX; ++e) {
@@ -1013,6 +1022,15 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
             for (int k = 0; k < NPH && !*abort_flag; ++k) {
                 const SPhase& ph = A.ph[k];
                 if (ph.kind == SP_ATTN) {
+                    // the next MoE routing's router weights into L2 (every CTA reads all of them)
+                    for (int k2 = k + 1; k2 < NPH && k2 <= k + 3; ++k2) {
+                        const SPhase& nx = A.ph[k2];
+                        if (nx.moe == SK_MOE_GU && nx.moe_slot == 0 && c < 4) {
+                            const uint32_t rb = (uint32_t)nx.n_exp * (uint32_t)nx.g.I * 256u;
+                            for (uint32_t o = (uint32_t)c * 32768u; o < rb; o += 4u * 32768u)
+                                bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(nx.route_w) + o, min(32768u, rb - o));
+                        }
+                    }
                     // pull this CTA's K/V rows of the coming attention phase into L2
                     const AttnArgs& at = ph.at;
                     const int seq = ppos + 1;
