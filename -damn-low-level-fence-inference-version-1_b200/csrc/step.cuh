@@ -311,20 +311,26 @@ __device__ __noinline__ void sk_route(const float* x, const float* nw, float eps
     float p[SK_MOE_EMAX];
 #pragma unroll
     for (int e = 0; e < SK_MOE_EMAX; ++e) p[e] = 0.f;
-    // 16-byte loads, every expert row's load of an iteration issued before any use (H % 64 == 0):
-    // a few L2 round trips per thread instead of one per element
+    // 16-byte loads, a group of 4 expert rows' loads issued before any use (H % 64 == 0): a few L2
+    // round trips per thread instead of one per element. Groups of 4, not all rows at once: this
+    // function's register footprint is what the step kernel must keep clear around the call, and
+    // 16 loads in flight made it spill its own loop state.
     const int H4 = H >> 2;
     for (int k4 = tid; k4 < H4; k4 += SK_NL) {
         const float4 xv = reinterpret_cast<const float4*>(x)[k4];
         const float4 wv = reinterpret_cast<const float4*>(nw)[k4];
-        float4 wr[SK_MOE_EMAX];
-#pragma unroll
-        for (int e = 0; e < SK_MOE_EMAX; ++e)
-            if (e < E) wr[e] = __ldg(reinterpret_cast<const float4*>(Wr + (size_t)e * H) + k4);
         const float x0 = xv.x * rms * wv.x, x1 = xv.y * rms * wv.y, x2 = xv.z * rms * wv.z, x3 = xv.w * rms * wv.w;
 #pragma unroll
-        for (int e = 0; e < SK_MOE_EMAX; ++e)
-            if (e < E) p[e] += wr[e].x * x0 + wr[e].y * x1 + wr[e].z * x2 + wr[e].w * x3;
+        for (int e0 = 0; e0 < SK_MOE_EMAX; e0 += 4) {
+            if (e0 >= E) break;
+            float4 wr[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e0 + e < E) wr[e] = __ldg(reinterpret_cast<const float4*>(Wr + (size_t)(e0 + e) * H) + k4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e0 + e < E) p[e0 + e] += wr[e].x * x0 + wr[e].y * x1 + wr[e].z * x2 + wr[e].w * x3;
+        }
     }
 #pragma unroll
     for (int e = 0; e < SK_MOE_EMAX; ++e) {
