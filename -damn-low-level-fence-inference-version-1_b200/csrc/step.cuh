@@ -586,7 +586,7 @@ __device__ __noinline__ void sk_attn_unit(const AttnArgs& a, int h, int c, int c
                                           volatile int* abort_flag, unsigned long long* tr) {
     using C = KVConv<KVT>;
     using M = SKMma<KVT>;
-    constexpr int HD = 128, EPC = 16 / (int)sizeof(KVT);
+    constexpr int HD = 128;
     constexpr int NT = ATTN_THREADS, NW = NT / 32, TILE = ATTN_CMAX, ML = SK_ATT_MAXLEN;
     static_assert(TILE == 64 && NT == 256 && NW == 8 && ATTN_MAX_G <= 8, "unit geometry");
     constexpr int RSTR = SK_ATT_RSTR;
@@ -1024,7 +1024,6 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
         // ================= producer (lane 0): stream every GEMV phase's rows of this CTA
         if (lane == 0) {
             uint32_t use = 0;
-            const int ppos = A.state->pos;
             for (int k = 0; k < NPH && !*abort_flag; ++k) {
                 const SPhase& ph = A.ph[k];
                 if (ph.kind == SP_ATTN) {
@@ -1037,18 +1036,9 @@ __global__ void __launch_bounds__(SK_NT, 1) step_kernel(const __grid_constant__ 
                                 bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(nx.route_w) + o, min(32768u, rb - o));
                         }
                     }
-                    // pull this CTA's K/V rows of the coming attention phase into L2
-                    const AttnArgs& at = ph.at;
-                    const int seq = ppos + 1;
-                    const int clen = sk_attn_clen(seq, at.nchunk, G, at.n_kv_heads, A.attn_solo);
-                    const int nch = (seq + clen - 1) / clen;
-                    for (int u = c; u < at.n_kv_heads * nch; u += G) {
-                        const int h = u / nch, t0 = (u % nch) * clen, t1 = min(t0 + clen, seq);
-                        const size_t off = ((size_t)h * at.stride_h + (size_t)t0 * at.stride_t) * sizeof(KVT);
-                        const uint32_t bytes = (uint32_t)((t1 - t0) * at.stride_t * sizeof(KVT));
-                        bulk_prefetch_l2(static_cast<const uint8_t*>(at.kc) + off, bytes);
-                        bulk_prefetch_l2(static_cast<const uint8_t*>(at.vc) + off, bytes);
-                    }
+                    // (the attention phase's K/V rows are not pulled into L2 here: on config 2 at 4000
+                    // positions that prefetch competed with the QKV phase's weights and made the step
+                    // 0.9 % slower; the units' own tile copies, issued at the QKV phase's end, read them)
                 }
                 if (ph.kind != SP_GEMV) continue;
                 const RGemvArgs& g = ph.g;
