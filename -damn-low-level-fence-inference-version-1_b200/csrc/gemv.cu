@@ -276,7 +276,11 @@ static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* 
     if (!W || !x || !y || M <= 0 || K <= 0 || K % 256 != 0)
         return set_error(FENCE_E_ARG, "gemv_q6k: need non-null pointers, M > 0, K %% 256 == 0 (M=%d K=%d)", M, K);
     const bool aligned = (reinterpret_cast<uintptr_t>(W) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-    const GQPlan gq = plan_q6k_reg(M, K);
+    // Stream-ordered launches take the register-resident kernel (config 0, 4096 x 4096, back to back
+    // in a CUDA graph on a B200: 8.4 us per launch against the streaming kernel's 10.0); launches
+    // chained by programmatic dependent launch take the streaming kernel (8.2 us against 8.7).
+    const bool pdl = (g_launch_flags & FENCE_LAUNCH_PDL) != 0;
+    const GQPlan gq = pdl ? GQPlan{} : plan_q6k_reg(M, K);
     if (aligned && gq.ok) {
         GQArgs a{};
         a.W = reinterpret_cast<const uint8_t*>(W);
@@ -291,7 +295,7 @@ static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* 
         a.RC = gq.RC;
         a.slots = gq.slots;
         a.slot_bytes = gq.slot_bytes;
-        return cuda_status(launch_q6k_reg(a, gq, st, (g_launch_flags & FENCE_LAUNCH_PDL) != 0), "gemv_q6k launch");
+        return cuda_status(launch_q6k_reg(a, gq, st, false), "gemv_q6k launch");
     }
     GemvPlan pl = plan_gemv(WT_Q6K, K, M, 0, 0);
     cudaError_t e;
@@ -303,7 +307,7 @@ static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* 
         a.K = K;
         a.x = x;
         fill_plan(a, pl);
-        e = launch_gemv<WT_Q6K, X_F16, EPI_STORE>(a, pl, st, (g_launch_flags & FENCE_LAUNCH_PDL) != 0);
+        e = launch_gemv<WT_Q6K, X_F16, EPI_STORE>(a, pl, st, pdl);
     } else {
         const int threads = 128;
         gemv_q6k_simple_kernel<<<(M + 3) / 4, threads, 0, st>>>(reinterpret_cast<const uint8_t*>(W), x,

@@ -504,9 +504,12 @@ def main():
     if args.mode == "gemv":
         fb = _load_pkg()
         peak, peak_kind = hbm_peak()
-        ms = measure_gemv_roofline(fb, torch, copies=16, launches=max(args.steps, 1), pdl=True)
+        ms = measure_gemv_roofline(fb, torch, copies=16, launches=max(args.steps, 1), pdl=False)
+        ms_pdl = measure_gemv_roofline(fb, torch, copies=16, launches=max(args.steps, 1), pdl=True)
         print(json.dumps({"metric": "gemv_q6k_config0_GBps", "value": round(CONFIG0_BYTES / (ms * 1e-3) / 1e9, 1),
-                          "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "peak": peak, "peak_kind": peak_kind}))
+                          "unit": "GB/s", "us_per_launch": round(ms * 1e3, 3), "kernel": "gemv_q6k_reg_kernel",
+                          "us_per_launch_pdl": round(ms_pdl * 1e3, 3), "kernel_pdl": "gemv_stream_kernel",
+                          "peak": peak, "peak_kind": peak_kind}))
         return
     if args.mode == "prefill":
         fb = _load_pkg()
@@ -644,7 +647,8 @@ def main():
         achieved = CONFIG0_BYTES / (gemv_ms * 1e-3) / 1e9
         grec = traffic_record("gemv_q6k_config0") or {}
         line["gemv_config0"] = {
-            "kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches in a CUDA graph",
+            "kernel": "drop-in gemv_q6k 4096x4096 (config 0), back-to-back launches in a CUDA graph: "
+                      "gemv_q6k_reg_kernel (stream-ordered launch); gemv_stream_kernel under PDL",
             "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
             "traffic": grec.get("bytes_per_launch"), "us_per_launch": round(gemv_ms * 1e3, 3),
             "us_per_launch_pdl": round(gemv_ms_pdl * 1e3, 3), "algorithmic_bytes_per_launch": CONFIG0_BYTES}
