@@ -218,9 +218,10 @@ extern "C" int fence_set_launch_flags(int flags) {
 }
 
 // Plan of the register-resident Q6_K GEMV (gemv_q6k_reg_kernel): rows of 16-byte multiple length
-// (K % 2048 == 0), K <= 4096 (one 64-element item per lane), rows split over one CTA per SM, each
-// CTA's rows in up to 4 chunk slots that fit half an SM's shared memory (so the next GEMV's CTA sits
-// beside it and loads its weights early); ok = 0 otherwise.
+// (K % 2048 == 0), K <= 4096 (one 64-element item per lane), rows split over one CTA per SM. A chunk
+// holds one row per row group of the consumers (GQ_NW warps, one or two per row), so each chunk is
+// one item dot per lane with no group idle; chunk slots fill half an SM's shared memory at most
+// (every chunk of a config-0 CTA in flight at once); ok = 0 otherwise.
 struct GQPlan {
     int ok = 0, grid = 0, rows_cta = 0, RC = 0, slots = 0, slot_bytes = 0, smem = 0;
 };
@@ -233,12 +234,13 @@ static GQPlan plan_q6k_reg(int M, int K) {
     const int sms = device_sms(dev);
     p.rows_cta = (M + sms - 1) / sms;
     p.grid = (M + p.rows_cta - 1) / p.rows_cta;
-    const int budget = std::min(device_smem_optin(dev) - 1024, 112 * 1024);
+    const int budget = device_smem_optin(dev) - 1024;
     const int fixed = I * XQ_WORDS * 4 + (2 * p.rows_cta + 2) * 4 + 8 + 2 * GQ_MAX_SLOTS * 8 + 16 + 64;
     const int avail = budget - fixed;
-    if (avail < 4 * rowB) return p;
-    p.RC = std::max(1, std::min((p.rows_cta + 3) / 4, avail / 4 / rowB));
-    p.slots = std::min(4, (p.rows_cta + p.RC - 1) / p.RC);
+    const int NG = GQ_NW / (I > 32 ? 2 : 1);  // row groups working at once
+    p.RC = std::min(NG, p.rows_cta);
+    if (avail < 2 * p.RC * rowB) return p;
+    p.slots = std::min(std::min(GQ_MAX_SLOTS, (p.rows_cta + p.RC - 1) / p.RC), avail / (p.RC * rowB));
     p.slot_bytes = (p.RC * rowB + 127) / 128 * 128;
     p.smem = p.slots * p.slot_bytes + fixed;
     if (p.smem > budget) return p;
@@ -253,7 +255,7 @@ static cudaError_t launch_q6k_reg(const GQArgs& a, const GQPlan& pl, cudaStream_
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     if (!attr_set[dev]) {
         const cudaError_t e =
-            cudaFuncSetAttribute(gemv_q6k_reg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+            cudaFuncSetAttribute(gemv_q6k_reg_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, device_smem_optin(dev));
         if (e != cudaSuccess) return e;
         attr_set[dev] = 1;
     }
@@ -277,8 +279,9 @@ static int gemv_q6k_common(const block_q6_K* W, const uint16_t* x, const float* 
         return set_error(FENCE_E_ARG, "gemv_q6k: need non-null pointers, M > 0, K %% 256 == 0 (M=%d K=%d)", M, K);
     const bool aligned = (reinterpret_cast<uintptr_t>(W) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     // Stream-ordered launches take the register-resident kernel (config 0, 4096 x 4096, back to back
-    // in a CUDA graph on a B200: 8.4 us per launch against the streaming kernel's 10.0); launches
-    // chained by programmatic dependent launch take the streaming kernel (8.2 us against 8.7).
+    // in a CUDA graph on a B200: 6.7 us per launch against the streaming kernel's 10.0); launches
+    // chained by programmatic dependent launch take the streaming kernel, whose two CTAs per SM let
+    // the next launch stream its weights beside the previous one (8.2 us).
     const bool pdl = (g_launch_flags & FENCE_LAUNCH_PDL) != 0;
     const GQPlan gq = pdl ? GQPlan{} : plan_q6k_reg(M, K);
     if (aligned && gq.ok) {

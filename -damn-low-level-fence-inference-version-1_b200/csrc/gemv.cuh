@@ -810,7 +810,7 @@ __global__ void __launch_bounds__(GEMV_MAX_NT, 2) gemv_stream_kernel(const __gri
 // worked on by LPR lanes (one item each: 64 lanes for K > 2048, else 32), so a row costs one item
 // dot per lane and one shuffle reduction per warp, with no x reloads; the two warps' pieces of a
 // row are summed in a fixed order at the end (deterministic). Consumer warps: GQ_NW.
-constexpr int GQ_NW = 12;
+constexpr int GQ_NW = 16;
 constexpr int GQ_NT = GQ_NW * 32 + 32;
 constexpr int GQ_MAX_SLOTS = 8;
 
@@ -827,7 +827,7 @@ struct GQArgs {
 
 __host__ __device__ inline uint32_t gq_xrec_off(int slots, int slot_bytes) { return (uint32_t)(slots * slot_bytes); }
 
-__global__ void __launch_bounds__(GQ_NT, 2) gemv_q6k_reg_kernel(const __grid_constant__ GQArgs a) {
+__global__ void __launch_bounds__(GQ_NT, 1) gemv_q6k_reg_kernel(const __grid_constant__ GQArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NTC = GQ_NW * 32;
