@@ -435,7 +435,12 @@ class Tokenizer:
         """One multi-turn helper (TURN_*) appended to tokens; returns the new list."""
         c = None if content is None else _b(content)
         cap = len(tokens) + 64 + (4 * len(c) if c else 0)
-        buf = (ctypes.c_int * cap)(*tokens)
-        n = ctypes.c_int(len(tokens))
-        check(lib().fence_chat_append(self._h, turn, c, buf, cap, ctypes.byref(n)), "chat_append")
-        return list(buf[:n.value])
+        while True:  # a buffer too small leaves the conversation unchanged and reports the size needed
+            buf = (ctypes.c_int * cap)(*tokens)
+            n = ctypes.c_int(len(tokens))
+            rc = lib().fence_chat_append(self._h, turn, c, buf, cap, ctypes.byref(n))
+            if rc == 0:
+                return list(buf[:n.value])
+            if n.value <= cap:
+                check(rc, "chat_append")
+            cap = n.value

@@ -424,6 +424,10 @@ extern "C" int fence_chat_append(fence_tokenizer* t, int turn, const char* conte
         return set_error(FENCE_E_ARG, "chat_append: null content");
     const size_t n0 = (size_t)*n_inout;
     std::vector<int> ids(tokens, tokens + n0);
+    // the conversation state a turn may change (a LLaMA-2 / Mistral system prompt held for the first
+    // user turn), restored when the ids do not fit, so the caller can retry with a larger buffer
+    const std::string held = t->pending_system;
+    const bool held_used = t->system_used;
     switch (turn) {
         case FENCE_TURN_BEGIN: t->begin(ids); break;
         case FENCE_TURN_SYSTEM: t->system_turn(ids, content); break;
@@ -432,5 +436,10 @@ extern "C" int fence_chat_append(fence_tokenizer* t, int turn, const char* conte
         case FENCE_TURN_END: t->turn_end(ids); break;
         default: return set_error(FENCE_E_ARG, "chat_append: unknown turn %d", turn);
     }
-    return emit(ids, n0, tokens, cap, n_inout);
+    const int rc = emit(ids, n0, tokens, cap, n_inout);
+    if (rc != FENCE_OK) {
+        t->pending_system = held;
+        t->system_used = held_used;
+    }
+    return rc;
 }

@@ -393,7 +393,9 @@ int fence_format_chat(fence_tokenizer* t, const char* system_prompt, const char*
  * append_assistant_header / append_turn_end (tokenizer.cpp:478-627): appends the turn's ids to
  * tokens[0 .. *n_inout) (capacity cap) and updates *n_inout. content is used by SYSTEM and USER.
  * As in the reference, a LLaMA-2 / Mistral system prompt is held in the tokenizer until the first
- * user turn, so a tokenizer carries one conversation at a time (not thread safe). */
+ * user turn, so a tokenizer carries one conversation at a time (not thread safe). When the ids do
+ * not fit cap, the call returns FENCE_E_ARG with the total needed in *n_inout and leaves tokens and
+ * the conversation state as they were: call again with a larger buffer and the original count. */
 #define FENCE_TURN_BEGIN     0
 #define FENCE_TURN_SYSTEM    1
 #define FENCE_TURN_USER      2

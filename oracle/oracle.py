@@ -116,6 +116,8 @@ def ref_tok() -> ctypes.CDLL | None:
         L.ref_tok_format_chat.argtypes = [_vp, ctypes.c_char_p, ctypes.c_char_p, _vp, ctypes.c_int]
         L.ref_tok_append.restype = ctypes.c_int
         L.ref_tok_append.argtypes = [_vp, ctypes.c_int, ctypes.c_char_p, _vp, ctypes.c_int, ctypes.c_int]
+        L.ref_tok_last.restype = ctypes.c_int
+        L.ref_tok_last.argtypes = [_vp, ctypes.c_int]
         _rt = L
     return _rt
 
@@ -156,6 +158,9 @@ class RefTokenizer:
         buf = np.zeros(4096, np.int32)
         b = [x if isinstance(x, bytes) else x.encode("utf-8") for x in (system_prompt, user_message)]
         n = self._L.ref_tok_format_chat(self._h, b[0], b[1], buf.ctypes.data, 4096)
+        if n > 4096:
+            buf = np.zeros(n, np.int32)
+            self._L.ref_tok_last(buf.ctypes.data, n)
         return [int(x) for x in buf[:n]]
 
     def append(self, tokens: list, turn: int, content=None) -> list:
@@ -164,6 +169,9 @@ class RefTokenizer:
         buf = np.zeros(cap, np.int32)
         buf[:len(tokens)] = tokens
         n = self._L.ref_tok_append(self._h, turn, c, buf.ctypes.data, len(tokens), cap)
+        if n > cap:  # a held system prompt came out with this turn: the whole result, not a second call
+            buf = np.zeros(n, np.int32)
+            self._L.ref_tok_last(buf.ctypes.data, n)
         return [int(x) for x in buf[:n]]
 
 

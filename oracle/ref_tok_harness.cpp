@@ -9,7 +9,11 @@
 #include "tokenizer/tokenizer.h"
 
 namespace {
+// the last id list a call produced, whole, for ref_tok_last (a caller whose buffer was too small
+// fetches it there instead of calling again: the turn helpers change the tokenizer's state)
+thread_local std::vector<int> g_last;
 int copy_ids(const std::vector<int>& v, int* out, int cap) {
+    g_last = v;
     for (int i = 0; i < (int)v.size() && i < cap; ++i) out[i] = v[i];
     return (int)v.size();
 }
@@ -58,5 +62,10 @@ int ref_tok_append(void* h, int turn, const char* content, int* tokens, int n, i
         default: t->append_turn_end(v); break;
     }
     return copy_ids(v, tokens, cap);
+}
+// copies the last call's ids (up to cap) and returns their count
+int ref_tok_last(int* out, int cap) {
+    for (int i = 0; i < (int)g_last.size() && i < cap; ++i) out[i] = g_last[i];
+    return (int)g_last.size();
 }
 }

@@ -111,3 +111,48 @@ def test_load_rejects_a_file_without_tokens(fb, tmp_path):
     tv.write_gguf(p, [], [], {"general.architecture": "qwen3"})
     with pytest.raises(fb.FenceError, match="tokenizer"):
         fb.Tokenizer(p)
+
+
+@pytest.mark.parametrize("name", ["llama2", "chatml"])
+def test_chat_append_small_buffer_keeps_the_conversation(fb, vocab_files, name):
+    """fence_chat_append with a buffer too small reports the total needed and changes neither the
+    caller's ids nor the conversation (a LLaMA-2 system prompt held for the first user turn stays
+    held), so a retry with the reported size gives the ids of an uninterrupted conversation."""
+    import ctypes
+    L = fb.lib()
+    path = vocab_files[name][0]
+    user = "a user message long enough to need many ids " * 4
+    ref = fb.Tokenizer(path)
+    want = ref.append(ref.append(ref.append([], fb.TURN_BEGIN), fb.TURN_SYSTEM, "be brief"), fb.TURN_USER, user)
+    ref.close()
+    t = fb.Tokenizer(path)
+    h = t.append(t.append([], fb.TURN_BEGIN), fb.TURN_SYSTEM, "be brief")
+    cap = len(h) + 2
+    buf = (ctypes.c_int * cap)(*h)
+    n = ctypes.c_int(len(h))
+    rc = L.fence_chat_append(t._h, fb.TURN_USER, user.encode(), buf, cap, ctypes.byref(n))
+    assert rc == -1 and n.value == len(want) and list(buf[:len(h)]) == h
+    buf = (ctypes.c_int * n.value)(*h)
+    need, n = n.value, ctypes.c_int(len(h))
+    assert L.fence_chat_append(t._h, fb.TURN_USER, user.encode(), buf, need, ctypes.byref(n)) == 0
+    assert list(buf[:n.value]) == want
+    t.close()
+
+
+def test_chat_append_grows_its_buffer(fb, orc, vocab_files):
+    """A LLaMA-2 system prompt is held until the first user turn and emitted with it, so a short user
+    turn can need far more ids than its own text: the Python helper retries with the size the C
+    call reports."""
+    path = vocab_files["llama2"][0]
+    system = "a long system prompt for the whole conversation " * 6
+    t = fb.Tokenizer(path)
+    h = t.append(t.append(t.append([], fb.TURN_BEGIN), fb.TURN_SYSTEM, system), fb.TURN_USER, "hi")
+    assert len(h) > 64 + 4 * len("hi") + 1  # more than the helper's first buffer
+    h = t.append(h, fb.TURN_ASSISTANT)
+    t.close()
+    if orc.ref_tok() is not None:
+        r = orc.RefTokenizer(path)
+        want = r.append(r.append(r.append(r.append([], fb.TURN_BEGIN), fb.TURN_SYSTEM, system), fb.TURN_USER, "hi"),
+                        fb.TURN_ASSISTANT)
+        r.close()
+        assert h == want
