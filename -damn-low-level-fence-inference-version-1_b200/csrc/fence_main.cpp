@@ -211,10 +211,16 @@ int main(int argc, char** argv) {
     printf("Type your message (empty line to quit).\n\n");
     std::vector<int> history;
     auto append = [&](int turn, const char* content) {
-        int n = (int)history.size();
+        const int n0 = (int)history.size();
         history.resize(history.size() + 4096 + (content ? 4 * strlen(content) : 0));
-        const int rc = fence_chat_append(tok, turn, content, history.data(), (int)history.size(), &n);
-        history.resize(rc == 0 ? n : 0);
+        int n = n0;
+        int rc = fence_chat_append(tok, turn, content, history.data(), (int)history.size(), &n);
+        if (rc != 0 && n > (int)history.size()) {  // too small (a long held system prompt): retry at the size needed
+            history.resize(n);
+            n = n0;
+            rc = fence_chat_append(tok, turn, content, history.data(), (int)history.size(), &n);
+        }
+        history.resize(rc == 0 ? n : n0);
         return rc == 0;
     };
     auto start = [&]() {
