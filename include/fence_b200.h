@@ -278,10 +278,11 @@ int fence_set_seed(fence_model* m, uint64_t seed);
  * scratch. */
 int fence_sample_nucleus_device(fence_model* m, const float* d_logits, const int* history, int n_history);
 
-/* Qwen3Model::generate (qwen3.cu:463-519): token-by-token prefill of `prompt`, then up to
- * max_new_tokens sampled tokens, stopping at eos_id (pass -1 for no stop token) or max_ctx.
- * out receives prompt + generated ids (capacity out_cap); *n_out their count. Every token crosses
- * to the host, as in the reference. */
+/* Qwen3Model::generate (qwen3.cu:463-519): prefill of `prompt` (all but its last token batched on
+ * the tensor cores, fence_prefill, where the model allows it; else token by token as in the
+ * reference), then up to max_new_tokens sampled tokens, stopping at eos_id (pass -1 for no stop
+ * token) or max_ctx. out receives prompt + generated ids (capacity out_cap); *n_out their count.
+ * Every sampled token crosses to the host, as in the reference. */
 int fence_generate(fence_model* m, const int* prompt, int n_prompt, int max_new_tokens,
                    int eos_id, int* out, int out_cap, int* n_out);
 
