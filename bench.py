@@ -12,7 +12,8 @@ copies of the config (weak scaling, no data-path collective).
 
 A step is one decode token (batch 1). Inputs are synthetic: a seeded random-init GGUF with the
 config's exact shapes and weight distributions (no checkpoints exist offline); the prompt is
-uniform-random token ids, prefilled token by token (untimed). The timed region is K device-resident
+uniform-random token ids, prefilled through fence_prefill (batched on the tensor cores where the
+model allows it, else token by token; untimed for the decode value). The timed region is K device-resident
 decode steps (one step-kernel launch each, CUDA events on the engine's stream), bracketed by a
 barrier and synchronisations; it is repeated R times at the same positions (R chosen so the timed
 regions span >= 1.5 s for the clock samples) and the median repeat, max over ranks, is reported.
@@ -166,7 +167,8 @@ def shm_dir(need_bytes):
 # ------------------------------------------------------------------ GPU decode measurement
 def measure_decode(fb, torch, model, prompt_len, steps, warmup, repeats, dist=None, tp=False, seed=7,
                    e2e_steps=None, clocks_index=None):
-    """Prefill (untimed, token by token as the reference), W warm-up steps, then R timed regions of
+    """Prefill through fence_prefill (untimed for the decode value; its own rate is reported), W
+    warm-up steps, then R timed regions of
     K device-resident decode steps at the same positions; e2e through fence_forward +
     fence_sample_greedy from the host. Returns a dict (times max over ranks)."""
     cfg = model.config
