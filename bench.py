@@ -168,8 +168,8 @@ def shm_dir(need_bytes):
 def measure_decode(fb, torch, model, prompt_len, steps, warmup, repeats, dist=None, tp=False, seed=7,
                    e2e_steps=None, clocks_index=None):
     """Prefill through fence_prefill (untimed for the decode value; its own rate is reported), W
-    warm-up steps, then R timed regions of
-    K device-resident decode steps at the same positions; e2e through fence_forward +
+    warm-up steps, then R timed regions of K device-resident decode steps at the same positions;
+    e2e through fence_forward +
     fence_sample_greedy from the host. Returns a dict (times max over ranks)."""
     cfg = model.config
     rng = np.random.default_rng(seed)
