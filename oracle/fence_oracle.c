@@ -699,6 +699,18 @@ static void moe_ffn(oracle_model* m, int l) {
     }
 }
 
+/* Test hook: moe_ffn of layer l (the function every MoE forward above runs) on a given normed
+ * input; out[H] = the block's output before the residual add, sel[n_used] = the chosen experts.
+ * Lets the tests set the oracle's MoE block beside a published implementation on the same input. */
+int oracle_moe_ffn_apply(oracle_model* m, int l, const float* normed, float* out, int* sel) {
+    if (!m || l < 0 || l >= m->L || m->n_exp <= 0 || !normed || !out) return -1;
+    memcpy(m->normed, normed, (size_t)m->H * 4);
+    moe_ffn(m, l);
+    memcpy(out, m->moe_out, (size_t)m->H * 4);
+    if (sel) memcpy(sel, m->last_sel + (size_t)l * m->n_used, (size_t)m->n_used * sizeof(int));
+    return 0;
+}
+
 int oracle_forward(oracle_model* m, int token, int pos, float* logits) {
     if (token < 0 || token >= m->V || pos < 0 || pos >= m->max_ctx) return -1;
     const int H = m->H, F = m->F, hd = m->hd, nh = m->nh, nkv = m->nkv;

@@ -87,6 +87,9 @@ void oracle_model_moe(const oracle_model* m, int* n_exp, int* n_used);
 float oracle_last_route(const oracle_model* m, int* sel);
 /* Hidden state after the final norm of the last forward (embed_dim floats). */
 void oracle_last_hidden(const oracle_model* m, float* out);
+/* Test hook: the sparse-MoE FFN of layer l on a given normed input (out[H] before the residual add,
+ * sel[n_used] the chosen experts); 0 on success. */
+int oracle_moe_ffn_apply(oracle_model* m, int l, const float* normed, float* out, int* sel);
 
 #ifdef __cplusplus
 }

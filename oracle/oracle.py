@@ -62,6 +62,7 @@ def oracle() -> ctypes.CDLL:
             "oracle_model_fill_kv": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_uint64]),
             "oracle_model_moe": (None, [_vp, _vp, _vp]),
             "oracle_last_route": (ctypes.c_float, [_vp, _vp]),
+            "oracle_moe_ffn_apply": (ctypes.c_int, [_vp, ctypes.c_int, _vp, _vp, _vp]),
         }
         for n, (res, args) in sig.items():
             f = getattr(L, n)
@@ -249,6 +250,16 @@ class OracleModel:
         sel = np.zeros((self.n_layers, max(1, self.n_experts_used)), dtype=np.int32)
         margin = oracle().oracle_last_route(self._h, _p(sel))
         return sel, float(margin)
+
+    def moe_ffn(self, layer: int, normed: np.ndarray):
+        """The oracle's sparse-MoE FFN of one layer on a given normed input: (output [H] before the
+        residual add, chosen experts [n_used])."""
+        x = np.ascontiguousarray(normed, dtype=np.float32)
+        out = np.empty(self.embed_dim, dtype=np.float32)
+        sel = np.zeros(max(1, self.n_experts_used), dtype=np.int32)
+        if oracle().oracle_moe_ffn_apply(self._h, layer, _p(x), _p(out), _p(sel)) != 0:
+            raise ValueError("moe_ffn: not a MoE model or bad layer")
+        return out, sel
 
     def fill_kv(self, n_pos: int, seed: int = 1) -> None:
         """Seeded K/V rows for positions [0, n_pos): stands in for a prefill (benchmark use)."""
