@@ -661,7 +661,9 @@ static size_t o_row_bytes(int type, int K) { return type == 14 ? (size_t)K / 256
  * (ties to the smaller expert index), weights softmax over the chosen logits (the same as the
  * full softmax renormalised over them), and out = sum_s w_s * down_e(SwiGLU(gate_e x, up_e x)),
  * each expert's linears exactly the dense FFN's (qwen3.cu:317-341: fp16-rounded inputs for Q6_K).
- * Parity unpinned: no reference fixture exists for it. */
+ * No reference fixture exists for it (the reference has no expert tensors); tests/test_moe_hf_pin.py
+ * pins it to the Mixtral sparse-MoE block of Hugging Face transformers, run in float64 on the same
+ * dequantised weights. */
 static void moe_ffn(oracle_model* m, int l) {
     const __typeof__(m->layer[0])* w = &m->layer[l];
     const int H = m->H, F = m->F, E = m->n_exp, K = m->n_used;

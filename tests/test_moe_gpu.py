@@ -1,6 +1,7 @@
 """Sparse mixture-of-experts decode (config 4's Mixtral shape; the reference has no expert tensors,
 so the checker is the CPU oracle's restatement of Mixtral routing over the reference's per-op math,
-oracle/fence_oracle.c moe_ffn: parity unpinned by reference fixtures).
+oracle/fence_oracle.c moe_ffn, itself pinned to transformers' Mixtral sparse-MoE block by
+tests/test_moe_hf_pin.py).
 
 One GPU: the step kernel routes in every CTA (fp32 router, top-k, softmax over the chosen logits)
 and streams only the routed experts' tiles. Tensor parallel: every rank holds a slice of every
