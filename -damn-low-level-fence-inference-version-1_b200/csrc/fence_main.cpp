@@ -52,16 +52,17 @@ std::string detok(const fence_tokenizer* t, int id) {
     return big;
 }
 
-// Qwen3Model::generate (qwen3.cu:463-519): token-by-token prefill of the whole history, then sample
-// (nucleus, the CLI's parameters), stop at eos or max_ctx, stream each new token's text. Returns
-// the history plus the reply (without eos), or an empty vector on an engine error.
+// Qwen3Model::generate (qwen3.cu:463-519): prefill of the whole history (fence_prefill: batched on
+// the tensor cores where the model allows it, as fence_generate does; the reference runs it token
+// by token), then sample (nucleus, the CLI's parameters), stop at eos or max_ctx, stream each new
+// token's text. Returns the history plus the reply (without eos), or an empty vector on an engine
+// error.
 std::vector<int> generate(fence_model* m, const fence_tokenizer* tok, const std::vector<int>& prompt, int max_new,
                           int eos, int max_ctx, bool debug) {
     std::vector<int> out(prompt);
     const auto t0 = std::chrono::steady_clock::now();
-    const float* logits = nullptr;
-    for (int i = 0; i < (int)prompt.size(); ++i)
-        if (!(logits = fence_forward(m, prompt[i], i))) return {};
+    const float* logits = fence_prefill(m, prompt.data(), (int)prompt.size(), 0);
+    if (!logits) return {};
     const auto t1 = std::chrono::steady_clock::now();
     const double pre_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
     printf("[prefill %zu tokens in %.0f ms (%.1f tok/s)]\n", prompt.size(), pre_ms, prompt.size() / (pre_ms / 1e3));
